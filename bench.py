@@ -1,0 +1,431 @@
+"""Benchmark of the MoE expert hot path on B200 -- one JSON line on rank 0.
+
+Workload (the OLMoE-1B-7B-shaped decode): the model's 16
+MoE layers (hidden 2048, 64 experts, top-8, SwiGLU intermediate 1024, MLX affine
+4-bit g64 with fp16 scales/biases, router N(0, 0.02) bf16 plus a per-expert
+N(0, 1) bias), batch-1 greedy-decode shape, each layer's expert pool capped at 16
+of 64 experts in HBM and refilled from pinned host DRAM on a side stream (LFUDA).
+A step is one token through all 16 MoE layers: router logits, warp-shuffle top-k
++ softmax, the pool's ensure (host readback of the routing, as the reference's),
+the fused dequantising GEMVs and the combine, plus the residual add.  Attention,
+embeddings and the LM head are not part of the hot path and are not run.  Inputs
+are seeded synthetic token embeddings, N(0, 1) bf16 -- no dataset exists here.
+
+Also reported (outside the K timed steps): the 2048-token prompt through the
+capped stack in layer-major order (prefill tok/s), the same decode with every
+expert resident (sync-free, one CUDA graph per token: the MoE-layer HBM GB/s and
+its fraction of the measured peak), and the CPU restatement's throughput.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Multi-GPU: one process per GPU under torchrun; every rank decodes its own token
+stream on its own copy of the layers (independent sequences, no data-path
+collective), the timed region is bracketed by barriers and the slowest rank's
+time is the job's.  value = tokens of all ranks / that time ("weak" scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = {"workload": "olmoe-1b-7b MoE stack decode, B=1, pool 16/64 per layer refilled from "
+                   "pinned host", "layers": 16, "hidden": 2048, "inter": 1024, "experts": 64,
+       "top_k": 8, "bits": 4, "group_size": 64, "scale_dtype": "float16", "capacity": 16,
+       "policy": "lfuda", "prompt": 2048, "prefill_chunk": 512, "family": "olmoe"}
+METRIC = "decode tok/s (MoE layers of an OLMoE-1B-7B-shaped model, pool 16/64)"
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampling every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = vis.split(",")[self.idx] if vis else str(self.idx)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={phys}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, IndexError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.remove(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ model
+def build_model(device, seed: int):
+    from bigrig_b200.block import fill_store, make_blocks
+    from bigrig_b200.fetch import HostExpertStore
+    from bigrig_b200.formats import bytes_per_expert, make_spec
+    c = CFG
+    blocks = make_blocks(c["layers"], c["hidden"], c["inter"], c["experts"], c["top_k"],
+                         c["family"], c["bits"], c["group_size"], c["scale_dtype"], True,
+                         seed=seed, device=device)
+    spec = make_spec(c["hidden"], c["inter"], c["bits"], c["group_size"], c["scale_dtype"])
+    store = HostExpertStore({li: (c["experts"], bytes_per_expert(spec)) for li in range(c["layers"])})
+    fill_store(store, c["layers"], c["hidden"], c["inter"], c["experts"], c["bits"],
+               c["group_size"], c["scale_dtype"], seed=seed + 1, device=device)
+    torch.cuda.synchronize(device)
+    return blocks, store
+
+
+def stack_step(blocks, x):
+    h = x
+    for blk in blocks:
+        h = h + blk(h)
+    return h
+
+
+def algorithmic_layer_bytes(T: int, distinct: int) -> int:
+    """Decode MoE layer bytes: U * bytes_per_expert + router E*H*2 + x in / y out."""
+    c = CFG
+    from bigrig_b200.formats import bytes_per_expert, make_spec
+    bpe = bytes_per_expert(make_spec(c["hidden"], c["inter"], c["bits"], c["group_size"],
+                                     c["scale_dtype"]))
+    return distinct * bpe + c["experts"] * c["hidden"] * 2 + T * c["hidden"] * 2 * 2
+
+
+def gate_up_bytes(T: int, distinct: int) -> int:
+    """Algorithmic bytes of one gemv_gate_up launch: the routed experts' gate and up codes,
+    scales and biases, the x rows in and the h rows out."""
+    c = CFG
+    H, I = c["hidden"], c["inter"]
+    per = 2 * (I * H * c["bits"] // 8 + 2 * I * (H // c["group_size"]) * 2)
+    return distinct * per + T * H * 2 + T * c["top_k"] * I * 2
+
+
+# ------------------------------------------------------------------ CPU restatement
+def cpu_decode_tokens(store, blocks_host, n_tokens: int, n_layers: int, threads: int, seed: int,
+                      first_layer: int = 0):
+    """Seconds per token of the numpy restatement over ``n_layers`` layers starting at
+    ``first_layer`` (a bounded sample of the workload)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from bigrig_b200.formats import make_spec, unpack_expert
+    from oracle import affine, moe, router
+    c = CFG
+    spec = make_spec(c["hidden"], c["inter"], c["bits"], c["group_size"], c["scale_dtype"])
+    rng = np.random.default_rng(seed)
+    pool = ThreadPoolExecutor(max_workers=threads)
+
+    def expert_w(li, e):
+        a = unpack_expert(store.layers[li][e].numpy(), spec)
+        return {p: affine.dequantize_f32(a[p]["weight"], a[p]["scales"], a[p]["biases"],
+                                         c["group_size"], c["bits"], c["scale_dtype"])
+                for p in moe.PROJ}
+
+    t0 = time.perf_counter()
+    for _ in range(n_tokens):
+        h = affine.bf16_round(rng.standard_normal((1, c["hidden"])).astype(np.float32))
+        for li in range(first_layer, first_layer + n_layers):
+            gw, gb = blocks_host[li]
+            lg = router.router_logits(h, gw, gb)
+            idx, sc = router.topk(lg, c["top_k"], "softmax_topk", False)
+            ws = list(pool.map(lambda e: expert_w(li, int(e)), idx[0]))
+            y = np.stack([moe.expert_forward(h, w) for w in ws])[None]
+            h = affine.bf16_round(h + moe.combine(y, sc))
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    return dt / n_tokens
+
+
+def _host_router(blocks):
+    return [(b.gate_w.float().cpu().numpy(), b.gate_b.float().cpu().numpy()) for b in blocks]
+
+
+def run_reference(args) -> None:
+    """The reference arm: the CPU restatement of the same workload on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    c = CFG
+    # weights are generated with the same seeded GPU quantiser when a GPU exists, else on CPU
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    blocks, store = build_model(dev, seed=0)
+    host = _host_router(blocks)
+    # one step = one token through ONE MoE layer (a bounded 1/16 sample of a token)
+    per_layer = []
+    for i in range(args.warmup + args.steps):
+        dt = cpu_decode_tokens(store, host, 1, 1, threads, seed=i, first_layer=i % c["layers"])
+        if i >= args.warmup:
+            per_layer.append(dt)
+    sec_per_token = statistics.mean(per_layer) * c["layers"]
+    v = 1.0 / sec_per_token
+    line = {"metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(per_layer) * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes, fp32 math",
+            "data": "synthetic", "config": {k: CFG[k] for k in ("workload", "layers", "hidden", "inter", "experts", "top_k", "bits")},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": "each step: one token through one of the 16 MoE layers "
+                                       "(numpy restatement, all experts resident in host RAM); "
+                                       "tok/s = 1 / (16 x mean layer time)"},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ the B200 arm
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="decode only (for profiling)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    from bigrig_b200 import _lib, layered, ops
+    from bigrig_b200.stream import attach
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    _lib.load(build_if_stale=False)
+    c = CFG
+    blocks, store = build_model(dev, seed=0)
+    handle = attach(blocks, store, c["capacity"], policy=c["policy"], warm="auto", device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    W, K = args.warmup, args.steps
+    tokens = torch.randn(W + K, 1, c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    extras = {}
+    # ---- prefill: the 2048-token prompt, layer-major, through the capped pools
+    if not args.no_extras:
+        prompt = torch.randn(c["prompt"], c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+        layers = [(lambda h, b=b: h + b(h)) for b in blocks]
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        layered.prefill(layers, layered.chunks(prompt, c["prefill_chunk"]),
+                        layer_scope=handle.prefill_layer)
+        e1.record()
+        barrier()
+        pf_ms = max_over_ranks(e0.elapsed_time(e1))
+        extras["prefill_tok_s"] = world * c["prompt"] / (pf_ms / 1e3)
+        extras["prefill_note"] = ("capped pools, expert-sorted spans of <= 16 experts, GEMV path "
+                                  "(the tcgen05 grouped GEMM is not in this build yet)")
+        handle.reset_stats()
+
+    # ---- decode, capped pool: warm-up then K timed steps
+    for i in range(W):
+        stack_step(blocks, tokens[i])
+    handle.reset_stats()
+    barrier()
+    counts0 = _lib.launch_counts()
+    _lib.timing_enable(["gate_up"])
+    clocks = Clocks(local)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(K):
+        stack_step(blocks, tokens[W + i])
+    t1.record()
+    barrier()
+    clk = clocks.stop()
+    _lib.timing_enable([])
+    counts1 = _lib.launch_counts()
+    gu_ms, gu_n = _lib.timing_read("gate_up")
+    ms = max_over_ranks(t0.elapsed_time(t1))
+    value = world * K / (ms / 1e3)
+    st = handle.stats()
+    launches = sum(counts1[k] - counts0[k] for k in counts1)
+
+    # ---- e2e through the public API with host buffers: pinned in, result read back
+    hbuf = tokens.cpu().pin_memory()
+    outbuf = torch.empty(1, c["hidden"], dtype=torch.bfloat16).pin_memory()
+    barrier()
+    w0 = time.perf_counter()
+    for i in range(K):
+        x = hbuf[W + i].to(dev, non_blocking=True)
+        y = stack_step(blocks, x)
+        outbuf.copy_(y, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - w0)
+    e2e = {"value": world * K / e2e_s, "unit": "tok/s",
+           "h2d_bytes_per_step": c["hidden"] * 2, "d2h_bytes_per_step": c["hidden"] * 2,
+           "note": "per step: token embedding copied from pinned host, 16 MoE layers, result "
+                   "read back; misses copied from pinned host inside the step"}
+
+    # ---- resident (sync-free) decode in one CUDA graph per token
+    if not args.no_extras:
+        handle = None                    # its pools' slabs are freed once the blocks let go
+        res = attach(blocks, store, c["experts"], policy=c["policy"], warm="auto", device=dev)
+        ws = ops.default_workspace(dev)
+        L0 = res.pools[0].layout
+        ws.reserve(ops.workspace_bytes(1, c["top_k"], c["experts"], L0))
+        for p in res.pools:
+            p.g2s_device()
+            p.settle()
+        xin = tokens[0].clone()
+        for i in range(3):
+            stack_step(blocks, xin)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                stack_step(blocks, xin)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        with torch.cuda.graph(graph):
+            yout = stack_step(blocks, xin)
+        for i in range(W):
+            xin.copy_(tokens[i])
+            graph.replay()
+        barrier()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for i in range(K):
+            xin.copy_(tokens[W + i])
+            graph.replay()
+        r1.record()
+        barrier()
+        rms = max_over_ranks(r0.elapsed_time(r1))
+        res_tok_s = K / (rms / 1e3)
+        layer_bytes = algorithmic_layer_bytes(1, c["top_k"])
+        hbm_peak, _, peak_kind = _peaks()
+        extras["resident_decode_tok_s"] = world * res_tok_s
+        extras["moe_layer_hbm_gbs"] = layer_bytes * c["layers"] * res_tok_s / 1e9
+        extras["moe_layer_hbm_frac"] = extras["moe_layer_hbm_gbs"] / hbm_peak
+        extras["moe_layer_bytes"] = layer_bytes
+        extras["resident_ms_per_token"] = rms / K
+        del graph, yout
+
+    # ---- CPU restatement on rank 0 at N=1 (bounded sample)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        per_tok = cpu_decode_tokens(store, _host_router(blocks), 2, c["layers"], threads, seed=7)
+        cpu = {"value": 1.0 / per_tok, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": "2 decode tokens through all 16 MoE layers, numpy restatement "
+                         "(dequantise the 8 routed experts per layer, fp32 math)"}
+
+    hbm_peak, _, peak_kind = _peaks()
+    gu_avg_ms = gu_ms / max(1, gu_n)
+    gu_bytes = gate_up_bytes(1, c["top_k"])
+    achieved = gu_bytes / (gu_avg_ms / 1e3) / 1e9 if gu_n else None
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.txt")
+    if os.path.exists(tpath):
+        for line in open(tpath):
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == "gemv_gate_up_kernel":
+                traffic = int(float(parts[1]))
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 activations, u4 affine codes, fp32 accumulate",
+            "data": "synthetic: N(0,1) bf16 token embeddings, N(0,0.02) experts quantised to "
+                    "MLX affine 4-bit g64, router bias N(0,1); random init",
+            "config": {**{k: c[k] for k in ("workload", "layers", "hidden", "inter", "experts",
+                                            "top_k", "bits", "group_size", "capacity", "policy")},
+                       "global_batch": world, "parallelism": f"replicas x{world}",
+                       "l2": "decode reads 28 MB of experts per layer, 453 MB per token; no flush"},
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "launches_by_kernel": {k: counts1[k] - counts0[k] for k in counts1},
+            "roofline": {"kernel": "gemv_gate_up_kernel", "bound": "hbm", "achieved": achieved,
+                         "peak": hbm_peak, "unit": "GB/s",
+                         "frac": (achieved / hbm_peak) if achieved else None,
+                         "peak_kind": peak_kind, "traffic": traffic,
+                         "bytes_per_launch": gu_bytes, "avg_launch_ms": gu_avg_ms,
+                         "timed_launches": gu_n},
+            "pool": {"miss_rate": st["miss_rate"], "hits": st["hits"], "misses": st["misses"],
+                     "admit_gb": st["admit_gb"], "sync_seconds": st["sync_seconds"]},
+            "clocks": clk,
+            "cpu_baseline": cpu,
+            **extras,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,148 @@
+"""ctypes binding of libbigrig_b200.so, the C-ABI library declared in include/bigrig_b200.h.
+
+There is no fallback: if the library is missing or fails to load, every compute
+entry point raises.  ``load()`` builds it first when the CUDA sources are newer
+than the library and nvcc is available (never on the hot path: the first call
+loads, later calls return the cached handle).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+OK = 0
+ERR_INVALID = -1
+ERR_CUDA = -2
+ERR_UNSUPPORTED = -3
+ERR_WORKSPACE = -4
+
+F32, F16, BF16 = 0, 1, 2
+SOFTMAX_TOPK, TOPK_SOFTMAX = 0, 1
+
+EXPORTS = (
+    "bigrig_version", "bigrig_last_error", "bigrig_check_layout", "bigrig_moe_workspace_bytes",
+    "bigrig_dequant", "bigrig_router_logits", "bigrig_router_topk", "bigrig_moe_permute",
+    "bigrig_switch_glu", "bigrig_combine", "bigrig_moe_forward", "bigrig_workspace_errors",
+    "bigrig_timing_enable", "bigrig_timing_read", "bigrig_launch_counts", "bigrig_kernel_name",
+)
+KERNELS = {"router_logits": 0, "router_topk": 1, "permute": 2, "gate_up": 3, "down": 4,
+           "combine": 5, "dequant": 6}
+
+
+class ExpertLayout(ctypes.Structure):
+    """Mirror of ``bigrig_expert_layout`` (include/bigrig_b200.h)."""
+    _fields_ = [
+        ("hidden", ctypes.c_int32), ("inter", ctypes.c_int32), ("bits", ctypes.c_int32),
+        ("group_size", ctypes.c_int32), ("scale_dtype", ctypes.c_int32),
+        ("reserved", ctypes.c_int32), ("bytes_per_expert", ctypes.c_int64),
+        ("slot_stride", ctypes.c_int64), ("weight_off", ctypes.c_int64 * 3),
+        ("scales_off", ctypes.c_int64 * 3), ("biases_off", ctypes.c_int64 * 3),
+    ]
+
+
+class LibraryError(RuntimeError):
+    """The CUDA library could not be loaded; there is no CPU path to fall back on."""
+
+
+_lock = threading.Lock()
+_lib = None
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SIG = {
+    "bigrig_version": (ctypes.c_char_p, []),
+    "bigrig_last_error": (ctypes.c_char_p, []),
+    "bigrig_check_layout": (_I, [ctypes.POINTER(ExpertLayout)]),
+    "bigrig_moe_workspace_bytes": (ctypes.c_size_t, [_I, _I, _I, ctypes.POINTER(ExpertLayout)]),
+    "bigrig_dequant": (_I, [_P, ctypes.POINTER(ExpertLayout), _I, _I, _P, _P]),
+    "bigrig_router_logits": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "bigrig_router_topk": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "bigrig_moe_permute": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "bigrig_switch_glu": (_I, [_P, _P, _I, _I, _I, _P, _P, ctypes.POINTER(ExpertLayout), _P, _P,
+                              ctypes.c_size_t, _P]),
+    "bigrig_combine": (_I, [_P, _P, _I, _I, _I, _P, _P]),
+    "bigrig_moe_forward": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _P,
+                               ctypes.POINTER(ExpertLayout), _P, _P, _P, _P, ctypes.c_size_t, _P]),
+    "bigrig_workspace_errors": (_I, [_P, _P, _P]),
+    "bigrig_timing_enable": (_I, [_I]),
+    "bigrig_timing_read": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
+    "bigrig_launch_counts": (_I, [ctypes.POINTER(ctypes.c_int64)]),
+    "bigrig_kernel_name": (ctypes.c_char_p, [_I]),
+}
+
+
+def library_path() -> str:
+    return _build.LIB
+
+
+def load(build_if_stale: bool = True):
+    """The loaded library (ctypes.CDLL).  Raises LibraryError when it cannot be had."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = library_path()
+        if build_if_stale:
+            try:
+                if _build._stale(path, _build.sources() + _build.headers()):
+                    _build.build()
+            except Exception as e:  # noqa: BLE001 -- a prebuilt library may still be usable
+                if not os.path.exists(path):
+                    raise LibraryError(f"cannot build {path}: {e}") from e
+        if not os.path.exists(path):
+            raise LibraryError(f"{path} is missing: run `python -m bigrig_b200.build`")
+        try:
+            lib = ctypes.CDLL(path)
+        except OSError as e:
+            raise LibraryError(f"cannot load {path}: {e}") from e
+        for name, (res, args) in _SIG.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return load().bigrig_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str = "") -> None:
+    """Map a BIGRIG_ERR_* return code onto the reference's exception types."""
+    if rc == OK:
+        return
+    msg = f"{what}: {last_error()}" if what else last_error()
+    if rc in (ERR_INVALID, ERR_WORKSPACE):
+        raise ValueError(msg)
+    if rc == ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise RuntimeError(msg)
+
+
+def launch_counts() -> dict:
+    """{kernel name: launches issued by the library since it loaded}."""
+    arr = (ctypes.c_int64 * len(KERNELS))()
+    check(load().bigrig_launch_counts(arr), "launch_counts")
+    return {name: int(arr[i]) for name, i in KERNELS.items()}
+
+
+def timing_enable(kernels=()) -> None:
+    """Time the named kernels' launches with CUDA events (empty: off)."""
+    mask = 0
+    for name in kernels:
+        mask |= 1 << KERNELS[name]
+    check(load().bigrig_timing_enable(mask), "timing_enable")
+
+
+def timing_read(kernel: str) -> tuple:
+    """(total ms, timed launches) of ``kernel`` since the last read."""
+    ms = ctypes.c_double(0.0)
+    n = ctypes.c_int64(0)
+    check(load().bigrig_timing_read(KERNELS[kernel], ctypes.byref(ms), ctypes.byref(n)),
+          "timing_read")
+    return float(ms.value), int(n.value)

@@ -1,0 +1,355 @@
+// extern "C" entry points of libbigrig_b200.so: argument checks, workspace carving
+// and the launch sequence of each hot-path call.  See include/bigrig_b200.h.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace bigrig {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(BIGRIG_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return BIGRIG_OK;
+}
+
+// ------------------------------------------------------------------ launch timing
+namespace {
+struct TimingRecord {
+  int id;
+  cudaEvent_t start, end;
+};
+std::atomic<int> g_timing_on{0};
+std::atomic<long long> g_launches[BIGRIG_K_COUNT];
+std::mutex g_timing_mu;
+std::vector<TimingRecord> g_records;
+std::vector<cudaEvent_t> g_event_pool;
+constexpr size_t kMaxRecords = 1 << 16;
+
+cudaEvent_t take_event() {
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+const char* kKernelNames[BIGRIG_K_COUNT] = {"router_logits_kernel", "router_topk_kernel",
+                                            "permute_kernel",       "gemv_gate_up_kernel",
+                                            "gemv_down_kernel",     "combine_kernel",
+                                            "dequant_kernel"};
+}  // namespace
+
+TimedLaunch::TimedLaunch(int kernel_id, cudaStream_t s) : id_(kernel_id), s_(s), start_(nullptr) {
+  g_launches[kernel_id].fetch_add(1, std::memory_order_relaxed);
+  if (!((g_timing_on.load(std::memory_order_relaxed) >> kernel_id) & 1)) return;
+  std::lock_guard<std::mutex> lock(g_timing_mu);
+  if (g_records.size() >= kMaxRecords) return;
+  cudaEvent_t e = take_event();
+  if (e && cudaEventRecord(e, s) == cudaSuccess) start_ = e;
+}
+
+TimedLaunch::~TimedLaunch() {
+  if (!start_) return;
+  std::lock_guard<std::mutex> lock(g_timing_mu);
+  cudaEvent_t e = take_event();
+  if (e && cudaEventRecord(e, s_) == cudaSuccess) {
+    g_records.push_back({id_, static_cast<cudaEvent_t>(start_), e});
+  } else {
+    g_event_pool.push_back(static_cast<cudaEvent_t>(start_));
+    if (e) g_event_pool.push_back(e);
+  }
+}
+
+namespace {
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t n) { return (n + kAlign - 1) / kAlign * kAlign; }
+
+// Scratch regions of one MoE call, carved in this order from the workspace.
+struct Workspace {
+  int32_t* err;
+  int32_t* order;
+  int32_t* inv;
+  int32_t* offsets;
+  int32_t* seg_expert;
+  int32_t* seg_start;
+  int32_t* num_seg;
+  uint16_t* h;        // [P, I] bf16, expert-sorted rows
+  uint16_t* y;        // [P, H] bf16, (token, k) order (moe_forward only)
+  int32_t* indices;   // [P] (moe_forward when the caller passes none)
+  float* scores;      // [P]
+};
+
+size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Workspace* w) {
+  const size_t P = static_cast<size_t>(T) * k;
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> void* {
+    void* p = base ? static_cast<char*>(base) + off : nullptr;
+    off += align_up(bytes);
+    return p;
+  };
+  Workspace ws;
+  ws.err = static_cast<int32_t*>(take(4 * sizeof(int32_t)));
+  ws.order = static_cast<int32_t*>(take(P * sizeof(int32_t)));
+  ws.inv = static_cast<int32_t*>(take(P * sizeof(int32_t)));
+  ws.offsets = static_cast<int32_t*>(take((E + 1) * sizeof(int32_t)));
+  ws.seg_expert = static_cast<int32_t*>(take(E * sizeof(int32_t)));
+  ws.seg_start = static_cast<int32_t*>(take((E + 1) * sizeof(int32_t)));
+  ws.num_seg = static_cast<int32_t*>(take(sizeof(int32_t)));
+  ws.h = static_cast<uint16_t*>(take(P * L.inter * sizeof(uint16_t)));
+  ws.y = static_cast<uint16_t*>(take(P * L.hidden * sizeof(uint16_t)));
+  ws.indices = static_cast<int32_t*>(take(P * sizeof(int32_t)));
+  ws.scores = static_cast<float*>(take(P * sizeof(float)));
+  if (w) *w = ws;
+  return off;
+}
+
+int check_layout(const bigrig_expert_layout* Lp) {
+  if (!Lp) return set_error(BIGRIG_ERR_INVALID, "layout is NULL");
+  const bigrig_expert_layout& L = *Lp;
+  if (L.bits != 4 && L.bits != 8)
+    return set_error(BIGRIG_ERR_UNSUPPORTED, "bits=%d: only 4 and 8 are built", L.bits);
+  if (L.scale_dtype != BIGRIG_F16 && L.scale_dtype != BIGRIG_BF16)
+    return set_error(BIGRIG_ERR_INVALID, "scale_dtype=%d: must be F16 or BF16", L.scale_dtype);
+  if (L.group_size < 32 || L.group_size % 32)
+    return set_error(BIGRIG_ERR_UNSUPPORTED, "group_size=%d: must be a multiple of 32",
+                     L.group_size);
+  if (L.hidden <= 0 || L.inter <= 0 || L.hidden % L.group_size || L.inter % L.group_size)
+    return set_error(BIGRIG_ERR_INVALID, "hidden=%d inter=%d must be positive multiples of %d",
+                     L.hidden, L.inter, L.group_size);
+  if (L.slot_stride < L.bytes_per_expert || L.slot_stride % 16)
+    return set_error(BIGRIG_ERR_INVALID, "slot_stride=%lld must be >= bytes_per_expert=%lld "
+                     "and a multiple of 16", (long long)L.slot_stride, (long long)L.bytes_per_expert);
+  for (int p = 0; p < 3; ++p) {
+    const int64_t rows = p == 2 ? L.hidden : L.inter;
+    const int64_t cols = p == 2 ? L.inter : L.hidden;
+    const int64_t wbytes = rows * cols * L.bits / 8;
+    const int64_t sbytes = rows * (cols / L.group_size) * 2;
+    if (L.weight_off[p] % 16 || L.scales_off[p] % 2 || L.biases_off[p] % 2)
+      return set_error(BIGRIG_ERR_INVALID, "projection %d: weight offset must be 16-byte and "
+                       "scale/bias offsets 2-byte aligned", p);
+    if (L.weight_off[p] < 0 || L.weight_off[p] + wbytes > L.bytes_per_expert ||
+        L.scales_off[p] < 0 || L.scales_off[p] + sbytes > L.bytes_per_expert ||
+        L.biases_off[p] < 0 || L.biases_off[p] + sbytes > L.bytes_per_expert)
+      return set_error(BIGRIG_ERR_INVALID, "projection %d lies outside the %lld-byte expert", p,
+                       (long long)L.bytes_per_expert);
+  }
+  return BIGRIG_OK;
+}
+
+int check_route(int T, int k, int E) {
+  if (T < 0) return set_error(BIGRIG_ERR_INVALID, "T=%d must be >= 0", T);
+  if (E < 1 || E > kMaxExperts)
+    return set_error(BIGRIG_ERR_UNSUPPORTED, "n_experts=%d: must be in [1, %d]", E, kMaxExperts);
+  if (k < 1 || k > E || k > 32)
+    return set_error(BIGRIG_ERR_INVALID, "top_k=%d: must be in [1, min(n_experts, 32)]", k);
+  return BIGRIG_OK;
+}
+
+int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, const int32_t* g2s,
+                   const void* slab, const bigrig_expert_layout& L, void* y, const Workspace& ws,
+                   cudaStream_t s) {
+  const int P = T * k;
+  if (int rc = launch_permute(indices, P, E, ws.order, ws.inv, ws.offsets, ws.seg_expert,
+                              ws.seg_start, ws.num_seg, ws.err, s))
+    return rc;
+  RouteView rv;
+  rv.order = ws.order;
+  rv.seg_expert = ws.seg_expert;
+  rv.seg_start = ws.seg_start;
+  rv.num_seg = ws.num_seg;
+  rv.g2s = g2s;
+  rv.err = ws.err;
+  rv.P = P;
+  rv.k = k;
+  rv.s_max = P < E ? P : E;
+  rv.max_rows = T;
+  if (int rc = launch_gemv_gate_up(x, rv, slab, L, ws.h, s)) return rc;
+  return launch_gemv_down(ws.h, rv, slab, L, y, s);
+}
+
+}  // namespace
+}  // namespace bigrig
+
+using namespace bigrig;
+
+extern "C" {
+
+const char* bigrig_version(void) { return "bigrig_b200 0.1 sm_100a"; }
+
+const char* bigrig_last_error(void) { return g_last_error.c_str(); }
+
+int bigrig_check_layout(const bigrig_expert_layout* layout) { return check_layout(layout); }
+
+size_t bigrig_moe_workspace_bytes(int T, int k, int n_experts, const bigrig_expert_layout* layout) {
+  if (!layout || T < 0 || k < 1 || n_experts < 1) return 0;
+  return carve(nullptr, T, k, n_experts, *layout, nullptr);
+}
+
+int bigrig_dequant(const void* slab, const bigrig_expert_layout* layout, int slot, int proj,
+                   void* out, void* stream) {
+  if (int rc = check_layout(layout)) return rc;
+  if (!slab || !out) return set_error(BIGRIG_ERR_INVALID, "dequant: NULL pointer");
+  if (slot < 0) return set_error(BIGRIG_ERR_INVALID, "dequant: slot=%d < 0", slot);
+  if (proj < 0 || proj > 2) return set_error(BIGRIG_ERR_INVALID, "dequant: proj=%d", proj);
+  return launch_dequant(slab, *layout, slot, proj, out, static_cast<cudaStream_t>(stream));
+}
+
+int bigrig_router_logits(const void* x, const void* w, const float* bias, float* logits, int T,
+                         int H, int E, void* stream) {
+  if (T < 0 || H <= 0 || E <= 0 || H % 8)
+    return set_error(BIGRIG_ERR_INVALID, "router_logits: T=%d H=%d E=%d (H must be a multiple of 8)",
+                     T, H, E);
+  if (T == 0) return BIGRIG_OK;
+  if (!x || !w || !logits) return set_error(BIGRIG_ERR_INVALID, "router_logits: NULL pointer");
+  return launch_router_logits(x, w, bias, logits, T, H, E, static_cast<cudaStream_t>(stream));
+}
+
+int bigrig_router_topk(const void* logits, int logits_dtype, int T, int E, int k, int mode,
+                       int norm_topk, int32_t* indices, float* scores, void* stream) {
+  if (int rc = check_route(T, k, E)) return rc;
+  if (logits_dtype != BIGRIG_F32 && logits_dtype != BIGRIG_BF16)
+    return set_error(BIGRIG_ERR_INVALID, "router_topk: logits dtype must be F32 or BF16");
+  if (mode != BIGRIG_SOFTMAX_TOPK && mode != BIGRIG_TOPK_SOFTMAX)
+    return set_error(BIGRIG_ERR_INVALID, "router_topk: mode=%d", mode);
+  if (T == 0) return BIGRIG_OK;
+  if (!logits || !indices || !scores) return set_error(BIGRIG_ERR_INVALID, "router_topk: NULL pointer");
+  return launch_router_topk(logits, logits_dtype, T, E, k, mode, norm_topk, indices, scores,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int bigrig_moe_permute(const int32_t* indices, int T, int k, int E, int32_t* order, int32_t* inv,
+                       int32_t* offsets, int32_t* seg_expert, int32_t* seg_start, int32_t* num_seg,
+                       int32_t* err_count, void* stream) {
+  if (int rc = check_route(T, k, E)) return rc;
+  if (!offsets || !seg_expert || !seg_start || !num_seg || (T > 0 && (!indices || !order || !inv)))
+    return set_error(BIGRIG_ERR_INVALID, "moe_permute: NULL pointer");
+  return launch_permute(indices, T * k, E, order, inv, offsets, seg_expert, seg_start, num_seg,
+                        err_count, static_cast<cudaStream_t>(stream));
+}
+
+int bigrig_switch_glu(const void* x, const int32_t* indices, int T, int k, int n_experts,
+                      const int32_t* g2s, const void* slab, const bigrig_expert_layout* layout,
+                      void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_layout(layout)) return rc;
+  if (int rc = check_route(T, k, n_experts)) return rc;
+  if (T == 0) return BIGRIG_OK;
+  if (!x || !indices || !slab || !y || !workspace)
+    return set_error(BIGRIG_ERR_INVALID, "switch_glu: NULL pointer");
+  const size_t need = carve(nullptr, T, k, n_experts, *layout, nullptr);
+  if (workspace_bytes < need)
+    return set_error(BIGRIG_ERR_WORKSPACE, "switch_glu: workspace %zu bytes < %zu needed",
+                     workspace_bytes, need);
+  Workspace ws;
+  carve(workspace, T, k, n_experts, *layout, &ws);
+  return run_switch_glu(x, indices, T, k, n_experts, g2s, slab, *layout, y, ws,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int bigrig_combine(const void* y, const float* scores, int T, int k, int H, void* out,
+                   void* stream) {
+  if (T < 0 || k < 1 || H <= 0 || H % 2)
+    return set_error(BIGRIG_ERR_INVALID, "combine: T=%d k=%d H=%d", T, k, H);
+  if (T == 0) return BIGRIG_OK;
+  if (!y || !scores || !out) return set_error(BIGRIG_ERR_INVALID, "combine: NULL pointer");
+  return launch_combine(y, scores, T, k, H, out, static_cast<cudaStream_t>(stream));
+}
+
+int bigrig_moe_forward(const void* x, const void* logits, int logits_dtype, int T, int E, int k,
+                       int mode, int norm_topk, const int32_t* g2s, const void* slab,
+                       const bigrig_expert_layout* layout, void* out, int32_t* indices_out,
+                       float* scores_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_layout(layout)) return rc;
+  if (int rc = check_route(T, k, E)) return rc;
+  if (T == 0) return BIGRIG_OK;
+  if (!x || !logits || !slab || !out || !workspace)
+    return set_error(BIGRIG_ERR_INVALID, "moe_forward: NULL pointer");
+  const size_t need = carve(nullptr, T, k, E, *layout, nullptr);
+  if (workspace_bytes < need)
+    return set_error(BIGRIG_ERR_WORKSPACE, "moe_forward: workspace %zu bytes < %zu needed",
+                     workspace_bytes, need);
+  Workspace ws;
+  carve(workspace, T, k, E, *layout, &ws);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* idx = indices_out ? indices_out : ws.indices;
+  float* sc = scores_out ? scores_out : ws.scores;
+  if (int rc = bigrig_router_topk(logits, logits_dtype, T, E, k, mode, norm_topk, idx, sc, stream))
+    return rc;
+  if (int rc = run_switch_glu(x, idx, T, k, E, g2s, slab, *layout, ws.y, ws, s)) return rc;
+  return launch_combine(ws.y, sc, T, k, layout->hidden, out, s);
+}
+
+int bigrig_timing_enable(int mask) {
+  g_timing_on.store(mask);
+  return BIGRIG_OK;
+}
+
+int bigrig_launch_counts(int64_t* out) {
+  if (!out) return set_error(BIGRIG_ERR_INVALID, "launch_counts: NULL pointer");
+  for (int i = 0; i < BIGRIG_K_COUNT; ++i) out[i] = g_launches[i].load();
+  return BIGRIG_OK;
+}
+
+int bigrig_timing_read(int kernel_id, double* total_ms, int64_t* launches) {
+  if (kernel_id < 0 || kernel_id >= BIGRIG_K_COUNT || !total_ms || !launches)
+    return set_error(BIGRIG_ERR_INVALID, "timing_read: kernel_id=%d", kernel_id);
+  std::lock_guard<std::mutex> lock(g_timing_mu);
+  double sum = 0.0;
+  int64_t n = 0;
+  std::vector<TimingRecord> keep;
+  for (const TimingRecord& r : g_records) {
+    if (r.id != kernel_id) {
+      keep.push_back(r);
+      continue;
+    }
+    float ms = 0.f;
+    if (cudaEventSynchronize(r.end) == cudaSuccess &&
+        cudaEventElapsedTime(&ms, r.start, r.end) == cudaSuccess) {
+      sum += ms;
+      ++n;
+    }
+    g_event_pool.push_back(r.start);
+    g_event_pool.push_back(r.end);
+  }
+  g_records.swap(keep);
+  *total_ms = sum;
+  *launches = n;
+  return BIGRIG_OK;
+}
+
+const char* bigrig_kernel_name(int kernel_id) {
+  return (kernel_id >= 0 && kernel_id < BIGRIG_K_COUNT) ? kKernelNames[kernel_id] : "";
+}
+
+int bigrig_workspace_errors(void* workspace, int32_t* out, void* stream) {
+  if (!workspace || !out) return set_error(BIGRIG_ERR_INVALID, "workspace_errors: NULL pointer");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* err = static_cast<int32_t*>(workspace);
+  if (cudaMemcpyAsync(out, err, sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaMemsetAsync(err, 0, sizeof(int32_t), s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return set_error(BIGRIG_ERR_CUDA, "workspace_errors: %s", cudaGetErrorString(cudaGetLastError()));
+  return BIGRIG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,82 @@
+// Shared device helpers for the B200 MoE expert path (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "bigrig_b200.h"
+
+namespace bigrig {
+
+constexpr int kWarp = 32;
+constexpr int kMaxExperts = 256;  // router / permutation kernels keep per-expert state in smem
+
+// Round-to-nearest-even fp32 -> bf16 bits; NaN -> 0x7FC0 (matches the numpy restatement).
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7FC0;
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>(u >> 16);
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+__device__ __forceinline__ float bf16_round(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); }
+
+// fp16 bits <-> fp32 with the hardware converters (round to nearest even).
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t b) {
+  float f;
+  asm("{ .reg .b16 h; mov.b16 h, %1; cvt.f32.f16 %0, h; }" : "=f"(f) : "h"(b));
+  return f;
+}
+
+__device__ __forceinline__ uint16_t f32_to_f16_bits(float f) {
+  uint16_t b;
+  asm("{ .reg .b16 h; cvt.rn.f16.f32 h, %1; mov.b16 %0, h; }" : "=h"(b) : "f"(f));
+  return b;
+}
+
+template <int SDT>
+__device__ __forceinline__ float half_to_f32(uint16_t b) {
+  if constexpr (SDT == BIGRIG_F16) return f16_bits_to_f32(b);
+  else return bf16_bits_to_f32(b);
+}
+
+template <int SDT>
+__device__ __forceinline__ uint16_t f32_to_half(float f) {
+  if constexpr (SDT == BIGRIG_F16) return f32_to_f16_bits(f);
+  else return f32_to_bf16_bits(f);
+}
+
+// Streaming 128-bit load of data read exactly once (expert codes): bypass L1.
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint16_t ld_nc_u16(const void* p) {
+  uint16_t v;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
+
+}  // namespace bigrig

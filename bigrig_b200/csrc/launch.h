@@ -1,0 +1,59 @@
+// Host-side launcher declarations shared by the translation units of the library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "bigrig_b200.h"
+
+namespace bigrig {
+
+// Record `msg` as the calling thread's last error and return `code`.
+int set_error(int code, const char* fmt, ...);
+// cudaGetLastError after a launch: 0, or BIGRIG_ERR_CUDA with the kernel name recorded.
+int check_launch(const char* what);
+
+// RAII bracket of one kernel launch with CUDA events when timing is enabled.
+class TimedLaunch {
+ public:
+  TimedLaunch(int kernel_id, cudaStream_t s);
+  ~TimedLaunch();
+ private:
+  int id_;
+  cudaStream_t s_;
+  void* start_;
+};
+
+int launch_router_logits(const void* x, const void* w, const float* bias, float* logits, int T,
+                         int H, int E, cudaStream_t s);
+int launch_router_topk(const void* logits, int dtype, int T, int E, int k, int mode, int norm,
+                       int32_t* indices, float* scores, cudaStream_t s);
+int launch_permute(const int32_t* indices, int P, int E, int32_t* order, int32_t* inv,
+                   int32_t* offsets, int32_t* seg_expert, int32_t* seg_start, int32_t* num_seg,
+                   int32_t* err, cudaStream_t s);
+
+int launch_dequant(const void* slab, const bigrig_expert_layout& L, int slot, int proj, void* out,
+                   cudaStream_t s);
+
+// Grouped GEMV path (decode-sized calls): gate/up -> SiLU*mul into h (expert-sorted rows),
+// then down written to y[t, j, :] at each pair's unpermuted position.
+struct RouteView {
+  const int32_t* order;      // [P] pair id at each sorted position
+  const int32_t* seg_expert; // [S_max]
+  const int32_t* seg_start;  // [S_max + 1]
+  const int32_t* num_seg;    // [1]
+  const int32_t* g2s;        // [E] expert -> slot, or nullptr for identity
+  int32_t* err;              // [1] device error counter
+  int P, k, s_max;
+  int max_rows;              // largest number of rows one expert can receive (<= T)
+};
+
+int launch_gemv_gate_up(const void* x, const RouteView& rv, const void* slab,
+                        const bigrig_expert_layout& L, void* h, cudaStream_t s);
+int launch_gemv_down(const void* h, const RouteView& rv, const void* slab,
+                     const bigrig_expert_layout& L, void* y, cudaStream_t s);
+int launch_combine(const void* y, const float* scores, int T, int k, int H, void* out,
+                   cudaStream_t s);
+
+}  // namespace bigrig

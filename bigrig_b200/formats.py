@@ -1,0 +1,160 @@
+"""The packed expert format: per-layer spec, byte layout of one expert, and packing.
+
+One expert is one contiguous byte region, its projections in the order the
+reference packs them (bigrig_engine/stream.py:106-186, ``PROJECTIONS`` at
+stream.py:55 and ``COMPONENTS`` at stream.py:79): gate_proj, up_proj, down_proj,
+each as weight (uint32 codes), scales, biases, and an optional affine ``bias``.
+The manifest ``spec`` of a layer gives each component's shape, dtype and byte
+count; ``bytes_per_expert`` is their sum.  For OLMoE-1B-7B 4-bit that is
+3,538,944 bytes (data/blobs/OLMoE-1B-7B-0125-4bit.experts.manifest.json).
+
+A slot of the HBM slab holds exactly these bytes, so admitting an expert is one
+copy of its region; the kernels read it in place through ``ExpertLayout``.
+"""
+from __future__ import annotations
+
+import dataclasses
+import json
+import os
+
+import numpy as np
+
+PROJECTIONS = ("gate_proj", "up_proj", "down_proj")
+COMPONENTS = ("weight", "scales", "biases", "bias")
+_NP = {"uint32": np.uint32, "float16": np.uint16, "bfloat16": np.uint16, "float32": np.float32,
+       "uint8": np.uint8}
+_SIZE = {"uint32": 4, "float16": 2, "bfloat16": 2, "float32": 4, "uint8": 1}
+
+
+def make_spec(hidden: int, inter: int, bits: int = 4, group_size: int = 64,
+              scale_dtype: str = "float16") -> dict:
+    """The manifest spec of a gated SwiGLU expert in MLX affine format."""
+    if bits not in (4, 8):
+        raise ValueError(f"bits must be 4 or 8, got {bits}")
+    spec = {}
+    for proj in PROJECTIONS:
+        out_dim, in_dim = (hidden, inter) if proj == "down_proj" else (inter, hidden)
+        if in_dim % group_size:
+            raise ValueError(f"{proj}: in={in_dim} is not a multiple of group_size={group_size}")
+        words = in_dim * bits // 32
+        groups = in_dim // group_size
+        spec[proj] = {
+            "weight": {"shape": [out_dim, words], "dtype": "uint32", "nbytes": out_dim * words * 4},
+            "scales": {"shape": [out_dim, groups], "dtype": scale_dtype, "nbytes": out_dim * groups * 2},
+            "biases": {"shape": [out_dim, groups], "dtype": scale_dtype, "nbytes": out_dim * groups * 2},
+        }
+    return spec
+
+
+def bytes_per_expert(spec: dict) -> int:
+    return sum(c["nbytes"] for p in spec.values() for c in p.values())
+
+
+def component_offsets(spec: dict) -> dict:
+    """{(proj, comp): byte offset inside one expert}, in packing order."""
+    out, pos = {}, 0
+    for proj in spec:
+        for comp, meta in spec[proj].items():
+            out[(proj, comp)] = pos
+            pos += meta["nbytes"]
+    return out
+
+
+@dataclasses.dataclass(frozen=True)
+class Layout:
+    """Python view of ``bigrig_expert_layout`` for one layer's experts."""
+    hidden: int
+    inter: int
+    bits: int
+    group_size: int
+    scale_dtype: str
+    bytes_per_expert: int
+    slot_stride: int
+    weight_off: tuple
+    scales_off: tuple
+    biases_off: tuple
+
+    @property
+    def scale_code(self) -> int:
+        return {"float16": 1, "bfloat16": 2}[self.scale_dtype]
+
+
+def layout_from_spec(spec: dict, quant: dict | None = None, slot_align: int = 256) -> Layout:
+    """The kernel layout of a gated 4/8-bit affine spec.  Raises ValueError otherwise."""
+    if tuple(spec) != PROJECTIONS:
+        raise NotImplementedError(f"projections {tuple(spec)}: only the gated gate/up/down "
+                                  f"expert is built")
+    for proj in PROJECTIONS:
+        if "bias" in spec[proj]:
+            raise NotImplementedError(f"{proj} carries an affine bias: not built")
+        for comp in ("weight", "scales", "biases"):
+            if comp not in spec[proj]:
+                raise NotImplementedError(f"{proj} lacks {comp}: only affine-quantised experts")
+    q = dict(quant or {"bits": 4, "group_size": 64, "mode": "affine"})
+    if q.get("mode", "affine") != "affine":
+        raise NotImplementedError(f"quant mode {q.get('mode')!r}: only affine is built")
+    bits, gs = int(q["bits"]), int(q["group_size"])
+    if bits not in (4, 8):
+        raise NotImplementedError(f"{bits}-bit experts: only 4- and 8-bit affine codes are built")
+    gw = spec["gate_proj"]["weight"]["shape"]
+    dw = spec["down_proj"]["weight"]["shape"]
+    inter, hidden = gw[0], gw[1] * 32 // bits
+    if dw != [hidden, inter * bits // 32]:
+        raise ValueError(f"down_proj weight {dw} does not match gate_proj {gw}")
+    sd = spec["gate_proj"]["scales"]["dtype"]
+    offs = component_offsets(spec)
+    bpe = bytes_per_expert(spec)
+    stride = (bpe + slot_align - 1) // slot_align * slot_align
+    return Layout(hidden=hidden, inter=inter, bits=bits, group_size=gs, scale_dtype=sd,
+                  bytes_per_expert=bpe, slot_stride=stride,
+                  weight_off=tuple(offs[(p, "weight")] for p in PROJECTIONS),
+                  scales_off=tuple(offs[(p, "scales")] for p in PROJECTIONS),
+                  biases_off=tuple(offs[(p, "biases")] for p in PROJECTIONS))
+
+
+def pack_expert(arrays: dict, spec: dict) -> np.ndarray:
+    """{proj: {comp: ndarray}} -> the expert's bytes (uint8) in spec order, length-checked."""
+    parts = []
+    for proj in spec:
+        for comp, meta in spec[proj].items():
+            a = np.ascontiguousarray(arrays[proj][comp])
+            b = a.view(np.uint8).reshape(-1)
+            if b.nbytes != meta["nbytes"]:
+                raise ValueError(f"{proj}.{comp}: {b.nbytes} bytes, spec says {meta['nbytes']}")
+            parts.append(b)
+    return np.concatenate(parts)
+
+
+def unpack_expert(blob, spec: dict) -> dict:
+    """The inverse of pack_expert: {proj: {comp: ndarray}} views of ``blob``."""
+    buf = np.frombuffer(blob, dtype=np.uint8) if not isinstance(blob, np.ndarray) else blob
+    if buf.nbytes != bytes_per_expert(spec):
+        raise ValueError(f"blob of {buf.nbytes} bytes, spec accounts for {bytes_per_expert(spec)}")
+    out, pos = {}, 0
+    for proj in spec:
+        out[proj] = {}
+        for comp, meta in spec[proj].items():
+            n = meta["nbytes"]
+            out[proj][comp] = buf[pos:pos + n].view(_NP[meta["dtype"]]).reshape(meta["shape"])
+            pos += n
+    return out
+
+
+# ------------------------------------------------------------------ manifests
+def load_manifest(path: str) -> dict:
+    """Read a packed-blob manifest (``<blob>.manifest.json``, version >= 4)."""
+    p = path if path.endswith(".manifest.json") else path + ".manifest.json"
+    if not os.path.exists(p):
+        raise FileNotFoundError(f"{p} not found: a blob without its manifest has no byte layout")
+    with open(p) as f:
+        m = json.load(f)
+    for key in ("regions", "layers", "total_bytes"):
+        if key not in m:
+            raise ValueError(f"{p}: manifest lacks {key!r}")
+    return m
+
+
+def manifest_regions(manifest: dict) -> dict:
+    """{(layer, expert): (offset, length)} from a manifest's ``regions``."""
+    return {tuple(int(x) for x in k.split(":")): (int(o), int(n))
+            for k, (o, n) in manifest["regions"].items()}

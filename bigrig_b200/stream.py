@@ -1,0 +1,669 @@
+"""The bounded expert pool on HBM and the SwitchGLU-style layer that computes over it.
+
+Drop-in for bigrig_engine/stream.py's ExpertPool (stream.py:454-810),
+StreamingSwitchGLU (stream.py:814-1631), attach/StreamHandle (stream.py:1842-2200).
+
+B200 design:
+
+* A layer's pool is one HBM slab ``[capacity, slot_stride]`` (uint8).  A slot
+  holds one expert's packed bytes exactly as they lie in the blob, so the sm_100a
+  kernels read codes, scales and biases in place and an admission is one copy.
+* Misses are copied from pinned host DRAM (fetch.HostExpertStore) with
+  ``cudaMemcpyAsync`` on the pool's side stream.  An event orders each layer's
+  copies before its kernels; a second event orders a slot's overwrite after the
+  last kernel that read it, so copy and compute overlap without a race.
+* Residency decisions are the reference's, step for step: ``touch`` in
+  ascending expert id with each expert's best router rank, staged admissions
+  first, then cold ones in ``need`` order, victims from the policy with
+  ``exclude=protect`` (or least-recently-admitted when the policy cannot name a
+  legal one), free slots popped from the end of the free list.  The golden replay
+  in tests/golden/ensure_golden.npz pins the slot ids and tables.
+* A pool holding every expert (``full``) is sync-free: expert ids become slots
+  on the device (``g2s_device``), nothing is read back to the host.
+
+The layer returns per-(token, k) outputs unreduced, ``y[..., k, H]``; the MoE
+block applies the router weights (stream.py:1523-1525).
+"""
+from __future__ import annotations
+
+import contextlib
+import inspect
+import json
+import os
+import time
+
+import numpy as np
+import torch
+
+from . import ops
+from .formats import PROJECTIONS, bytes_per_expert, layout_from_spec
+from .pool import _policy_factory
+
+
+def projections_of(spec: dict) -> tuple:
+    """The projections this layer's experts carry, in packed byte order (stream.py:66-68)."""
+    return tuple(spec)
+
+
+def is_gated(projections) -> bool:
+    return "gate_proj" in tuple(projections)
+
+
+def _as_u8(blob) -> torch.Tensor:
+    """Host bytes of any kind (bytes, memoryview, numpy, tensor) as a flat uint8 tensor."""
+    if isinstance(blob, torch.Tensor):
+        return blob.reshape(-1).view(torch.uint8) if blob.dtype != torch.uint8 else blob.reshape(-1)
+    if isinstance(blob, np.ndarray):
+        return torch.from_numpy(np.ascontiguousarray(blob).view(np.uint8).reshape(-1))
+    return torch.from_numpy(np.frombuffer(blob, dtype=np.uint8).copy())
+
+
+class ExpertPool:
+    """C slots of one layer's experts in HBM, plus the tables saying which expert is where.
+
+    Same constructor, methods, counters and exceptions as the reference
+    (stream.py:501-810).  ``views`` is accepted for interface compatibility: on a
+    discrete GPU there are no page-cache views, every resident expert is a slot.
+    """
+
+    def __init__(self, layer: int, sg, n_experts: int, capacity: int, spec: dict,
+                 policy: str = "lfuda", quant: dict | None = None, views: bool = False,
+                 device=None, copy_stream: torch.cuda.Stream | None = None):
+        if not 1 <= capacity <= n_experts:
+            raise ValueError(
+                f"capacity must be in [1, {n_experts}], got {capacity}. A pool larger than the "
+                f"expert count wastes memory; a pool of zero cannot serve any token.")
+        self.layer, self.sg, self.n_experts, self.capacity = layer, sg, n_experts, capacity
+        self.spec = spec
+        self.projections = projections_of(spec)
+        self.gated = is_gated(self.projections)
+        self.spec_quant = dict(quant or {"bits": 4, "group_size": 64, "mode": "affine"})
+        self.layout = layout_from_spec(spec, self.spec_quant)
+        self.device = torch.device(device) if device is not None else (
+            torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
+            else torch.device("cpu"))
+        self.policy = _policy_factory(policy, capacity, n_experts)(capacity, n_experts)
+        try:
+            self._policy_excludes = "exclude" in inspect.signature(self.policy.victim).parameters
+        except (TypeError, ValueError):
+            self._policy_excludes = False
+        self._slot_tick = np.zeros(capacity, dtype=np.int64)
+        self._tick = 0
+        self.g2s = np.full(n_experts, -1, dtype=np.int32)
+        self.s2g = np.full(capacity, -1, dtype=np.int32)
+        self._g2s_dev = None
+        self._g2s_dirty = True
+        self._free = list(range(capacity))
+        self._resident = 0
+        self.hits = 0
+        self.misses = 0
+        self.uses = np.zeros(n_experts, dtype=np.int64)
+        self.admits = 0
+        self.admit_seconds = 0.0
+        self.admit_bytes = 0
+        self.stage_pred = None
+        self.stage = {}
+        self.stage_issued = 0
+        self.stage_hits = 0
+        self.zero_copy_admits = 0
+        self.evicts = 0
+        self.views = bool(views)
+        self.slab: torch.Tensor | None = None
+        self._built = False
+        self._pending_rank: dict = {}
+        self._copy_stream = copy_stream
+        self._copies_done = None     # event: this pool's queued admissions have landed
+        self._reads_done = None      # event: the last kernel that read the slab has finished
+
+    # -- construction -------------------------------------------------------
+    @property
+    def bytes_per_expert(self) -> int:
+        return bytes_per_expert(self.spec)
+
+    def build(self):
+        """Allocate the HBM slab.  The model's (E, ...) expert tensors, if ``sg`` holds
+        any, are dropped first so both never coexist (stream.py:570-597)."""
+        if self.sg is not None:
+            for proj in self.projections:
+                mod = getattr(self.sg, proj, None)
+                if isinstance(mod, dict):
+                    for comp in list(self.spec[proj]):
+                        mod.pop(comp, None)
+        self.slab = torch.empty((self.capacity, self.layout.slot_stride), dtype=torch.uint8,
+                                device=self.device)
+        if self.device.type == "cuda" and self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(device=self.device)
+        self._built = True
+        return self
+
+    def nbytes(self) -> int:
+        return 0 if self.slab is None else self.slab.numel()
+
+    def expert_arrays(self, e: int) -> torch.Tensor:
+        """Resident expert e's packed bytes (a view of its slot).  KeyError if absent."""
+        slot = int(self.g2s[int(e)])
+        if slot < 0:
+            raise KeyError(e)
+        return self.slab[slot, :self.layout.bytes_per_expert]
+
+    views_of = expert_arrays
+
+    def slot_of(self, e: int) -> int:
+        return int(self.g2s[e])
+
+    # -- residency ----------------------------------------------------------
+    def touch(self, experts, ranks=None) -> list:
+        """Record a request for each expert; return those not resident (stream.py:622-642)."""
+        need, nrank = [], []
+        ranks = list(ranks) if ranks is not None else [0] * len(experts)
+        for e, r in zip(experts, ranks):
+            e, r = int(e), int(r)
+            self.uses[e] += 1
+            if self.g2s[e] >= 0:
+                self.hits += 1
+                self.policy.touch(e, r)
+            else:
+                self.misses += 1
+                need.append(e)
+                nrank.append(r)
+        self._pending_rank = dict(zip(need, nrank))
+        return need
+
+    def _victim(self, protect=()) -> int:
+        """Free a slot, telling the policy only about real evictions (stream.py:644-690)."""
+        if self._free:
+            return self._free.pop()
+        protect = {int(x) for x in protect}
+        v = self.policy.victim(exclude=protect) if self._policy_excludes else self.policy.victim()
+        ev = int(v) if v is not None and v >= 0 and v not in protect and self.g2s[v] >= 0 else -1
+        if ev < 0:
+            best, best_t = -1, None
+            for slot in range(self.capacity):
+                g = int(self.s2g[slot])
+                if g < 0 or g in protect:
+                    continue
+                if best_t is None or self._slot_tick[slot] < best_t:
+                    best, best_t = g, self._slot_tick[slot]
+            ev = best
+        if ev < 0:
+            raise RuntimeError(
+                f"layer {self.layer}: every one of {self.capacity} slots holds an expert this "
+                f"step still needs. Capacity must be at least top-k.")
+        slot = int(self.g2s[ev])
+        if hasattr(self.policy, "evicted"):
+            self.policy.evicted(ev)
+        self.g2s[ev] = -1
+        self.s2g[slot] = -1
+        self._resident -= 1
+        self._g2s_dirty = True
+        self.evicts += 1
+        return slot
+
+    def admit(self, e: int, blob, protect=()) -> int:
+        """Copy expert e's packed bytes into a slot and return the slot (stream.py:692-705)."""
+        if not self._built:
+            raise RuntimeError("build() must run before admit()")
+        src = _as_u8(blob)
+        want = self.bytes_per_expert
+        if src.numel() != want:
+            raise ValueError(
+                f"layer {self.layer} expert {e}: the manifest accounts for {want} bytes but the "
+                f"region supplied {src.numel()}. Refusing to write a partially-filled slot.")
+        t0 = time.perf_counter()
+        return self.admit_arrays(e, src, protect=protect, _t0=t0)
+
+    def build_arrays(self, e: int, blob) -> torch.Tensor:
+        """One expert's bytes staged on the device, ready for admit_arrays (stream.py:707-755).
+
+        A staged expert is bit-for-bit what a direct admit writes: the same bytes."""
+        src = _as_u8(blob)
+        if src.numel() != self.bytes_per_expert:
+            raise ValueError(f"expert {e}: manifest accounts for {self.bytes_per_expert} bytes "
+                             f"but the region is {src.numel()}.")
+        if self.device.type != "cuda":
+            return src.clone()
+        with torch.cuda.stream(self._copy_stream):
+            return src.to(self.device, non_blocking=src.is_pinned())
+
+    def admit_arrays(self, e: int, arrays, protect=(), _t0=None) -> int:
+        """Place bytes (host or device) into a slot; bookkeeping as admit (stream.py:757-780)."""
+        if _t0 is None:
+            _t0 = time.perf_counter()
+        slot = self._victim(protect=protect)
+        self._write_slot(slot, arrays)
+        if self.s2g[slot] < 0:
+            self._resident += 1
+        self.g2s[e] = slot
+        self.s2g[slot] = e
+        self._g2s_dirty = True
+        self._tick += 1
+        self._slot_tick[slot] = self._tick
+        self.policy.admit(e, int(self._pending_rank.get(e, 0)))
+        self.admits += 1
+        self.admit_seconds += time.perf_counter() - _t0
+        return slot
+
+    def _write_slot(self, slot: int, src: torch.Tensor) -> None:
+        n = self.layout.bytes_per_expert
+        dst = self.slab[slot, :n]
+        if self.device.type != "cuda":
+            dst.copy_(src.reshape(-1))
+            return
+        cs = self._copy_stream
+        if self._reads_done is not None:
+            cs.wait_event(self._reads_done)     # a kernel may still be reading this slot
+        with torch.cuda.stream(cs):
+            dst.copy_(src.reshape(-1), non_blocking=True)
+            if src.device.type == "cuda":
+                src.record_stream(cs)
+        if self._copies_done is None:
+            self._copies_done = torch.cuda.Event()
+        self._copies_done.record(cs)
+        self.admit_bytes += n
+
+    def ready(self, stream: torch.cuda.Stream | None = None) -> None:
+        """Order ``stream`` (default: current) after every admission queued so far.
+
+        Skipped while a CUDA graph is being captured: only a settled pool (see
+        ``settle``) may be captured, and a capture cannot wait on outside events."""
+        if self._copies_done is not None and self.device.type == "cuda":
+            if torch.cuda.is_current_stream_capturing():
+                return
+            (stream or torch.cuda.current_stream(self.device)).wait_event(self._copies_done)
+
+    def mark_read(self, stream: torch.cuda.Stream | None = None) -> None:
+        """Record that kernels reading the slab were queued on ``stream`` (default: current)."""
+        if self.device.type == "cuda" and not torch.cuda.is_current_stream_capturing():
+            if self._reads_done is None:
+                self._reads_done = torch.cuda.Event()
+            self._reads_done.record(stream or torch.cuda.current_stream(self.device))
+
+    def settle(self) -> None:
+        """Wait for every queued admission and kernel read; afterwards the pool's tables
+        and slab are quiescent, which a CUDA-graph capture of a full pool requires."""
+        if self.device.type == "cuda":
+            if self._copy_stream is not None:
+                self._copy_stream.synchronize()
+            torch.cuda.current_stream(self.device).synchronize()
+        self._copies_done = None
+        self._reads_done = None
+
+    @property
+    def full(self) -> bool:
+        """True when every expert is resident, so no request can miss (stream.py:782-789)."""
+        return self.capacity == self.n_experts and self._resident == self.n_experts
+
+    def g2s_device(self) -> torch.Tensor:
+        """The expert->slot table on the device, re-uploaded only when residency changed."""
+        if self._g2s_dirty or self._g2s_dev is None:
+            t = torch.from_numpy(self.g2s.copy())
+            if self._g2s_dev is None:
+                self._g2s_dev = t.to(self.device)
+            elif self.device.type == "cuda":
+                # pinned staging from torch's caching host allocator, which keeps the
+                # block alive until the asynchronous copy has consumed it
+                self._g2s_dev.copy_(t.pin_memory(), non_blocking=True)
+            else:
+                self._g2s_dev.copy_(t)
+            self._g2s_dirty = False
+        return self._g2s_dev
+
+    def stats(self) -> dict:
+        tot = self.hits + self.misses
+        return {"layer": self.layer, "capacity": self.capacity, "n_experts": self.n_experts,
+                "hits": self.hits, "misses": self.misses,
+                "miss_rate": self.misses / tot if tot else 0.0,
+                "admits": self.admits, "evicts": self.evicts,
+                "resident_bytes": self.nbytes()}
+
+
+def _pair_chunks(sorted_experts: np.ndarray, C: int):
+    """Spans of expert-sorted pairs holding at most C distinct experts (stream.py:1098-1126)."""
+    uniq, starts = np.unique(sorted_experts, return_index=True)
+    n = int(sorted_experts.shape[0])
+    return [(int(starts[i]), int(starts[i + C]) if i + C < len(uniq) else n)
+            for i in range(0, len(uniq), C)]
+
+
+class StreamingSwitchGLU:
+    """Drop-in for mlx_lm's SwitchGLU that computes over a pool's HBM slots (stream.py:814).
+
+    ``__call__(x, indices) -> y[..., k, H]``: ``x`` bf16 ``[..., H]`` and ``indices``
+    integer ``[..., k]`` on the pool's device.  Router weights are applied by the
+    caller.  Raises ValueError when top-k exceeds the capacity (stream.py:1462-1465)
+    and RuntimeError when one step needs more distinct misses than slots
+    (stream.py:952-956).
+    """
+
+    def __init__(self, pool: ExpertPool, fetcher, activation=None, quantized: bool = True,
+                 qparams: dict | None = None):
+        if not quantized:
+            raise NotImplementedError("only affine-quantised experts are built")
+        if activation not in (None, "swiglu"):
+            raise NotImplementedError("only the SwiGLU activation silu(gate) * up is built")
+        self._pool = pool
+        self._fetcher = fetcher
+        self._q = dict(qparams or pool.spec_quant)
+        self.fetch_seconds = 0.0
+        self.fetch_bytes = 0
+        self.chunked_calls = 0
+        self.views_calls = 0
+        self.sync_seconds = 0.0
+        self.bypass = False
+        self._sync_free = False
+        self.same_answers = True
+        self._held = None
+        self._ahead = []
+        self._then = None
+        self.prefill_routed = None
+        self._next = None
+        self._next_gate = None
+        self._pred_m = 0
+        self._pred_budget = 0
+        self.pred_issued = 0
+        self.reroutes = 0
+        self.reroute_lost = 0.0
+        self.workspace = None
+
+    # -- residency ----------------------------------------------------------
+    def ensure(self, indices, ranks=None) -> np.ndarray:
+        """Make every requested expert resident; return the slot-remapped indices
+        (stream.py:922-978).  ``ranks`` overrides the rank read off the last axis."""
+        gi = np.asarray(indices).astype(np.int64)
+        best: dict = {}
+        if ranks is not None:
+            for e, r in zip(gi.reshape(-1), np.asarray(ranks).reshape(-1)):
+                e, r = int(e), int(r)
+                if e not in best or r < best[e]:
+                    best[e] = r
+        else:
+            for row in gi.reshape(-1, gi.shape[-1]):
+                for r, e in enumerate(row):
+                    e = int(e)
+                    if e not in best or r < best[e]:
+                        best[e] = r
+        uniq = sorted(best)
+        pool = self._pool
+        need = pool.touch(uniq, [best[e] for e in uniq])
+        if need:
+            if len(need) > pool.capacity:
+                raise RuntimeError(
+                    f"layer {pool.layer} needs {len(need)} experts for one step but the pool "
+                    f"holds {pool.capacity}. Capacity must be at least top-k; below that a "
+                    f"token evicts an expert it is still using.")
+            staged = [int(e) for e in need if int(e) in pool.stage]
+            cold = [int(e) for e in need if int(e) not in pool.stage]
+            for e in staged:
+                pool.admit_arrays(e, pool.stage[e], protect=uniq)
+                pool.stage_hits += 1
+            if cold:
+                t0 = time.perf_counter()
+                blobs = self._fetch([(pool.layer, e) for e in cold])
+                self.fetch_seconds += time.perf_counter() - t0
+                for e in cold:
+                    b = blobs[(pool.layer, e)]
+                    self.fetch_bytes += pool.bytes_per_expert
+                    pool.admit(e, b, protect=uniq)
+        pool.stage = {}
+        return pool.g2s[gi]
+
+    def _fetch(self, keys) -> dict:
+        local = getattr(self._fetcher, "fetch_local", None)
+        blobs = local(keys) if local is not None else None
+        return self._fetcher.fetch(keys) if blobs is None else blobs
+
+    def refresh(self) -> bool:
+        """Re-decide whether this layer can skip the host round-trip (stream.py:1579-1603)."""
+        self._sync_free = self._pool.full
+        return self._sync_free
+
+    # -- compute ------------------------------------------------------------
+    def _run(self, x2: torch.Tensor, idx2: torch.Tensor, g2s: torch.Tensor | None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+        pool = self._pool
+        pool.ready()
+        y = ops.switch_glu(x2, idx2, pool.slab, pool.layout, pool.n_experts, g2s=g2s, out=out,
+                           workspace=self.workspace)
+        pool.mark_read()
+        return y
+
+    def __call__(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        pool = self._pool
+        H = x.shape[-1]
+        k = indices.shape[-1]
+        lead = tuple(indices.shape[:-1])
+        x2 = x.reshape(-1, H)
+        if x2.dtype != torch.bfloat16:
+            x2 = x2.to(torch.bfloat16)
+        x2 = x2.contiguous()
+        if self._sync_free or self.bypass:
+            idx2 = indices.reshape(-1, k).to(torch.int32)
+            if self.bypass:                      # timing control: slots scrambled, output wrong
+                idx2 = torch.remainder(idx2, pool.capacity).contiguous()
+                y = self._run(x2, idx2, None)
+            else:
+                y = self._run(x2, idx2.contiguous(), pool.g2s_device())
+            return y.reshape(*lead, k, H)
+        if k > pool.capacity:
+            raise ValueError(
+                f"layer {pool.layer}: top-k is {k} but the pool holds {pool.capacity}. A single "
+                f"token cannot be served, so no capacity below top-k is ever valid.")
+        t0 = time.perf_counter()
+        gi = indices.reshape(-1, k).to("cpu").numpy().astype(np.int64)   # the host readback
+        self.sync_seconds += time.perf_counter() - t0
+        self._count_routing(gi.reshape(-1))
+        if len(np.unique(gi)) <= pool.capacity:
+            self.ensure(gi)
+            idx2 = indices.reshape(-1, k).to(torch.int32).contiguous()
+            y = self._run(x2, idx2, pool.g2s_device())
+            return y.reshape(*lead, k, H)
+        # More distinct experts than slots: expert-sorted spans of <= C experts, each made
+        # resident and computed before the next span may evict it (stream.py:1509-1561).
+        self.chunked_calls += 1
+        pe = gi.reshape(-1)
+        order = np.argsort(pe, kind="stable")
+        spe = pe[order]
+        tok = order // k
+        rank = order % k
+        y = torch.empty(pe.shape[0], H, dtype=torch.bfloat16, device=x2.device)
+        order_dev = torch.from_numpy(order).to(x2.device)
+        tok_dev = torch.from_numpy(tok).to(x2.device)
+        spe_dev = torch.from_numpy(spe.astype(np.int32)).to(x2.device)
+        for lo, hi in _pair_chunks(spe, pool.capacity):
+            self.ensure(spe[lo:hi], ranks=rank[lo:hi])
+            rows = x2.index_select(0, tok_dev[lo:hi]).contiguous()
+            part = self._run(rows, spe_dev[lo:hi].reshape(-1, 1).contiguous(), pool.g2s_device())
+            y.index_copy_(0, order_dev[lo:hi], part.reshape(hi - lo, H))
+        return y.reshape(*lead, k, H)
+
+    # -- prefill holding / read-ahead (stream.py:1174-1235) ----------------------
+    def _count_routing(self, pe) -> None:
+        if self._held is not None:
+            self.prefill_routed += np.bincount(pe, minlength=self._pool.n_experts)
+
+    @contextlib.contextmanager
+    def holding(self, then=None):
+        """Scope of one layer's layer-major prefill: routing is counted for ``rewarm`` and
+        ``then`` (the next layer's read-ahead) runs once, after the first chunk."""
+        self._held, self._then = {}, then
+        self.prefill_routed = np.zeros(self._pool.n_experts, dtype=np.int64)
+        try:
+            yield
+        finally:
+            self._held, self._then = None, None
+            if self._ahead:
+                self._fetcher.drop(self._ahead)
+                self._ahead = []
+
+    def read_ahead(self) -> None:
+        """Queue every expert of this layer for reading (prefill); nothing to move when the
+        store is already in host DRAM."""
+        keys = [(self._pool.layer, e) for e in range(self._pool.n_experts)]
+        try:
+            self._fetcher.prefetch(keys)
+        except RuntimeError:
+            return
+        self._ahead = keys
+
+
+class StreamHandle:
+    """Warm, measure and tear down a set of streamed layers (stream.py:1961-2200)."""
+
+    def __init__(self, model, pools, mods, fetcher, manifest=None, full_layers=()):
+        self.model, self.pools, self.mods = model, pools, mods
+        self.fetcher, self.manifest = fetcher, manifest or {}
+        self.full_layers = list(full_layers)
+
+    def release_prefill(self) -> None:
+        for m in self.mods:
+            if m._ahead and m._fetcher is not None:
+                m._fetcher.drop(m._ahead)
+            m._ahead = []
+
+    def rewarm(self, per_layer: int) -> int:
+        keys = []
+        for m in sorted((m for m in self.mods if m._pool is not None and m.prefill_routed is not None),
+                        key=lambda m: m._pool.layer):
+            counts = m.prefill_routed
+            top = np.argsort(-counts, kind="stable")[:per_layer]
+            keys += [(m._pool.layer, int(e)) for e in top if counts[e] > 0]
+        return self.fetcher.refresh(keys) if keys else 0
+
+    def prefill_layer(self, layer: int, read_ahead: bool = False):
+        """Context held while layer-major prefill runs every chunk through ``layer``
+        (stream.py:2009-2034).  Whole layers (capacity == experts) get a no-op scope."""
+        by_layer = {m._pool.layer: m for m in self.mods
+                    if m._pool is not None and m._pool.capacity < m._pool.n_experts}
+        m = by_layer.get(layer)
+        nxt = by_layer.get(layer + 1) if read_ahead else None
+        if m is None:
+            if nxt is not None:
+                nxt.read_ahead()
+            return contextlib.nullcontext()
+        return m.holding(then=nxt.read_ahead if nxt is not None else None)
+
+    def warm(self, mode="auto"):
+        """Fill the pools: "auto" fills only pools with C == E, "full" all, "lazy" none
+        (stream.py:2036-2073)."""
+        if mode not in ("auto", "full", "lazy", True, False):
+            raise ValueError(f"warm mode must be auto/full/lazy, got {mode!r}")
+        mode = {True: "full", False: "lazy"}.get(mode, mode)
+        if mode == "lazy":
+            return self
+        for p in self.pools:
+            if mode == "auto" and p.capacity < p.n_experts:
+                p.hits = p.misses = 0
+                continue
+            blobs = self.fetcher.fetch([(p.layer, e) for e in range(p.capacity)])
+            for e in range(p.capacity):
+                p.touch([e], [0])
+                p.admit(e, blobs[(p.layer, e)])
+            p.hits = p.misses = 0
+        return self
+
+    def usage(self) -> dict:
+        out = {}
+        for m in self.mods:
+            p = m._pool
+            for e in np.nonzero(p.uses)[0]:
+                out[f"{p.layer}:{int(e)}"] = int(p.uses[e])
+        return out
+
+    def save_usage(self, path: str, decay: float = 0.5) -> str:
+        """Merge this run's use counts into earlier ones, halved first (stream.py:2084-2105)."""
+        prev = {}
+        try:
+            with open(path) as fh:
+                prev = json.load(fh) or {}
+        except (OSError, ValueError):
+            prev = {}
+        merged = {k: int(v * decay) for k, v in prev.items() if int(v * decay) > 0}
+        for k, v in self.usage().items():
+            merged[k] = merged.get(k, 0) + v
+        os.makedirs(os.path.dirname(path) or ".", exist_ok=True)
+        tmp = path + ".tmp"
+        with open(tmp, "w") as fh:
+            json.dump(merged, fh)
+        os.replace(tmp, path)
+        return path
+
+    def resident_gb(self) -> float:
+        return sum(p.nbytes() for p in self.pools) / 1e9
+
+    def stats(self) -> dict:
+        h = sum(p.hits for p in self.pools)
+        m = sum(p.misses for p in self.pools)
+        return {"layers": len(self.pools),
+                "full_layers": sum(1 for p in self.pools if p.capacity == p.n_experts),
+                "sync_free": sum(1 for m_ in self.mods if m_._sync_free),
+                "hits": h, "misses": m, "miss_rate": m / (h + m) if (h + m) else 0.0,
+                "capacity": min((p.capacity for p in self.pools if p.capacity < p.n_experts),
+                                default=(self.pools[0].capacity if self.pools else 0)),
+                "n_experts": self.pools[0].n_experts if self.pools else 0,
+                "resident_gb": self.resident_gb(),
+                "admit_gb": sum(p.admit_bytes for p in self.pools) / 1e9,
+                "fetch_seconds": sum(m_.fetch_seconds for m_ in self.mods),
+                "admit_seconds": sum(m_._pool.admit_seconds for m_ in self.mods),
+                "sync_seconds": sum(m_.sync_seconds for m_ in self.mods),
+                "chunked_calls": sum(m_.chunked_calls for m_ in self.mods),
+                "stage_issued": sum(p.stage_issued for p in self.pools),
+                "stage_hits": sum(p.stage_hits for p in self.pools)}
+
+    def reset_stats(self):
+        for p in self.pools:
+            p.hits = p.misses = 0
+            p.admit_seconds = 0.0
+            p.admit_bytes = 0
+        for m in self.mods:
+            m.fetch_seconds = 0.0
+            m.sync_seconds = 0.0
+            m.fetch_bytes = 0
+        return self
+
+    def close(self) -> None:
+        """Release every slab explicitly (stream.py:2160-2191)."""
+        for p in self.pools:
+            p.slab = None
+            p._built = False
+        for m in self.mods:
+            m._pool = None
+            m._fetcher = None
+        self.pools, self.mods = [], []
+        try:
+            self.fetcher.close()
+        except Exception:  # noqa: BLE001 -- teardown must not raise
+            pass
+
+
+def attach(blocks, store, capacity, policy: str = "lfuda", full_layers=(), warm=True,
+           device=None) -> StreamHandle:
+    """Give each MoE block a pool-backed StreamingSwitchGLU over ``store`` (stream.py:1842-1958).
+
+    ``blocks``: list of objects with ``layer``, ``n_experts``, ``spec``, ``quant`` and a
+    ``switch`` attribute to replace.  ``capacity`` is an int or a fraction of E in (0, 1].
+    """
+    full = set(full_layers or ())
+    pools, mods = [], []
+    for blk in blocks:
+        E = blk.n_experts
+        if blk.layer in full:
+            C = E
+        else:
+            C = int(round(capacity * E)) if isinstance(capacity, float) and capacity <= 1.0 \
+                else int(capacity)
+        C = max(1, min(E, C))
+        pool = ExpertPool(blk.layer, None, E, C, blk.spec, policy=policy, quant=blk.quant,
+                          device=device).build()
+        mod = StreamingSwitchGLU(pool, store)
+        blk.switch = mod
+        pools.append(pool)
+        mods.append(mod)
+    h = StreamHandle(blocks, pools, mods, store, full_layers=sorted(full))
+    h.warm(warm if warm is not True else "auto")
+    for m in mods:
+        m.refresh()
+    return h
+
+
+__all__ = ["ExpertPool", "StreamingSwitchGLU", "StreamHandle", "attach", "PROJECTIONS",
+           "projections_of", "is_gated"]

@@ -1,0 +1,165 @@
+/*
+ * bigrig_b200.h -- C ABI of the B200 (sm_100a) MoE expert hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*, a cudaStream_t; NULL is the legacy default stream), never
+ * allocates on the hot path, and returns 0 or a negative BIGRIG_ERR_* code.
+ * bigrig_last_error() gives the calling thread's message for the last failure.
+ * Scratch memory is passed in by the caller (bigrig_moe_workspace_bytes says
+ * how much); the library keeps no device state between calls.
+ *
+ * Reference interfaces replaced (paths relative to the BigRig tree):
+ *   bigrig_switch_glu     StreamingSwitchGLU.__call__(x, indices) -> y[..., k, H]
+ *                         bigrig_engine/stream.py:1377-1577 (decode: _forward_views_one
+ *                         1278-1318; prefill: _forward_views 1237-1276, _forward/_proj
+ *                         1128-1172, 1605-1631)
+ *   bigrig_moe_forward    the MoE block around it: router top-k/softmax, the call above,
+ *                         then sum_k score * y (stream.py:1523-1525; router rule
+ *                         bigrig_engine/adapter.py:74-92)
+ *   bigrig_router_logits  the router gate x . W^T (+ bias) (stream.py:1436, 895)
+ *   bigrig_router_topk    mx.softmax + mx.argpartition top-k (stream.py:1436-1439)
+ *   bigrig_moe_permute    host np.argsort(kind="stable") permutation, order // k,
+ *                         inverse argsort (stream.py:1246-1250, 1275-1276, 1527-1531)
+ *   bigrig_dequant        mx.dequantize of one expert projection (tune.py:64-70,
+ *                         precision.py:186-189)
+ *   bigrig_combine        sum_k score * y of the calling MoE block
+ */
+#ifndef BIGRIG_B200_H
+#define BIGRIG_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BIGRIG_API __attribute__((visibility("default")))
+#else
+#define BIGRIG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The Python host maps them onto the reference's exception types. */
+#define BIGRIG_OK 0
+#define BIGRIG_ERR_INVALID (-1)     /* bad argument            -> ValueError          */
+#define BIGRIG_ERR_CUDA (-2)        /* CUDA runtime failure    -> RuntimeError        */
+#define BIGRIG_ERR_UNSUPPORTED (-3) /* format not built        -> NotImplementedError */
+#define BIGRIG_ERR_WORKSPACE (-4)   /* workspace too small     -> ValueError          */
+
+/* Element types. */
+#define BIGRIG_F32 0
+#define BIGRIG_F16 1
+#define BIGRIG_BF16 2
+
+/* Router orders (see bigrig_router_topk). */
+#define BIGRIG_SOFTMAX_TOPK 0 /* softmax over E, keep top-k (OLMoE; Qwen3 with norm) */
+#define BIGRIG_TOPK_SOFTMAX 1 /* keep top-k logits, softmax over k (Mixtral, gpt-oss)  */
+
+/* Byte layout of one expert inside a slot, in the reference's packed order
+ * (bigrig_engine/stream.py:106-186): gate_proj{weight,scales,biases},
+ * up_proj{...}, down_proj{...}.  weight is uint32 codes [out, in*bits/32],
+ * scales/biases are half [out, in/group_size].  Index 0 gate, 1 up, 2 down. */
+typedef struct bigrig_expert_layout {
+  int32_t hidden;      /* H: input of gate/up, output of down            */
+  int32_t inter;       /* I: output of gate/up, input of down            */
+  int32_t bits;        /* 4 or 8                                         */
+  int32_t group_size;  /* 64                                             */
+  int32_t scale_dtype; /* BIGRIG_F16 or BIGRIG_BF16                      */
+  int32_t reserved;    /* 0                                              */
+  int64_t bytes_per_expert;
+  int64_t slot_stride; /* bytes between slots of a slab, >= bytes_per_expert, multiple of 16 */
+  int64_t weight_off[3];
+  int64_t scales_off[3];
+  int64_t biases_off[3];
+} bigrig_expert_layout;
+
+/* Library identity and the calling thread's last error message. */
+BIGRIG_API const char* bigrig_version(void);
+BIGRIG_API const char* bigrig_last_error(void);
+
+/* Check a layout for the shapes this build supports. 0 or BIGRIG_ERR_*. */
+BIGRIG_API int bigrig_check_layout(const bigrig_expert_layout* layout);
+
+/* Bytes of scratch bigrig_switch_glu / bigrig_moe_forward need for T tokens. */
+BIGRIG_API size_t bigrig_moe_workspace_bytes(int T, int k, int n_experts, const bigrig_expert_layout* layout);
+
+/* Dequantise projection `proj` (0 gate, 1 up, 2 down) of the expert in slot
+ * `slot` into out[rows, cols] of the scale dtype:
+ * out = round_to_scale_dtype(f32(scale) * q + f32(bias)). */
+BIGRIG_API int bigrig_dequant(const void* slab, const bigrig_expert_layout* layout, int slot, int proj,
+                   void* out, void* stream);
+
+/* logits[T, E] (fp32) = x[T, H] (bf16) . w[E, H]^T (bf16) + bias[E] (fp32, may be NULL). */
+BIGRIG_API int bigrig_router_logits(const void* x, const void* w, const float* bias, float* logits,
+                         int T, int H, int E, void* stream);
+
+/* Top-k routing over logits[T, E] (BIGRIG_F32 or BIGRIG_BF16).  indices[T, k] in
+ * rank order (largest logit first, ties to the lower expert id); scores[T, k]
+ * fp32 per `mode`; norm_topk renormalises softmax_topk scores to sum to 1. */
+BIGRIG_API int bigrig_router_topk(const void* logits, int logits_dtype, int T, int E, int k, int mode,
+                       int norm_topk, int32_t* indices, float* scores, void* stream);
+
+/* Stable expert-sorted permutation of the T*k (token, k) pairs in indices[T, k].
+ * order[P]: pair ids sorted by expert (stable); inv[P]: inverse permutation;
+ * offsets[E+1]: counting-sort offsets per expert id; seg_expert[E] / seg_start[E+1]
+ * / num_seg[1]: the non-empty experts in ascending id and where their run starts.
+ * An expert id outside [0, E) returns BIGRIG_ERR_INVALID only when it is detected
+ * on the host; on the device it is counted in err_count[1] (may be NULL). */
+BIGRIG_API int bigrig_moe_permute(const int32_t* indices, int T, int k, int E, int32_t* order, int32_t* inv,
+                       int32_t* offsets, int32_t* seg_expert, int32_t* seg_start, int32_t* num_seg,
+                       int32_t* err_count, void* stream);
+
+/* Unreduced SwiGLU experts: y[T, k, H] (bf16) with
+ * y[t, j] = down(silu(gate(x[t])) * up(x[t])) of expert indices[t, j], read from
+ * slot g2s[indices[t, j]] of `slab` (g2s NULL: slot == expert id).  x is bf16
+ * [T, H].  A slot id < 0 is counted in the workspace error word and its rows are
+ * written as zeros (the host pool guarantees residency before the call). */
+BIGRIG_API int bigrig_switch_glu(const void* x, const int32_t* indices, int T, int k, int n_experts,
+                      const int32_t* g2s, const void* slab, const bigrig_expert_layout* layout,
+                      void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[T, H] (bf16) = sum_j scores[t, j] * y[t, j, :], fp32 accumulation in j order. */
+BIGRIG_API int bigrig_combine(const void* y, const float* scores, int T, int k, int H, void* out,
+                   void* stream);
+
+/* The whole MoE layer from router logits: top-k + softmax (mode, norm_topk),
+ * bigrig_switch_glu, combine.  Writes out[T, H] bf16 and, when not NULL,
+ * indices_out[T, k] / scores_out[T, k]. */
+BIGRIG_API int bigrig_moe_forward(const void* x, const void* logits, int logits_dtype, int T, int E, int k,
+                       int mode, int norm_topk, const int32_t* g2s, const void* slab,
+                       const bigrig_expert_layout* layout, void* out, int32_t* indices_out,
+                       float* scores_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Kernel ids for the timing hooks below. */
+#define BIGRIG_K_ROUTER_LOGITS 0
+#define BIGRIG_K_ROUTER_TOPK 1
+#define BIGRIG_K_PERMUTE 2
+#define BIGRIG_K_GATE_UP 3
+#define BIGRIG_K_DOWN 4
+#define BIGRIG_K_COMBINE 5
+#define BIGRIG_K_DEQUANT 6
+#define BIGRIG_K_COUNT 7
+
+/* CUDA-event timing of this library's kernel launches, off by default.  `mask`
+ * selects kernel ids (bit i = id i); each selected launch is bracketed by two
+ * events on its own stream (do not enable it while a stream is being captured
+ * into a graph).  bigrig_timing_read waits for the recorded events of
+ * `kernel_id`, returns the sum of their durations and how many launches were
+ * timed since the last read, and forgets them.  bigrig_launch_counts fills
+ * out[BIGRIG_K_COUNT] with every launch issued since the library loaded, timed
+ * or not. */
+BIGRIG_API int bigrig_timing_enable(int mask);
+BIGRIG_API int bigrig_timing_read(int kernel_id, double* total_ms, int64_t* launches);
+BIGRIG_API int bigrig_launch_counts(int64_t* out);
+BIGRIG_API const char* bigrig_kernel_name(int kernel_id);
+
+/* Device error word of a workspace (slots < 0, ids out of range), copied to *out
+ * with a synchronous read on `stream`; resets it to 0.  For tests and debugging. */
+BIGRIG_API int bigrig_workspace_errors(void* workspace, int32_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BIGRIG_B200_H */

@@ -1,0 +1,70 @@
+"""SwiGLU expert layer over MLX-affine experts, restated in numpy.  TEST INFRASTRUCTURE ONLY.
+
+Follows the reference's by-hand oracle (tests/test_plan_invariance.py:149-160):
+``y = (silu(x . Wg^T) * (x . Wu^T)) . Wd^T`` per (token, expert) pair, with the
+weights dequantised from their affine codes, and the per-expert call order of
+``_forward_views_one`` (bigrig_engine/stream.py:1278-1318): up, gate,
+``act(up, gate) = silu(gate) * up``, down.  The layer returns the pairs
+unreduced, ``y[..., k, H]`` (bigrig_engine/stream.py:1523-1525); the caller's
+MoE block applies ``sum_k score_k * y_k``.
+
+Rounding points mirror a bf16 model: every projection output and the activation
+are stored as bf16 (the activation dtype), accumulation is fp32.  The
+``intermediate="f32"`` switch keeps them in fp32 instead; the two agree within
+the 1e-2 relative / 2e-3 absolute tolerance the parity tests use, which is the
+point of offering both.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .affine import bf16_round, dequantize_f32
+
+PROJ = ("gate_proj", "up_proj", "down_proj")
+
+
+def silu(g: np.ndarray) -> np.ndarray:
+    g = g.astype(np.float32)
+    return (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
+
+
+def expert_weights_f32(expert: dict, group_size: int, bits: int, scale_dtype: str) -> dict:
+    """{proj: fp32 [out, in]} for one expert given {proj: (codes, scales_bits, biases_bits)}."""
+    return {p: dequantize_f32(*expert[p], group_size, bits, scale_dtype) for p in PROJ}
+
+
+def expert_forward(x: np.ndarray, w: dict, intermediate: str = "bf16") -> np.ndarray:
+    """x fp32 [R, H] (values of a bf16 tensor) -> y fp32 [R, H] (values of bf16)."""
+    rnd = bf16_round if intermediate == "bf16" else (lambda a: a.astype(np.float32))
+    up = rnd(x @ w["up_proj"].T)
+    gate = rnd(x @ w["gate_proj"].T)
+    h = rnd(silu(gate) * up)
+    return bf16_round(h @ w["down_proj"].T)
+
+
+def switch_glu(x: np.ndarray, indices: np.ndarray, weights_of, intermediate: str = "bf16"):
+    """Unreduced expert outputs.  x [T, H] fp32, indices [T, k] int -> y [T, k, H] fp32.
+
+    ``weights_of(e)`` returns the fp32 weight dict of expert ``e``.  Pairs are
+    grouped by expert (each expert's weights dequantised once) and written back
+    in the caller's (token, k) order, which is what the inverse permutation of
+    bigrig_engine/stream.py:1246-1276 achieves.
+    """
+    T, k = indices.shape
+    H = x.shape[1]
+    y = np.zeros((T, k, H), dtype=np.float32)
+    flat = indices.reshape(-1)
+    for e in np.unique(flat):
+        pos = np.nonzero(flat == e)[0]
+        rows = x[pos // k]
+        y.reshape(T * k, H)[pos] = expert_forward(rows, weights_of(int(e)), intermediate)
+    return y
+
+
+def combine(y: np.ndarray, scores: np.ndarray) -> np.ndarray:
+    """sum_k score[t, k] * y[t, k, :] accumulated in fp32 in k order, stored as bf16."""
+    T, k, H = y.shape
+    acc = np.zeros((T, H), dtype=np.float32)
+    for j in range(k):
+        acc = (acc + scores[:, j:j + 1].astype(np.float32) * y[:, j, :]).astype(np.float32)
+    return bf16_round(acc)

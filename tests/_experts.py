@@ -1,0 +1,74 @@
+"""Seeded synthetic MoE layers for the parity tests: oracle-quantised experts packed into
+an HBM slab, plus the oracle's fp32 view of the same bytes.  Test infrastructure."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import affine, moe
+from bigrig_b200 import formats
+
+
+class Layer:
+    """E experts of an (H, I) SwiGLU layer, weights N(0, std) quantised to the affine format."""
+
+    def __init__(self, H, I, E, bits=4, scale_dtype="float16", seed=0, std=0.02, device="cuda",
+                 slot_order=None):
+        self.H, self.I, self.E, self.bits, self.sd = H, I, E, bits, scale_dtype
+        self.spec = formats.make_spec(H, I, bits, 64, scale_dtype)
+        self.layout = formats.layout_from_spec(self.spec, {"bits": bits, "group_size": 64,
+                                                           "mode": "affine"})
+        rng = np.random.default_rng(seed)
+        self.q = {}
+        blobs = []
+        for e in range(E):
+            parts, qe = {}, {}
+            for p in moe.PROJ:
+                o, i = (H, I) if p == "down_proj" else (I, H)
+                w = (rng.standard_normal((o, i), dtype=np.float32) * std).astype(np.float32)
+                codes, s, b = affine.quantize(w, 64, bits, scale_dtype)
+                qe[p] = (codes, s, b)
+                parts[p] = {"weight": codes, "scales": s, "biases": b}
+            self.q[e] = qe
+            blobs.append(formats.pack_expert(parts, self.spec))
+        self.blobs = blobs
+        order = list(range(E)) if slot_order is None else list(slot_order)
+        self.slot_of = {e: s for s, e in enumerate(order)}
+        slab = np.zeros((E, self.layout.slot_stride), dtype=np.uint8)
+        for e in range(E):
+            slab[self.slot_of[e], :self.layout.bytes_per_expert] = blobs[e]
+        self.slab = torch.from_numpy(slab).to(device)
+        self.g2s = torch.tensor([self.slot_of[e] for e in range(E)], dtype=torch.int32,
+                                device=device)
+        self._w = {}
+
+    def weights(self, e):
+        if e not in self._w:
+            self._w[e] = moe.expert_weights_f32(self.q[e], 64, self.bits, self.sd)
+        return self._w[e]
+
+    def oracle_switch(self, x_f32, idx):
+        return moe.switch_glu(x_f32, idx, self.weights)
+
+
+def bf16_tensor(a: np.ndarray, device="cuda") -> torch.Tensor:
+    bits = affine.f32_to_bf16_bits(a)
+    return torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(device)
+
+
+def to_f32(t: torch.Tensor) -> np.ndarray:
+    return t.float().cpu().numpy()
+
+
+def random_routing(T, k, E, rng):
+    return np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32)
+
+
+def assert_close(got, want, rtol=1e-2, atol=2e-3):
+    """The parity bar for expert outputs: |got - want| <= atol + rtol * |want| (bf16)."""
+    got = np.asarray(got, dtype=np.float32)
+    want = np.asarray(want, dtype=np.float32)
+    err = np.abs(got - want)
+    bad = err > atol + rtol * np.abs(want)
+    assert not bad.any(), (f"{int(bad.sum())} of {bad.size} outside rtol={rtol} atol={atol}; "
+                           f"max |d| {err.max():.3g}")

@@ -1,0 +1,97 @@
+"""Parity at the BASELINE configurations' full layer sizes.
+
+The numpy restatement is too slow for 128 full-size experts, so the reference
+here is built from pieces already pinned bit for bit against it: the dequant
+kernel (test_gpu_kernels) feeds a plain torch fp32 computation with the same
+bf16 rounding points.  Size-independent properties ride along: a token's outputs
+do not depend on the batch around it (bit for bit), and the permutation is a
+stable sort at the largest prefill size.
+"""
+import numpy as np
+import pytest
+import torch
+
+from bigrig_b200 import formats, ops
+from bigrig_b200.block import random_expert_bytes
+from tests._experts import assert_close
+
+pytestmark = pytest.mark.gpu
+
+torch.backends.cuda.matmul.allow_tf32 = False
+
+CONFIGS = {
+    # name: H, I, E, k, bits, scale dtype
+    "olmoe": (2048, 1024, 64, 8, 4, "float16"),
+    "qwen3": (2048, 768, 128, 8, 4, "bfloat16"),
+    "gpt_oss": (2880, 2880, 128, 4, 4, "bfloat16"),
+    "mixtral": (4096, 14336, 8, 2, 8, "float16"),
+}
+
+
+def _slab(name, device):
+    H, I, E, k, bits, sd = CONFIGS[name]
+    spec = formats.make_spec(H, I, bits, 64, sd)
+    L = formats.layout_from_spec(spec, {"bits": bits, "group_size": 64, "mode": "affine"})
+    g = torch.Generator(device=device)
+    g.manual_seed(sum(map(ord, name)))
+    slab = torch.zeros(E, L.slot_stride, dtype=torch.uint8, device=device)
+    tdt = torch.float16 if sd == "float16" else torch.bfloat16
+    for e in range(E):
+        slab[e, :L.bytes_per_expert] = random_expert_bytes(H, I, bits, 64, tdt, g, device)
+    return slab, L
+
+
+def _reference(slab, L, x, idx):
+    """y[t, j] from dequantised weights in fp32 torch, bf16 at the kernel's rounding points."""
+    T, k = idx.shape
+    y = torch.empty(T, k, L.hidden, dtype=torch.float32, device=x.device)
+    xf = x.float()
+    for e in torch.unique(idx).tolist():
+        w = [ops.dequant(slab, L, e, p).float() for p in range(3)]
+        rows = (idx == e).nonzero()
+        xe = xf[rows[:, 0]]
+        gate = (xe @ w[0].T).bfloat16().float()
+        up = (xe @ w[1].T).bfloat16().float()
+        h = (torch.nn.functional.silu(gate) * up).bfloat16().float()
+        y[rows[:, 0], rows[:, 1]] = (h @ w[2].T).bfloat16().float()
+    return y
+
+
+def _routing(T, E, k, device, seed):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    lg = torch.randn(T, E, generator=g, device=device) + torch.randn(E, generator=g, device=device)
+    return ops.router_topk(lg, k)[0]
+
+
+@pytest.mark.parametrize("name,T", [("olmoe", 1), ("olmoe", 128), ("qwen3", 1), ("qwen3", 8),
+                                    ("gpt_oss", 64), ("mixtral", 1), ("mixtral", 4)])
+def test_full_size_layer(cuda, name, T):
+    H, I, E, k, bits, sd = CONFIGS[name]
+    slab, L = _slab(name, cuda)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(T)
+    x = torch.randn(T, H, generator=g, device=cuda).bfloat16()
+    idx = _routing(T, E, k, cuda, seed=T + 1)
+    y = ops.switch_glu(x, idx, slab, L, E)
+    assert_close(y.float().cpu().numpy(), _reference(slab, L, x, idx).cpu().numpy())
+    # batch invariance: each token alone gives the same bits
+    for t in sorted({0, T // 2, T - 1}):
+        yt = ops.switch_glu(x[t:t + 1].contiguous(), idx[t:t + 1].contiguous(), slab, L, E)
+        assert torch.equal(yt[0], y[t])
+
+
+def test_permutation_is_stable_sort_at_prefill_size(cuda):
+    T, k, E = 8 * 2048, 4, 128                      # gpt-oss-shaped prefill: 65536 pairs
+    idx = _routing(T, E, k, cuda, seed=3)
+    p = ops.moe_permute(idx, E)
+    flat = idx.reshape(-1).long()
+    order = p["order"].long()
+    srt = flat[order]
+    assert torch.all(srt[1:] >= srt[:-1])
+    same = srt[1:] == srt[:-1]
+    assert torch.all(order[1:][same] > order[:-1][same])      # stable
+    assert torch.equal(torch.sort(order).values, torch.arange(T * k, device=cuda))
+    assert torch.equal(order[p["inv"].long()], torch.arange(T * k, device=cuda))
+    counts = torch.bincount(flat, minlength=E)
+    assert torch.equal(p["offsets"][1:].long() - p["offsets"][:-1].long(), counts)

@@ -1,0 +1,154 @@
+"""The numpy restatement itself: format round trips, dequant rule, router and permutation
+semantics, and the packed byte layout against the reference's shipped manifests."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import affine, moe, router
+from bigrig_b200 import formats
+from bigrig_b200.block import quantize_affine
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_pack_unpack_roundtrip(bits):
+    rng = np.random.default_rng(0)
+    q = rng.integers(0, 1 << bits, size=(7, 128)).astype(np.uint32)
+    w = affine.pack_codes(q, bits)
+    assert w.shape == (7, 128 * bits // 32) and w.dtype == np.uint32
+    np.testing.assert_array_equal(affine.unpack_codes(w, bits), q)
+    # element j of a word sits at bits [j*bits, (j+1)*bits)
+    assert int(w[0, 0]) & ((1 << bits) - 1) == int(q[0, 0])
+    assert (int(w[0, 0]) >> bits) & ((1 << bits) - 1) == int(q[0, 1])
+
+
+@pytest.mark.parametrize("sd", ["float16", "bfloat16"])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_quantize_dequantize_error_bound(sd, bits):
+    rng = np.random.default_rng(1)
+    w = (rng.standard_normal((32, 256)) * 0.02).astype(np.float32)
+    codes, s, b = affine.quantize(w, 64, bits, sd)
+    deq = affine.dequantize_f32(codes, s, b, 64, bits, sd)
+    step = affine.half_bits_to_f32(s, sd).repeat(64, axis=1)
+    assert np.all(np.abs(deq - w) <= 0.5 * step + np.abs(w) * 2e-2 + 1e-6)
+
+
+def test_dequant_rule_is_one_rounding():
+    # scale * q is exact in fp32, so the half output is round(fp32(s*q + b))
+    s = affine.f32_to_half_bits(np.float32(0.0123), "float16")
+    b = affine.f32_to_half_bits(np.float32(-0.077), "float16")
+    q = np.arange(16, dtype=np.uint32).reshape(1, 16)
+    q = np.tile(q, (1, 4))
+    codes = affine.pack_codes(q, 4)
+    out = affine.dequantize(codes, np.full((1, 1), s, np.uint16), np.full((1, 1), b, np.uint16),
+                            64, 4, "float16")
+    sf = np.float16(np.uint16(s).view(np.float16)).astype(np.float64)
+    bf = np.float16(np.uint16(b).view(np.float16)).astype(np.float64)
+    exact = (sf * q.astype(np.float64) + bf).astype(np.float32).astype(np.float16)
+    np.testing.assert_array_equal(out.view(np.float16), exact)
+
+
+def test_bf16_rounding_ties_to_even():
+    x = np.array([1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5, np.nan, np.inf], dtype=np.float32)
+    bits = affine.f32_to_bf16_bits(x)
+    assert bits[0] == 0x3F80 and bits[1] == 0x3F82
+    assert bits[3] == 0x7FC0 and bits[4] == 0x7F80
+    ref = torch.from_numpy(x[:3]).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    np.testing.assert_array_equal(bits[:3], ref)
+
+
+@pytest.mark.parametrize("sd", ["float16", "bfloat16"])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_torch_quantizer_equals_restatement(sd, bits):
+    rng = np.random.default_rng(2)
+    w = (rng.standard_normal((48, 192)) * 0.02).astype(np.float32)
+    codes, s, b = affine.quantize(w, 64, bits, sd)
+    tw, ts, tb = quantize_affine(torch.from_numpy(w), 64, bits,
+                                 torch.float16 if sd == "float16" else torch.bfloat16)
+    np.testing.assert_array_equal(tw.numpy().view(np.uint32), codes)
+    np.testing.assert_array_equal(ts.view(torch.int16).numpy().view(np.uint16), s)
+    np.testing.assert_array_equal(tb.view(torch.int16).numpy().view(np.uint16), b)
+
+
+def test_router_modes_and_ties():
+    lg = np.array([[0.5, 2.0, 2.0, -1.0, 3.0, 0.0]], dtype=np.float32)
+    idx, sc = router.topk(lg, 3, "softmax_topk")
+    assert idx.tolist() == [[4, 1, 2]]                    # ties to the lower id
+    p = router.softmax(lg)
+    np.testing.assert_allclose(sc, p[:, [4, 1, 2]], rtol=1e-6)
+    _, scn = router.topk(lg, 3, "softmax_topk", norm_topk=True)
+    np.testing.assert_allclose(scn.sum(), 1.0, rtol=1e-6)
+    idx2, sc2 = router.topk(lg, 2, "topk_softmax")
+    assert idx2.tolist() == [[4, 1]]
+    np.testing.assert_allclose(sc2, router.softmax(np.array([[3.0, 2.0]], np.float32)), rtol=1e-6)
+    with pytest.raises(ValueError):
+        router.topk(lg, 7)
+
+
+def test_permutation_semantics():
+    idx = np.array([[3, 1], [1, 0], [3, 2]])
+    p = router.permutation(idx, 4)
+    assert p["order"].tolist() == [3, 1, 2, 5, 0, 4]
+    assert p["tok"].tolist() == [1, 0, 1, 2, 0, 2]
+    assert p["rank"].tolist() == [1, 1, 0, 1, 0, 0]
+    np.testing.assert_array_equal(p["order"][p["inv"]], np.arange(6))
+    assert p["offsets"].tolist() == [0, 1, 3, 4, 6]
+    assert p["seg_expert"].tolist() == [0, 1, 2, 3]
+
+
+def test_expert_forward_matches_by_hand_formula():
+    # the reference's by-hand oracle (tests/test_plan_invariance.py:149-160), fp32 throughout
+    rng = np.random.default_rng(4)
+    H, I = 128, 64
+    ws = {}
+    for p in moe.PROJ:
+        o, i = (H, I) if p == "down_proj" else (I, H)
+        ws[p] = affine.quantize((rng.standard_normal((o, i)) * 0.05).astype(np.float32), 64, 4,
+                                "bfloat16")
+    w = moe.expert_weights_f32(ws, 64, 4, "bfloat16")
+    x = affine.bf16_round(rng.standard_normal((3, H)).astype(np.float32))
+    ref = (moe.silu(x @ w["gate_proj"].T) * (x @ w["up_proj"].T)) @ w["down_proj"].T
+    got = moe.expert_forward(x, w, "bf16")
+    got32 = moe.expert_forward(x, w, "f32")
+    assert np.abs(got - ref).max() / np.abs(ref).max() < 0.02
+    np.testing.assert_allclose(got, got32, rtol=1e-2, atol=2e-3)
+
+
+def test_spec_matches_shipped_manifests():
+    with open(os.path.join(GOLD, "manifest_golden.json")) as f:
+        m = json.load(f)
+    ol = m["OLMoE-1B-7B-0125-4bit"]
+    spec = formats.make_spec(2048, 1024, 4, 64, "float16")
+    assert spec == ol["layer0"]["spec"]
+    assert formats.bytes_per_expert(spec) == ol["layer0"]["bytes_per_expert"] == 3538944
+    assert ol["n_layers"] * 64 * 3538944 == ol["total_bytes"]
+    regions = formats.manifest_regions({"regions": ol["regions_head"]})
+    assert regions[(0, 1)] == (3538944, 3538944)
+    L = formats.layout_from_spec(spec, ol["layer0"]["quant"])
+    assert (L.hidden, L.inter, L.bits) == (2048, 1024, 4)
+    assert L.weight_off == (0, 1179648, 2359296)
+    assert L.scales_off == (1048576, 2228224, 3407872)
+    # the 3-bit manifest is a format this build does not compute
+    q3 = m["Qwen3-30B-A3B-3bit"]["layer0"]
+    with pytest.raises((NotImplementedError, ValueError)):
+        formats.layout_from_spec(q3["spec"], q3["quant"])
+
+
+def test_pack_unpack_expert_roundtrip():
+    spec = formats.make_spec(128, 64, 8, 64, "bfloat16")
+    rng = np.random.default_rng(5)
+    arrays = {p: {c: rng.integers(0, 2 ** 16, size=meta["shape"]).astype(
+        np.uint32 if meta["dtype"] == "uint32" else np.uint16) for c, meta in spec[p].items()}
+        for p in spec}
+    blob = formats.pack_expert(arrays, spec)
+    assert blob.nbytes == formats.bytes_per_expert(spec)
+    back = formats.unpack_expert(blob, spec)
+    for p in spec:
+        for c in spec[p]:
+            np.testing.assert_array_equal(back[p][c], arrays[p][c])
+    with pytest.raises(ValueError):
+        formats.unpack_expert(blob[:-1], spec)
