@@ -179,7 +179,7 @@ def cpu_decode_tokens(store, blocks_host, n_tokens: int, n_layers: int, threads:
             lg = router.router_logits(h, gw, gb)
             idx, sc = router.topk(lg, c["top_k"], "softmax_topk", False)
             ws = list(pool.map(lambda e: expert_w(li, int(e)), idx[0]))
-            y = np.stack([moe.expert_forward(h, w) for w in ws])[None]
+            y = np.concatenate([moe.expert_forward(h, w) for w in ws])[None]
             h = affine.bf16_round(h + moe.combine(y, sc))
     dt = time.perf_counter() - t0
     pool.shutdown()

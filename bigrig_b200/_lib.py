@@ -27,9 +27,11 @@ EXPORTS = (
     "bigrig_dequant", "bigrig_router_logits", "bigrig_router_topk", "bigrig_moe_permute",
     "bigrig_switch_glu", "bigrig_combine", "bigrig_moe_forward", "bigrig_workspace_errors",
     "bigrig_timing_enable", "bigrig_timing_read", "bigrig_launch_counts", "bigrig_kernel_name",
+    "bigrig_set_path",
 )
 KERNELS = {"router_logits": 0, "router_topk": 1, "permute": 2, "gate_up": 3, "down": 4,
-           "combine": 5, "dequant": 6}
+           "combine": 5, "dequant": 6, "gemm_gate_up": 7, "gemm_down": 8}
+PATHS = {"auto": 0, "gemv": 1, "gemm": 2}
 
 
 class ExpertLayout(ctypes.Structure):
@@ -71,6 +73,7 @@ _SIG = {
     "bigrig_timing_read": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
     "bigrig_launch_counts": (_I, [ctypes.POINTER(ctypes.c_int64)]),
     "bigrig_kernel_name": (ctypes.c_char_p, [_I]),
+    "bigrig_set_path": (_I, [_I, _I]),
 }
 
 
@@ -146,3 +149,13 @@ def timing_read(kernel: str) -> tuple:
     check(load().bigrig_timing_read(KERNELS[kernel], ctypes.byref(ms), ctypes.byref(n)),
           "timing_read")
     return float(ms.value), int(n.value)
+
+
+def set_path(mode: str = "auto", gemm_min_rows: int = 8) -> str:
+    """Choose the expert kernels: "auto" (GEMV for decode-sized calls, the tcgen05 grouped
+    GEMM once the mean rows per routed expert reaches ``gemm_min_rows``), "gemv" or
+    "gemm".  Returns the previous mode."""
+    rc = load().bigrig_set_path(PATHS[mode], int(gemm_min_rows))
+    if rc < 0:
+        check(rc, "set_path")
+    return {v: k for k, v in PATHS.items()}[rc]

@@ -53,10 +53,12 @@ cudaEvent_t take_event() {
   if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
   return e;
 }
-const char* kKernelNames[BIGRIG_K_COUNT] = {"router_logits_kernel", "router_topk_kernel",
-                                            "permute_kernel",       "gemv_gate_up_kernel",
-                                            "gemv_down_kernel",     "combine_kernel",
-                                            "dequant_kernel"};
+const char* kKernelNames[BIGRIG_K_COUNT] = {
+    "router_logits_kernel", "router_topk_kernel", "permute_kernel",
+    "gemv_gate_up_kernel",  "gemv_down_kernel",   "combine_kernel",
+    "dequant_kernel",       "grouped_gemm_kernel<gate_up>", "grouped_gemm_kernel<down>"};
+std::atomic<int> g_path{BIGRIG_PATH_AUTO};
+std::atomic<int> g_gemm_min_rows{8};
 }  // namespace
 
 TimedLaunch::TimedLaunch(int kernel_id, cudaStream_t s) : id_(kernel_id), s_(s), start_(nullptr) {
@@ -184,6 +186,14 @@ int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, c
   rv.k = k;
   rv.s_max = P < E ? P : E;
   rv.max_rows = T;
+  const int path = g_path.load();
+  const bool gemm = path == BIGRIG_PATH_GEMM ||
+                    (path == BIGRIG_PATH_AUTO && P >= g_gemm_min_rows.load() * (P < E ? P : E));
+  if (gemm) {
+    const int bn = gemm_token_tile(T, k, E);
+    if (int rc = launch_gemm_gate_up(x, rv, slab, L, ws.h, bn, s)) return rc;
+    return launch_gemm_down(ws.h, rv, slab, L, y, bn, s);
+  }
   if (int rc = launch_gemv_gate_up(x, rv, slab, L, ws.h, s)) return rc;
   return launch_gemv_down(ws.h, rv, slab, L, y, s);
 }
@@ -297,6 +307,14 @@ int bigrig_moe_forward(const void* x, const void* logits, int logits_dtype, int 
     return rc;
   if (int rc = run_switch_glu(x, idx, T, k, E, g2s, slab, *layout, ws.y, ws, s)) return rc;
   return launch_combine(ws.y, sc, T, k, layout->hidden, out, s);
+}
+
+int bigrig_set_path(int mode, int gemm_min_rows) {
+  if (mode < BIGRIG_PATH_AUTO || mode > BIGRIG_PATH_GEMM || gemm_min_rows < 1)
+    return set_error(BIGRIG_ERR_INVALID, "set_path: mode=%d gemm_min_rows=%d", mode, gemm_min_rows);
+  const int prev = g_path.exchange(mode);
+  g_gemm_min_rows.store(gemm_min_rows);
+  return prev;
 }
 
 int bigrig_timing_enable(int mask) {

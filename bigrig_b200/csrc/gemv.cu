@@ -68,27 +68,50 @@ __device__ __forceinline__ float chunk_dot(const uint4 w, const float4* __restri
 // Stage `nr` activation rows (bf16, gathered through `row_of`) into shared memory
 // as pre-scaled fp32 in a [row][CPL/4][chunk] float4 layout, so that lanes reading
 // consecutive chunks hit consecutive banks; plus the plain fp32 sum of each chunk.
+// Rows are read as 128-bit vectors; the lanes holding one chunk's vectors are
+// adjacent, so a chunk's sum is a two- or four-lane shuffle reduction.
 template <int BITS, typename RowOf>
 __device__ __forceinline__ void stage_rows(float* __restrict__ smem, const uint16_t* __restrict__ src,
                                            int K, int nr, int rows_cap, RowOf row_of) {
   constexpr int CPL = 128 / BITS;
   constexpr int Q = CPL / 4;
+  constexpr int VPC = CPL / 8;             // 8-element vectors per chunk (4 or 2)
   const int nchunk = K / CPL;
+  const int nvec = K / 8;
   float4* xs = reinterpret_cast<float4*>(smem);
   float* cs = smem + static_cast<size_t>(rows_cap) * K;
-  for (int idx = threadIdx.x; idx < nr * K; idx += blockDim.x) {
-    const int rr = idx / K, kk = idx - rr * K;
-    const float v = bf16_bits_to_f32(src[row_of(rr) * static_cast<size_t>(K) + kk]);
-    const int c = kk / CPL, j = kk - c * CPL;
-    float* dst = reinterpret_cast<float*>(&xs[(static_cast<size_t>(rr) * Q + (j >> 2)) * nchunk + c]);
-    dst[j & 3] = v * prescale<BITS>(kk);
-  }
-  for (int idx = threadIdx.x; idx < nr * nchunk; idx += blockDim.x) {
-    const int rr = idx / nchunk, c = idx - rr * nchunk;
-    const uint16_t* p = src + row_of(rr) * static_cast<size_t>(K) + static_cast<size_t>(c) * CPL;
-    float sacc = 0.f;
-    for (int j = 0; j < CPL; ++j) sacc += bf16_bits_to_f32(p[j]);
-    cs[rr * nchunk + c] = sacc;
+  const int total = nr * nvec;
+  for (int base = 0; base < total; base += blockDim.x) {
+    const int idx = base + threadIdx.x;
+    const bool active = idx < total;
+    float part = 0.f;
+    int rr = 0, v = 0;
+    if (active) {
+      rr = idx / nvec;
+      v = idx - rr * nvec;
+      const uint4 raw = *reinterpret_cast<const uint4*>(src + row_of(rr) * static_cast<size_t>(K) + v * 8);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+      float f[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) part += f[i];
+      const int kk0 = v * 8;
+      const int c = kk0 / CPL, q0 = (kk0 - c * CPL) >> 2;
+      xs[(static_cast<size_t>(rr) * Q + q0) * nchunk + c] =
+          make_float4(f[0] * prescale<BITS>(kk0), f[1] * prescale<BITS>(kk0 + 1),
+                      f[2] * prescale<BITS>(kk0 + 2), f[3] * prescale<BITS>(kk0 + 3));
+      xs[(static_cast<size_t>(rr) * Q + q0 + 1) * nchunk + c] =
+          make_float4(f[4] * prescale<BITS>(kk0 + 4), f[5] * prescale<BITS>(kk0 + 5),
+                      f[6] * prescale<BITS>(kk0 + 6), f[7] * prescale<BITS>(kk0 + 7));
+    }
+    // the VPC vectors of a chunk sit in adjacent lanes (nvec is a multiple of VPC)
+#pragma unroll
+    for (int o = 1; o < VPC; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (active && (v % VPC) == 0) cs[rr * nchunk + v / VPC] = part;
   }
 }
 
@@ -117,6 +140,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_gate_up_kernel(
     const uint16_t* __restrict__ x, RouteView rv, const uint8_t* __restrict__ slab,
     bigrig_expert_layout L, uint16_t* __restrict__ h, int rows_cap) {
   extern __shared__ __align__(16) float smem[];
+  __shared__ int row_tok[kGemvRows];
   constexpr int CPL = 128 / BITS;
   constexpr int Q = CPL / 4;
   const int s = blockIdx.y;
@@ -144,7 +168,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_gate_up_kernel(
   for (int r0 = 0; r0 < R; r0 += rows_cap) {
     const int nr = min(rows_cap, R - r0);
     __syncthreads();
-    stage_rows<BITS>(smem, x, H, nr, rows_cap, [&](int rr) { return rv.order[row0 + r0 + rr] / rv.k; });
+    if (threadIdx.x < nr) row_tok[threadIdx.x] = rv.order[row0 + r0 + threadIdx.x] / rv.k;
+    __syncthreads();
+    stage_rows<BITS>(smem, x, H, nr, rows_cap, [&](int rr) { return row_tok[rr]; });
     __syncthreads();
     float acc[2][NR][ROWS];
 #pragma unroll

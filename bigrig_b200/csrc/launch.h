@@ -53,6 +53,11 @@ int launch_gemv_gate_up(const void* x, const RouteView& rv, const void* slab,
                         const bigrig_expert_layout& L, void* h, cudaStream_t s);
 int launch_gemv_down(const void* h, const RouteView& rv, const void* slab,
                      const bigrig_expert_layout& L, void* y, cudaStream_t s);
+int gemm_token_tile(int T, int k, int E);
+int launch_gemm_gate_up(const void* x, const RouteView& rv, const void* slab,
+                        const bigrig_expert_layout& L, void* h, int bn, cudaStream_t s);
+int launch_gemm_down(const void* h, const RouteView& rv, const void* slab,
+                     const bigrig_expert_layout& L, void* y, int bn, cudaStream_t s);
 int launch_combine(const void* y, const float* scores, int T, int k, int H, void* out,
                    cudaStream_t s);
 

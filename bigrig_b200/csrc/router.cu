@@ -192,6 +192,56 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
   }
 }
 
+// Decode-sized permutation (P <= 32 pairs): one warp.  Lane i holds pair i; its
+// sorted position is the number of pairs (e_j, j) lexicographically below (e_i, i),
+// which is the stable order; runs of equal experts become the segments.
+__global__ void __launch_bounds__(32) permute_warp_kernel(
+    const int32_t* __restrict__ idx, int P, int E, int32_t* __restrict__ order,
+    int32_t* __restrict__ inv, int32_t* __restrict__ offsets, int32_t* __restrict__ seg_expert,
+    int32_t* __restrict__ seg_start, int32_t* __restrict__ num_seg, int32_t* __restrict__ err) {
+  const int lane = threadIdx.x;
+  int e = lane < P ? idx[lane] : 0x7fffffff;
+  const bool bad = lane < P && (e < 0 || e >= E);
+  if (bad) e = 0x7ffffffe;                      // sorts after every valid id, before padding
+  const unsigned nbad = __popc(__ballot_sync(0xffffffffu, bad));
+  if (lane == 0 && nbad && err) atomicAdd(err, static_cast<int>(nbad));
+  int rank = 0;
+  for (int j = 0; j < 32; ++j) {
+    const int ej = __shfl_sync(0xffffffffu, e, j);
+    rank += (ej < e) || (ej == e && j < lane);
+  }
+  if (lane < P) {
+    order[rank] = lane;
+    inv[lane] = rank;
+  }
+  // expert of sorted position `lane`
+  int se = 0x7fffffff;
+  for (int j = 0; j < 32; ++j) {
+    const int rj = __shfl_sync(0xffffffffu, rank, j);
+    const int ej = __shfl_sync(0xffffffffu, e, j);
+    if (rj == lane) se = ej;
+  }
+  const int prev = __shfl_up_sync(0xffffffffu, se, 1);
+  const bool first = lane < P && se < E && (lane == 0 || prev != se);
+  const unsigned firsts = __ballot_sync(0xffffffffu, first);
+  if (first) {
+    const int si = __popc(firsts & ((1u << lane) - 1u));
+    seg_expert[si] = se;
+    seg_start[si] = lane;
+  }
+  const int nvalid = P - static_cast<int>(nbad);
+  if (lane == 0) {
+    *num_seg = __popc(firsts);
+    seg_start[__popc(firsts)] = nvalid;
+  }
+  for (int x0 = 0; x0 <= E; x0 += 32) {          // uniform trip count: every lane shuffles
+    const int x = x0 + lane;
+    int below = 0;
+    for (int j = 0; j < P; ++j) below += __shfl_sync(0xffffffffu, e, j) < x;
+    if (x <= E) offsets[x] = below;
+  }
+}
+
 // ---------------------------------------------------------------- launchers
 int launch_router_logits(const void* x, const void* w, const float* bias, float* logits, int T,
                          int H, int E, cudaStream_t s) {
@@ -232,6 +282,11 @@ int launch_permute(const int32_t* indices, int P, int E, int32_t* order, int32_t
                    int32_t* offsets, int32_t* seg_expert, int32_t* seg_start, int32_t* num_seg,
                    int32_t* err, cudaStream_t s) {
   TimedLaunch tl(BIGRIG_K_PERMUTE, s);
+  if (P <= 32) {
+    permute_warp_kernel<<<1, 32, 0, s>>>(indices, P, E, order, inv, offsets, seg_expert, seg_start,
+                                         num_seg, err);
+    return check_launch("permute_warp_kernel");
+  }
   permute_kernel<<<1, kPermThreads, 0, s>>>(indices, P, E, order, inv, offsets, seg_expert,
                                             seg_start, num_seg, err);
   return check_launch("permute_kernel");

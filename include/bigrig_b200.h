@@ -139,7 +139,19 @@ BIGRIG_API int bigrig_moe_forward(const void* x, const void* logits, int logits_
 #define BIGRIG_K_DOWN 4
 #define BIGRIG_K_COMBINE 5
 #define BIGRIG_K_DEQUANT 6
-#define BIGRIG_K_COUNT 7
+#define BIGRIG_K_GEMM_GATE_UP 7
+#define BIGRIG_K_GEMM_DOWN 8
+#define BIGRIG_K_COUNT 9
+
+/* Which expert kernels bigrig_switch_glu / bigrig_moe_forward use:
+ * BIGRIG_PATH_AUTO picks the grouped GEMV when an expert gets few rows (decode)
+ * and the tcgen05 grouped GEMM when the mean rows per routed expert reaches
+ * `gemm_min_rows`; the other two force one path.  Process-wide; returns the
+ * previous mode. */
+#define BIGRIG_PATH_AUTO 0
+#define BIGRIG_PATH_GEMV 1
+#define BIGRIG_PATH_GEMM 2
+BIGRIG_API int bigrig_set_path(int mode, int gemm_min_rows);
 
 /* CUDA-event timing of this library's kernel launches, off by default.  `mask`
  * selects kernel ids (bit i = id i); each selected launch is bracketed by two

@@ -28,9 +28,20 @@ def silu(g: np.ndarray) -> np.ndarray:
     return (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
 
 
-def expert_weights_f32(expert: dict, group_size: int, bits: int, scale_dtype: str) -> dict:
-    """{proj: fp32 [out, in]} for one expert given {proj: (codes, scales_bits, biases_bits)}."""
-    return {p: dequantize_f32(*expert[p], group_size, bits, scale_dtype) for p in PROJ}
+def expert_weights_f32(expert: dict, group_size: int, bits: int, scale_dtype: str,
+                       weight_round: str | None = None) -> dict:
+    """{proj: fp32 [out, in]} for one expert given {proj: (codes, scales_bits, biases_bits)}.
+
+    ``weight_round="bf16"`` rounds each dequantised weight to bf16 once, as a
+    multi-row quantized matmul does when it dequantises a weight tile into the
+    activation dtype before the matrix product; None keeps the exact fp32 value,
+    as the one-row (GEMV) form ``s * sum(q x) + b * sum(x)`` effectively uses."""
+    out = {p: dequantize_f32(*expert[p], group_size, bits, scale_dtype) for p in PROJ}
+    if weight_round == "bf16":
+        out = {p: bf16_round(w) for p, w in out.items()}
+    elif weight_round is not None:
+        raise ValueError(f"weight_round must be None or 'bf16', got {weight_round!r}")
+    return out
 
 
 def expert_forward(x: np.ndarray, w: dict, intermediate: str = "bf16") -> np.ndarray:

@@ -42,13 +42,14 @@ class Layer:
                                 device=device)
         self._w = {}
 
-    def weights(self, e):
-        if e not in self._w:
-            self._w[e] = moe.expert_weights_f32(self.q[e], 64, self.bits, self.sd)
-        return self._w[e]
+    def weights(self, e, weight_round=None):
+        key = (e, weight_round)
+        if key not in self._w:
+            self._w[key] = moe.expert_weights_f32(self.q[e], 64, self.bits, self.sd, weight_round)
+        return self._w[key]
 
-    def oracle_switch(self, x_f32, idx):
-        return moe.switch_glu(x_f32, idx, self.weights)
+    def oracle_switch(self, x_f32, idx, weight_round=None):
+        return moe.switch_glu(x_f32, idx, lambda e: self.weights(e, weight_round))
 
 
 def bf16_tensor(a: np.ndarray, device="cuda") -> torch.Tensor:

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from bigrig_b200 import formats, ops
+from bigrig_b200 import _lib, formats, ops
 from bigrig_b200.block import random_expert_bytes
 from tests._experts import assert_close
 
@@ -41,13 +41,16 @@ def _slab(name, device):
     return slab, L
 
 
-def _reference(slab, L, x, idx):
-    """y[t, j] from dequantised weights in fp32 torch, bf16 at the kernel's rounding points."""
+def _reference(slab, L, x, idx, bf16_weights=False):
+    """y[t, j] from dequantised weights in fp32 torch, bf16 at the kernel's rounding points
+    (and the weights themselves rounded to bf16 for the tensor-core path)."""
     T, k = idx.shape
     y = torch.empty(T, k, L.hidden, dtype=torch.float32, device=x.device)
     xf = x.float()
     for e in torch.unique(idx).tolist():
         w = [ops.dequant(slab, L, e, p).float() for p in range(3)]
+        if bf16_weights:
+            w = [t.bfloat16().float() for t in w]
         rows = (idx == e).nonzero()
         xe = xf[rows[:, 0]]
         gate = (xe @ w[0].T).bfloat16().float()
@@ -64,21 +67,30 @@ def _routing(T, E, k, device, seed):
     return ops.router_topk(lg, k)[0]
 
 
-@pytest.mark.parametrize("name,T", [("olmoe", 1), ("olmoe", 128), ("qwen3", 1), ("qwen3", 8),
-                                    ("gpt_oss", 64), ("mixtral", 1), ("mixtral", 4)])
-def test_full_size_layer(cuda, name, T):
+@pytest.mark.parametrize("name,T,path", [
+    ("olmoe", 1, "gemv"), ("olmoe", 128, "gemv"), ("olmoe", 128, "gemm"), ("olmoe", 2048, "gemm"),
+    ("qwen3", 1, "gemv"), ("qwen3", 8, "gemv"), ("qwen3", 4096, "gemm"),
+    ("gpt_oss", 64, "gemv"), ("gpt_oss", 512, "gemm"),
+    ("mixtral", 1, "gemv"), ("mixtral", 4, "gemv"), ("mixtral", 1024, "gemm")])
+def test_full_size_layer(cuda, name, T, path):
     H, I, E, k, bits, sd = CONFIGS[name]
     slab, L = _slab(name, cuda)
     g = torch.Generator(device=cuda)
     g.manual_seed(T)
     x = torch.randn(T, H, generator=g, device=cuda).bfloat16()
     idx = _routing(T, E, k, cuda, seed=T + 1)
-    y = ops.switch_glu(x, idx, slab, L, E)
-    assert_close(y.float().cpu().numpy(), _reference(slab, L, x, idx).cpu().numpy())
-    # batch invariance: each token alone gives the same bits
-    for t in sorted({0, T // 2, T - 1}):
-        yt = ops.switch_glu(x[t:t + 1].contiguous(), idx[t:t + 1].contiguous(), slab, L, E)
-        assert torch.equal(yt[0], y[t])
+    prev = _lib.set_path(path)
+    try:
+        y = ops.switch_glu(x, idx, slab, L, E)
+        ref = _reference(slab, L, x, idx, bf16_weights=(path == "gemm"))
+        assert_close(y.float().cpu().numpy(), ref.cpu().numpy())
+        if path == "gemv":
+            # batch invariance: each token alone gives the same bits
+            for t in sorted({0, T // 2, T - 1}):
+                yt = ops.switch_glu(x[t:t + 1].contiguous(), idx[t:t + 1].contiguous(), slab, L, E)
+                assert torch.equal(yt[0], y[t])
+    finally:
+        _lib.set_path(prev)
 
 
 def test_permutation_is_stable_sort_at_prefill_size(cuda):
