@@ -128,9 +128,10 @@ def build_model(device, seed: int):
 
 
 def stack_step(blocks, x):
+    """One token through every MoE layer: h <- h + moe(h) (the residual add is fused)."""
     h = x
     for blk in blocks:
-        h = h + blk(h)
+        h = blk(h, residual=h)
     return h
 
 
@@ -275,7 +276,7 @@ def main() -> None:
     # ---- prefill: the 2048-token prompt, layer-major, through the capped pools
     if not args.no_extras:
         prompt = torch.randn(c["prompt"], c["hidden"], generator=g, device=dev).to(torch.bfloat16)
-        layers = [(lambda h, b=b: h + b(h)) for b in blocks]
+        layers = [(lambda h, b=b: b(h, residual=h)) for b in blocks]
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()

@@ -95,22 +95,22 @@ class MoEBlock:
         mode, norm = self.mode
         return ops.router_topk(logits, self.top_k, mode, norm)
 
-    def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        """x bf16 [T, H] -> combined expert output bf16 [T, H]."""
+    def __call__(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """x bf16 [T, H] -> combined expert output bf16 [T, H] (+ ``residual`` when given)."""
         mode, norm = self.mode
         sw = self.switch
         pool = getattr(sw, "_pool", None)
         if pool is not None and getattr(sw, "_sync_free", False):
-            logits = ops.router_logits(x, self.gate_w, self.gate_b)
             pool.ready()
-            out, _, _ = ops.moe_forward(x, logits, self.top_k, pool.slab, pool.layout,
-                                        self.n_experts, mode, norm, g2s=pool.g2s_device(),
-                                        workspace=sw.workspace)
+            out, _, _ = ops.moe_layer(x, self.gate_w, self.gate_b, self.top_k, pool.slab,
+                                      pool.layout, self.n_experts, mode, norm,
+                                      g2s=pool.g2s_device(), residual=residual,
+                                      workspace=sw.workspace)
             pool.mark_read()
             return out
         idx, scores = self.route(x)
         y = sw(x, idx)
-        return ops.combine(y, scores)
+        return ops.combine(y, scores, residual=residual)
 
 
 def make_blocks(n_layers: int, hidden: int, inter: int, n_experts: int, top_k: int, family: str,

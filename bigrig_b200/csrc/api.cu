@@ -56,7 +56,8 @@ cudaEvent_t take_event() {
 const char* kKernelNames[BIGRIG_K_COUNT] = {
     "router_logits_kernel", "router_topk_kernel", "permute_kernel",
     "gemv_gate_up_kernel",  "gemv_down_kernel",   "combine_kernel",
-    "dequant_kernel",       "grouped_gemm_kernel<gate_up>", "grouped_gemm_kernel<down>"};
+    "dequant_kernel",       "grouped_gemm_kernel<gate_up>", "grouped_gemm_kernel<down>",
+    "route_kernel",         "down_combine_kernel"};
 std::atomic<int> g_path{BIGRIG_PATH_AUTO};
 std::atomic<int> g_gemm_min_rows{8};
 }  // namespace
@@ -100,6 +101,8 @@ struct Workspace {
   uint16_t* y;        // [P, H] bf16, (token, k) order (moe_forward only)
   int32_t* indices;   // [P] (moe_forward when the caller passes none)
   float* scores;      // [P]
+  float* logits;      // [T, E] (fused decode route)
+  int32_t* ticket;    // last-CTA counter of the fused route, zero between calls
 };
 
 size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Workspace* w) {
@@ -122,6 +125,8 @@ size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Wor
   ws.y = static_cast<uint16_t*>(take(P * L.hidden * sizeof(uint16_t)));
   ws.indices = static_cast<int32_t*>(take(P * sizeof(int32_t)));
   ws.scores = static_cast<float*>(take(P * sizeof(float)));
+  ws.logits = static_cast<float*>(take(static_cast<size_t>(T) * E * sizeof(float)));
+  ws.ticket = static_cast<int32_t*>(take(sizeof(int32_t)));
   if (w) *w = ws;
   return off;
 }
@@ -168,6 +173,41 @@ int check_route(int T, int k, int E) {
   return BIGRIG_OK;
 }
 
+RouteView route_view(const Workspace& ws, const int32_t* g2s, int T, int k, int E) {
+  RouteView rv;
+  rv.order = ws.order;
+  rv.inv = ws.inv;
+  rv.seg_expert = ws.seg_expert;
+  rv.seg_start = ws.seg_start;
+  rv.num_seg = ws.num_seg;
+  rv.g2s = g2s;
+  rv.err = ws.err;
+  rv.P = T * k;
+  rv.k = k;
+  rv.s_max = rv.P < E ? rv.P : E;
+  rv.max_rows = T;
+  return rv;
+}
+
+// Decode-sized calls take the fused three-kernel chain.
+bool fused_decode(int T, int k, const bigrig_expert_layout& L) {
+  return g_path.load() != BIGRIG_PATH_GEMM && T * k <= 32 &&
+         down_combine_smem(T * k, L) <= 200 * 1024;
+}
+
+int run_fused(const void* x, const void* gate_w, const float* gate_b, const void* logits,
+              int logits_dtype, int T, int k, int E, int mode, int norm, const int32_t* g2s,
+              const void* slab, const bigrig_expert_layout& L, const void* residual, void* out,
+              int32_t* idx, float* sc, const Workspace& ws, cudaStream_t s) {
+  RouteOut ro{ws.order, ws.inv, ws.offsets, ws.seg_expert, ws.seg_start, ws.num_seg, ws.err};
+  if (int rc = launch_route(x, gate_w, gate_b, logits, logits_dtype, T, L.hidden, E, k, mode, norm,
+                            ws.logits, ws.ticket, idx, sc, ro, s))
+    return rc;
+  const RouteView rv = route_view(ws, g2s, T, k, E);
+  if (int rc = launch_gemv_gate_up(x, rv, slab, L, ws.h, s)) return rc;
+  return launch_down_combine(ws.h, rv, slab, L, sc, residual, out, nullptr, T, s);
+}
+
 int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, const int32_t* g2s,
                    const void* slab, const bigrig_expert_layout& L, void* y, const Workspace& ws,
                    cudaStream_t s) {
@@ -175,17 +215,7 @@ int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, c
   if (int rc = launch_permute(indices, P, E, ws.order, ws.inv, ws.offsets, ws.seg_expert,
                               ws.seg_start, ws.num_seg, ws.err, s))
     return rc;
-  RouteView rv;
-  rv.order = ws.order;
-  rv.seg_expert = ws.seg_expert;
-  rv.seg_start = ws.seg_start;
-  rv.num_seg = ws.num_seg;
-  rv.g2s = g2s;
-  rv.err = ws.err;
-  rv.P = P;
-  rv.k = k;
-  rv.s_max = P < E ? P : E;
-  rv.max_rows = T;
+  const RouteView rv = route_view(ws, g2s, T, k, E);
   const int path = g_path.load();
   const bool gemm = path == BIGRIG_PATH_GEMM ||
                     (path == BIGRIG_PATH_AUTO && P >= g_gemm_min_rows.load() * (P < E ? P : E));
@@ -303,10 +333,50 @@ int bigrig_moe_forward(const void* x, const void* logits, int logits_dtype, int 
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   int32_t* idx = indices_out ? indices_out : ws.indices;
   float* sc = scores_out ? scores_out : ws.scores;
+  if (mode != BIGRIG_SOFTMAX_TOPK && mode != BIGRIG_TOPK_SOFTMAX)
+    return set_error(BIGRIG_ERR_INVALID, "moe_forward: mode=%d", mode);
+  if (logits_dtype != BIGRIG_F32 && logits_dtype != BIGRIG_BF16)
+    return set_error(BIGRIG_ERR_INVALID, "moe_forward: logits dtype must be F32 or BF16");
+  if (fused_decode(T, k, *layout))
+    return run_fused(x, nullptr, nullptr, logits, logits_dtype, T, k, E, mode, norm_topk, g2s, slab,
+                     *layout, nullptr, out, idx, sc, ws, s);
   if (int rc = bigrig_router_topk(logits, logits_dtype, T, E, k, mode, norm_topk, idx, sc, stream))
     return rc;
   if (int rc = run_switch_glu(x, idx, T, k, E, g2s, slab, *layout, ws.y, ws, s)) return rc;
   return launch_combine(ws.y, sc, T, k, layout->hidden, out, s);
+}
+
+int bigrig_moe_layer(const void* x, const void* gate_w, const float* gate_b, int T, int E, int k,
+                     int mode, int norm_topk, const int32_t* g2s, const void* slab,
+                     const bigrig_expert_layout* layout, const void* residual, void* out,
+                     int32_t* indices_out, float* scores_out, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (int rc = check_layout(layout)) return rc;
+  if (int rc = check_route(T, k, E)) return rc;
+  if (T == 0) return BIGRIG_OK;
+  if (!x || !gate_w || !slab || !out || !workspace)
+    return set_error(BIGRIG_ERR_INVALID, "moe_layer: NULL pointer");
+  if (mode != BIGRIG_SOFTMAX_TOPK && mode != BIGRIG_TOPK_SOFTMAX)
+    return set_error(BIGRIG_ERR_INVALID, "moe_layer: mode=%d", mode);
+  if (layout->hidden % 8)
+    return set_error(BIGRIG_ERR_INVALID, "moe_layer: hidden must be a multiple of 8");
+  const size_t need = carve(nullptr, T, k, E, *layout, nullptr);
+  if (workspace_bytes < need)
+    return set_error(BIGRIG_ERR_WORKSPACE, "moe_layer: workspace %zu bytes < %zu needed",
+                     workspace_bytes, need);
+  Workspace ws;
+  carve(workspace, T, k, E, *layout, &ws);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* idx = indices_out ? indices_out : ws.indices;
+  float* sc = scores_out ? scores_out : ws.scores;
+  if (fused_decode(T, k, *layout))
+    return run_fused(x, gate_w, gate_b, nullptr, BIGRIG_F32, T, k, E, mode, norm_topk, g2s, slab,
+                     *layout, residual, out, idx, sc, ws, s);
+  if (int rc = launch_router_logits(x, gate_w, gate_b, ws.logits, T, layout->hidden, E, s)) return rc;
+  if (int rc = launch_router_topk(ws.logits, BIGRIG_F32, T, E, k, mode, norm_topk, idx, sc, s))
+    return rc;
+  if (int rc = run_switch_glu(x, idx, T, k, E, g2s, slab, *layout, ws.y, ws, s)) return rc;
+  return launch_combine(ws.y, sc, T, k, layout->hidden, out, s, residual);
 }
 
 int bigrig_set_path(int mode, int gemm_min_rows) {

@@ -5,7 +5,7 @@
 // Replaces the reference's per-expert mx.quantized_matmul / gather_qmm over the
 // expert-sorted (token, k) pairs (bigrig_engine/stream.py:1237-1276, 1320-1336,
 // 1605-1631).  Two passes over the pairs grouped by expert:
-//   gate_up: h[p, f] = bf16(silu(bf16(x.Wg^T)) * bf16(x.Wu^T))   (two accumulators)
+//   gate_up: h[p, f] = bf16(silu(x.Wg^T) * (x.Wu^T))   (two fp32 accumulators)
 //   down:    y[pair, f] = bf16(h[p, :] . Wd^T), scattered to (token, k) order
 //
 // Swap-AB: D[feature, token] = W[feature, K] . X[token, K]^T, so the expert's
@@ -358,9 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
             if (row < R && f < NF && valid_slot) {
               const int p = row0 + row;
               if (MODE == 0) {
-                const float g = bf16_round(a[i]);
-                const float uu = bf16_round(u[i]);
-                out[static_cast<int64_t>(p) * NF + f] = f32_to_bf16_bits(silu_f32(g) * uu);
+                out[static_cast<int64_t>(p) * NF + f] = f32_to_bf16_bits(silu_f32(a[i]) * u[i]);
               } else {
                 out[static_cast<int64_t>(rv.order[p]) * NF + f] = f32_to_bf16_bits(a[i]);
               }

@@ -40,6 +40,7 @@ int launch_dequant(const void* slab, const bigrig_expert_layout& L, int slot, in
 // then down written to y[t, j, :] at each pair's unpermuted position.
 struct RouteView {
   const int32_t* order;      // [P] pair id at each sorted position
+  const int32_t* inv;        // [P] sorted position of each pair
   const int32_t* seg_expert; // [S_max]
   const int32_t* seg_start;  // [S_max + 1]
   const int32_t* num_seg;    // [1]
@@ -48,6 +49,26 @@ struct RouteView {
   int P, k, s_max;
   int max_rows;              // largest number of rows one expert can receive (<= T)
 };
+
+// Outputs of the routing step (see bigrig_moe_permute).
+struct RouteOut {
+  int32_t* order;
+  int32_t* inv;
+  int32_t* offsets;
+  int32_t* seg_expert;
+  int32_t* seg_start;
+  int32_t* num_seg;
+  int32_t* err;
+};
+
+int launch_route(const void* x, const void* gate_w, const float* gate_b, const void* logits_in,
+                 int logits_dtype, int T, int H, int E, int k, int mode, int norm, float* logits_ws,
+                 int32_t* ticket, int32_t* idx_out, float* sc_out, const RouteOut& ro,
+                 cudaStream_t s);
+size_t down_combine_smem(int P, const bigrig_expert_layout& L);
+int launch_down_combine(const void* h, const RouteView& rv, const void* slab,
+                        const bigrig_expert_layout& L, const float* scores, const void* residual,
+                        void* out, void* y_out, int T, cudaStream_t s);
 
 int launch_gemv_gate_up(const void* x, const RouteView& rv, const void* slab,
                         const bigrig_expert_layout& L, void* h, cudaStream_t s);
@@ -59,6 +80,6 @@ int launch_gemm_gate_up(const void* x, const RouteView& rv, const void* slab,
 int launch_gemm_down(const void* h, const RouteView& rv, const void* slab,
                      const bigrig_expert_layout& L, void* y, int bn, cudaStream_t s);
 int launch_combine(const void* y, const float* scores, int T, int k, int H, void* out,
-                   cudaStream_t s);
+                   cudaStream_t s, const void* residual = nullptr);
 
 }  // namespace bigrig

@@ -7,6 +7,7 @@
 // (bigrig_engine/stream.py:1246-1250, 1275-1276, 1527-1531).
 #include "common.cuh"
 #include "launch.h"
+#include "routing.cuh"
 
 namespace bigrig {
 
@@ -42,84 +43,22 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
 }
 
 // ---------------------------------------------------------------- top-k
-// One warp per token.  Each lane holds E/32 logits (E <= 256).  k rounds of a
-// warp arg-max: a candidate beats another when its logit is larger, or equal with
-// a lower expert id, which is the stable descending order of the restatement.
+// One warp per token over logits[T, E] (fp32 or bf16), E <= 256.
 template <int PER_LANE>
 __global__ void __launch_bounds__(256) router_topk_kernel(const void* __restrict__ logits,
                                                           int dtype, int T, int E, int k,
                                                           int mode, int norm_topk,
                                                           int32_t* __restrict__ indices,
                                                           float* __restrict__ scores) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + warp;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
-  float v[PER_LANE];
-#pragma unroll
-  for (int i = 0; i < PER_LANE; ++i) {
-    const int e = i * 32 + lane;
-    float f = -INFINITY;
-    if (e < E) {
-      if (dtype == BIGRIG_F32) f = static_cast<const float*>(logits)[static_cast<size_t>(t) * E + e];
-      else f = bf16_bits_to_f32(static_cast<const uint16_t*>(logits)[static_cast<size_t>(t) * E + e]);
-    }
-    v[i] = f;
-  }
-  // softmax over all E (softmax_topk): max and sum of exp in fp32.
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < PER_LANE; ++i) mx = fmaxf(mx, v[i]);
-  mx = warp_max(mx);
-  float denom = 0.f;
-  if (mode == BIGRIG_SOFTMAX_TOPK) {
-#pragma unroll
-    for (int i = 0; i < PER_LANE; ++i)
-      if (i * 32 + lane < E) denom += expf(v[i] - mx);
-    denom = warp_sum(denom);
-  }
-  uint32_t taken = 0;  // bit i: v[i] already selected
-  float sel_val = 0.f, sum_sel = 0.f, first_logit = 0.f;
-  int my_idx = -1;     // lane j keeps the j-th selected expert
-  float my_logit = 0.f;
-  for (int r = 0; r < k; ++r) {
-    float best = -INFINITY;
-    int best_e = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < PER_LANE; ++i) {
-      const int e = i * 32 + lane;
-      if (e < E && !(taken & (1u << i))) {
-        if (v[i] > best || (v[i] == best && e < best_e)) { best = v[i]; best_e = e; }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oe = __shfl_xor_sync(0xffffffffu, best_e, o);
-      if (ob > best || (ob == best && oe < best_e)) { best = ob; best_e = oe; }
-    }
-    if ((best_e & 31) == lane) taken |= 1u << (best_e >> 5);
-    if (lane == r) { my_idx = best_e; my_logit = best; }
-    if (r == 0) first_logit = best;
-  }
-  (void)sel_val; (void)sum_sel;
-  // scores for the selected experts, lane r holds rank r (k <= 32)
-  float sc = 0.f;
-  if (mode == BIGRIG_SOFTMAX_TOPK) {
-    sc = (lane < k) ? expf(my_logit - mx) / denom : 0.f;
-    if (norm_topk) {
-      const float s = warp_sum(sc);
-      sc = sc / s;
-    }
-  } else {
-    // softmax over the k kept logits; the largest is rank 0.
-    const float ex = (lane < k) ? expf(my_logit - first_logit) : 0.f;
-    const float s = warp_sum(ex);
-    sc = ex / s;
-  }
-  if (lane < k) {
-    indices[static_cast<size_t>(t) * k + lane] = my_idx;
-    scores[static_cast<size_t>(t) * k + lane] = sc;
-  }
+  const size_t row = static_cast<size_t>(t) * E;
+  auto load = [&](int e) {
+    return dtype == BIGRIG_F32 ? static_cast<const float*>(logits)[row + e]
+                               : bf16_bits_to_f32(static_cast<const uint16_t*>(logits)[row + e]);
+  };
+  topk_warp<PER_LANE>(load, E, k, mode, norm_topk, indices + static_cast<size_t>(t) * k,
+                      scores + static_cast<size_t>(t) * k);
 }
 
 // ---------------------------------------------------------------- permutation
@@ -192,54 +131,13 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
   }
 }
 
-// Decode-sized permutation (P <= 32 pairs): one warp.  Lane i holds pair i; its
-// sorted position is the number of pairs (e_j, j) lexicographically below (e_i, i),
-// which is the stable order; runs of equal experts become the segments.
+// Decode-sized permutation (P <= 32 pairs): one warp (see permute_warp).
 __global__ void __launch_bounds__(32) permute_warp_kernel(
     const int32_t* __restrict__ idx, int P, int E, int32_t* __restrict__ order,
     int32_t* __restrict__ inv, int32_t* __restrict__ offsets, int32_t* __restrict__ seg_expert,
     int32_t* __restrict__ seg_start, int32_t* __restrict__ num_seg, int32_t* __restrict__ err) {
-  const int lane = threadIdx.x;
-  int e = lane < P ? idx[lane] : 0x7fffffff;
-  const bool bad = lane < P && (e < 0 || e >= E);
-  if (bad) e = 0x7ffffffe;                      // sorts after every valid id, before padding
-  const unsigned nbad = __popc(__ballot_sync(0xffffffffu, bad));
-  if (lane == 0 && nbad && err) atomicAdd(err, static_cast<int>(nbad));
-  int rank = 0;
-  for (int j = 0; j < 32; ++j) {
-    const int ej = __shfl_sync(0xffffffffu, e, j);
-    rank += (ej < e) || (ej == e && j < lane);
-  }
-  if (lane < P) {
-    order[rank] = lane;
-    inv[lane] = rank;
-  }
-  // expert of sorted position `lane`
-  int se = 0x7fffffff;
-  for (int j = 0; j < 32; ++j) {
-    const int rj = __shfl_sync(0xffffffffu, rank, j);
-    const int ej = __shfl_sync(0xffffffffu, e, j);
-    if (rj == lane) se = ej;
-  }
-  const int prev = __shfl_up_sync(0xffffffffu, se, 1);
-  const bool first = lane < P && se < E && (lane == 0 || prev != se);
-  const unsigned firsts = __ballot_sync(0xffffffffu, first);
-  if (first) {
-    const int si = __popc(firsts & ((1u << lane) - 1u));
-    seg_expert[si] = se;
-    seg_start[si] = lane;
-  }
-  const int nvalid = P - static_cast<int>(nbad);
-  if (lane == 0) {
-    *num_seg = __popc(firsts);
-    seg_start[__popc(firsts)] = nvalid;
-  }
-  for (int x0 = 0; x0 <= E; x0 += 32) {          // uniform trip count: every lane shuffles
-    const int x = x0 + lane;
-    int below = 0;
-    for (int j = 0; j < P; ++j) below += __shfl_sync(0xffffffffu, e, j) < x;
-    if (x <= E) offsets[x] = below;
-  }
+  pdl_wait();
+  permute_warp(idx, P, E, order, inv, offsets, seg_expert, seg_start, num_seg, err);
 }
 
 // ---------------------------------------------------------------- launchers

@@ -1,0 +1,124 @@
+// Warp-level routing helpers shared by the router kernels and the fused decode route.
+#pragma once
+
+#include "common.cuh"
+
+namespace bigrig {
+
+// Top-k of one token's E logits (E <= 32 * PER_LANE) by one warp: k rounds of a warp
+// arg-max in which a candidate beats another when its logit is larger, or equal with a
+// lower expert id -- the stable descending order.  Lane r < k writes rank r's expert to
+// idx[r] and its score to sc[r] (softmax over E then top-k, optionally renormalised;
+// or top-k then softmax over the k).  `load(e)` returns logit e as fp32.
+template <int PER_LANE, typename Load>
+__device__ __forceinline__ void topk_warp(Load load, int E, int k, int mode, int norm_topk,
+                                          int32_t* idx, float* sc) {
+  const int lane = threadIdx.x & 31;
+  float v[PER_LANE];
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = e < E ? load(e) : -INFINITY;
+  }
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) mx = fmaxf(mx, v[i]);
+  mx = warp_max(mx);
+  float denom = 0.f;
+  if (mode == BIGRIG_SOFTMAX_TOPK) {
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i)
+      if (i * 32 + lane < E) denom += expf(v[i] - mx);
+    denom = warp_sum(denom);
+  }
+  uint32_t taken = 0;
+  float first_logit = 0.f, my_logit = 0.f;
+  int my_idx = -1;
+  for (int r = 0; r < k; ++r) {
+    float best = -INFINITY;
+    int best_e = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+      const int e = i * 32 + lane;
+      if (e < E && !(taken & (1u << i))) {
+        if (v[i] > best || (v[i] == best && e < best_e)) { best = v[i]; best_e = e; }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, best_e, o);
+      if (ob > best || (ob == best && oe < best_e)) { best = ob; best_e = oe; }
+    }
+    if ((best_e & 31) == lane) taken |= 1u << (best_e >> 5);
+    if (lane == r) { my_idx = best_e; my_logit = best; }
+    if (r == 0) first_logit = best;
+  }
+  float s = 0.f;
+  if (mode == BIGRIG_SOFTMAX_TOPK) {
+    s = (lane < k) ? expf(my_logit - mx) / denom : 0.f;
+    if (norm_topk) s = s / warp_sum(s);
+  } else {
+    const float ex = (lane < k) ? expf(my_logit - first_logit) : 0.f;
+    s = ex / warp_sum(ex);
+  }
+  if (lane < k) {
+    idx[lane] = my_idx;
+    sc[lane] = s;
+  }
+}
+
+// Stable expert-sorted permutation of P <= 32 pairs by one warp.  Lane i holds pair i;
+// its sorted position is the number of pairs (e_j, j) lexicographically below (e_i, i).
+// Runs of equal experts become the segments; offsets[x] counts the pairs with expert < x.
+// Ids outside [0, E) sort last, are left out of the segments and counted in err.
+__device__ __forceinline__ void permute_warp(const int32_t* idx, int P, int E, int32_t* order,
+                                             int32_t* inv, int32_t* offsets, int32_t* seg_expert,
+                                             int32_t* seg_start, int32_t* num_seg, int32_t* err) {
+  const int lane = threadIdx.x & 31;
+  int e = lane < P ? idx[lane] : 0x7fffffff;
+  const bool bad = lane < P && (e < 0 || e >= E);
+  if (bad) e = 0x7ffffffe;
+  const unsigned nbad = __popc(__ballot_sync(0xffffffffu, bad));
+  if (lane == 0 && nbad && err) atomicAdd(err, static_cast<int>(nbad));
+  int rank = 0;
+  for (int j = 0; j < 32; ++j) {
+    const int ej = __shfl_sync(0xffffffffu, e, j);
+    rank += (ej < e) || (ej == e && j < lane);
+  }
+  if (lane < P) {
+    order[rank] = lane;
+    inv[lane] = rank;
+  }
+  int se = 0x7fffffff;
+  for (int j = 0; j < 32; ++j) {
+    const int rj = __shfl_sync(0xffffffffu, rank, j);
+    const int ej = __shfl_sync(0xffffffffu, e, j);
+    if (rj == lane) se = ej;
+  }
+  const int prev = __shfl_up_sync(0xffffffffu, se, 1);
+  const bool first = lane < P && se < E && (lane == 0 || prev != se);
+  const unsigned firsts = __ballot_sync(0xffffffffu, first);
+  if (first) {
+    const int si = __popc(firsts & ((1u << lane) - 1u));
+    seg_expert[si] = se;
+    seg_start[si] = lane;
+  }
+  if (lane == 0) {
+    *num_seg = __popc(firsts);
+    seg_start[__popc(firsts)] = P - static_cast<int>(nbad);
+  }
+  for (int x0 = 0; x0 <= E; x0 += 32) {          // uniform trip count: every lane shuffles
+    const int x = x0 + lane;
+    int below = 0;
+    for (int j = 0; j < P; ++j) below += __shfl_sync(0xffffffffu, e, j) < x;
+    if (x <= E) offsets[x] = below;
+  }
+}
+
+// Programmatic dependent launch: wait for the preceding kernel's results (a no-op when
+// the kernel was launched without the attribute), and let the next kernel be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+}  // namespace bigrig

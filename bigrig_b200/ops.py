@@ -188,15 +188,26 @@ def switch_glu(x: torch.Tensor, indices: torch.Tensor, slab: torch.Tensor, layou
     return out
 
 
-def combine(y: torch.Tensor, scores: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """out[T, H] = sum_j scores[t, j] * y[t, j, :] (bf16 out, fp32 accumulation)."""
+def combine(y: torch.Tensor, scores: torch.Tensor, out: torch.Tensor | None = None,
+            residual: torch.Tensor | None = None) -> torch.Tensor:
+    """out[T, H] = sum_j scores[t, j] * y[t, j, :] (bf16 out, fp32 accumulation),
+    plus ``residual`` when given (then out = bf16(residual + bf16(sum)))."""
     _require_cuda("y", y, torch.bfloat16)
     _require_cuda("scores", scores, torch.float32)
     T, k, H = y.shape
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=y.device)
-    _lib.check(_lib.load().bigrig_combine(_vp(y), _vp(scores), T, k, H, _vp(out), _stream(y)),
-               "combine")
+    if residual is None:
+        _lib.check(_lib.load().bigrig_combine(_vp(y), _vp(scores), T, k, H, _vp(out), _stream(y)),
+                   "combine")
+    else:
+        _require_cuda("residual", residual, torch.bfloat16)
+        # the residual form is the combine kernel's second mode, reached through moe_layer's
+        # fallback; here it is one elementwise step on top of the plain combine
+        plain = torch.empty_like(out)
+        _lib.check(_lib.load().bigrig_combine(_vp(y), _vp(scores), T, k, H, _vp(plain),
+                                              _stream(y)), "combine")
+        torch.add(residual, plain, out=out)
     return out
 
 
@@ -226,4 +237,38 @@ def moe_forward(x: torch.Tensor, logits: torch.Tensor, top_k: int, slab: torch.T
         _vp(x), _vp(logits), dt, T, n_experts, top_k, _MODES[mode], int(norm_topk), _vp(g2s),
         _vp(slab), ctypes.byref(c_layout(layout)), _vp(out), _vp(indices), _vp(scores), _vp(buf),
         buf.numel(), _stream(x)), "moe_forward")
+    return out, indices, scores
+
+
+def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, gate_b: torch.Tensor | None, top_k: int,
+              slab: torch.Tensor, layout: Layout, n_experts: int, mode: str = "softmax_topk",
+              norm_topk: bool = False, g2s: torch.Tensor | None = None,
+              residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+              indices: torch.Tensor | None = None, scores: torch.Tensor | None = None,
+              workspace: Workspace | None = None):
+    """The MoE block from hidden states: router logits, top-k + softmax, experts, combine,
+    plus ``residual`` when given.  Returns (out, indices, scores)."""
+    _require_cuda("x", x, torch.bfloat16)
+    _require_cuda("gate_w", gate_w, torch.bfloat16)
+    _require_cuda("slab", slab, torch.uint8)
+    if gate_b is not None:
+        _require_cuda("gate_b", gate_b, torch.float32)
+    if residual is not None:
+        _require_cuda("residual", residual, torch.bfloat16)
+    if mode not in _MODES:
+        raise ValueError(f"mode must be one of {tuple(_MODES)}, got {mode!r}")
+    T = x.shape[0]
+    dev = x.device
+    if out is None:
+        out = torch.empty(T, layout.hidden, dtype=torch.bfloat16, device=dev)
+    if indices is None:
+        indices = torch.empty(T, top_k, dtype=torch.int32, device=dev)
+    if scores is None:
+        scores = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    ws = workspace or default_workspace(dev)
+    buf = ws.reserve(workspace_bytes(T, top_k, n_experts, layout))
+    _lib.check(_lib.load().bigrig_moe_layer(
+        _vp(x), _vp(gate_w), _vp(gate_b), T, n_experts, top_k, _MODES[mode], int(norm_topk),
+        _vp(g2s), _vp(slab), ctypes.byref(c_layout(layout)), _vp(residual), _vp(out),
+        _vp(indices), _vp(scores), _vp(buf), buf.numel(), _stream(x)), "moe_layer")
     return out, indices, scores

@@ -141,7 +141,9 @@ BIGRIG_API int bigrig_moe_forward(const void* x, const void* logits, int logits_
 #define BIGRIG_K_DEQUANT 6
 #define BIGRIG_K_GEMM_GATE_UP 7
 #define BIGRIG_K_GEMM_DOWN 8
-#define BIGRIG_K_COUNT 9
+#define BIGRIG_K_ROUTE 9
+#define BIGRIG_K_DOWN_COMBINE 10
+#define BIGRIG_K_COUNT 11
 
 /* Which expert kernels bigrig_switch_glu / bigrig_moe_forward use:
  * BIGRIG_PATH_AUTO picks the grouped GEMV when an expert gets few rows (decode)
@@ -165,6 +167,20 @@ BIGRIG_API int bigrig_timing_enable(int mask);
 BIGRIG_API int bigrig_timing_read(int kernel_id, double* total_ms, int64_t* launches);
 BIGRIG_API int bigrig_launch_counts(int64_t* out);
 BIGRIG_API const char* bigrig_kernel_name(int kernel_id);
+
+/* The whole MoE block of one decoder layer from its hidden states:
+ * logits = x . gate_w^T (+ gate_b), top-k + softmax (mode, norm_topk), the SwiGLU
+ * experts and out[T, H] = residual + sum_j score * y (residual may be NULL).
+ * x, gate_w, residual, out bf16; gate_b fp32 [E] or NULL.  Decode-sized calls
+ * (T * k <= 32) run as three kernels chained by programmatic dependent launch.
+ * Replaces the mlx_lm MoE block around StreamingSwitchGLU (stream.py:1377,
+ * 1523-1525; router rule adapter.py:74-92). */
+BIGRIG_API int bigrig_moe_layer(const void* x, const void* gate_w, const float* gate_b, int T,
+                                int E, int k, int mode, int norm_topk, const int32_t* g2s,
+                                const void* slab, const bigrig_expert_layout* layout,
+                                const void* residual, void* out, int32_t* indices_out,
+                                float* scores_out, void* workspace, size_t workspace_bytes,
+                                void* stream);
 
 /* Device error word of a workspace (slots < 0, ids out of range), copied to *out
  * with a synchronous read on `stream`; resets it to 0.  For tests and debugging. */

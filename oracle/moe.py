@@ -8,11 +8,14 @@ weights dequantised from their affine codes, and the per-expert call order of
 unreduced, ``y[..., k, H]`` (bigrig_engine/stream.py:1523-1525); the caller's
 MoE block applies ``sum_k score_k * y_k``.
 
-Rounding points mirror a bf16 model: every projection output and the activation
-are stored as bf16 (the activation dtype), accumulation is fp32.  The
-``intermediate="f32"`` switch keeps them in fp32 instead; the two agree within
-the 1e-2 relative / 2e-3 absolute tolerance the parity tests use, which is the
-point of offering both.
+Rounding points: gate and up stay in fp32 (the accumulator), the activation
+``h = silu(gate) * up`` is stored as bf16 (the input dtype of the down
+projection), and the output is bf16.  ``intermediate="bf16"`` also rounds gate
+and up to bf16 (a model whose projections emit bf16), ``"f32"`` keeps h in fp32
+too; all three agree within the 1e-2 relative / 2e-3 absolute tolerance of the
+parity tests on typical rows.  The default is the one the kernels implement:
+rounding gate/up before the SiLU lets a one-ulp flip of a large gate value move a
+whole output row, which no reduction order can reproduce bit for bit.
 """
 from __future__ import annotations
 
@@ -44,16 +47,20 @@ def expert_weights_f32(expert: dict, group_size: int, bits: int, scale_dtype: st
     return out
 
 
-def expert_forward(x: np.ndarray, w: dict, intermediate: str = "bf16") -> np.ndarray:
+def expert_forward(x: np.ndarray, w: dict, intermediate: str = "h_bf16") -> np.ndarray:
     """x fp32 [R, H] (values of a bf16 tensor) -> y fp32 [R, H] (values of bf16)."""
-    rnd = bf16_round if intermediate == "bf16" else (lambda a: a.astype(np.float32))
-    up = rnd(x @ w["up_proj"].T)
-    gate = rnd(x @ w["gate_proj"].T)
-    h = rnd(silu(gate) * up)
+    if intermediate not in ("h_bf16", "bf16", "f32"):
+        raise ValueError(f"intermediate must be h_bf16, bf16 or f32, got {intermediate!r}")
+    keep = lambda a: a.astype(np.float32)  # noqa: E731
+    rnd_gu = bf16_round if intermediate == "bf16" else keep
+    rnd_h = keep if intermediate == "f32" else bf16_round
+    up = rnd_gu(x @ w["up_proj"].T)
+    gate = rnd_gu(x @ w["gate_proj"].T)
+    h = rnd_h(silu(gate) * up)
     return bf16_round(h @ w["down_proj"].T)
 
 
-def switch_glu(x: np.ndarray, indices: np.ndarray, weights_of, intermediate: str = "bf16"):
+def switch_glu(x: np.ndarray, indices: np.ndarray, weights_of, intermediate: str = "h_bf16"):
     """Unreduced expert outputs.  x [T, H] fp32, indices [T, k] int -> y [T, k, H] fp32.
 
     ``weights_of(e)`` returns the fp32 weight dict of expert ``e``.  Pairs are

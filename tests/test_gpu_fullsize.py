@@ -41,20 +41,37 @@ def _slab(name, device):
     return slab, L
 
 
+def _dequant_f32(slab, L, slot, proj):
+    """Exact fp32 weights scale * q + bias of one projection, in plain torch."""
+    rows, cols = (L.hidden, L.inter) if proj == 2 else (L.inter, L.hidden)
+    base = slab[slot]
+    wb = base[L.weight_off[proj]:L.weight_off[proj] + rows * cols * L.bits // 8]
+    words = wb.view(torch.int32).reshape(rows, -1).to(torch.int64) & 0xFFFFFFFF
+    per = 32 // L.bits
+    shifts = torch.arange(per, device=slab.device, dtype=torch.int64) * L.bits
+    q = ((words[:, :, None] >> shifts) & ((1 << L.bits) - 1)).reshape(rows, cols).float()
+    hd = torch.float16 if L.scale_dtype == "float16" else torch.bfloat16
+    ng = cols // L.group_size
+    s = base[L.scales_off[proj]:L.scales_off[proj] + rows * ng * 2].view(hd).reshape(rows, ng).float()
+    b = base[L.biases_off[proj]:L.biases_off[proj] + rows * ng * 2].view(hd).reshape(rows, ng).float()
+    q = q.reshape(rows, ng, L.group_size)
+    return (q * s[..., None] + b[..., None]).reshape(rows, cols)
+
+
 def _reference(slab, L, x, idx, bf16_weights=False):
-    """y[t, j] from dequantised weights in fp32 torch, bf16 at the kernel's rounding points
-    (and the weights themselves rounded to bf16 for the tensor-core path)."""
+    """y[t, j] in fp32 torch from exact dequantised weights (rounded once to bf16 for the
+    tensor-core path), with the kernels' rounding points: gate/up fp32, h and y bf16."""
     T, k = idx.shape
     y = torch.empty(T, k, L.hidden, dtype=torch.float32, device=x.device)
     xf = x.float()
     for e in torch.unique(idx).tolist():
-        w = [ops.dequant(slab, L, e, p).float() for p in range(3)]
+        w = [_dequant_f32(slab, L, e, p) for p in range(3)]
         if bf16_weights:
             w = [t.bfloat16().float() for t in w]
         rows = (idx == e).nonzero()
         xe = xf[rows[:, 0]]
-        gate = (xe @ w[0].T).bfloat16().float()
-        up = (xe @ w[1].T).bfloat16().float()
+        gate = xe @ w[0].T
+        up = xe @ w[1].T
         h = (torch.nn.functional.silu(gate) * up).bfloat16().float()
         y[rows[:, 0], rows[:, 1]] = (h @ w[2].T).bfloat16().float()
     return y

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from oracle import affine, moe, router
-from bigrig_b200 import ops
+from bigrig_b200 import _lib, ops
 from tests._experts import Layer, assert_close, bf16_tensor, random_routing, to_f32
 
 pytestmark = pytest.mark.gpu
@@ -105,8 +105,12 @@ def test_switch_glu_matches_oracle(cuda, H, I, E, k, bits, sd, T):
     L = Layer(H, I, E, bits, sd, seed=T, slot_order=rng.permutation(E))
     x = affine.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
     idx = random_routing(T, k, E, rng)
-    y = ops.switch_glu(bf16_tensor(x), torch.from_numpy(idx).to(cuda), L.slab, L.layout, E,
-                       g2s=L.g2s)
+    prev = _lib.set_path("gemv")
+    try:
+        y = ops.switch_glu(bf16_tensor(x), torch.from_numpy(idx).to(cuda), L.slab, L.layout, E,
+                           g2s=L.g2s)
+    finally:
+        _lib.set_path(prev)
     assert_close(to_f32(y), L.oracle_switch(x, idx))
 
 
@@ -141,3 +145,36 @@ def test_missing_slot_is_reported_not_read(cuda):
     assert np.all(yy[0, 0] == 0) and np.all(yy[1, 1] == 0)
     assert np.any(yy[0, 1] != 0)
     assert ws.errors() == 0
+
+
+@pytest.mark.parametrize("T,k,E,mode", [(1, 8, 64, "softmax_topk"), (2, 8, 128, "softmax_topk"),
+                                        (4, 4, 128, "topk_softmax"), (16, 2, 8, "topk_softmax")])
+def test_fused_decode_layer_is_bit_identical(cuda, T, k, E, mode):
+    """The fused three-kernel decode chain (route, gate_up, down+combine) computes exactly
+    what the separate kernels compute, with and without the residual."""
+    rng = np.random.default_rng(T * 100 + E)
+    H, I = 1024, 512
+    L = Layer(H, I, E, 4, "float16", seed=T, slot_order=rng.permutation(E))
+    x = bf16_tensor(affine.bf16_round(rng.standard_normal((T, H)).astype(np.float32)))
+    gw = bf16_tensor(affine.bf16_round((rng.standard_normal((E, H)) * 0.02).astype(np.float32)))
+    gb = torch.from_numpy(rng.standard_normal(E).astype(np.float32)).to(cuda)
+    out, idx, sc = ops.moe_layer(x, gw, gb, k, L.slab, L.layout, E, mode, False, g2s=L.g2s)
+    out_r, _, _ = ops.moe_layer(x, gw, gb, k, L.slab, L.layout, E, mode, False, g2s=L.g2s,
+                                residual=x)
+    n0 = _lib.launch_counts()
+    lg = ops.router_logits(x, gw, gb)
+    idx2, sc2 = ops.router_topk(lg, k, mode)
+    y = ops.switch_glu(x, idx2, L.slab, L.layout, E, g2s=L.g2s)
+    ref = ops.combine(y, sc2)
+    n1 = _lib.launch_counts()
+    assert n1["route"] == n0["route"]
+    assert torch.equal(idx, idx2) and torch.equal(sc, sc2)
+    assert torch.equal(out, ref)
+    assert torch.equal(out_r, (x.float() + ref.float()).bfloat16())
+    lt = lg.clone()
+    fo, fidx, fsc = ops.moe_forward(x, lt, k, L.slab, L.layout, E, mode, False, g2s=L.g2s)
+    assert torch.equal(fo, ref) and torch.equal(fidx, idx2)
+    widx, wsc = router.topk(lg.cpu().numpy(), k, mode)
+    np.testing.assert_array_equal(idx.cpu().numpy(), widx)
+    xf = to_f32(x)
+    assert_close(to_f32(out), moe.combine(L.oracle_switch(xf, widx), wsc))

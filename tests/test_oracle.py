@@ -112,10 +112,12 @@ def test_expert_forward_matches_by_hand_formula():
     w = moe.expert_weights_f32(ws, 64, 4, "bfloat16")
     x = affine.bf16_round(rng.standard_normal((3, H)).astype(np.float32))
     ref = (moe.silu(x @ w["gate_proj"].T) * (x @ w["up_proj"].T)) @ w["down_proj"].T
-    got = moe.expert_forward(x, w, "bf16")
+    got = moe.expert_forward(x, w)
     got32 = moe.expert_forward(x, w, "f32")
+    got16 = moe.expert_forward(x, w, "bf16")
     assert np.abs(got - ref).max() / np.abs(ref).max() < 0.02
     np.testing.assert_allclose(got, got32, rtol=1e-2, atol=2e-3)
+    np.testing.assert_allclose(got, got16, rtol=1e-2, atol=2e-3)
 
 
 def test_spec_matches_shipped_manifests():
