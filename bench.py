@@ -18,10 +18,14 @@ its fraction of the measured peak), and the CPU restatement's throughput.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Multi-GPU: one process per GPU under torchrun; every rank decodes its own token
-stream on its own copy of the layers (independent sequences, no data-path
-collective), the timed region is bracketed by barriers and the slowest rank's
-time is the job's.  value = tokens of all ranks / that time ("weak" scaling).
+Multi-GPU: one process per GPU under torchrun, expert parallel.  Rank r owns the
+contiguous block r of every layer's experts (E/N of them, in a pool of
+min(16, E/N) slots refilled from its own pinned host store); every rank decodes
+its own token stream with the replicated router and sends each routed pair to the
+owning rank by NCCL all-to-all (fixed-capacity blocks when the local pool holds
+all its experts, exact counts otherwise), which computes it and sends it back for
+the combine.  The timed region is bracketed by barriers and the slowest rank's
+time is the job's; value = tokens of all ranks / that time ("weak" scaling).
 """
 from __future__ import annotations
 
@@ -111,7 +115,9 @@ class Clocks:
 
 
 # ------------------------------------------------------------------ model
-def build_model(device, seed: int):
+def build_model(device, seed: int, experts=None):
+    """Router weights (replicated on every rank) and a pinned host store holding the
+    given global expert ids of every layer (all of them by default)."""
     from bigrig_b200.block import fill_store, make_blocks
     from bigrig_b200.fetch import HostExpertStore
     from bigrig_b200.formats import bytes_per_expert, make_spec
@@ -120,9 +126,10 @@ def build_model(device, seed: int):
                          c["family"], c["bits"], c["group_size"], c["scale_dtype"], True,
                          seed=seed, device=device)
     spec = make_spec(c["hidden"], c["inter"], c["bits"], c["group_size"], c["scale_dtype"])
-    store = HostExpertStore({li: (c["experts"], bytes_per_expert(spec)) for li in range(c["layers"])})
+    ids = list(range(c["experts"])) if experts is None else list(experts)
+    store = HostExpertStore({li: (len(ids), bytes_per_expert(spec)) for li in range(c["layers"])})
     fill_store(store, c["layers"], c["hidden"], c["inter"], c["experts"], c["bits"],
-               c["group_size"], c["scale_dtype"], seed=seed + 1, device=device)
+               c["group_size"], c["scale_dtype"], seed=seed + 1, device=device, experts=ids)
     torch.cuda.synchronize(device)
     return blocks, store
 
@@ -253,8 +260,29 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     _lib.load(build_if_stale=False)
     c = CFG
-    blocks, store = build_model(dev, seed=0)
-    handle = attach(blocks, store, c["capacity"], policy=c["policy"], warm="auto", device=dev)
+    if world == 1:
+        blocks, store = build_model(dev, seed=0)
+        handle = attach(blocks, store, c["capacity"], policy=c["policy"], warm="auto", device=dev)
+        stack = blocks
+    else:
+        # expert parallel: this rank owns a contiguous block of every layer's experts, held
+        # in a pool of min(capacity, E/N) slots; routed pairs travel by NCCL all-to-all
+        from bigrig_b200.block import EPMoEBlock
+        from bigrig_b200.ep import ExpertParallel
+        from bigrig_b200.stream import ExpertPool, StreamHandle, StreamingSwitchGLU
+        ep = ExpertParallel(c["experts"])
+        lo, hi = ep.local_range()
+        blocks, store = build_model(dev, seed=0, experts=range(lo, hi))
+        pools, mods = [], []
+        for b in blocks:
+            pool = ExpertPool(b.layer, None, hi - lo, min(c["capacity"], hi - lo), b.spec,
+                              policy=c["policy"], quant=b.quant, device=dev).build()
+            pools.append(pool)
+            mods.append(StreamingSwitchGLU(pool, store))
+        handle = StreamHandle(blocks, pools, mods, store).warm("auto")
+        for m in mods:
+            m.refresh()
+        stack = [EPMoEBlock(b, ep, m, padded=m._sync_free) for b, m in zip(blocks, mods)]
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
     W, K = args.warmup, args.steps
@@ -276,7 +304,10 @@ def main() -> None:
     # ---- prefill: the 2048-token prompt, layer-major, through the capped pools
     if not args.no_extras:
         prompt = torch.randn(c["prompt"], c["hidden"], generator=g, device=dev).to(torch.bfloat16)
-        layers = [(lambda h, b=b: b(h, residual=h)) for b in blocks]
+        layers = [(lambda h, b=b: b(h, residual=h)) for b in stack]
+        if world > 1:
+            for b in stack:
+                b.padded = False             # prompt chunks exchange exact row counts
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -286,13 +317,16 @@ def main() -> None:
         barrier()
         pf_ms = max_over_ranks(e0.elapsed_time(e1))
         extras["prefill_tok_s"] = world * c["prompt"] / (pf_ms / 1e3)
-        extras["prefill_note"] = ("capped pools, expert-sorted spans of <= 16 experts, GEMV path "
-                                  "(the tcgen05 grouped GEMM is not in this build yet)")
+        extras["prefill_note"] = ("2048-token prompt, layer-major in chunks of 512, expert-sorted "
+                                  "spans through the capped pools, tcgen05 grouped GEMM")
+        if world > 1:
+            for b in stack:
+                b.padded = b.switch._sync_free
         handle.reset_stats()
 
     # ---- decode, capped pool: warm-up then K timed steps
     for i in range(W):
-        stack_step(blocks, tokens[i])
+        stack_step(stack, tokens[i])
     handle.reset_stats()
     barrier()
     counts0 = _lib.launch_counts()
@@ -302,7 +336,7 @@ def main() -> None:
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for i in range(K):
-        stack_step(blocks, tokens[W + i])
+        stack_step(stack, tokens[W + i])
     t1.record()
     barrier()
     clk = clocks.stop()
@@ -321,7 +355,7 @@ def main() -> None:
     w0 = time.perf_counter()
     for i in range(K):
         x = hbuf[W + i].to(dev, non_blocking=True)
-        y = stack_step(blocks, x)
+        y = stack_step(stack, x)
         outbuf.copy_(y, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
     barrier()
@@ -331,8 +365,8 @@ def main() -> None:
            "note": "per step: token embedding copied from pinned host, 16 MoE layers, result "
                    "read back; misses copied from pinned host inside the step"}
 
-    # ---- resident (sync-free) decode in one CUDA graph per token
-    if not args.no_extras:
+    # ---- resident (sync-free) decode in one CUDA graph per token (single GPU)
+    if not args.no_extras and world == 1:
         handle = None                    # its pools' slabs are freed once the blocks let go
         res = attach(blocks, store, c["experts"], policy=c["policy"], warm="auto", device=dev)
         ws = ops.default_workspace(dev)
@@ -405,7 +439,10 @@ def main() -> None:
                     "MLX affine 4-bit g64, router bias N(0,1); random init",
             "config": {**{k: c[k] for k in ("workload", "layers", "hidden", "inter", "experts",
                                             "top_k", "bits", "group_size", "capacity", "policy")},
-                       "global_batch": world, "parallelism": f"replicas x{world}",
+                       "global_batch": world,
+                       "parallelism": "single GPU" if world == 1 else
+                       f"ep{world}: {c['experts'] // world} experts per rank per layer, "
+                       f"pool {min(c['capacity'], c['experts'] // world)} slots, NCCL all-to-all",
                        "l2": "decode reads 28 MB of experts per layer, 453 MB per token; no flush"},
             "e2e": e2e,
             "gpu_launches": launches,

@@ -131,12 +131,37 @@ def make_blocks(n_layers: int, hidden: int, inter: int, n_experts: int, top_k: i
 
 def fill_store(store, n_layers: int, hidden: int, inter: int, n_experts: int, bits: int = 4,
                group_size: int = 64, scale_dtype: str = "float16", seed: int = 1,
-               device="cuda") -> None:
-    """Quantise synthetic experts on the GPU and write them into a HostExpertStore."""
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
+               device="cuda", experts=None) -> None:
+    """Quantise synthetic experts on the GPU and write them into a HostExpertStore.
+
+    Expert e of layer l is drawn from its own generator (seeded from seed, l, e), so
+    a rank holding only a block of experts (``experts``: the global ids to fill, in
+    store order) gets exactly the bytes a single GPU holding all of them would."""
     sd = {"float16": torch.float16, "bfloat16": torch.bfloat16}[scale_dtype]
+    ids = list(range(n_experts)) if experts is None else list(experts)
+    g = torch.Generator(device=device)
     for li in range(n_layers):
-        for e in range(n_experts):
+        for slot, e in enumerate(ids):
+            g.manual_seed(seed * 1_000_003 + li * 10_007 + e)
             b = random_expert_bytes(hidden, inter, bits, group_size, sd, g, device)
-            store.layers[li][e].copy_(b)
+            store.layers[li][slot].copy_(b)
+
+
+class EPMoEBlock:
+    """An expert-parallel MoE layer: the replicated router, then ``ep.dispatch_combine``
+    to the ranks owning the routed experts, whose ``switch`` (a StreamingSwitchGLU over
+    this rank's experts) computes the pairs it receives."""
+
+    def __init__(self, block: MoEBlock, ep, switch, padded: bool):
+        self.block, self.ep, self.switch, self.padded = block, ep, switch, padded
+
+    def __call__(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        idx, scores = self.block.route(x)
+        sw = self.switch
+
+        def expert_fn(rows, ids):
+            return sw(rows.contiguous(), ids.reshape(-1, 1).contiguous()).reshape(rows.shape)
+
+        return self.ep.dispatch_combine(
+            x, idx, scores, expert_fn, padded=self.padded,
+            combine_fn=lambda y, sc: ops.combine(y.contiguous(), sc, residual=residual))

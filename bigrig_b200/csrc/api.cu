@@ -102,7 +102,7 @@ struct Workspace {
   int32_t* indices;   // [P] (moe_forward when the caller passes none)
   float* scores;      // [P]
   float* logits;      // [T, E] (fused decode route)
-  int32_t* ticket;    // last-CTA counter of the fused route, zero between calls
+  int32_t* ticket;    // last-CTA counter of the fused route, zero between calls (err[3])
 };
 
 size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Workspace* w) {
@@ -126,7 +126,9 @@ size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Wor
   ws.indices = static_cast<int32_t*>(take(P * sizeof(int32_t)));
   ws.scores = static_cast<float*>(take(P * sizeof(float)));
   ws.logits = static_cast<float*>(take(static_cast<size_t>(T) * E * sizeof(float)));
-  ws.ticket = static_cast<int32_t*>(take(sizeof(int32_t)));
+  // the fused route's ticket lives at a fixed place -- word 3 of the error words -- so a
+  // call of any shape finds it where the previous call left it, back at zero
+  ws.ticket = ws.err ? ws.err + 3 : nullptr;
   if (w) *w = ws;
   return off;
 }
@@ -152,9 +154,9 @@ int check_layout(const bigrig_expert_layout* Lp) {
     const int64_t cols = p == 2 ? L.inter : L.hidden;
     const int64_t wbytes = rows * cols * L.bits / 8;
     const int64_t sbytes = rows * (cols / L.group_size) * 2;
-    if (L.weight_off[p] % 16 || L.scales_off[p] % 2 || L.biases_off[p] % 2)
-      return set_error(BIGRIG_ERR_INVALID, "projection %d: weight offset must be 16-byte and "
-                       "scale/bias offsets 2-byte aligned", p);
+    if (L.weight_off[p] % 16 || L.scales_off[p] % 16 || L.biases_off[p] % 16)
+      return set_error(BIGRIG_ERR_INVALID, "projection %d: weight, scale and bias offsets must "
+                       "be 16-byte aligned", p);
     if (L.weight_off[p] < 0 || L.weight_off[p] + wbytes > L.bytes_per_expert ||
         L.scales_off[p] < 0 || L.scales_off[p] + sbytes > L.bytes_per_expert ||
         L.biases_off[p] < 0 || L.biases_off[p] + sbytes > L.bytes_per_expert)
@@ -186,6 +188,7 @@ RouteView route_view(const Workspace& ws, const int32_t* g2s, int T, int k, int 
   rv.k = k;
   rv.s_max = rv.P < E ? rv.P : E;
   rv.max_rows = T;
+  rv.n_experts = E;
   return rv;
 }
 
@@ -296,6 +299,8 @@ int bigrig_switch_glu(const void* x, const int32_t* indices, int T, int k, int n
   if (T == 0) return BIGRIG_OK;
   if (!x || !indices || !slab || !y || !workspace)
     return set_error(BIGRIG_ERR_INVALID, "switch_glu: NULL pointer");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(slab) % 16)
+    return set_error(BIGRIG_ERR_INVALID, "switch_glu: x and slab must be 16-byte aligned");
   const size_t need = carve(nullptr, T, k, n_experts, *layout, nullptr);
   if (workspace_bytes < need)
     return set_error(BIGRIG_ERR_WORKSPACE, "switch_glu: workspace %zu bytes < %zu needed",
@@ -324,6 +329,8 @@ int bigrig_moe_forward(const void* x, const void* logits, int logits_dtype, int 
   if (T == 0) return BIGRIG_OK;
   if (!x || !logits || !slab || !out || !workspace)
     return set_error(BIGRIG_ERR_INVALID, "moe_forward: NULL pointer");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(slab) % 16)
+    return set_error(BIGRIG_ERR_INVALID, "moe_forward: x and slab must be 16-byte aligned");
   const size_t need = carve(nullptr, T, k, E, *layout, nullptr);
   if (workspace_bytes < need)
     return set_error(BIGRIG_ERR_WORKSPACE, "moe_forward: workspace %zu bytes < %zu needed",
@@ -356,6 +363,9 @@ int bigrig_moe_layer(const void* x, const void* gate_w, const float* gate_b, int
   if (T == 0) return BIGRIG_OK;
   if (!x || !gate_w || !slab || !out || !workspace)
     return set_error(BIGRIG_ERR_INVALID, "moe_layer: NULL pointer");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(gate_w) % 16 ||
+      reinterpret_cast<uintptr_t>(slab) % 16)
+    return set_error(BIGRIG_ERR_INVALID, "moe_layer: x, gate_w and slab must be 16-byte aligned");
   if (mode != BIGRIG_SOFTMAX_TOPK && mode != BIGRIG_TOPK_SOFTMAX)
     return set_error(BIGRIG_ERR_INVALID, "moe_layer: mode=%d", mode);
   if (layout->hidden % 8)

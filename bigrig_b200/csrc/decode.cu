@@ -86,107 +86,141 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
 }
 
 // ------------------------------------------------------------------ down + combine
-constexpr int kDcWarps = 4;
-constexpr int kDcFeatures = 8;     // hidden features per CTA
-constexpr int kDcBatch = 4;        // (expert, feature) items a warp keeps in flight
+constexpr int kDcMaxSeg = 32;      // decode calls: at most 32 pairs, so at most 32 experts
 
-template <int BITS, int SDT, int ROWS>
-__global__ void __launch_bounds__(kDcWarps * 32) down_combine_kernel(
+size_t down_combine_smem(int P, const bigrig_expert_layout& L, int nf) {
+  const size_t pitch = static_cast<size_t>(L.inter) * L.bits / 8;
+  const size_t G = L.inter / L.group_size;
+  const size_t nchunk = L.inter / (128 / L.bits);
+  const size_t S = P < kDcMaxSeg ? P : kDcMaxSeg;
+  return 128 + round128(S * nf * pitch) + round128(S * 2 * nf * G * 2) +
+         round128(static_cast<size_t>(P) * L.inter * 2) +
+         round128(static_cast<size_t>(P) * L.inter * 4) + round128(P * nchunk * 4) +
+         round128(static_cast<size_t>(P) * nf * 4);
+}
+
+size_t down_combine_smem(int P, const bigrig_expert_layout& L) { return down_combine_smem(P, L, 8); }
+
+// Each CTA owns NF hidden features for every routed expert of the call: the experts'
+// down-projection rows for those features and every pair's h row arrive by bulk copy,
+// each warp computes NR features for all pairs, and the CTA combines its features.
+template <int BITS, int SDT, int NR, int ROWS>
+__global__ void __launch_bounds__(kGemvWarps * 32) down_combine_kernel(
     const uint16_t* __restrict__ h, RouteView rv, const uint8_t* __restrict__ slab,
     bigrig_expert_layout L, const float* __restrict__ scores, const uint16_t* __restrict__ residual,
     uint16_t* __restrict__ out, uint16_t* __restrict__ y_out, int T) {
-  extern __shared__ __align__(16) float smem[];
+  constexpr int NF = kGemvWarps * NR;
   constexpr int CPL = 128 / BITS;
   constexpr int Q = CPL / 4;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int seg_slot[kDcMaxSeg];
+  __shared__ int seg_row0[kDcMaxSeg + 1];
+  __shared__ int s_nvalid, abort_flag;
   pdl_wait();
   pdl_trigger();
   const int H = L.hidden, I = L.inter;
   const int P = rv.P;
-  const int nseg = *rv.num_seg;
+  const int nseg = min(min(*rv.num_seg, rv.s_max), kDcMaxSeg);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int f0 = blockIdx.x * kDcFeatures;
+  const int f0 = blockIdx.x * NF;
+  const int64_t pitch = static_cast<int64_t>(I) * BITS / 8;
+  const int G = I / L.group_size;
   const int nchunk = I / CPL;
-  // every routed pair's h row, pre-scaled, then a [P][kDcFeatures] buffer of y values
-  stage_rows<BITS>(smem, h, I, P, P, [](int rr) { return rr; });
-  float* ybuf = smem + static_cast<size_t>(P) * (I + nchunk);
-  for (int i = threadIdx.x; i < P * kDcFeatures; i += blockDim.x) ybuf[i] = 0.f;
-  __syncthreads();
-  const float4* xs = reinterpret_cast<const float4*>(smem);
-  const float* cs = smem + static_cast<size_t>(P) * I;
-  const int items = nseg * kDcFeatures;
-  for (int it0 = warp * kDcBatch; it0 < items; it0 += kDcWarps * kDcBatch) {
-    uint4 w[kDcBatch];
-    float sc[kDcBatch], bi[kDcBatch];
-    int row0[kDcBatch], nrow[kDcBatch], fl[kDcBatch];
-    bool ok[kDcBatch];
-#pragma unroll
-    for (int b = 0; b < kDcBatch; ++b) {
-      const int it = it0 + b;
-      ok[b] = it < items;
-      const int s = ok[b] ? it / kDcFeatures : 0;
-      fl[b] = it - s * kDcFeatures;
-      const int f = min(f0 + fl[b], H - 1);
-      const int e = rv.seg_expert[s];
-      int slot = rv.g2s ? rv.g2s[e] : e;
-      row0[b] = rv.seg_start[s];
-      nrow[b] = rv.seg_start[s + 1] - row0[b];
-      if (slot < 0) { ok[b] = false; slot = 0; }
-      const uint8_t* base = slab + static_cast<int64_t>(slot) * L.slot_stride;
-      const int64_t pitch = static_cast<int64_t>(I) * BITS / 8;
-      const int gp = I / L.group_size;
-      w[b] = make_uint4(0, 0, 0, 0);
-      sc[b] = bi[b] = 0.f;
-      if (ok[b] && lane < nchunk) {
-        w[b] = ld_stream_v4(base + L.weight_off[2] + f * pitch + lane * 16);
-        const int grp = (lane * CPL) / L.group_size;
-        sc[b] = half_to_f32<SDT>(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + L.scales_off[2]) + static_cast<int64_t>(f) * gp + grp));
-        bi[b] = half_to_f32<SDT>(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + L.biases_off[2]) + static_cast<int64_t>(f) * gp + grp));
-      }
+  const int S = P < kDcMaxSeg ? P : kDcMaxSeg;
+  SmemCarve sc(smem);
+  uint64_t* bar = sc.take<uint64_t>(8);
+  uint8_t* wc = sc.take<uint8_t>(static_cast<size_t>(S) * NF * pitch);
+  uint16_t* wsb = sc.take<uint16_t>(static_cast<size_t>(S) * 2 * NF * G * 2);
+  uint16_t* hraw = sc.take<uint16_t>(static_cast<size_t>(P) * I * 2);
+  float* hs = sc.take<float>(static_cast<size_t>(P) * I * 4);
+  float* cs = sc.take<float>(static_cast<size_t>(P) * nchunk * 4);
+  float* ybuf = sc.take<float>(static_cast<size_t>(P) * NF * 4);
+  const float4* h4 = reinterpret_cast<const float4*>(hs);
+  if (threadIdx.x == 0) {
+    bar_init(bar, 1);
+    abort_flag = 0;
+    // validate every segment and issue all copies of the CTA at once
+    uint32_t bytes = 0;
+    int nvalid = 0;
+    for (int s = 0; s < nseg; ++s) {
+      int row0, R;
+      const int slot = segment_slot(rv, s, row0, R);
+      seg_slot[s] = slot;
+      seg_row0[s] = row0;
+      seg_row0[s + 1] = row0 + R;
+      if (R > 0) nvalid = row0 + R;
+      if (slot >= 0) bytes += static_cast<uint32_t>(NF * pitch + 2 * NF * G * 2);
+      else if (R > 0) atomicAdd(rv.err, 1);
     }
+    s_nvalid = nvalid;
+    bytes += static_cast<uint32_t>(nvalid) * I * 2;
+    bar_expect_tx(bar, bytes);
+    for (int s = 0; s < nseg; ++s) {
+      if (seg_slot[s] < 0) continue;
+      const uint8_t* base = slab + static_cast<int64_t>(seg_slot[s]) * L.slot_stride;
+      bulk_g2s(wc + static_cast<size_t>(s) * NF * pitch, base + L.weight_off[2] + f0 * pitch,
+               NF * pitch, bar);
+      bulk_g2s(wsb + static_cast<size_t>(s) * 2 * NF * G,
+               base + L.scales_off[2] + static_cast<int64_t>(f0) * G * 2, NF * G * 2, bar);
+      bulk_g2s(wsb + (static_cast<size_t>(s) * 2 + 1) * NF * G,
+               base + L.biases_off[2] + static_cast<int64_t>(f0) * G * 2, NF * G * 2, bar);
+    }
+    if (nvalid > 0) bulk_g2s(hraw, h, nvalid * I * 2, bar);
+  }
+  for (int i = threadIdx.x; i < P * NF; i += blockDim.x) ybuf[i] = 0.f;
+  __syncthreads();
+  if (!bar_wait(bar, 0, rv.err)) {
+    abort_flag = 1;
+    bar_wait(bar, 0, nullptr);         // let this CTA's own copies land before it exits
+  }
+  __syncthreads();
+  if (!abort_flag) {
+    relayout_rows<BITS>(hs, cs, hraw, I, s_nvalid);
+    __syncthreads();
+    for (int s = 0; s < nseg; ++s) {
+      if (seg_slot[s] < 0) continue;
+      const uint8_t* ws = wc + static_cast<size_t>(s) * NF * pitch;
+      const uint16_t* sbs = wsb + static_cast<size_t>(s) * 2 * NF * G;
+      const int ra = seg_row0[s], rb = seg_row0[s + 1];
+      for (int r0 = ra; r0 < rb; r0 += ROWS) {
+        float acc[NR][ROWS];
 #pragma unroll
-    for (int b = 0; b < kDcBatch; ++b) {
-      if (it0 + b >= items) break;
-      for (int r0 = 0; r0 < nrow[b]; r0 += ROWS) {
-        float acc[ROWS];
+        for (int i = 0; i < NR; ++i)
 #pragma unroll
-        for (int rr = 0; rr < ROWS; ++rr) acc[rr] = 0.f;
-        // lane < nchunk holds this feature's first chunk; further chunks stream here
+          for (int rr = 0; rr < ROWS; ++rr) acc[i][rr] = 0.f;
         for (int c = lane; c < nchunk; c += 32) {
-          uint4 wc = w[b];
-          float s_ = sc[b], b_ = bi[b];
-          if (c != lane) {
-            if (ok[b]) {
-              const int f = min(f0 + fl[b], H - 1);
-              const int s = (it0 + b) / kDcFeatures;
-              const int e = rv.seg_expert[s];
-              const int slot = rv.g2s ? rv.g2s[e] : e;
-              const uint8_t* base = slab + static_cast<int64_t>(slot) * L.slot_stride;
-              const int64_t pitch = static_cast<int64_t>(I) * BITS / 8;
-              const int gp = I / L.group_size;
-              const int grp = (c * CPL) / L.group_size;
-              wc = ld_stream_v4(base + L.weight_off[2] + f * pitch + c * 16);
-              s_ = half_to_f32<SDT>(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + L.scales_off[2]) + static_cast<int64_t>(f) * gp + grp));
-              b_ = half_to_f32<SDT>(ld_nc_u16(reinterpret_cast<const uint16_t*>(base + L.biases_off[2]) + static_cast<int64_t>(f) * gp + grp));
-            } else {
-              wc = make_uint4(0, 0, 0, 0);
-              s_ = b_ = 0.f;
-            }
+          const int grp = (c * CPL) / L.group_size;
+          uint4 cw[NR];
+          float sw[NR], bw[NR];
+#pragma unroll
+          for (int i = 0; i < NR; ++i) {
+            const int fl = warp * NR + i;
+            cw[i] = *reinterpret_cast<const uint4*>(ws + fl * pitch + c * 16);
+            sw[i] = half_to_f32<SDT>(sbs[fl * G + grp]);
+            bw[i] = half_to_f32<SDT>(sbs[(NF + fl) * G + grp]);
           }
 #pragma unroll
           for (int rr = 0; rr < ROWS; ++rr) {
-            if (r0 + rr < nrow[b]) {
-              const int row = row0[b] + r0 + rr;
-              const float4* xq = xs + static_cast<size_t>(row) * Q * nchunk + c;
-              const float d = chunk_dot<BITS>(wc, xq, nchunk);
-              acc[rr] = fmaf(s_, d, fmaf(b_, cs[row * nchunk + c], acc[rr]));
+            if (r0 + rr < rb) {
+              ChunkX<BITS> cx;
+              load_chunk_x<BITS>(cx, h4 + static_cast<size_t>(r0 + rr) * Q * nchunk + c, nchunk);
+              const float csum = cs[(r0 + rr) * nchunk + c];
+#pragma unroll
+              for (int i = 0; i < NR; ++i) {
+                const float d = chunk_dot2<BITS>(cw[i], cx);
+                acc[i][rr] = fmaf(sw[i], d, fmaf(bw[i], csum, acc[i][rr]));
+              }
             }
           }
         }
 #pragma unroll
-        for (int rr = 0; rr < ROWS; ++rr) {
-          if (r0 + rr < nrow[b]) {
-            const float v = warp_sum(acc[rr]);
-            if (lane == 0) ybuf[(row0[b] + r0 + rr) * kDcFeatures + fl[b]] = ok[b] ? bf16_round(v) : 0.f;
+        for (int i = 0; i < NR; ++i) {
+#pragma unroll
+          for (int rr = 0; rr < ROWS; ++rr) {
+            if (r0 + rr < rb) {
+              const float v = warp_sum(acc[i][rr]);
+              if (lane == 0) ybuf[(r0 + rr) * NF + warp * NR + i] = bf16_round(v);
+            }
           }
         }
       }
@@ -195,13 +229,13 @@ __global__ void __launch_bounds__(kDcWarps * 32) down_combine_kernel(
   __syncthreads();
   // combine in rank order (the standalone combine's arithmetic), plus the residual
   const int k = rv.k;
-  for (int idx = threadIdx.x; idx < T * kDcFeatures; idx += blockDim.x) {
-    const int t = idx / kDcFeatures, fl = idx - t * kDcFeatures;
+  for (int idx = threadIdx.x; idx < T * NF; idx += blockDim.x) {
+    const int t = idx / NF, fl = idx - t * NF;
     const int f = f0 + fl;
-    if (f >= H) continue;
     float a = 0.f;
     for (int j = 0; j < k; ++j) {
-      const float yv = ybuf[rv.inv[t * k + j] * kDcFeatures + fl];
+      const int pos = rv.inv[t * k + j];
+      const float yv = (pos >= 0 && pos < P) ? ybuf[pos * NF + fl] : 0.f;
       a = a + scores[t * k + j] * yv;
       if (y_out) y_out[(static_cast<size_t>(t) * k + j) * H + f] = f32_to_bf16_bits(yv);
     }
@@ -256,24 +290,19 @@ int launch_route(const void* x, const void* gate_w, const float* gate_b, const v
   return set_error(BIGRIG_ERR_UNSUPPORTED, "route: n_experts must be <= 256");
 }
 
-size_t down_combine_smem(int P, const bigrig_expert_layout& L) {
-  const int nchunk = L.inter / (128 / L.bits);
-  return static_cast<size_t>(P) * (L.inter + nchunk) * sizeof(float) +
-         static_cast<size_t>(P) * kDcFeatures * sizeof(float);
-}
-
 template <int BITS, int SDT, int ROWS>
 static int dc_launch(const void* h, const RouteView& rv, const void* slab,
                      const bigrig_expert_layout& L, const float* scores, const void* residual,
                      void* out, void* y_out, int T, cudaStream_t s) {
-  const size_t smem = down_combine_smem(rv.P, L);
-  auto kern = down_combine_kernel<BITS, SDT, ROWS>;
+  constexpr int NR = 2;          // 8 features per CTA: 256 CTAs for a 2048-wide hidden
+  const size_t smem = down_combine_smem(rv.P, L, kGemvWarps * NR);
+  auto kern = down_combine_kernel<BITS, SDT, NR, ROWS>;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return set_error(BIGRIG_ERR_CUDA, "down_combine: cannot reserve %zu bytes of smem", smem);
-  const dim3 grid((L.hidden + kDcFeatures - 1) / kDcFeatures);
+  const dim3 grid(L.hidden / (kGemvWarps * NR));
   TimedLaunch tl(BIGRIG_K_DOWN_COMBINE, s);
-  return launch_pdl(kern, grid, dim3(kDcWarps * 32), smem, s, "down_combine_kernel",
+  return launch_pdl(kern, grid, dim3(kGemvWarps * 32), smem, s, "down_combine_kernel",
                     static_cast<const uint16_t*>(h), rv, static_cast<const uint8_t*>(slab), L,
                     scores, static_cast<const uint16_t*>(residual), static_cast<uint16_t*>(out),
                     static_cast<uint16_t*>(y_out), T);

@@ -28,8 +28,7 @@
 // Every mbarrier wait is bounded: past the limit the CTA records an error,
 // raises a shared abort flag so every other wait returns at once, drains the
 // MMAs it issued, frees its TMEM and returns.
-#include "common.cuh"
-#include "launch.h"
+#include "gemv_common.cuh"
 
 namespace bigrig {
 namespace sm100 {
@@ -243,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   const int NF = MODE == 0 ? L.inter : L.hidden;       // output features
   const int m_tiles = (NF + kBlockM - 1) / kBlockM;
   const int k_iters = K / kBlockK;
-  const int nseg = *rv.num_seg;
+  const int nseg = min(min(*rv.num_seg, rv.s_max), kMaxExperts);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -262,7 +261,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       int acc = 0;
       for (int s = 0; s < nseg; ++s) {
         tile_start[s] = acc;
-        const int R = rv.seg_start[s + 1] - rv.seg_start[s];
+        int row0, R;
+        segment_slot(rv, s, row0, R);      // R = 0 for inconsistent metadata: no tiles
         acc += m_tiles * ((R + BN - 1) / BN);
       }
       tile_start[nseg] = acc;
@@ -283,13 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       int s = 0;
       while (s + 1 < nseg && tile_start[s + 1] <= tile) ++s;
       const int local = tile - tile_start[s];
-      const int row0 = rv.seg_start[s];
-      const int R = rv.seg_start[s + 1] - row0;
+      int row0, R;
+      const int slot = segment_slot(rv, s, row0, R);
       const int n_tiles = (R + BN - 1) / BN;
       const int mt = local / n_tiles, nt = local - mt * n_tiles;
       const int m0 = mt * kBlockM, n0 = nt * BN;
-      const int e = rv.seg_expert[s];
-      const int slot = rv.g2s ? rv.g2s[e] : e;
       const bool valid_slot = slot >= 0;
       if (!valid_slot && ptid == 0 && mt == 0 && nt == 0) atomicAdd(rv.err, 1);
       const uint8_t* base = slab + static_cast<int64_t>(valid_slot ? slot : 0) * L.slot_stride;

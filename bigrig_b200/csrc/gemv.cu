@@ -6,92 +6,132 @@
 //   gate_up: h[p, :] = bf16(silu(x.Wg^T) * (x.Wu^T)) for every pair p (gate/up in fp32)
 //   down:    y[pair, :] = bf16(h[p, :] . Wd^T), written at the pair's unpermuted
 //            (token, k) position, so no separate unpermute pass exists.
-//
-// Weights stream once from HBM as 128-bit non-allocating loads, 16 bytes of codes
-// per lane per step, coalesced along the row.  Codes become floats without integer
-// conversions: OR-ing a code field into the mantissa of 2^23 and subtracting 2^23
-// yields q * 16^j (4-bit) or q * 256^j (8-bit) for the field's position j inside a
-// half-word, and the activation is pre-scaled by 16^-j (or 256^-j) once in shared
-// memory, so each code costs one LOP3, one FADD and one FFMA.  The group affine is
-// applied once per 16-byte chunk: sum (s q + b) x = s sum(q x) + b sum(x).
+// A CTA owns NF output features of one expert: its weight rows arrive once by bulk
+// copy and serve every pass over the expert's rows (see gemv_common.cuh).
 #include "gemv_common.cuh"
 #include "routing.cuh"
 
 namespace bigrig {
+
+size_t gemv_gate_up_smem(const bigrig_expert_layout& L, int nf, int rows) {
+  const size_t pitch = static_cast<size_t>(L.hidden) * L.bits / 8;
+  const size_t G = L.hidden / L.group_size;
+  const size_t nchunk = L.hidden / (128 / L.bits);
+  return 128 + round128(2 * nf * pitch) + round128(4 * nf * G * 2) +
+         round128(static_cast<size_t>(rows) * L.hidden * 2) +
+         round128(static_cast<size_t>(rows) * L.hidden * 4) + round128(rows * nchunk * 4);
+}
+
+size_t gemv_down_smem(const bigrig_expert_layout& L, int nf, int rows) {
+  const size_t pitch = static_cast<size_t>(L.inter) * L.bits / 8;
+  const size_t G = L.inter / L.group_size;
+  const size_t nchunk = L.inter / (128 / L.bits);
+  return 128 + round128(nf * pitch) + round128(2 * nf * G * 2) +
+         round128(static_cast<size_t>(rows) * L.inter * 2) +
+         round128(static_cast<size_t>(rows) * L.inter * 4) + round128(rows * nchunk * 4);
+}
 
 // ------------------------------------------------------------------ gate/up
 template <int BITS, int SDT, int NR, int ROWS>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_gate_up_kernel(
     const uint16_t* __restrict__ x, RouteView rv, const uint8_t* __restrict__ slab,
     bigrig_expert_layout L, uint16_t* __restrict__ h, int rows_cap) {
-  extern __shared__ __align__(16) float smem[];
-  __shared__ int row_tok[kGemvRows];
+  constexpr int NF = kGemvWarps * NR;
   constexpr int CPL = 128 / BITS;
   constexpr int Q = CPL / 4;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int abort_flag;
   pdl_wait();
   pdl_trigger();
   const int s = blockIdx.y;
-  if (s >= *rv.num_seg) return;
+  if (s >= min(*rv.num_seg, rv.s_max)) return;
   const int H = L.hidden, I = L.inter;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = rv.seg_expert[s];
-  const int slot = rv.g2s ? rv.g2s[e] : e;
-  const int row0 = rv.seg_start[s], R = rv.seg_start[s + 1] - row0;
-  const int fbase = blockIdx.x * (kGemvWarps * NR) + warp * NR;
+  const int f0 = blockIdx.x * NF;
+  int row0, R;
+  const int slot = segment_slot(rv, s, row0, R);
   if (slot < 0) {
     if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(rv.err, 1);
-    for (int idx = threadIdx.x; idx < R * kGemvWarps * NR; idx += blockDim.x) {
-      const int rr = idx / (kGemvWarps * NR), f = blockIdx.x * (kGemvWarps * NR) + idx % (kGemvWarps * NR);
-      if (f < I) h[static_cast<size_t>(row0 + rr) * I + f] = 0;
-    }
+    for (int i = threadIdx.x; i < R * NF; i += blockDim.x)
+      h[static_cast<size_t>(row0 + i / NF) * I + f0 + i % NF] = 0;
     return;
   }
-  const uint8_t* base = slab + static_cast<int64_t>(slot) * L.slot_stride;
-  const ProjView pg = proj_view(base, L, 0, H), pu = proj_view(base, L, 1, H);
+  const int64_t pitch = static_cast<int64_t>(H) * BITS / 8;
+  const int G = H / L.group_size;
   const int nchunk = H / CPL;
-  const float4* xs = reinterpret_cast<const float4*>(smem);
-  const float* cs = smem + static_cast<size_t>(rows_cap) * H;
-
+  SmemCarve sc(smem);
+  uint64_t* bar = sc.take<uint64_t>(8);
+  uint8_t* wc = sc.take<uint8_t>(2 * NF * pitch);
+  uint16_t* wsb = sc.take<uint16_t>(4 * NF * G * 2);
+  uint16_t* xraw = sc.take<uint16_t>(static_cast<size_t>(rows_cap) * H * 2);
+  float* xs = sc.take<float>(static_cast<size_t>(rows_cap) * H * 4);
+  float* cs = sc.take<float>(static_cast<size_t>(rows_cap) * nchunk * 4);
+  const float4* x4 = reinterpret_cast<const float4*>(xs);
+  const uint8_t* base = slab + static_cast<int64_t>(slot) * L.slot_stride;
+  if (threadIdx.x == 0) {
+    bar_init(bar, 1);
+    abort_flag = 0;
+  }
+  __syncthreads();
+  uint32_t phase = 0;
   for (int r0 = 0; r0 < R; r0 += rows_cap) {
     const int nr = min(rows_cap, R - r0);
+    if (threadIdx.x == 0) {
+      uint32_t bytes = static_cast<uint32_t>(nr) * H * 2;
+      if (r0 == 0) bytes += static_cast<uint32_t>(2 * NF * pitch + 4 * NF * G * 2);
+      bar_expect_tx(bar, bytes);
+      if (r0 == 0) {
+        for (int m = 0; m < 2; ++m) {
+          bulk_g2s(wc + m * NF * pitch, base + L.weight_off[m] + f0 * pitch, NF * pitch, bar);
+          bulk_g2s(wsb + (2 * m) * NF * G, base + L.scales_off[m] + static_cast<int64_t>(f0) * G * 2,
+                   NF * G * 2, bar);
+          bulk_g2s(wsb + (2 * m + 1) * NF * G,
+                   base + L.biases_off[m] + static_cast<int64_t>(f0) * G * 2, NF * G * 2, bar);
+        }
+      }
+      for (int rr = 0; rr < nr; ++rr) {
+        const int tok = rv.order[row0 + r0 + rr] / rv.k;
+        bulk_g2s(xraw + static_cast<size_t>(rr) * H, x + static_cast<int64_t>(tok) * H, H * 2, bar);
+      }
+    }
+    if (!bar_wait(bar, phase, rv.err)) {
+      abort_flag = 1;
+      bar_wait(bar, phase, nullptr);   // let this CTA's own copies land before it exits
+    }
+    phase ^= 1;
     __syncthreads();
-    if (threadIdx.x < nr) row_tok[threadIdx.x] = rv.order[row0 + r0 + threadIdx.x] / rv.k;
-    __syncthreads();
-    stage_rows<BITS>(smem, x, H, nr, rows_cap, [&](int rr) { return row_tok[rr]; });
+    if (abort_flag) break;
+    relayout_rows<BITS>(xs, cs, xraw, H, nr);
     __syncthreads();
     float acc[2][NR][ROWS];
 #pragma unroll
     for (int i = 0; i < NR; ++i)
 #pragma unroll
       for (int rr = 0; rr < ROWS; ++rr) acc[0][i][rr] = acc[1][i][rr] = 0.f;
-
     for (int c = lane; c < nchunk; c += 32) {
-      uint4 wg[NR], wu[NR];
-      float sg[NR], bg[NR], su[NR], bu[NR];
       const int grp = (c * CPL) / L.group_size;
+      uint4 cg[NR], cu[NR];
+      float sg[NR], bg[NR], su[NR], bu[NR];
 #pragma unroll
       for (int i = 0; i < NR; ++i) {
-        const int f = min(fbase + i, I - 1);
-        wg[i] = ld_stream_v4(pg.codes + f * pg.code_pitch + c * 16);
-        wu[i] = ld_stream_v4(pu.codes + f * pu.code_pitch + c * 16);
-      }
-#pragma unroll
-      for (int i = 0; i < NR; ++i) {
-        const int f = min(fbase + i, I - 1);
-        sg[i] = half_to_f32<SDT>(ld_nc_u16(pg.scales + f * pg.group_pitch + grp));
-        bg[i] = half_to_f32<SDT>(ld_nc_u16(pg.biases + f * pg.group_pitch + grp));
-        su[i] = half_to_f32<SDT>(ld_nc_u16(pu.scales + f * pu.group_pitch + grp));
-        bu[i] = half_to_f32<SDT>(ld_nc_u16(pu.biases + f * pu.group_pitch + grp));
+        const int fl = warp * NR + i;
+        cg[i] = *reinterpret_cast<const uint4*>(wc + fl * pitch + c * 16);
+        cu[i] = *reinterpret_cast<const uint4*>(wc + (NF + fl) * pitch + c * 16);
+        sg[i] = half_to_f32<SDT>(wsb[(0 * NF + fl) * G + grp]);
+        bg[i] = half_to_f32<SDT>(wsb[(1 * NF + fl) * G + grp]);
+        su[i] = half_to_f32<SDT>(wsb[(2 * NF + fl) * G + grp]);
+        bu[i] = half_to_f32<SDT>(wsb[(3 * NF + fl) * G + grp]);
       }
 #pragma unroll
       for (int rr = 0; rr < ROWS; ++rr) {
         if (rr < nr) {
-          const float4* xq = xs + static_cast<size_t>(rr) * Q * nchunk + c;
+          ChunkX<BITS> cx;
+          load_chunk_x<BITS>(cx, x4 + static_cast<size_t>(rr) * Q * nchunk + c, nchunk);
           const float csum = cs[rr * nchunk + c];
 #pragma unroll
           for (int i = 0; i < NR; ++i) {
-            const float dg = chunk_dot<BITS>(wg[i], xq, nchunk);
-            const float du = chunk_dot<BITS>(wu[i], xq, nchunk);
+            const float dg = chunk_dot2<BITS>(cg[i], cx);
+            const float du = chunk_dot2<BITS>(cu[i], cx);
             acc[0][i][rr] = fmaf(sg[i], dg, fmaf(bg[i], csum, acc[0][i][rr]));
             acc[1][i][rr] = fmaf(su[i], du, fmaf(bu[i], csum, acc[1][i][rr]));
           }
@@ -105,12 +145,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_gate_up_kernel(
         if (rr < nr) {
           const float g = warp_sum(acc[0][i][rr]);
           const float u = warp_sum(acc[1][i][rr]);
-          const int f = fbase + i;
-          if (lane == 0 && f < I)
-            h[static_cast<size_t>(row0 + r0 + rr) * I + f] = f32_to_bf16_bits(silu_f32(g) * u);
+          if (lane == 0)
+            h[static_cast<size_t>(row0 + r0 + rr) * I + f0 + warp * NR + i] =
+                f32_to_bf16_bits(silu_f32(g) * u);
         }
       }
     }
+    __syncthreads();      // the next pass overwrites xraw / xs
   }
 }
 
@@ -119,67 +160,92 @@ template <int BITS, int SDT, int NR, int ROWS>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_down_kernel(
     const uint16_t* __restrict__ h, RouteView rv, const uint8_t* __restrict__ slab,
     bigrig_expert_layout L, uint16_t* __restrict__ y, int rows_cap) {
-  extern __shared__ __align__(16) float smem[];
+  constexpr int NF = kGemvWarps * NR;
   constexpr int CPL = 128 / BITS;
   constexpr int Q = CPL / 4;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int abort_flag;
   pdl_wait();
   pdl_trigger();
   const int s = blockIdx.y;
-  if (s >= *rv.num_seg) return;
+  if (s >= min(*rv.num_seg, rv.s_max)) return;
   const int H = L.hidden, I = L.inter;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = rv.seg_expert[s];
-  const int slot = rv.g2s ? rv.g2s[e] : e;
-  const int row0 = rv.seg_start[s], R = rv.seg_start[s + 1] - row0;
-  const int fbase = blockIdx.x * (kGemvWarps * NR) + warp * NR;
+  const int f0 = blockIdx.x * NF;
+  int row0, R;
+  const int slot = segment_slot(rv, s, row0, R);
   if (slot < 0) {
-    for (int idx = threadIdx.x; idx < R * kGemvWarps * NR; idx += blockDim.x) {
-      const int rr = idx / (kGemvWarps * NR), f = blockIdx.x * (kGemvWarps * NR) + idx % (kGemvWarps * NR);
-      if (f < H) y[static_cast<size_t>(rv.order[row0 + rr]) * H + f] = 0;
-    }
+    for (int i = threadIdx.x; i < R * NF; i += blockDim.x)
+      y[static_cast<size_t>(rv.order[row0 + i / NF]) * H + f0 + i % NF] = 0;
     return;
   }
-  const uint8_t* base = slab + static_cast<int64_t>(slot) * L.slot_stride;
-  const ProjView pd = proj_view(base, L, 2, I);
+  const int64_t pitch = static_cast<int64_t>(I) * BITS / 8;
+  const int G = I / L.group_size;
   const int nchunk = I / CPL;
-  const float4* xs = reinterpret_cast<const float4*>(smem);
-  const float* cs = smem + static_cast<size_t>(rows_cap) * I;
-
+  SmemCarve sc(smem);
+  uint64_t* bar = sc.take<uint64_t>(8);
+  uint8_t* wc = sc.take<uint8_t>(NF * pitch);
+  uint16_t* wsb = sc.take<uint16_t>(2 * NF * G * 2);
+  uint16_t* hraw = sc.take<uint16_t>(static_cast<size_t>(rows_cap) * I * 2);
+  float* hs = sc.take<float>(static_cast<size_t>(rows_cap) * I * 4);
+  float* cs = sc.take<float>(static_cast<size_t>(rows_cap) * nchunk * 4);
+  const float4* h4 = reinterpret_cast<const float4*>(hs);
+  const uint8_t* base = slab + static_cast<int64_t>(slot) * L.slot_stride;
+  if (threadIdx.x == 0) {
+    bar_init(bar, 1);
+    abort_flag = 0;
+  }
+  __syncthreads();
+  uint32_t phase = 0;
   for (int r0 = 0; r0 < R; r0 += rows_cap) {
     const int nr = min(rows_cap, R - r0);
+    if (threadIdx.x == 0) {
+      uint32_t bytes = static_cast<uint32_t>(nr) * I * 2;
+      if (r0 == 0) bytes += static_cast<uint32_t>(NF * pitch + 2 * NF * G * 2);
+      bar_expect_tx(bar, bytes);
+      if (r0 == 0) {
+        bulk_g2s(wc, base + L.weight_off[2] + f0 * pitch, NF * pitch, bar);
+        bulk_g2s(wsb, base + L.scales_off[2] + static_cast<int64_t>(f0) * G * 2, NF * G * 2, bar);
+        bulk_g2s(wsb + NF * G, base + L.biases_off[2] + static_cast<int64_t>(f0) * G * 2,
+                 NF * G * 2, bar);
+      }
+      bulk_g2s(hraw, h + static_cast<int64_t>(row0 + r0) * I, nr * I * 2, bar);
+    }
+    if (!bar_wait(bar, phase, rv.err)) {
+      abort_flag = 1;
+      bar_wait(bar, phase, nullptr);   // let this CTA's own copies land before it exits
+    }
+    phase ^= 1;
     __syncthreads();
-    stage_rows<BITS>(smem, h, I, nr, rows_cap, [&](int rr) { return row0 + r0 + rr; });
+    if (abort_flag) break;
+    relayout_rows<BITS>(hs, cs, hraw, I, nr);
     __syncthreads();
     float acc[NR][ROWS];
 #pragma unroll
     for (int i = 0; i < NR; ++i)
 #pragma unroll
       for (int rr = 0; rr < ROWS; ++rr) acc[i][rr] = 0.f;
-
     for (int c = lane; c < nchunk; c += 32) {
-      uint4 wd[NR];
-      float sd[NR], bd[NR];
       const int grp = (c * CPL) / L.group_size;
+      uint4 cw[NR];
+      float sw[NR], bw[NR];
 #pragma unroll
       for (int i = 0; i < NR; ++i) {
-        const int f = min(fbase + i, H - 1);
-        wd[i] = ld_stream_v4(pd.codes + f * pd.code_pitch + c * 16);
-      }
-#pragma unroll
-      for (int i = 0; i < NR; ++i) {
-        const int f = min(fbase + i, H - 1);
-        sd[i] = half_to_f32<SDT>(ld_nc_u16(pd.scales + f * pd.group_pitch + grp));
-        bd[i] = half_to_f32<SDT>(ld_nc_u16(pd.biases + f * pd.group_pitch + grp));
+        const int fl = warp * NR + i;
+        cw[i] = *reinterpret_cast<const uint4*>(wc + fl * pitch + c * 16);
+        sw[i] = half_to_f32<SDT>(wsb[fl * G + grp]);
+        bw[i] = half_to_f32<SDT>(wsb[(NF + fl) * G + grp]);
       }
 #pragma unroll
       for (int rr = 0; rr < ROWS; ++rr) {
         if (rr < nr) {
-          const float4* xq = xs + static_cast<size_t>(rr) * Q * nchunk + c;
+          ChunkX<BITS> cx;
+          load_chunk_x<BITS>(cx, h4 + static_cast<size_t>(rr) * Q * nchunk + c, nchunk);
           const float csum = cs[rr * nchunk + c];
 #pragma unroll
           for (int i = 0; i < NR; ++i) {
-            const float d = chunk_dot<BITS>(wd[i], xq, nchunk);
-            acc[i][rr] = fmaf(sd[i], d, fmaf(bd[i], csum, acc[i][rr]));
+            const float d = chunk_dot2<BITS>(cw[i], cx);
+            acc[i][rr] = fmaf(sw[i], d, fmaf(bw[i], csum, acc[i][rr]));
           }
         }
       }
@@ -190,14 +256,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_down_kernel(
       for (int rr = 0; rr < ROWS; ++rr) {
         if (rr < nr) {
           const float v = warp_sum(acc[i][rr]);
-          const int f = fbase + i;
-          if (lane == 0 && f < H) {
-            const int pair = rv.order[row0 + r0 + rr];
-            y[static_cast<size_t>(pair) * H + f] = f32_to_bf16_bits(v);
-          }
+          if (lane == 0)
+            y[static_cast<size_t>(rv.order[row0 + r0 + rr]) * H + f0 + warp * NR + i] =
+                f32_to_bf16_bits(v);
         }
       }
     }
+    __syncthreads();
   }
 }
 
@@ -229,79 +294,93 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const float* __re
 }
 
 // ------------------------------------------------------------------ launchers
-// Rows staged per pass: at most kGemvRows, at most the largest number of rows one
-// expert can receive (an expert appears once per token, so <= T), and within a
-// 200 KB shared-memory budget (Mixtral's 14336-wide down projection fits 3).
-static int gemv_rows_cap(int K, int bits, int max_rows) {
-  const size_t per_row = static_cast<size_t>(K) * sizeof(float) + (K / (128 / bits)) * sizeof(float);
-  int cap = static_cast<int>((200u * 1024u) / per_row);
-  cap = cap < kGemvRows ? cap : kGemvRows;
-  cap = cap < max_rows ? cap : max_rows;
-  return cap < 1 ? 1 : cap;
-}
+constexpr size_t kGemvSmemBudget = 200 * 1024;
 
-static size_t gemv_smem(int K, int bits, int rows_cap) {
-  return static_cast<size_t>(rows_cap) * (static_cast<size_t>(K) + K / (128 / bits)) * sizeof(float);
+// Features per CTA and rows per pass: the most features (16, else 8) and rows (<= 4,
+// <= the rows one expert can get) whose staging fits the shared-memory budget.
+template <typename SmemFn>
+static bool pick_tile(SmemFn fn, int max_rows, int* nf, int* rows) {
+  for (int f : {16, 8}) {
+    for (int r = max_rows < kGemvRows ? max_rows : kGemvRows; r >= 1; --r) {
+      if (fn(f, r) <= kGemvSmemBudget) {
+        *nf = f;
+        *rows = r;
+        return true;
+      }
+    }
+  }
+  return false;
 }
 
 template <typename Kern>
-static int prepare(Kern kern, size_t smem) {
-  if (smem > 48 * 1024) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return set_error(BIGRIG_ERR_CUDA, "cudaFuncSetAttribute(smem=%zu) failed", smem);
-  }
-  return 0;
+static int launch_gemv(Kern kern, dim3 grid, size_t smem, cudaStream_t s, const char* name,
+                       const void* act, const RouteView& rv, const void* slab,
+                       const bigrig_expert_layout& L, void* out, int rows) {
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return set_error(BIGRIG_ERR_CUDA, "%s: cannot reserve %zu bytes of smem", name, smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kGemvWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, static_cast<const uint16_t*>(act), rv,
+                     static_cast<const uint8_t*>(slab), L, static_cast<uint16_t*>(out), rows);
+  return check_launch(name);
 }
 
-template <int BITS, int SDT, int ROWS>
-static int gate_up_rows(const void* x, const RouteView& rv, const void* slab,
-                        const bigrig_expert_layout& L, void* h, int cap, cudaStream_t s) {
-  constexpr int NR = 4;
-  const size_t smem = gemv_smem(L.hidden, BITS, cap);
-  auto kern = gemv_gate_up_kernel<BITS, SDT, NR, ROWS>;
-  if (int rc = prepare(kern, smem)) return rc;
-  const dim3 grid((L.inter + kGemvWarps * NR - 1) / (kGemvWarps * NR), rv.s_max);
-  TimedLaunch tl(BIGRIG_K_GATE_UP, s);
-  kern<<<grid, kGemvWarps * 32, smem, s>>>(static_cast<const uint16_t*>(x), rv,
-                                           static_cast<const uint8_t*>(slab), L,
-                                           static_cast<uint16_t*>(h), cap);
-  return check_launch("gemv_gate_up_kernel");
-}
-
-template <int BITS, int SDT, int ROWS>
-static int down_rows(const void* h, const RouteView& rv, const void* slab,
-                     const bigrig_expert_layout& L, void* y, int cap, cudaStream_t s) {
-  constexpr int NR = 8;
-  const size_t smem = gemv_smem(L.inter, BITS, cap);
-  auto kern = gemv_down_kernel<BITS, SDT, NR, ROWS>;
-  if (int rc = prepare(kern, smem)) return rc;
-  const dim3 grid((L.hidden + kGemvWarps * NR - 1) / (kGemvWarps * NR), rv.s_max);
-  TimedLaunch tl(BIGRIG_K_DOWN, s);
-  kern<<<grid, kGemvWarps * 32, smem, s>>>(static_cast<const uint16_t*>(h), rv,
-                                           static_cast<const uint8_t*>(slab), L,
-                                           static_cast<uint16_t*>(y), cap);
-  return check_launch("gemv_down_kernel");
-}
-
-// Accumulator rows are a template parameter (1, 2 or 4) so a one-token decode keeps
-// its register footprint, and with it the occupancy that hides HBM latency.
 template <int BITS, int SDT>
 static int gate_up_impl(const void* x, const RouteView& rv, const void* slab,
                         const bigrig_expert_layout& L, void* h, cudaStream_t s) {
-  const int cap = gemv_rows_cap(L.hidden, BITS, rv.max_rows);
-  if (cap == 1) return gate_up_rows<BITS, SDT, 1>(x, rv, slab, L, h, 1, s);
-  if (cap == 2) return gate_up_rows<BITS, SDT, 2>(x, rv, slab, L, h, 2, s);
-  return gate_up_rows<BITS, SDT, 4>(x, rv, slab, L, h, cap, s);
+  int nf = 0, rows = 0;
+  if (!pick_tile([&](int f, int r) { return gemv_gate_up_smem(L, f, r); }, rv.max_rows, &nf, &rows))
+    return set_error(BIGRIG_ERR_UNSUPPORTED, "gemv gate_up: hidden=%d does not fit shared memory",
+                     L.hidden);
+  const size_t smem = gemv_gate_up_smem(L, nf, rows);
+  const dim3 grid(L.inter / nf, rv.s_max);
+  TimedLaunch tl(BIGRIG_K_GATE_UP, s);
+  const char* n = "gemv_gate_up_kernel";
+#define BIGRIG_GU(NR, RW) \
+  return launch_gemv(gemv_gate_up_kernel<BITS, SDT, NR, RW>, grid, smem, s, n, x, rv, slab, L, h, rows)
+  if (nf == 16) {
+    if (rows == 1) BIGRIG_GU(4, 1);
+    if (rows == 2) BIGRIG_GU(4, 2);
+    BIGRIG_GU(4, 4);
+  }
+  if (rows == 1) BIGRIG_GU(2, 1);
+  if (rows == 2) BIGRIG_GU(2, 2);
+  BIGRIG_GU(2, 4);
+#undef BIGRIG_GU
 }
 
 template <int BITS, int SDT>
 static int down_impl(const void* h, const RouteView& rv, const void* slab,
                      const bigrig_expert_layout& L, void* y, cudaStream_t s) {
-  const int cap = gemv_rows_cap(L.inter, BITS, rv.max_rows);
-  if (cap == 1) return down_rows<BITS, SDT, 1>(h, rv, slab, L, y, 1, s);
-  if (cap == 2) return down_rows<BITS, SDT, 2>(h, rv, slab, L, y, 2, s);
-  return down_rows<BITS, SDT, 4>(h, rv, slab, L, y, cap, s);
+  int nf = 0, rows = 0;
+  if (!pick_tile([&](int f, int r) { return gemv_down_smem(L, f, r); }, rv.max_rows, &nf, &rows))
+    return set_error(BIGRIG_ERR_UNSUPPORTED, "gemv down: inter=%d does not fit shared memory",
+                     L.inter);
+  const size_t smem = gemv_down_smem(L, nf, rows);
+  const dim3 grid(L.hidden / nf, rv.s_max);
+  TimedLaunch tl(BIGRIG_K_DOWN, s);
+  const char* n = "gemv_down_kernel";
+#define BIGRIG_DN(NR, RW) \
+  return launch_gemv(gemv_down_kernel<BITS, SDT, NR, RW>, grid, smem, s, n, h, rv, slab, L, y, rows)
+  if (nf == 16) {
+    if (rows == 1) BIGRIG_DN(4, 1);
+    if (rows == 2) BIGRIG_DN(4, 2);
+    BIGRIG_DN(4, 4);
+  }
+  if (rows == 1) BIGRIG_DN(2, 1);
+  if (rows == 2) BIGRIG_DN(2, 2);
+  BIGRIG_DN(2, 4);
+#undef BIGRIG_DN
 }
 
 #define BIGRIG_DISPATCH_FMT(FN, ...)                                                  \

@@ -1,5 +1,17 @@
-// Helpers of the dequantising GEMV kernels: code-to-float conversion, the per-chunk
-// dot product and the activation staging (see gemv.cu for the scheme).
+// Building blocks of the dequantising GEMV kernels (gemv.cu, decode.cu).
+//
+// Scheme.  A CTA owns a few output features of one expert (or of every routed expert,
+// for the fused down+combine).  One thread moves the CTA's weight rows -- codes, scales,
+// biases -- and the routed activation rows from global memory into shared memory with
+// bulk asynchronous copies completed on an mbarrier, so every byte a CTA needs is in
+// flight at once; the activation rows are then re-laid as pre-scaled fp32.  Each warp
+// computes its features from shared memory, a lane owning one 16-byte code chunk
+// (32 four-bit or 16 eight-bit codes) per step.  Codes become floats without integer
+// conversions: a code field OR-ed into the mantissa of 2^23, minus 2^23, is q * 16^j
+// (4-bit) or q * 256^j (8-bit) for the field's position j in its half-word, and the
+// activation is pre-scaled by 16^-j (or 256^-j) once.  Pairs of codes go through
+// Blackwell's packed fp32x2 subtract and fused multiply-add.  The group affine is
+// applied once per chunk: sum (s q + b) x = s sum(q x) + b sum(x).
 #pragma once
 
 #include "common.cuh"
@@ -8,7 +20,7 @@
 namespace bigrig {
 
 constexpr int kGemvWarps = 4;
-constexpr int kGemvRows = 4;  // token rows per pass (rows of one expert <= tokens)
+constexpr int kGemvRows = 4;  // activation rows per pass (rows of one expert <= tokens)
 
 template <int BITS>
 __device__ __forceinline__ float prescale(int kk) {
@@ -16,58 +28,75 @@ __device__ __forceinline__ float prescale(int kk) {
   else return __uint_as_float((127u - 8u * static_cast<uint32_t>(kk & 1)) << 23);
 }
 
-// Partial dot of one 16-byte code chunk with its CPL pre-scaled activations.
+// The CPL pre-scaled activations of one chunk, as float2 pairs in code order.
 template <int BITS>
-__device__ __forceinline__ float chunk_dot(const uint4 w, const float4* __restrict__ xq,
-                                           int qstride) {
-  constexpr float M = 8388608.f;
+struct ChunkX {
+  float2 v[128 / BITS / 2];
+};
+
+template <int BITS>
+__device__ __forceinline__ void load_chunk_x(ChunkX<BITS>& cx, const float4* __restrict__ xq,
+                                             int qstride) {
+  constexpr int Q = 128 / BITS / 4;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const float4 f = xq[q * qstride];
+    cx.v[2 * q] = make_float2(f.x, f.y);
+    cx.v[2 * q + 1] = make_float2(f.z, f.w);
+  }
+}
+
+// sum over the chunk of q_j * x_j (pre-scaled activations), packed fp32x2 arithmetic.
+template <int BITS>
+__device__ __forceinline__ float chunk_dot2(const uint4 w, const ChunkX<BITS>& cx) {
+  const float2 NM2 = make_float2(-8388608.f, -8388608.f);
   constexpr uint32_t E23 = 0x4B000000u;
   const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-  float a0 = 0.f, a1 = 0.f;
+  float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
   if constexpr (BITS == 4) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint32_t lo = ws[i], hi = ws[i] >> 16;
-      const float4 xa = xq[(2 * i) * qstride];
-      const float4 xb = xq[(2 * i + 1) * qstride];
-      a0 = fmaf(__uint_as_float((lo & 0x000Fu) | E23) - M, xa.x, a0);
-      a1 = fmaf(__uint_as_float((lo & 0x00F0u) | E23) - M, xa.y, a1);
-      a0 = fmaf(__uint_as_float((lo & 0x0F00u) | E23) - M, xa.z, a0);
-      a1 = fmaf(__uint_as_float((lo & 0xF000u) | E23) - M, xa.w, a1);
-      a0 = fmaf(__uint_as_float((hi & 0x000Fu) | E23) - M, xb.x, a0);
-      a1 = fmaf(__uint_as_float((hi & 0x00F0u) | E23) - M, xb.y, a1);
-      a0 = fmaf(__uint_as_float((hi & 0x0F00u) | E23) - M, xb.z, a0);
-      a1 = fmaf(__uint_as_float((hi & 0xF000u) | E23) - M, xb.w, a1);
+      const float2 q01 = __fadd2_rn(make_float2(__uint_as_float((lo & 0x000Fu) | E23),
+                                                __uint_as_float((lo & 0x00F0u) | E23)), NM2);
+      const float2 q23 = __fadd2_rn(make_float2(__uint_as_float((lo & 0x0F00u) | E23),
+                                                __uint_as_float((lo & 0xF000u) | E23)), NM2);
+      const float2 q45 = __fadd2_rn(make_float2(__uint_as_float((hi & 0x000Fu) | E23),
+                                                __uint_as_float((hi & 0x00F0u) | E23)), NM2);
+      const float2 q67 = __fadd2_rn(make_float2(__uint_as_float((hi & 0x0F00u) | E23),
+                                                __uint_as_float((hi & 0xF000u) | E23)), NM2);
+      a = __ffma2_rn(q01, cx.v[4 * i + 0], a);
+      b = __ffma2_rn(q23, cx.v[4 * i + 1], b);
+      a = __ffma2_rn(q45, cx.v[4 * i + 2], a);
+      b = __ffma2_rn(q67, cx.v[4 * i + 3], b);
     }
   } else {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint32_t lo = ws[i], hi = ws[i] >> 16;
-      const float4 xa = xq[i * qstride];
-      a0 = fmaf(__uint_as_float((lo & 0x00FFu) | E23) - M, xa.x, a0);
-      a1 = fmaf(__uint_as_float((lo & 0xFF00u) | E23) - M, xa.y, a1);
-      a0 = fmaf(__uint_as_float((hi & 0x00FFu) | E23) - M, xa.z, a0);
-      a1 = fmaf(__uint_as_float((hi & 0xFF00u) | E23) - M, xa.w, a1);
+      const float2 q01 = __fadd2_rn(make_float2(__uint_as_float((lo & 0x00FFu) | E23),
+                                                __uint_as_float((lo & 0xFF00u) | E23)), NM2);
+      const float2 q23 = __fadd2_rn(make_float2(__uint_as_float((hi & 0x00FFu) | E23),
+                                                __uint_as_float((hi & 0xFF00u) | E23)), NM2);
+      a = __ffma2_rn(q01, cx.v[2 * i + 0], a);
+      b = __ffma2_rn(q23, cx.v[2 * i + 1], b);
     }
   }
-  return a0 + a1;
+  return (a.x + a.y) + (b.x + b.y);
 }
 
-// Stage `nr` activation rows (bf16, gathered through `row_of`) into shared memory
-// as pre-scaled fp32 in a [row][CPL/4][chunk] float4 layout, so that lanes reading
-// consecutive chunks hit consecutive banks; plus the plain fp32 sum of each chunk.
-// Rows are read as 128-bit vectors; the lanes holding one chunk's vectors are
-// adjacent, so a chunk's sum is a two- or four-lane shuffle reduction.
-template <int BITS, typename RowOf>
-__device__ __forceinline__ void stage_rows(float* __restrict__ smem, const uint16_t* __restrict__ src,
-                                           int K, int nr, int rows_cap, RowOf row_of) {
+// Re-lay `nr` bf16 rows (row r at src + r * K, in shared memory) as pre-scaled fp32 in a
+// [row][CPL/4][chunk] float4 layout -- lanes reading consecutive chunks hit consecutive
+// banks -- plus the fp32 sum of every chunk at cs[row * nchunk + chunk].
+template <int BITS>
+__device__ __forceinline__ void relayout_rows(float* __restrict__ xs, float* __restrict__ cs,
+                                              const uint16_t* __restrict__ src, int K, int nr) {
   constexpr int CPL = 128 / BITS;
   constexpr int Q = CPL / 4;
   constexpr int VPC = CPL / 8;             // 8-element vectors per chunk (4 or 2)
   const int nchunk = K / CPL;
   const int nvec = K / 8;
-  float4* xs = reinterpret_cast<float4*>(smem);
-  float* cs = smem + static_cast<size_t>(rows_cap) * K;
+  float4* x4 = reinterpret_cast<float4*>(xs);
   const int total = nr * nvec;
   for (int base = 0; base < total; base += blockDim.x) {
     const int idx = base + threadIdx.x;
@@ -77,7 +106,7 @@ __device__ __forceinline__ void stage_rows(float* __restrict__ smem, const uint1
     if (active) {
       rr = idx / nvec;
       v = idx - rr * nvec;
-      const uint4 raw = *reinterpret_cast<const uint4*>(src + row_of(rr) * static_cast<size_t>(K) + v * 8);
+      const uint4 raw = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(rr) * K + v * 8);
       const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
       float f[8];
 #pragma unroll
@@ -89,10 +118,10 @@ __device__ __forceinline__ void stage_rows(float* __restrict__ smem, const uint1
       for (int i = 0; i < 8; ++i) part += f[i];
       const int kk0 = v * 8;
       const int c = kk0 / CPL, q0 = (kk0 - c * CPL) >> 2;
-      xs[(static_cast<size_t>(rr) * Q + q0) * nchunk + c] =
+      x4[(static_cast<size_t>(rr) * Q + q0) * nchunk + c] =
           make_float4(f[0] * prescale<BITS>(kk0), f[1] * prescale<BITS>(kk0 + 1),
                       f[2] * prescale<BITS>(kk0 + 2), f[3] * prescale<BITS>(kk0 + 3));
-      xs[(static_cast<size_t>(rr) * Q + q0 + 1) * nchunk + c] =
+      x4[(static_cast<size_t>(rr) * Q + q0 + 1) * nchunk + c] =
           make_float4(f[4] * prescale<BITS>(kk0 + 4), f[5] * prescale<BITS>(kk0 + 5),
                       f[6] * prescale<BITS>(kk0 + 6), f[7] * prescale<BITS>(kk0 + 7));
     }
@@ -103,23 +132,33 @@ __device__ __forceinline__ void stage_rows(float* __restrict__ smem, const uint1
   }
 }
 
-struct ProjView {
-  const uint8_t* codes;     // row 0 of the projection
-  const uint16_t* scales;
-  const uint16_t* biases;
-  int64_t code_pitch;       // bytes per output row
-  int group_pitch;          // half entries per output row
+// Validate one segment's routing metadata; the slot to read, or -1 (R = 0 when the
+// metadata itself is inconsistent, so nothing is written for it).
+__device__ __forceinline__ int segment_slot(const RouteView& rv, int s, int& row0, int& R) {
+  const int e = rv.seg_expert[s];
+  row0 = rv.seg_start[s];
+  R = rv.seg_start[s + 1] - row0;
+  const bool ok = e >= 0 && e < rv.n_experts && row0 >= 0 && R > 0 && row0 + R <= rv.P;
+  if (!ok) {
+    R = 0;
+    row0 = 0;
+    return -1;
+  }
+  return rv.g2s ? rv.g2s[e] : e;
+}
+
+// Shared-memory carve helper: 128-byte aligned bump allocation.
+struct SmemCarve {
+  uint8_t* p;
+  __device__ explicit SmemCarve(uint8_t* base) : p(base) {}
+  template <typename T>
+  __device__ T* take(size_t bytes) {
+    T* r = reinterpret_cast<T*>(p);
+    p += (bytes + 127) / 128 * 128;
+    return r;
+  }
 };
 
-__device__ __forceinline__ ProjView proj_view(const uint8_t* base, const bigrig_expert_layout& L,
-                                              int proj, int K) {
-  ProjView v;
-  v.codes = base + L.weight_off[proj];
-  v.scales = reinterpret_cast<const uint16_t*>(base + L.scales_off[proj]);
-  v.biases = reinterpret_cast<const uint16_t*>(base + L.biases_off[proj]);
-  v.code_pitch = static_cast<int64_t>(K) * L.bits / 8;
-  v.group_pitch = K / L.group_size;
-  return v;
-}
+__host__ __device__ inline size_t round128(size_t n) { return (n + 127) / 128 * 128; }
 
 }  // namespace bigrig

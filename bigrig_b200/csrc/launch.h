@@ -48,6 +48,7 @@ struct RouteView {
   int32_t* err;              // [1] device error counter
   int P, k, s_max;
   int max_rows;              // largest number of rows one expert can receive (<= T)
+  int n_experts;             // valid expert ids are [0, n_experts)
 };
 
 // Outputs of the routing step (see bigrig_moe_permute).
@@ -66,6 +67,7 @@ int launch_route(const void* x, const void* gate_w, const float* gate_b, const v
                  int32_t* ticket, int32_t* idx_out, float* sc_out, const RouteOut& ro,
                  cudaStream_t s);
 size_t down_combine_smem(int P, const bigrig_expert_layout& L);
+size_t down_combine_smem(int P, const bigrig_expert_layout& L, int nf);
 int launch_down_combine(const void* h, const RouteView& rv, const void* slab,
                         const bigrig_expert_layout& L, const float* scores, const void* residual,
                         void* out, void* y_out, int T, cudaStream_t s);

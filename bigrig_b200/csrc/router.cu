@@ -84,7 +84,8 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
   int bad = 0;
   for (int i = tid; i < P; i += kPermThreads) {
     const int e = idx[i];
-    if (e < 0 || e >= E) { ++bad; continue; }
+    if (e < 0) continue;                 // padding row (expert-parallel dispatch), skipped
+    if (e >= E) { ++bad; continue; }
     atomicAdd(&cnt[e], 1);
   }
   if (bad && err) atomicAdd(err, bad);

@@ -71,15 +71,18 @@ __device__ __forceinline__ void topk_warp(Load load, int E, int k, int mode, int
 // Stable expert-sorted permutation of P <= 32 pairs by one warp.  Lane i holds pair i;
 // its sorted position is the number of pairs (e_j, j) lexicographically below (e_i, i).
 // Runs of equal experts become the segments; offsets[x] counts the pairs with expert < x.
-// Ids outside [0, E) sort last, are left out of the segments and counted in err.
+// Negative ids mark padding rows and ids >= E are errors (counted in err); both sort
+// last and are left out of the segments.
 __device__ __forceinline__ void permute_warp(const int32_t* idx, int P, int E, int32_t* order,
                                              int32_t* inv, int32_t* offsets, int32_t* seg_expert,
                                              int32_t* seg_start, int32_t* num_seg, int32_t* err) {
   const int lane = threadIdx.x & 31;
   int e = lane < P ? idx[lane] : 0x7fffffff;
-  const bool bad = lane < P && (e < 0 || e >= E);
-  if (bad) e = 0x7ffffffe;
+  const bool bad = lane < P && e >= E;
+  const bool pad = lane < P && e < 0;       // padding row (expert-parallel dispatch)
+  if (bad || pad) e = 0x7ffffffe;
   const unsigned nbad = __popc(__ballot_sync(0xffffffffu, bad));
+  const unsigned nskip = __popc(__ballot_sync(0xffffffffu, bad || pad));
   if (lane == 0 && nbad && err) atomicAdd(err, static_cast<int>(nbad));
   int rank = 0;
   for (int j = 0; j < 32; ++j) {
@@ -106,7 +109,7 @@ __device__ __forceinline__ void permute_warp(const int32_t* idx, int P, int E, i
   }
   if (lane == 0) {
     *num_seg = __popc(firsts);
-    seg_start[__popc(firsts)] = P - static_cast<int>(nbad);
+    seg_start[__popc(firsts)] = P - static_cast<int>(nskip);
   }
   for (int x0 = 0; x0 <= E; x0 += 32) {          // uniform trip count: every lane shuffles
     const int x = x0 + lane;

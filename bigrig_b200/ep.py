@@ -1,0 +1,131 @@
+"""Expert parallelism across the GPUs of one node: all-to-all token dispatch and combine.
+
+The reference runs on one Mac and has no distributed code; this is the B200
+design's way of sharding its hot path.  Experts split into contiguous blocks, rank r
+owning ``[r * E/G, (r + 1) * E/G)`` of every layer; tokens stay data-parallel (each
+rank routes its own tokens with the replicated router).  One MoE layer is then
+
+1. plan: each (token, k) pair goes to the rank owning its expert; pairs are grouped
+   by destination with a stable sort, so a rank's rows arrive in the sender's
+   (token, k) order;
+2. dispatch: ``all_to_all_single`` of the pair rows (bf16 [H]) and their local
+   expert ids;
+3. the owner computes its experts over the received rows (k = 1 per row);
+4. combine: the reverse ``all_to_all_single`` returns each pair's output to its
+   sender, which applies the router weights (``sum_k score * y``).
+
+Two exchange modes.  ``padded`` (decode): every peer block has a fixed capacity of
+T*k rows (the most one rank can send to one peer), padding rows carry expert id -1
+and are skipped by the kernels; no sizes cross to the host, so the step can be
+captured in a CUDA graph.  ``exact`` (prefill): counts are exchanged first
+(int32 [G]), then rows with those split sizes.
+
+Transport is NCCL over NVLink 5 / NVSwitch.  Nothing here issues TMA or multicast
+loads; peer memory is only touched by NCCL.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+class ExpertParallel:
+    """Dispatch/combine of one MoE layer's pairs across the ranks of ``group``."""
+
+    def __init__(self, n_experts: int, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if n_experts % self.world:
+            raise ValueError(f"{n_experts} experts do not split evenly over {self.world} ranks")
+        self.n_experts = n_experts
+        self.per_rank = n_experts // self.world
+
+    def local_range(self) -> tuple:
+        return self.rank * self.per_rank, (self.rank + 1) * self.per_rank
+
+    def plan(self, indices: torch.Tensor) -> dict:
+        """Destination of every pair, pairs grouped by destination (stable), counts."""
+        T, k = indices.shape
+        flat = indices.reshape(-1).long()
+        dest = torch.div(flat, self.per_rank, rounding_mode="floor")
+        order = torch.sort(dest, stable=True).indices
+        counts = torch.bincount(dest, minlength=self.world)
+        return {"T": T, "k": k, "order": order, "tok": torch.div(order, k, rounding_mode="floor"),
+                "local": (flat[order] - dest[order] * self.per_rank).to(torch.int32),
+                "dest": dest[order], "counts": counts}
+
+    # -------------------------------------------------------------- exchanges
+    def _a2a(self, out, inp, out_splits=None, in_splits=None):
+        if self.world == 1:
+            out.copy_(inp)
+            return out
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+        return out
+
+    def dispatch_combine(self, x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor,
+                         expert_fn, padded: bool = True, combine_fn=None) -> torch.Tensor:
+        """Combined output [T, H] of a layer whose experts are split over the group.
+
+        ``expert_fn(rows [R, H], local_ids [R] int32) -> [R, H]`` computes this rank's
+        experts (ids < 0 are padding: any output, never read).  ``combine_fn(y [T, k, H],
+        scores) -> [T, H]`` applies the router weights (default: fp32 weighted sum in k
+        order, stored in x's dtype)."""
+        p = self.plan(indices)
+        T, k = p["T"], p["k"]
+        H = x.shape[1]
+        G = self.world
+        P = T * k
+        rows = x.index_select(0, p["tok"])
+        if padded:
+            cap = P
+            # position of each sorted pair inside its destination's block
+            start = torch.cumsum(p["counts"], 0) - p["counts"]
+            within = torch.arange(P, device=x.device) - start[p["dest"]]
+            slot = p["dest"] * cap + within
+            send_x = torch.zeros(G * cap, H, dtype=x.dtype, device=x.device)
+            send_id = torch.full((G * cap,), -1, dtype=torch.int32, device=x.device)
+            send_x.index_copy_(0, slot, rows)
+            send_id.index_copy_(0, slot, p["local"])
+            recv_x = torch.empty_like(send_x)
+            recv_id = torch.empty_like(send_id)
+            self._a2a(recv_x, send_x)
+            self._a2a(recv_id, send_id)
+            y_recv = expert_fn(recv_x, recv_id)
+            back = torch.empty_like(y_recv)
+            self._a2a(back, y_recv)
+            y_sorted = back.index_select(0, slot)
+        else:
+            counts = p["counts"].to(torch.int64)
+            recv_counts = torch.empty_like(counts)
+            self._a2a(recv_counts, counts)
+            in_splits = counts.tolist()
+            out_splits = recv_counts.tolist()
+            recv_x = torch.empty(sum(out_splits), H, dtype=x.dtype, device=x.device)
+            recv_id = torch.empty(sum(out_splits), dtype=torch.int32, device=x.device)
+            self._a2a(recv_x, rows, out_splits, in_splits)
+            self._a2a(recv_id, p["local"], out_splits, in_splits)
+            y_recv = expert_fn(recv_x, recv_id)
+            y_sorted = torch.empty(P, H, dtype=y_recv.dtype, device=x.device)
+            self._a2a(y_sorted, y_recv, in_splits, out_splits)
+        y = torch.empty(P, H, dtype=y_sorted.dtype, device=x.device)
+        y.index_copy_(0, p["order"], y_sorted)
+        y = y.reshape(T, k, H)
+        if combine_fn is not None:
+            return combine_fn(y, scores)
+        acc = torch.zeros(T, H, dtype=torch.float32, device=x.device)
+        for j in range(k):
+            acc = acc + scores[:, j:j + 1].float() * y[:, j].float()
+        return acc.to(x.dtype)
+
+
+def local_expert_fn(slab, layout, n_local: int, g2s=None, workspace=None):
+    """``expert_fn`` over this rank's experts on the sm_100a kernels (one pair per row)."""
+    from . import ops
+
+    def fn(rows: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+        y = ops.switch_glu(rows.contiguous(), ids.reshape(-1, 1).contiguous(), slab, layout,
+                           n_local, g2s=g2s, workspace=workspace)
+        return y.reshape(rows.shape[0], rows.shape[1])
+
+    return fn

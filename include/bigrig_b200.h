@@ -104,8 +104,9 @@ BIGRIG_API int bigrig_router_topk(const void* logits, int logits_dtype, int T, i
  * order[P]: pair ids sorted by expert (stable); inv[P]: inverse permutation;
  * offsets[E+1]: counting-sort offsets per expert id; seg_expert[E] / seg_start[E+1]
  * / num_seg[1]: the non-empty experts in ascending id and where their run starts.
- * An expert id outside [0, E) returns BIGRIG_ERR_INVALID only when it is detected
- * on the host; on the device it is counted in err_count[1] (may be NULL). */
+ * A negative expert id marks a padding row (expert-parallel dispatch buffers): it is
+ * left out of the segments silently.  An id >= E is left out and counted in
+ * err_count[1] (may be NULL). */
 BIGRIG_API int bigrig_moe_permute(const int32_t* indices, int T, int k, int E, int32_t* order, int32_t* inv,
                        int32_t* offsets, int32_t* seg_expert, int32_t* seg_start, int32_t* num_seg,
                        int32_t* err_count, void* stream);
@@ -114,7 +115,8 @@ BIGRIG_API int bigrig_moe_permute(const int32_t* indices, int T, int k, int E, i
  * y[t, j] = down(silu(gate(x[t])) * up(x[t])) of expert indices[t, j], read from
  * slot g2s[indices[t, j]] of `slab` (g2s NULL: slot == expert id).  x is bf16
  * [T, H].  A slot id < 0 is counted in the workspace error word and its rows are
- * written as zeros (the host pool guarantees residency before the call). */
+ * written as zeros (the host pool guarantees residency before the call).  Pairs
+ * whose expert id is negative are padding: skipped, their y rows left untouched. */
 BIGRIG_API int bigrig_switch_glu(const void* x, const int32_t* indices, int T, int k, int n_experts,
                       const int32_t* g2s, const void* slab, const bigrig_expert_layout* layout,
                       void* y, void* workspace, size_t workspace_bytes, void* stream);
