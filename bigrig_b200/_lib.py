@@ -27,8 +27,9 @@ EXPORTS = (
     "bigrig_dequant", "bigrig_router_logits", "bigrig_router_topk", "bigrig_moe_permute",
     "bigrig_switch_glu", "bigrig_combine", "bigrig_moe_forward", "bigrig_workspace_errors",
     "bigrig_timing_enable", "bigrig_timing_read", "bigrig_launch_counts", "bigrig_kernel_name",
-    "bigrig_set_path", "bigrig_moe_layer",
+    "bigrig_set_path", "bigrig_moe_layer", "bigrig_switch_glu_noalloc",
 )
+NOALLOC_SCRATCH_BYTES = 4 << 20
 KERNELS = {"router_logits": 0, "router_topk": 1, "permute": 2, "gate_up": 3, "down": 4,
            "combine": 5, "dequant": 6, "gemm_gate_up": 7, "gemm_down": 8, "route": 9,
            "down_combine": 10}
@@ -77,6 +78,8 @@ _SIG = {
     "bigrig_set_path": (_I, [_I, _I]),
     "bigrig_moe_layer": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, ctypes.POINTER(ExpertLayout),
                               _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
+    "bigrig_switch_glu_noalloc": (_I, [_P, _P, _I, _I, _I, _P, _P, ctypes.POINTER(ExpertLayout),
+                                       _P, _P]),
 }
 
 

@@ -451,3 +451,66 @@ int bigrig_workspace_errors(void* workspace, int32_t* out, void* stream) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ no-allocation entry point
+// For callers that cannot allocate device memory at call time (see the header): the
+// scratch of bigrig_switch_glu_noalloc lives in a file-scope device array that every
+// GPU loading this library holds until the process exits.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[BIGRIG_NOALLOC_SCRATCH_BYTES];
+
+namespace bigrig {
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// The device address of the scratch array on the current device, resolved once per
+// device (cudaGetSymbolAddress with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return set_error(BIGRIG_ERR_CUDA, "switch_glu_noalloc: no usable current device (%d)", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(BIGRIG_ERR_CUDA, "switch_glu_noalloc: cudaGetSymbolAddress failed: %s",
+                       cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return BIGRIG_OK;
+}
+}  // namespace
+}  // namespace bigrig
+
+extern "C" int bigrig_switch_glu_noalloc(const void* x, const int32_t* indices, int T, int k,
+                                         int n_experts, const int32_t* g2s, const void* slab,
+                                         const bigrig_expert_layout* layout, void* y,
+                                         void* stream) {
+  if (int rc = check_layout(layout)) return rc;
+  if (int rc = check_route(T, k, n_experts)) return rc;
+  if (T == 0) return BIGRIG_OK;
+  if (!x || !indices || !slab || !y)
+    return set_error(BIGRIG_ERR_INVALID, "switch_glu_noalloc: NULL pointer");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(slab) % 16)
+    return set_error(BIGRIG_ERR_INVALID, "switch_glu_noalloc: x and slab must be 16-byte aligned");
+  const size_t need = carve(nullptr, T, k, n_experts, *layout, nullptr);
+  if (need > BIGRIG_NOALLOC_SCRATCH_BYTES)
+    return set_error(BIGRIG_ERR_WORKSPACE,
+                     "switch_glu_noalloc: this call needs %zu bytes of scratch but the static "
+                     "array holds %zu; use bigrig_switch_glu with a workspace for calls this large",
+                     need, static_cast<size_t>(BIGRIG_NOALLOC_SCRATCH_BYTES));
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the error words at the head of the scratch must start at zero; everything else is
+  // written before it is read
+  if (cudaMemsetAsync(scratch, 0, 4 * sizeof(int32_t), s) != cudaSuccess)
+    return set_error(BIGRIG_ERR_CUDA, "switch_glu_noalloc: %s", cudaGetErrorString(cudaGetLastError()));
+  Workspace ws;
+  carve(scratch, T, k, n_experts, *layout, &ws);
+  return run_switch_glu(x, indices, T, k, n_experts, g2s, slab, *layout, y, ws, s);
+}
+

@@ -272,3 +272,27 @@ def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, gate_b: torch.Tensor | None
         _vp(g2s), _vp(slab), ctypes.byref(c_layout(layout)), _vp(residual), _vp(out),
         _vp(indices), _vp(scores), _vp(buf), buf.numel(), _stream(x)), "moe_layer")
     return out, indices, scores
+
+
+def switch_glu_noalloc(x: torch.Tensor, indices: torch.Tensor, slab: torch.Tensor, layout: Layout,
+                       n_experts: int, g2s: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """switch_glu for callers that cannot allocate device memory when they call.
+
+    The library keeps this call's scratch in a fixed 4 MiB device array (per GPU, for the
+    life of the process) instead of a workspace; ``out`` must be preallocated for the call
+    itself to allocate nothing.  Calls needing more scratch raise ValueError.  Concurrent
+    calls on different streams share that array and must be serialised by the caller.
+    """
+    _require_cuda("x", x, torch.bfloat16)
+    _require_cuda("indices", indices, torch.int32)
+    _require_cuda("slab", slab, torch.uint8)
+    if g2s is not None:
+        _require_cuda("g2s", g2s, torch.int32)
+    T, k = indices.shape
+    if out is None:
+        out = torch.empty(T, k, layout.hidden, dtype=torch.bfloat16, device=x.device)
+    _lib.check(_lib.load().bigrig_switch_glu_noalloc(
+        _vp(x), _vp(indices), T, k, n_experts, _vp(g2s), _vp(slab), ctypes.byref(c_layout(layout)),
+        _vp(out), _stream(x)), "switch_glu_noalloc")
+    return out

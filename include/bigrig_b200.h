@@ -188,6 +188,24 @@ BIGRIG_API int bigrig_moe_layer(const void* x, const void* gate_w, const float* 
  * with a synchronous read on `stream`; resets it to 0.  For tests and debugging. */
 BIGRIG_API int bigrig_workspace_errors(void* workspace, int32_t* out, void* stream);
 
+/* bigrig_switch_glu for callers that cannot allocate device memory when they call: a
+ * process whose device memory is carved up once at start-up by another allocator, or a
+ * caller in a latency-critical loop where cudaMalloc (which synchronises the device) is
+ * not allowed.  No counterpart in the reference (MLX allocates inside every call).
+ * Same arguments and result as bigrig_switch_glu minus the workspace: the scratch is a
+ * file-scope device array of BIGRIG_NOALLOC_SCRATCH_BYTES (4 MiB) that every GPU that
+ * loads the library holds until the process exits.  Calls needing more scratch than that
+ * (bigrig_moe_workspace_bytes) return BIGRIG_ERR_WORKSPACE.  The first call on a device
+ * resolves the array's address with cudaGetSymbolAddress; make it before any stream
+ * capture.  Every call shares the one array, so calls that overlap on the GPU (different
+ * streams, or different host threads) race: serialise them.  The call itself allocates
+ * nothing (no cudaMalloc/cudaFree, no library allocator). */
+#define BIGRIG_NOALLOC_SCRATCH_BYTES (4u << 20)
+BIGRIG_API int bigrig_switch_glu_noalloc(const void* x, const int32_t* indices, int T, int k,
+                                         int n_experts, const int32_t* g2s, const void* slab,
+                                         const bigrig_expert_layout* layout, void* y,
+                                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif
