@@ -294,13 +294,15 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const float* __re
 }
 
 // ------------------------------------------------------------------ launchers
-constexpr size_t kGemvSmemBudget = 200 * 1024;
+constexpr size_t kGemvSmemBudget = 220 * 1024;
 
-// Features per CTA and rows per pass: the most features (16, else 8) and rows (<= 4,
-// <= the rows one expert can get) whose staging fits the shared-memory budget.
+// Features per CTA and rows per pass: the most features (16, 8, else 4) and rows (<= 4,
+// <= the rows one expert can get) whose staging fits the shared-memory budget.  A tile's
+// scale/bias block (features x groups x 2 bytes) must be a multiple of 16 bytes.
 template <typename SmemFn>
-static bool pick_tile(SmemFn fn, int max_rows, int* nf, int* rows) {
-  for (int f : {16, 8}) {
+static bool pick_tile(SmemFn fn, int max_rows, int groups, int* nf, int* rows) {
+  for (int f : {16, 8, 4}) {
+    if ((f * groups) % 8) continue;
     for (int r = max_rows < kGemvRows ? max_rows : kGemvRows; r >= 1; --r) {
       if (fn(f, r) <= kGemvSmemBudget) {
         *nf = f;
@@ -339,7 +341,8 @@ template <int BITS, int SDT>
 static int gate_up_impl(const void* x, const RouteView& rv, const void* slab,
                         const bigrig_expert_layout& L, void* h, cudaStream_t s) {
   int nf = 0, rows = 0;
-  if (!pick_tile([&](int f, int r) { return gemv_gate_up_smem(L, f, r); }, rv.max_rows, &nf, &rows))
+  if (!pick_tile([&](int f, int r) { return gemv_gate_up_smem(L, f, r); }, rv.max_rows,
+                 L.hidden / L.group_size, &nf, &rows))
     return set_error(BIGRIG_ERR_UNSUPPORTED, "gemv gate_up: hidden=%d does not fit shared memory",
                      L.hidden);
   const size_t smem = gemv_gate_up_smem(L, nf, rows);
@@ -353,9 +356,14 @@ static int gate_up_impl(const void* x, const RouteView& rv, const void* slab,
     if (rows == 2) BIGRIG_GU(4, 2);
     BIGRIG_GU(4, 4);
   }
-  if (rows == 1) BIGRIG_GU(2, 1);
-  if (rows == 2) BIGRIG_GU(2, 2);
-  BIGRIG_GU(2, 4);
+  if (nf == 8) {
+    if (rows == 1) BIGRIG_GU(2, 1);
+    if (rows == 2) BIGRIG_GU(2, 2);
+    BIGRIG_GU(2, 4);
+  }
+  if (rows == 1) BIGRIG_GU(1, 1);
+  if (rows == 2) BIGRIG_GU(1, 2);
+  BIGRIG_GU(1, 4);
 #undef BIGRIG_GU
 }
 
@@ -363,7 +371,8 @@ template <int BITS, int SDT>
 static int down_impl(const void* h, const RouteView& rv, const void* slab,
                      const bigrig_expert_layout& L, void* y, cudaStream_t s) {
   int nf = 0, rows = 0;
-  if (!pick_tile([&](int f, int r) { return gemv_down_smem(L, f, r); }, rv.max_rows, &nf, &rows))
+  if (!pick_tile([&](int f, int r) { return gemv_down_smem(L, f, r); }, rv.max_rows,
+                 L.inter / L.group_size, &nf, &rows))
     return set_error(BIGRIG_ERR_UNSUPPORTED, "gemv down: inter=%d does not fit shared memory",
                      L.inter);
   const size_t smem = gemv_down_smem(L, nf, rows);
@@ -377,9 +386,14 @@ static int down_impl(const void* h, const RouteView& rv, const void* slab,
     if (rows == 2) BIGRIG_DN(4, 2);
     BIGRIG_DN(4, 4);
   }
-  if (rows == 1) BIGRIG_DN(2, 1);
-  if (rows == 2) BIGRIG_DN(2, 2);
-  BIGRIG_DN(2, 4);
+  if (nf == 8) {
+    if (rows == 1) BIGRIG_DN(2, 1);
+    if (rows == 2) BIGRIG_DN(2, 2);
+    BIGRIG_DN(2, 4);
+  }
+  if (rows == 1) BIGRIG_DN(1, 1);
+  if (rows == 2) BIGRIG_DN(1, 2);
+  BIGRIG_DN(1, 4);
 #undef BIGRIG_DN
 }
 

@@ -101,7 +101,7 @@ def test_full_size_layer(cuda, name, T, path):
         y = ops.switch_glu(x, idx, slab, L, E)
         ref = _reference(slab, L, x, idx, bf16_weights=(path == "gemm"))
         assert_close(y.float().cpu().numpy(), ref.cpu().numpy(),
-                     long_reduction=max(H, I) >= 4096 or (path == "gemm" and T >= 512))
+                     long_reduction=path == "gemm" or max(H, I) >= 4096)
         if path == "gemv":
             # batch invariance: each token alone gives the same bits
             for t in sorted({0, T // 2, T - 1}):
