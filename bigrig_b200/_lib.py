@@ -32,8 +32,8 @@ EXPORTS = (
 NOALLOC_SCRATCH_BYTES = 4 << 20
 KERNELS = {"router_logits": 0, "router_topk": 1, "permute": 2, "gate_up": 3, "down": 4,
            "combine": 5, "dequant": 6, "gemm_gate_up": 7, "gemm_down": 8, "route": 9,
-           "down_combine": 10}
-PATHS = {"auto": 0, "gemv": 1, "gemm": 2}
+           "down_combine": 10, "decode_layer": 11}
+PATHS = {"auto": 0, "gemv": 1, "gemm": 2, "chain": 3}
 
 
 class ExpertLayout(ctypes.Structure):
@@ -159,8 +159,10 @@ def timing_read(kernel: str) -> tuple:
 
 def set_path(mode: str = "auto", gemm_min_rows: int = 8) -> str:
     """Choose the expert kernels: "auto" (GEMV for decode-sized calls, the tcgen05 grouped
-    GEMM once the mean rows per routed expert reaches ``gemm_min_rows``), "gemv" or
-    "gemm".  Returns the previous mode."""
+    GEMM once the mean rows per routed expert reaches ``gemm_min_rows``, one-token
+    ``moe_layer`` calls as one persistent kernel), "gemv" or "gemm" (force one expert
+    path), or "chain" ("auto" with one-token layers on the three-kernel chain).  Returns
+    the previous mode."""
     rc = load().bigrig_set_path(PATHS[mode], int(gemm_min_rows))
     if rc < 0:
         check(rc, "set_path")

@@ -57,7 +57,7 @@ const char* kKernelNames[BIGRIG_K_COUNT] = {
     "router_logits_kernel", "router_topk_kernel", "permute_kernel",
     "gemv_gate_up_kernel",  "gemv_down_kernel",   "combine_kernel",
     "dequant_kernel",       "grouped_gemm_kernel<gate_up>", "grouped_gemm_kernel<down>",
-    "route_kernel",         "down_combine_kernel"};
+    "route_kernel",         "down_combine_kernel", "decode_layer_kernel"};
 std::atomic<int> g_path{BIGRIG_PATH_AUTO};
 std::atomic<int> g_gemm_min_rows{8};
 }  // namespace
@@ -103,6 +103,8 @@ struct Workspace {
   float* scores;      // [P]
   float* logits;      // [T, E] (fused decode route)
   int32_t* ticket;    // last-CTA counter of the fused route, zero between calls (err[3])
+  uint32_t* sync;     // router count, barrier count, generation of the persistent decode
+                      // kernel (err[4..6]); the counts are zero between calls
 };
 
 size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Workspace* w) {
@@ -114,7 +116,7 @@ size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Wor
     return p;
   };
   Workspace ws;
-  ws.err = static_cast<int32_t*>(take(4 * sizeof(int32_t)));
+  ws.err = static_cast<int32_t*>(take(8 * sizeof(int32_t)));
   ws.order = static_cast<int32_t*>(take(P * sizeof(int32_t)));
   ws.inv = static_cast<int32_t*>(take(P * sizeof(int32_t)));
   ws.offsets = static_cast<int32_t*>(take((E + 1) * sizeof(int32_t)));
@@ -129,6 +131,7 @@ size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Wor
   // the fused route's ticket lives at a fixed place -- word 3 of the error words -- so a
   // call of any shape finds it where the previous call left it, back at zero
   ws.ticket = ws.err ? ws.err + 3 : nullptr;
+  ws.sync = ws.err ? reinterpret_cast<uint32_t*>(ws.err + 4) : nullptr;
   if (w) *w = ws;
   return off;
 }
@@ -194,7 +197,8 @@ RouteView route_view(const Workspace& ws, const int32_t* g2s, int T, int k, int 
 
 // Decode-sized calls take the fused three-kernel chain.
 bool fused_decode(int T, int k, const bigrig_expert_layout& L) {
-  return g_path.load() != BIGRIG_PATH_GEMM && T * k <= 32 &&
+  const int path = g_path.load();
+  return path != BIGRIG_PATH_GEMM && T * k <= 32 &&
          down_combine_smem(T * k, L) <= 200 * 1024;
 }
 
@@ -221,7 +225,7 @@ int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, c
   const RouteView rv = route_view(ws, g2s, T, k, E);
   const int path = g_path.load();
   const bool gemm = path == BIGRIG_PATH_GEMM ||
-                    (path == BIGRIG_PATH_AUTO && P >= g_gemm_min_rows.load() * (P < E ? P : E));
+                    ((path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_CHAIN) && P >= g_gemm_min_rows.load() * (P < E ? P : E));
   if (gemm) {
     const int bn = gemm_token_tile(T, k, E);
     if (int rc = launch_gemm_gate_up(x, rv, slab, L, ws.h, bn, s)) return rc;
@@ -379,6 +383,11 @@ int bigrig_moe_layer(const void* x, const void* gate_w, const float* gate_b, int
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   int32_t* idx = indices_out ? indices_out : ws.indices;
   float* sc = scores_out ? scores_out : ws.scores;
+  const int path = g_path.load();
+  if (T == 1 && (path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_GEMV) &&
+      decode_layer_fits(*layout, k, E))
+    return launch_decode_layer(x, gate_w, gate_b, E, k, mode, norm_topk, g2s, slab, *layout,
+                               residual, out, idx, sc, ws.h, ws.logits, ws.sync, ws.err, s);
   if (fused_decode(T, k, *layout))
     return run_fused(x, gate_w, gate_b, nullptr, BIGRIG_F32, T, k, E, mode, norm_topk, g2s, slab,
                      *layout, residual, out, idx, sc, ws, s);
@@ -390,7 +399,7 @@ int bigrig_moe_layer(const void* x, const void* gate_w, const float* gate_b, int
 }
 
 int bigrig_set_path(int mode, int gemm_min_rows) {
-  if (mode < BIGRIG_PATH_AUTO || mode > BIGRIG_PATH_GEMM || gemm_min_rows < 1)
+  if (mode < BIGRIG_PATH_AUTO || mode > BIGRIG_PATH_CHAIN || gemm_min_rows < 1)
     return set_error(BIGRIG_ERR_INVALID, "set_path: mode=%d gemm_min_rows=%d", mode, gemm_min_rows);
   const int prev = g_path.exchange(mode);
   g_gemm_min_rows.store(gemm_min_rows);

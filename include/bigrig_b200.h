@@ -145,16 +145,21 @@ BIGRIG_API int bigrig_moe_forward(const void* x, const void* logits, int logits_
 #define BIGRIG_K_GEMM_DOWN 8
 #define BIGRIG_K_ROUTE 9
 #define BIGRIG_K_DOWN_COMBINE 10
-#define BIGRIG_K_COUNT 11
+#define BIGRIG_K_DECODE_LAYER 11
+#define BIGRIG_K_COUNT 12
 
-/* Which expert kernels bigrig_switch_glu / bigrig_moe_forward use:
+/* Which expert kernels bigrig_switch_glu / bigrig_moe_forward / bigrig_moe_layer use:
  * BIGRIG_PATH_AUTO picks the grouped GEMV when an expert gets few rows (decode)
  * and the tcgen05 grouped GEMM when the mean rows per routed expert reaches
- * `gemm_min_rows`; the other two force one path.  Process-wide; returns the
- * previous mode. */
+ * `gemm_min_rows`, and runs a one-token bigrig_moe_layer as one persistent kernel;
+ * BIGRIG_PATH_GEMV and BIGRIG_PATH_GEMM force one expert path; BIGRIG_PATH_CHAIN is
+ * AUTO with one-token layers on the three-kernel chain instead of the persistent
+ * kernel (the two give bit-identical results).  Process-wide; returns the previous
+ * mode. */
 #define BIGRIG_PATH_AUTO 0
 #define BIGRIG_PATH_GEMV 1
 #define BIGRIG_PATH_GEMM 2
+#define BIGRIG_PATH_CHAIN 3
 BIGRIG_API int bigrig_set_path(int mode, int gemm_min_rows);
 
 /* CUDA-event timing of this library's kernel launches, off by default.  `mask`
@@ -173,8 +178,12 @@ BIGRIG_API const char* bigrig_kernel_name(int kernel_id);
 /* The whole MoE block of one decoder layer from its hidden states:
  * logits = x . gate_w^T (+ gate_b), top-k + softmax (mode, norm_topk), the SwiGLU
  * experts and out[T, H] = residual + sum_j score * y (residual may be NULL).
- * x, gate_w, residual, out bf16; gate_b fp32 [E] or NULL.  Decode-sized calls
- * (T * k <= 32) run as three kernels chained by programmatic dependent launch.
+ * x, gate_w, residual, out bf16; gate_b fp32 [E] or NULL.  A one-token call runs as
+ * ONE cooperative kernel, a CTA per SM (router, top-k, gate/up, down and combine
+ * separated by a flag and one grid barrier whose words live in the workspace); other
+ * decode-sized calls (T * k <= 32), and one-token layers too wide for that kernel,
+ * run as three kernels chained by programmatic dependent launch.  The workspace must
+ * start zero-filled and calls sharing one workspace must not overlap on the GPU.
  * Replaces the mlx_lm MoE block around StreamingSwitchGLU (stream.py:1377,
  * 1523-1525; router rule adapter.py:74-92). */
 BIGRIG_API int bigrig_moe_layer(const void* x, const void* gate_w, const float* gate_b, int T,
