@@ -88,9 +88,11 @@ __device__ __forceinline__ float chunk_dot2(const uint4 w, const ChunkX<BITS>& c
 // Re-lay `nr` bf16 rows (row r at src + r * K, in shared memory) as pre-scaled fp32 in a
 // [row][CPL/4][chunk] float4 layout -- lanes reading consecutive chunks hit consecutive
 // banks -- plus the fp32 sum of every chunk at cs[row * nchunk + chunk].
+// Threads tid < nthreads (whole warps) take part.
 template <int BITS>
 __device__ __forceinline__ void relayout_rows(float* __restrict__ xs, float* __restrict__ cs,
-                                              const uint16_t* __restrict__ src, int K, int nr) {
+                                              const uint16_t* __restrict__ src, int K, int nr,
+                                              int tid, int nthreads) {
   constexpr int CPL = 128 / BITS;
   constexpr int Q = CPL / 4;
   constexpr int VPC = CPL / 8;             // 8-element vectors per chunk (4 or 2)
@@ -98,8 +100,8 @@ __device__ __forceinline__ void relayout_rows(float* __restrict__ xs, float* __r
   const int nvec = K / 8;
   float4* x4 = reinterpret_cast<float4*>(xs);
   const int total = nr * nvec;
-  for (int base = 0; base < total; base += blockDim.x) {
-    const int idx = base + threadIdx.x;
+  for (int base = 0; base < total; base += nthreads) {
+    const int idx = base + tid;
     const bool active = idx < total;
     float part = 0.f;
     int rr = 0, v = 0;
@@ -130,6 +132,12 @@ __device__ __forceinline__ void relayout_rows(float* __restrict__ xs, float* __r
     for (int o = 1; o < VPC; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
     if (active && (v % VPC) == 0) cs[rr * nchunk + v / VPC] = part;
   }
+}
+
+template <int BITS>
+__device__ __forceinline__ void relayout_rows(float* __restrict__ xs, float* __restrict__ cs,
+                                              const uint16_t* __restrict__ src, int K, int nr) {
+  relayout_rows<BITS>(xs, cs, src, K, nr, threadIdx.x, blockDim.x);
 }
 
 // Validate one segment's routing metadata; the slot to read, or -1 (R = 0 when the

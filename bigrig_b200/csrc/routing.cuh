@@ -68,6 +68,68 @@ __device__ __forceinline__ void topk_warp(Load load, int E, int k, int mode, int
   }
 }
 
+// topk_warp's result for one token whose E logits sit in shared memory, without its k
+// dependent arg-max rounds: every candidate's rank in the (logit descending, expert id
+// ascending) order is counted directly against all E logits, the k best are scattered to
+// their ranks, and the scores come from the same formulas and reductions as topk_warp, so
+// indices and scores are bit-identical to it.  NaN logits are never selected (as in
+// topk_warp); a rank no finite logit fills keeps idx -1.  `rank_lg` is 32 floats of
+// shared scratch.
+template <int PER_LANE>
+__device__ __forceinline__ void topk_rank_warp(const float* lg, int E, int k, int mode,
+                                               int norm_topk, int32_t* idx, float* sc,
+                                               float* rank_lg) {
+  const int lane = threadIdx.x & 31;
+  if (lane < k) idx[lane] = -1;
+  float v[PER_LANE];
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = e < E ? lg[e] : -INFINITY;
+  }
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) mx = fmaxf(mx, v[i]);
+  mx = warp_max(mx);
+  float denom = 0.f;
+  if (mode == BIGRIG_SOFTMAX_TOPK) {
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i)
+      if (i * 32 + lane < E) denom += expf(v[i] - mx);
+    denom = warp_sum(denom);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) {
+    const int e = i * 32 + lane;
+    if (e < E && v[i] == v[i]) {
+      int r = 0;
+      for (int u = 0; u < E; ++u) {
+        const float w = lg[u];
+        r += (w > v[i]) || (w == v[i] && u < e);
+      }
+      if (r < k) {
+        idx[r] = e;
+        rank_lg[r] = v[i];
+      }
+    }
+  }
+  __syncwarp();
+  const int my_idx = lane < k ? idx[lane] : -1;
+  const float my_logit = (lane < k && my_idx >= 0) ? rank_lg[lane] : -INFINITY;
+  const float first_logit = idx[0] >= 0 ? rank_lg[0] : -INFINITY;
+  float s = 0.f;
+  if (mode == BIGRIG_SOFTMAX_TOPK) {
+    s = (lane < k) ? expf(my_logit - mx) / denom : 0.f;
+    if (norm_topk) s = s / warp_sum(s);
+  } else {
+    const float ex = (lane < k) ? expf(my_logit - first_logit) : 0.f;
+    s = ex / warp_sum(ex);
+  }
+  if (lane < k) sc[lane] = s;
+  __syncwarp();
+}
+
 // Stable expert-sorted permutation of P <= 32 pairs by one warp.  Lane i holds pair i;
 // its sorted position is the number of pairs (e_j, j) lexicographically below (e_i, i).
 // Runs of equal experts become the segments; offsets[x] counts the pairs with expert < x.
