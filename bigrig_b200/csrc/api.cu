@@ -103,8 +103,8 @@ struct Workspace {
   float* scores;      // [P]
   float* logits;      // [T, E] (fused decode route)
   int32_t* ticket;    // last-CTA counter of the fused route, zero between calls (err[3])
-  uint32_t* sync;     // barrier count, barrier generation, launch epoch of the persistent
-                      // decode kernel (err[5..7]); the count is zero between calls
+  uint64_t* arrivals; // grid-barrier arrivals of the persistent decode kernel over all its
+                      // launches on this workspace (err[4..5]); its launch index is this / G
   uint64_t* tagged;   // [E] the persistent decode kernel's logits, tagged with the epoch
 };
 
@@ -133,7 +133,7 @@ size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Wor
   // the fused route's ticket lives at a fixed place -- word 3 of the error words -- so a
   // call of any shape finds it where the previous call left it, back at zero
   ws.ticket = ws.err ? ws.err + 3 : nullptr;
-  ws.sync = ws.err ? reinterpret_cast<uint32_t*>(ws.err + 5) : nullptr;
+  ws.arrivals = ws.err ? reinterpret_cast<uint64_t*>(ws.err + 4) : nullptr;
   if (w) *w = ws;
   return off;
 }
@@ -389,7 +389,7 @@ int bigrig_moe_layer(const void* x, const void* gate_w, const float* gate_b, int
   if (T == 1 && (path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_GEMV) &&
       decode_layer_fits(*layout, k, E))
     return launch_decode_layer(x, gate_w, gate_b, E, k, mode, norm_topk, g2s, slab, *layout,
-                               residual, out, idx, sc, ws.h, ws.tagged, ws.sync, ws.err, s);
+                               residual, out, idx, sc, ws.h, ws.tagged, ws.arrivals, ws.err, s);
   if (fused_decode(T, k, *layout))
     return run_fused(x, gate_w, gate_b, nullptr, BIGRIG_F32, T, k, E, mode, norm_topk, g2s, slab,
                      *layout, residual, out, idx, sc, ws, s);

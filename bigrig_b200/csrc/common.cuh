@@ -117,6 +117,29 @@ __device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, int32_t
   return false;
 }
 
+// L2 eviction policies for bulk copies: weights read once per token stream through L2
+// (evict first), small tables every step reads stay (evict last).
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// bulk_g2s with an L2 cache policy from l2_evict_first / l2_evict_last
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], "
+      "%2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
 // bytes and both addresses must be multiples of 16
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -4,29 +4,37 @@
 // (decode.cu, gemv.cu), and with it the mlx_lm block's router, the per-expert
 // quantized_matmul calls of _forward_views_one (bigrig_engine/stream.py:1278-1318) and
 // the caller's weighted sum (stream.py:1523-1525).  An OLMoE decode layer moves ~28 MB,
-// ~4 us of HBM time; as a chain of kernels every step also paid launches and dependent
-// global round trips.  Here one CTA per SM runs the whole layer with CW consumer warps
-// and one producer warp:
+// ~4 us of HBM time.  One CTA per SM runs the whole layer with 16 consumer warps and
+// one producer warp:
 //
 //   logits   CTA c < ceil(E/4) computes the logits of experts 4c..4c+3 (one warp each,
 //            router rows bulk-copied as the kernel starts) and publishes each as a
 //            64-bit (value, tag) word, the tag naming this launch -- no fence, no counter
 //   routing  the producer warp of every CTA polls the E tagged words, ranks them
-//            (topk_rank_warp: the same indices and scores as the chain's top-k) and
-//            reads the slots from a copy of g2s staged at start
-//   gate/up  items of (routed expert, 8 features), dealt round-robin to CTAs; the
-//            producer streams a CTA's items through a ring of bulk copies with full /
-//            empty mbarriers; consumer warp w computes feature w % 8 of every item of
-//            its group with x held in registers, no block-wide barrier per item; h rows
-//            go to global
+//            (topk_rank_warp: the chain's indices and scores bit for bit) and reads the
+//            slots from a copy of g2s staged at start
+//   gate/up  items of (routed expert, 8 features), dealt round-robin to CTAs and
+//            streamed by the producer through a ring of bulk copies with full / empty
+//            mbarriers.  A pair of consumer warps takes an item, each warp half of the
+//            hidden dimension, on the tensor cores: warp-level bf16 MMAs (m16n8k16)
+//            whose 16 rows are the item's 8 gate and 8 up rows, A converted in
+//            registers from the codes to exact bf16 integers q, B the token.
 //   barrier  grid-wide, consumer threads only (the producer is already streaming the
 //            down-projection weights into the ring)
-//   down     items of (8 hidden features, a group of routed experts); a warp per expert
-//            of an item; then the combine in rank order plus the residual
+//   down     items of (16 hidden features, a group of routed experts), a pair of warps
+//            per expert of an item (each half of the intermediate dimension), the same
+//            MMAs with h as B; then the combine in rank order plus the residual
 //
-// Per-feature arithmetic is the chain's (same chunk order per lane, same fp32x2 dot,
-// same group affine, same warp sums, same combine), so the output is bit-identical to
-// it.  Every wait -- mbarriers, tagged logits, the grid barrier -- is bounded; a timeout
+// Group affine.  w = s q + b per group of 64 inputs, so sum_k w_k x_k = s sum(q x) +
+// b sum(x) per group.  The MMA's 8 output columns keep 8 groups apart: B's column c
+// holds the token's values for the group whose window position is c and zeros
+// elsewhere, so column c of the accumulator is that group's sum(q x); every 8 groups
+// the accumulator is scaled by s in fp32, b sum(x) is added and the columns restart.
+// Products q x are exact, sums fp32: the precision of the fp32 GEMV in a different
+// summation order.  Rounding points are the chain's: gate/up fp32, h bf16, each
+// expert's y bf16, the combine fp32 in rank order.
+//
+// Every wait -- mbarriers, tagged logits, the grid barrier -- is bounded; a timeout
 // counts in the error words and the kernel carries on to its end.
 #include "gemv_common.cuh"
 #include "routing.cuh"
@@ -39,9 +47,13 @@
 
 namespace bigrig {
 
-constexpr int kDlFeat = 8;               // features of a gate/up item and of a down tile
+constexpr int kDlFeat = 8;               // features of a gate/up item (x2: its gate and up rows)
+constexpr int kDlFeatDown = 16;          // hidden features of a down tile (the MMA's 16 rows)
 constexpr int kDlRouterPerCta = 4;       // experts whose logits one CTA computes
 constexpr int kDlMaxStages = 12;
+constexpr int kDlCW = 16;                // consumer warps
+constexpr int kDlPairs = kDlCW / 2;
+constexpr int kDlGroup = 64;             // quantisation group size the kernel is built for
 constexpr uint32_t kDlSpinLimit = 1u << 22;
 
 struct DecodeLayerArgs {
@@ -57,15 +69,15 @@ struct DecodeLayerArgs {
   float* sc_out;              // [k]
   uint16_t* h;                // [k, I] scratch, rank-ordered rows
   unsigned long long* tagged; // [E] logit bits | tag << 32
-  uint32_t* sync;             // [3]: barrier count, barrier generation, launch epoch
+  unsigned long long* arrivals;  // grid-barrier arrivals over all launches
   int32_t* err;
   int E, k, mode, norm;
   int stage_bytes, nstages, seg_per_item, max_tiles;
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -100,41 +112,216 @@ __device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity, int32
   return false;
 }
 
-template <int BITS, int SDT, int NCH, int CW>
-__global__ void __launch_bounds__((CW + 1) * 32, 1) decode_layer_kernel(DecodeLayerArgs a) {
-  constexpr int CPL = 128 / BITS;
-  constexpr int Q = CPL / 4;
+// ------------------------------------------------------------------ MMA building blocks
+// D[16x8] += A[16x16] B[16x8], bf16 inputs, fp32 accumulators.  Lane (g = lane/4,
+// t = lane%4) holds A rows g and g+8 at k-slots {2t, 2t+1} (a0 / a1) and {2t+8, 2t+9}
+// (a2 / a3), B column g at k-slots {2t, 2t+1} (b0) and {2t+8, 2t+9} (b1), and D rows g
+// and g+8 at columns {2t, 2t+1}.  The lower half of a register is the lower k-slot.
+__device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Two 4-bit fields -- bits 0-3 and 16-19 of v -- as an exact bf16x2 pair: OR-ed into the
+// mantissa of 128.0 they read 128 + q, and subtracting 128 leaves q.
+__device__ __forceinline__ uint32_t nibble_pair(uint32_t v) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x43004300, 0xEA;" : "=r"(r) : "r"(v));
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(r), "r"(0x43004300u));
+  return r;
+}
+
+// Code layout of a k-block (the K a lane's 16-byte chunk of a row covers, times 4 lanes):
+//   4-bit: 128 K (2 groups), 8 k-steps; lane t owns words 4t..4t+3 = K [32t, 32t+32);
+//          k-step s uses word s/2: slots {2t,2t+1} <- codes (j, j+4), {2t+8,2t+9} <-
+//          codes (j+1, j+5) of the word, j = 2 (s%2)
+//   8-bit: 64 K (1 group), 4 k-steps; lane t owns K [16t, 16t+16); k-step s uses word s:
+//          slots {2t,2t+1} <- codes (0, 2), {2t+8,2t+9} <- codes (1, 3), low nibbles in
+//          one MMA and high nibbles in another (whose sum counts 16x)
+template <int BITS>
+struct KBlock {
+  static constexpr int K = BITS == 4 ? 128 : 64;
+  static constexpr int STEPS = BITS == 4 ? 8 : 4;
+  static constexpr int GROUPS = K / kDlGroup;
+  static constexpr int BYTES = K * BITS / 8;   // bytes of one row in one k-block
+};
+
+// The K indices (within the k-block) of the lower and upper halves of a lane's k-slot
+// pair: pair 0 is slots {2t, 2t+1}, pair 1 is {2t+8, 2t+9}.
+template <int BITS>
+__device__ __forceinline__ void slot_k(int t, int s, int pair, int& k_lo, int& k_hi) {
+  if constexpr (BITS == 4) {
+    const int base = 32 * t + 8 * (s >> 1) + 2 * (s & 1) + pair;
+    k_lo = base;
+    k_hi = base + 4;
+  } else {
+    const int base = 16 * t + 4 * s + pair;
+    k_lo = base;
+    k_hi = base + 2;
+  }
+}
+
+// nr rows of length K (row r at src + r * K) re-laid as B fragments: row r's (b0, b1) of
+// k-step s of k-block blk for lane t at perm[r * rstride + (blk * STEPS + s) * 4 + t], plus
+// the fp32 sum of each group of 64 at gsum[r * (K / 64) + group] (eight lanes per group,
+// a fixed shuffle tree).  Threads tid < nthr (whole warps) take part.
+template <int BITS>
+__device__ __forceinline__ void build_bperm(const uint16_t* __restrict__ src, int K, int nr,
+                                            uint2* __restrict__ perm, int rstride,
+                                            float* __restrict__ gsum, int tid, int nthr) {
+  using KB = KBlock<BITS>;
+  const int nblk = (K + KB::K - 1) / KB::K;
+  const int per_row = nblk * KB::STEPS * 4;
+  for (int i = tid; i < nr * per_row; i += nthr) {
+    const int r = i / per_row, j = i - r * per_row;
+    const int t = j & 3, s = (j >> 2) % KB::STEPS, blk = (j >> 2) / KB::STEPS;
+    const uint16_t* row = src + static_cast<size_t>(r) * K;
+    uint32_t b[2];
+#pragma unroll
+    for (int pair = 0; pair < 2; ++pair) {
+      int klo, khi;
+      slot_k<BITS>(t, s, pair, klo, khi);
+      klo += blk * KB::K;
+      khi += blk * KB::K;
+      const uint32_t lo = klo < K ? row[klo] : 0u;
+      const uint32_t hi = khi < K ? row[khi] : 0u;
+      b[pair] = lo | (hi << 16);
+    }
+    perm[static_cast<size_t>(r) * rstride + j] = make_uint2(b[0], b[1]);
+  }
+  // group sums: lane l of an 8-lane team adds elements 8l..8l+7 of its group
+  const int ng = K / kDlGroup;
+  const int total = nr * ng * 8;
+  for (int base = 0; base < total; base += nthr) {
+    const int i = base + tid;
+    float v = 0.f;
+    if (i < total) {
+      const int grp = i >> 3, l = i & 7;
+      const uint4 raw = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(grp) * kDlGroup + 8 * l);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        v += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xffff0000u);
+    }
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    if (i < total && (i & 7) == 0) gsum[i >> 3] = v;
+  }
+}
+
+// One warp's share of an MMA GEMV over k-blocks [blk0, blk1) of rows whose codes start at
+// rows_g (rows g) and, when TWO, rows_u (rows g+8; otherwise those rows are zero).  Scales / biases of
+// row r, group G at sc[r * ng + G] / bi[r * ng + G] (rows g: sc_g / bi_g, rows g+8: sc_u /
+// bi_u).  Returns the lane's fp32 partial sums of rows g (pg) and g+8 (pu) over its
+// groups; the caller adds the four lanes of a row.
+template <int BITS, int SDT, bool TWO>
+__device__ __forceinline__ void mma_rows(const uint8_t* rows_g, const uint8_t* rows_u, int pitch,
+                                         const uint16_t* sc_g, const uint16_t* bi_g,
+                                         const uint16_t* sc_u, const uint16_t* bi_u, int ng,
+                                         const uint2* __restrict__ bperm,
+                                         const float* __restrict__ gsum, int blk0, int blk1,
+                                         float& pg, float& pu) {
+  using KB = KBlock<BITS>;
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const uint8_t* rg = rows_g + g * pitch + 16 * t;
+  const uint8_t* ru = TWO ? rows_u + g * pitch + 16 * t : nullptr;
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  float dh[4] = {0.f, 0.f, 0.f, 0.f};            // 8-bit: high-nibble sums
+  int wstart = blk0 * KB::GROUPS;                // first group of the open column window
+  pg = 0.f;
+  pu = 0.f;
+  auto flush = [&](int wend) {
+    // columns 2t, 2t+1 of the window [wstart, wend)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int G = wstart + 2 * t + c;
+      if (G < wend) {
+        const float vg = BITS == 4 ? d[c] : fmaf(16.f, dh[c], d[c]);
+        const float vu = BITS == 4 ? d[2 + c] : fmaf(16.f, dh[2 + c], d[2 + c]);
+        const float xs = gsum[G];
+        pg = fmaf(half_to_f32<SDT>(sc_g[g * ng + G]), vg, fmaf(half_to_f32<SDT>(bi_g[g * ng + G]), xs, pg));
+        if (TWO)
+          pu = fmaf(half_to_f32<SDT>(sc_u[g * ng + G]), vu, fmaf(half_to_f32<SDT>(bi_u[g * ng + G]), xs, pu));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = dh[i] = 0.f;
+    wstart = wend;
+  };
+  for (int blk = blk0; blk < blk1; ++blk) {
+    const int g_lane = blk * KB::GROUPS + (BITS == 4 ? (t >> 1) : 0);   // group of this lane's K
+    const bool live = g_lane < ng;
+    uint4 wg = make_uint4(0, 0, 0, 0), wu = make_uint4(0, 0, 0, 0);
+    if (live) {
+      wg = *reinterpret_cast<const uint4*>(rg + blk * KB::BYTES);
+      if (TWO) wu = *reinterpret_cast<const uint4*>(ru + blk * KB::BYTES);
+    }
+    const int col = g_lane - wstart;             // this lane's B column in the window
+    const uint32_t gw[4] = {wg.x, wg.y, wg.z, wg.w};
+    const uint32_t uw[4] = {wu.x, wu.y, wu.z, wu.w};
+#pragma unroll
+    for (int s = 0; s < KB::STEPS; ++s) {
+      uint2 b = make_uint2(0u, 0u);
+      if (live && g == col) b = bperm[(blk * KB::STEPS + s) * 4 + t];
+      if constexpr (BITS == 4) {
+        const uint32_t G = gw[s >> 1], U = uw[s >> 1];
+        const int sh = 8 * (s & 1);
+        const uint32_t a0 = nibble_pair(G >> sh), a2 = nibble_pair(G >> (sh + 4));
+        const uint32_t a1 = TWO ? nibble_pair(U >> sh) : 0u, a3 = TWO ? nibble_pair(U >> (sh + 4)) : 0u;
+        mma_bf16_16816(d, a0, a1, a2, a3, b.x, b.y);
+      } else {
+        const uint32_t G = gw[s], U = uw[s];
+        const uint32_t l0 = nibble_pair(G), l2 = nibble_pair(G >> 8);
+        const uint32_t h0 = nibble_pair(G >> 4), h2 = nibble_pair(G >> 12);
+        const uint32_t l1 = TWO ? nibble_pair(U) : 0u, l3 = TWO ? nibble_pair(U >> 8) : 0u;
+        const uint32_t h1 = TWO ? nibble_pair(U >> 4) : 0u, h3 = TWO ? nibble_pair(U >> 12) : 0u;
+        mma_bf16_16816(d, l0, l1, l2, l3, b.x, b.y);
+        mma_bf16_16816(dh, h0, h1, h2, h3, b.x, b.y);
+      }
+    }
+    const int gnext = (blk + 1) * KB::GROUPS;
+    if (gnext - wstart >= 8 || blk + 1 == blk1) flush(min(gnext, ng));
+  }
+}
+
+template <int BITS, int SDT>
+__global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(DecodeLayerArgs a) {
+  using KB = KBlock<BITS>;
   constexpr int NF = kDlFeat;
-  constexpr int NGRP = CW / NF;            // consumer groups sharing the gate/up items
+  constexpr int ND = kDlFeatDown;
+  constexpr int CW = kDlCW;
   constexpr int CT = CW * 32;              // consumer threads
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float s_lg[kMaxExperts];
   __shared__ int32_t s_g2s[kMaxExperts];
   __shared__ int32_t s_idx[32], s_slot[32];
   __shared__ float s_sc[32], s_rank_lg[32];
-  __shared__ uint32_t s_epoch;
+  __shared__ unsigned long long s_epoch;
+  __shared__ float2 s_pair[2][kDlPairs][NF];
   const bigrig_expert_layout& L = a.L;
   const int H = L.hidden, I = L.inter, E = a.E, k = a.k;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool producer = warp == CW;
   const int G = gridDim.x, cta = blockIdx.x;
   const int pitch_h = H * BITS / 8, pitch_i = I * BITS / 8;
-  const int gh = H / L.group_size, gi = I / L.group_size;
-  const int nch_h = H / CPL, nch_i = I / CPL;
+  const int gh = H / kDlGroup, gi = I / kDlGroup;
+  const int nblk_h = (gh + KB::GROUPS - 1) / KB::GROUPS, nblk_i = (gi + KB::GROUPS - 1) / KB::GROUPS;
   const int nst = a.nstages, stage_bytes = a.stage_bytes;
-  uint32_t* bar_count = a.sync;
-  uint32_t* bar_gen = a.sync + 1;
-  uint32_t* epoch = a.sync + 2;
 
   SmemCarve sc(smem);
   uint64_t* bars = sc.take<uint64_t>((2 * kDlMaxStages + 3) * 8);
   uint16_t* xraw = sc.take<uint16_t>(static_cast<size_t>(H) * 2);
-  float* xs = sc.take<float>(static_cast<size_t>(H) * 4);
-  float* xcs = sc.take<float>(static_cast<size_t>(nch_h) * 4);
+  uint2* xperm = sc.take<uint2>(static_cast<size_t>(nblk_h) * KB::STEPS * 4 * 8);
+  float* xgs = sc.take<float>(static_cast<size_t>(gh) * 4);
   uint16_t* hraw = sc.take<uint16_t>(static_cast<size_t>(k) * I * 2);
-  float* hs = sc.take<float>(static_cast<size_t>(k) * I * 4);
-  float* hcs = sc.take<float>(static_cast<size_t>(k) * nch_i * 4);
-  float* ybuf = sc.take<float>(static_cast<size_t>(a.max_tiles) * k * NF * 4);
+  uint2* hperm = sc.take<uint2>(static_cast<size_t>(k) * nblk_i * KB::STEPS * 4 * 8);
+  float* hgs = sc.take<float>(static_cast<size_t>(k) * gi * 4);
+  float* ybuf = sc.take<float>(static_cast<size_t>(a.max_tiles) * k * ND * 4);
   uint8_t* ring = sc.take<uint8_t>(static_cast<size_t>(nst) * stage_bytes);
   uint16_t* wr = reinterpret_cast<uint16_t*>(ring);     // router rows, before any item
   uint64_t* full = bars;
@@ -157,17 +344,21 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) decode_layer_kernel(DecodeLa
     bar_expect_tx(bar_x, H * 2);
     bulk_g2s(xraw, a.x, H * 2, bar_x);
     if (n_mine > 0) {
+      // router rows are read every step: keep them in L2 against the streamed experts
       bar_expect_tx(bar_r, static_cast<uint32_t>(n_mine) * H * 2);
-      bulk_g2s(wr, a.gate_w + static_cast<size_t>(cta) * kDlRouterPerCta * H, n_mine * H * 2,
-               bar_r);
+      bulk_g2s_hint(wr, a.gate_w + static_cast<size_t>(cta) * kDlRouterPerCta * H, n_mine * H * 2,
+                    bar_r, l2_evict_last());
     }
   }
   if (producer) {
-    if (lane == 0) s_epoch = ld_acquire_u32(epoch);
+    // this launch's index: the barrier arrivals of all earlier launches over G (arrivals
+    // of this launch that are already in add fewer than G)
+    if (lane == 0) s_epoch = ld_acquire_u64(a.arrivals) / static_cast<unsigned long long>(G);
     for (int e = lane; e < E; e += 32) s_g2s[e] = a.g2s ? a.g2s[e] : e;
   }
   __syncthreads();
-  const unsigned long long tag = static_cast<unsigned long long>(s_epoch + 1u) << 32;
+  const unsigned long long epoch = s_epoch;
+  const unsigned long long tag = ((epoch + 1ull) & 0xffffffffull) << 32;
 
   // ---------------------------------------------------------------- router logits
   bool xok = true;
@@ -201,12 +392,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) decode_layer_kernel(DecodeLa
   const int tiles_g = I / NF;
   const int n_items = k * tiles_g;
   const int my_items = cta < n_items ? (n_items - 1 - cta) / G + 1 : 0;
-  const int tiles_d = H / NF;
+  const int tiles_d = H / ND;
   const int my_tiles = cta < tiles_d ? (tiles_d - 1 - cta) / G + 1 : 0;
   const int spi = a.seg_per_item;
   const int ipt = (k + spi - 1) / spi;           // down items per tile
   const int n_down = my_tiles * ipt;
-  const int seg_bytes = NF * pitch_i + 2 * NF * gi * 2;
+  const int item_bytes = 2 * NF * pitch_h + 4 * NF * gh * 2;
+  const int seg_bytes = ND * pitch_i + 2 * ND * gi * 2;
 
   if (producer) {
     // ------------------------------------------------------------ routing
@@ -252,7 +444,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) decode_layer_kernel(DecodeLa
     DL_STAMP(2);
     // ------------------------------------------------------------ stream the ring
     if (lane == 0) {
-      const uint32_t item_bytes = static_cast<uint32_t>(2 * NF * pitch_h + 4 * NF * gh * 2);
+      const uint64_t once = l2_evict_first();   // expert weights: read once per token
       for (int q = 0; q < my_items + n_down; ++q) {
         const int b = q % nst;
         if (q >= nst) stage_wait(empty + b, ((q / nst) - 1) & 1, a.err);
@@ -261,21 +453,24 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) decode_layer_kernel(DecodeLa
           const int it = cta + q * G;
           const int s = it / tiles_g, f0 = (it - s * tiles_g) * NF;
           const int slot = s_slot[s];
-          bar_expect_tx(full + b, slot >= 0 ? item_bytes : 0u);
+          bar_expect_tx(full + b, slot >= 0 ? static_cast<uint32_t>(item_bytes) : 0u);
           if (slot < 0) continue;
           const uint8_t* base = a.slab + static_cast<int64_t>(slot) * L.slot_stride;
           uint16_t* sb = reinterpret_cast<uint16_t*>(dst + 2 * NF * pitch_h);
           for (int m = 0; m < 2; ++m) {
-            bulk_g2s(dst + m * NF * pitch_h, base + L.weight_off[m] + static_cast<int64_t>(f0) * pitch_h,
-                     NF * pitch_h, full + b);
-            bulk_g2s(sb + (2 * m) * NF * gh, base + L.scales_off[m] + static_cast<int64_t>(f0) * gh * 2,
-                     NF * gh * 2, full + b);
-            bulk_g2s(sb + (2 * m + 1) * NF * gh,
-                     base + L.biases_off[m] + static_cast<int64_t>(f0) * gh * 2, NF * gh * 2, full + b);
+            bulk_g2s_hint(dst + m * NF * pitch_h,
+                          base + L.weight_off[m] + static_cast<int64_t>(f0) * pitch_h, NF * pitch_h,
+                          full + b, once);
+            bulk_g2s_hint(sb + (2 * m) * NF * gh,
+                          base + L.scales_off[m] + static_cast<int64_t>(f0) * gh * 2, NF * gh * 2,
+                          full + b, once);
+            bulk_g2s_hint(sb + (2 * m + 1) * NF * gh,
+                          base + L.biases_off[m] + static_cast<int64_t>(f0) * gh * 2, NF * gh * 2,
+                          full + b, once);
           }
         } else {
           const int d = q - my_items;
-          const int f0 = (cta + (d / ipt) * G) * NF;
+          const int f0 = (cta + (d / ipt) * G) * ND;
           const int s0 = (d % ipt) * spi, s1 = min(k, s0 + spi);
           uint32_t bytes = 0;
           for (int s = s0; s < s1; ++s) bytes += s_slot[s] >= 0 ? seg_bytes : 0;
@@ -284,13 +479,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) decode_layer_kernel(DecodeLa
             if (s_slot[s] < 0) continue;
             const uint8_t* base = a.slab + static_cast<int64_t>(s_slot[s]) * L.slot_stride;
             uint8_t* dd = dst + static_cast<size_t>(s - s0) * seg_bytes;
-            uint16_t* sb = reinterpret_cast<uint16_t*>(dd + NF * pitch_i);
-            bulk_g2s(dd, base + L.weight_off[2] + static_cast<int64_t>(f0) * pitch_i, NF * pitch_i,
-                     full + b);
-            bulk_g2s(sb, base + L.scales_off[2] + static_cast<int64_t>(f0) * gi * 2, NF * gi * 2,
-                     full + b);
-            bulk_g2s(sb + NF * gi, base + L.biases_off[2] + static_cast<int64_t>(f0) * gi * 2,
-                     NF * gi * 2, full + b);
+            uint16_t* sb = reinterpret_cast<uint16_t*>(dd + ND * pitch_i);
+            bulk_g2s_hint(dd, base + L.weight_off[2] + static_cast<int64_t>(f0) * pitch_i,
+                          ND * pitch_i, full + b, once);
+            bulk_g2s_hint(sb, base + L.scales_off[2] + static_cast<int64_t>(f0) * gi * 2,
+                          ND * gi * 2, full + b, once);
+            bulk_g2s_hint(sb + ND * gi, base + L.biases_off[2] + static_cast<int64_t>(f0) * gi * 2,
+                          ND * gi * 2, full + b, once);
           }
         }
       }
@@ -298,91 +493,65 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) decode_layer_kernel(DecodeLa
     return;                                      // consumers wait for every stage it filled
   }
 
-  // ---------------------------------------------------------------- consumers: x in registers
-  relayout_rows<BITS>(xs, xcs, xraw, H, 1, threadIdx.x, CT);
+  // ---------------------------------------------------------------- consumers: x as B
+  build_bperm<BITS>(xraw, H, 1, xperm, 0, xgs, threadIdx.x, CT);
   named_sync(1, CT);
-  ChunkX<BITS> cx[NCH];
-  float xc[NCH];
-  {
-    const float4* x4 = reinterpret_cast<const float4*>(xs);
-#pragma unroll
-    for (int i = 0; i < NCH; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nch_h) {
-        load_chunk_x<BITS>(cx[i], x4 + c, nch_h);
-        xc[i] = xcs[c];
-      } else {
-        xc[i] = 0.f;
-#pragma unroll
-        for (int q = 0; q < CPL / 2; ++q) cx[i].v[q] = make_float2(0.f, 0.f);
-      }
-    }
-  }
 
   // ---------------------------------------------------------------- gate/up
-  const int grp = warp / NF, fl = warp % NF;
+  // pair p = warp / 2 takes items j with j % 8 == p; warp half hh takes k-blocks
+  // [hh * half, ...) of the hidden dimension
+  const int pair = warp >> 1, hh = warp & 1;
+  const int half_blk = (nblk_h + 1) / 2;
+  const int kb0 = hh * half_blk, kb1 = min(nblk_h, kb0 + half_blk);
   for (int j = 0; j < my_items; ++j) {
     const int b = j % nst;
     const bool landed = stage_wait(full + b, (j / nst) & 1, a.err);
     if (j == 0) DL_STAMP(3);
-    if (j % NGRP == grp) {
+    if (j % kDlPairs == pair) {
       const int it = cta + j * G;
       const int s = it / tiles_g, f0 = (it - s * tiles_g) * NF;
       const bool have = s_slot[s] >= 0 && landed && xok;
       const uint8_t* st = ring + static_cast<size_t>(b) * stage_bytes;
       const uint16_t* sb = reinterpret_cast<const uint16_t*>(st + 2 * NF * pitch_h);
-      float ag = 0.f, au = 0.f;
-      if (have) {
-        const uint8_t* wg = st + fl * pitch_h;
-        const uint8_t* wu = st + (NF + fl) * pitch_h;
-#pragma unroll
-        for (int i = 0; i < NCH; ++i) {
-          const int c = lane + 32 * i;
-          if (c < nch_h) {
-            const int g = (c * CPL) / L.group_size;
-            const uint4 cg = *reinterpret_cast<const uint4*>(wg + c * 16);
-            const uint4 cu = *reinterpret_cast<const uint4*>(wu + c * 16);
-            const float dg = chunk_dot2<BITS>(cg, cx[i]);
-            const float du = chunk_dot2<BITS>(cu, cx[i]);
-            ag = fmaf(half_to_f32<SDT>(sb[(0 * NF + fl) * gh + g]), dg,
-                      fmaf(half_to_f32<SDT>(sb[(1 * NF + fl) * gh + g]), xc[i], ag));
-            au = fmaf(half_to_f32<SDT>(sb[(2 * NF + fl) * gh + g]), du,
-                      fmaf(half_to_f32<SDT>(sb[(3 * NF + fl) * gh + g]), xc[i], au));
-          }
-        }
+      float pg = 0.f, pu = 0.f;
+      if (have)
+        mma_rows<BITS, SDT, true>(st, st + NF * pitch_h, pitch_h, sb, sb + NF * gh, sb + 2 * NF * gh,
+                            sb + 3 * NF * gh, gh, xperm, xgs, kb0, kb1, pg, pu);
+      pg += __shfl_xor_sync(0xffffffffu, pg, 1);
+      pu += __shfl_xor_sync(0xffffffffu, pu, 1);
+      pg += __shfl_xor_sync(0xffffffffu, pg, 2);
+      pu += __shfl_xor_sync(0xffffffffu, pu, 2);
+      __syncwarp();
+      if (lane == 0) bar_arrive(empty + b);     // stage b read by this warp
+      const int buf = (j / kDlPairs) & 1;
+      if (hh == 1 && (lane & 3) == 0) s_pair[buf][pair][lane >> 2] = make_float2(pg, pu);
+      named_sync(2 + pair, 64);
+      if (hh == 0 && (lane & 3) == 0) {
+        const float2 o = s_pair[buf][pair][lane >> 2];
+        const float gv = pg + o.x, uv = pu + o.y;
+        a.h[static_cast<size_t>(s) * I + f0 + (lane >> 2)] = have ? f32_to_bf16_bits(silu_f32(gv) * uv) : 0;
       }
-      const float gv = warp_sum(ag);
-      const float uv = warp_sum(au);
-      if (lane == 0)
-        a.h[static_cast<size_t>(s) * I + f0 + fl] = have ? f32_to_bf16_bits(silu_f32(gv) * uv) : 0;
+    } else {
+      __syncwarp();
+      if (lane == 0) bar_arrive(empty + b);
     }
-    __syncwarp();
-    if (lane == 0) bar_arrive(empty + b);
   }
   DL_STAMP(4);
 
   // ---------------------------------------------------------------- grid barrier
-  __threadfence();
   named_sync(1, CT);
   if (threadIdx.x == 0) {
-    const uint32_t gen = ld_acquire_u32(bar_gen);
-    if (atomicAdd(bar_count, 1u) == static_cast<uint32_t>(G) - 1) {
-      // every CTA read this launch's epoch at its start: advance it for the next launch
-      atomicExch(bar_count, 0u);
-      atomicAdd(epoch, 1u);
-      __threadfence();
-      atomicAdd(bar_gen, 1u);
-    } else {
-      uint32_t n = 0;
-      while (ld_acquire_u32(bar_gen) == gen) {
-        if (++n > kDlSpinLimit) {
-          atomicAdd(a.err + 1, 1);
-          break;
-        }
-        __nanosleep(20);
-      }
-    }
     __threadfence();
+    atomicAdd(a.arrivals, 1ull);
+    const unsigned long long target = (epoch + 1ull) * static_cast<unsigned long long>(G);
+    uint32_t n = 0;
+    while (static_cast<long long>(ld_acquire_u64(a.arrivals) - target) < 0) {
+      if (++n > kDlSpinLimit) {
+        atomicAdd(a.err + 1, 1);
+        break;
+      }
+      __nanosleep(20);
+    }
     fence_proxy_async_global();                  // h, written by other CTAs, is read by bulk copy
     if (n_down > 0) {
       bar_expect_tx(bar_h, static_cast<uint32_t>(k) * I * 2);
@@ -397,47 +566,49 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) decode_layer_kernel(DecodeLa
 
   // ---------------------------------------------------------------- down + combine
   const bool hok = stage_wait(bar_h, 0, a.err);
-  relayout_rows<BITS>(hs, hcs, hraw, I, k, threadIdx.x, CT);
+  const int hstride = nblk_i * KB::STEPS * 4;
+  build_bperm<BITS>(hraw, I, k, hperm, hstride, hgs, threadIdx.x, CT);
   named_sync(1, CT);
   DL_STAMP(6);
-  const float4* h4 = reinterpret_cast<const float4*>(hs);
-  const int dgroups = CW / spi;                  // down items in flight at once
-  const int dgrp = warp / spi, dseg = warp % spi;
+  // a down item holds spi experts; warps 2m, 2m+1 of a team of 2*spi take expert m of the
+  // item, each half of the intermediate dimension; teams take items round-robin
+  const int team = 2 * spi;
+  const int dteams = CW / team;
+  const int dteam = warp / team, dseg = (warp % team) >> 1;
+  const int dhalf_blk = (nblk_i + 1) / 2;
+  const int db0 = hh * dhalf_blk, db1 = min(nblk_i, db0 + dhalf_blk);
   for (int d = 0; d < n_down; ++d) {
     const int q = my_items + d;
     const int b = q % nst;
     const bool landed = stage_wait(full + b, (q / nst) & 1, a.err) && hok;
-    if (dgrp < dgroups && d % dgroups == dgrp) {
+    if (dteam < dteams && d % dteams == dteam) {
       const int tl = d / ipt;
-      const int s0 = (d % ipt) * spi;
-      const int s = s0 + dseg;
+      const int s = (d % ipt) * spi + dseg;
       if (s < k) {
         const bool have = s_slot[s] >= 0 && landed;
         const uint8_t* wc = ring + static_cast<size_t>(b) * stage_bytes + static_cast<size_t>(dseg) * seg_bytes;
-        const uint16_t* sb = reinterpret_cast<const uint16_t*>(wc + NF * pitch_i);
-        float acc[NF];
-#pragma unroll
-        for (int f = 0; f < NF; ++f) acc[f] = 0.f;
-        if (have) {
-          for (int c = lane; c < nch_i; c += 32) {
-            const int g = (c * CPL) / L.group_size;
-            ChunkX<BITS> ch;
-            load_chunk_x<BITS>(ch, h4 + static_cast<size_t>(s) * Q * nch_i + c, nch_i);
-            const float csum = hcs[s * nch_i + c];
-#pragma unroll
-            for (int f = 0; f < NF; ++f) {
-              const uint4 cw = *reinterpret_cast<const uint4*>(wc + f * pitch_i + c * 16);
-              const float dv = chunk_dot2<BITS>(cw, ch);
-              acc[f] = fmaf(half_to_f32<SDT>(sb[f * gi + g]), dv,
-                            fmaf(half_to_f32<SDT>(sb[(NF + f) * gi + g]), csum, acc[f]));
-            }
-          }
+        const uint16_t* sb = reinterpret_cast<const uint16_t*>(wc + ND * pitch_i);
+        float p0 = 0.f, p8 = 0.f;
+        if (have)
+          mma_rows<BITS, SDT, true>(wc, wc + 8 * pitch_i, pitch_i, sb, sb + ND * gi, sb + 8 * gi,
+                                    sb + ND * gi + 8 * gi, gi, hperm + static_cast<size_t>(s) * hstride,
+                                    hgs + s * gi, db0, db1, p0, p8);
+        p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
+        p8 += __shfl_xor_sync(0xffffffffu, p8, 1);
+        p0 += __shfl_xor_sync(0xffffffffu, p0, 2);
+        p8 += __shfl_xor_sync(0xffffffffu, p8, 2);
+        __syncwarp();
+        if (lane == 0) bar_arrive(empty + b);
+        const int buf = (d / dteams) & 1;
+        if (hh == 1 && (lane & 3) == 0) s_pair[buf][pair][lane >> 2] = make_float2(p0, p8);
+        named_sync(2 + pair, 64);
+        if (hh == 0 && (lane & 3) == 0) {
+          const float2 o = s_pair[buf][pair][lane >> 2];
+          float* yb = ybuf + (tl * k + s) * ND;
+          yb[lane >> 2] = have ? bf16_round(p0 + o.x) : 0.f;
+          yb[8 + (lane >> 2)] = have ? bf16_round(p8 + o.y) : 0.f;
         }
-#pragma unroll
-        for (int f = 0; f < NF; ++f) {
-          const float v = warp_sum(acc[f]);
-          if (lane == 0) ybuf[(tl * k + s) * NF + f] = have ? bf16_round(v) : 0.f;
-        }
+        continue;
       }
     }
     __syncwarp();
@@ -445,11 +616,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) decode_layer_kernel(DecodeLa
   }
   named_sync(1, CT);
   // combine in rank order, plus the residual
-  if (threadIdx.x < my_tiles * NF) {
-    const int tl = threadIdx.x / NF, f = threadIdx.x % NF;
-    const int o = (cta + tl * G) * NF + f;
+  if (threadIdx.x < my_tiles * ND) {
+    const int tl = threadIdx.x / ND, f = threadIdx.x % ND;
+    const int o = (cta + tl * G) * ND + f;
     float acc = 0.f;
-    for (int r = 0; r < k; ++r) acc = acc + s_sc[r] * ybuf[(tl * k + r) * NF + f];
+    for (int r = 0; r < k; ++r) acc = acc + s_sc[r] * ybuf[(tl * k + r) * ND + f];
     if (a.residual) acc = bf16_bits_to_f32(a.residual[o]) + bf16_round(acc);
     a.out[o] = f32_to_bf16_bits(acc);
   }
@@ -473,40 +644,36 @@ int sm_count_dl() {
 }
 
 struct DlPlan {
-  int nch;          // 16-byte code chunks per lane of a hidden row (register-resident x)
-  int cw;           // consumer warps
   int stage_bytes, nstages, seg_per_item, max_tiles;
   size_t smem;
 };
 
 // The persistent kernel's plan for a layer, or false when it cannot run it: more than
-// 32 routed experts, a hidden row too wide to keep in registers, a layer whose fixed
-// shared memory leaves no room for a ring of two stages.
+// 32 routed experts, a quantisation group other than 64, a layer whose fixed shared
+// memory leaves no room for a ring of two stages.
 bool decode_layer_plan(const bigrig_expert_layout& L, int k, int E, int G, DlPlan* p) {
-  if (G <= 0 || k > 32 || E > kMaxExperts || L.hidden % kDlFeat || L.inter % kDlFeat) return false;
-  const int cpl = 128 / L.bits;
-  const int nch_h = L.hidden / cpl, nch_i = L.inter / cpl;
-  const int nch = (nch_h + 31) / 32;
-  if (nch > 4) return false;
-  p->nch = nch <= 2 ? 2 : 4;
-  p->cw = p->nch == 2 ? 16 : 8;
+  if (G <= 0 || k > 32 || E > kMaxExperts || L.group_size != kDlGroup) return false;
+  if (L.hidden % kDlGroup || L.inter % kDlGroup) return false;
+  const int kb_k = L.bits == 4 ? 128 : 64, steps = L.bits == 4 ? 8 : 4;
+  const size_t gh = L.hidden / kDlGroup, gi = L.inter / kDlGroup;
+  const size_t nblk_h = (L.hidden + kb_k - 1) / kb_k, nblk_i = (L.inter + kb_k - 1) / kb_k;
   const size_t ph = static_cast<size_t>(L.hidden) * L.bits / 8;
   const size_t pi = static_cast<size_t>(L.inter) * L.bits / 8;
-  const size_t gh = L.hidden / L.group_size, gi = L.inter / L.group_size;
   const size_t item = 2 * kDlFeat * ph + 4 * kDlFeat * gh * 2;
-  const size_t seg = kDlFeat * pi + 2 * kDlFeat * gi * 2;
+  const size_t seg = kDlFeatDown * pi + 2 * kDlFeatDown * gi * 2;
   const size_t stage = item > seg ? item : seg;
   int spi = static_cast<int>(stage / seg);
   if (spi > k) spi = k;
-  if (spi > p->cw) spi = p->cw;
-  const int tiles_d = L.hidden / kDlFeat;
+  if (spi > kDlCW / 2) spi = kDlCW / 2;
+  if (L.hidden % kDlFeatDown) return false;
+  const int tiles_d = L.hidden / kDlFeatDown;
   p->max_tiles = (tiles_d + G - 1) / G;
   const size_t fixed = round128((2 * kDlMaxStages + 3) * 8) + round128(L.hidden * 2) +
-                       round128(L.hidden * 4) + round128(nch_h * 4) +
+                       round128(nblk_h * steps * 4 * 8) + round128(gh * 4) +
                        round128(static_cast<size_t>(k) * L.inter * 2) +
-                       round128(static_cast<size_t>(k) * L.inter * 4) +
-                       round128(static_cast<size_t>(k) * nch_i * 4) +
-                       round128(static_cast<size_t>(p->max_tiles) * k * kDlFeat * 4);
+                       round128(static_cast<size_t>(k) * nblk_i * steps * 4 * 8) +
+                       round128(static_cast<size_t>(k) * gi * 4) +
+                       round128(static_cast<size_t>(p->max_tiles) * k * kDlFeatDown * 4);
   if (fixed >= kDlSmemLimit) return false;
   size_t nst = (kDlSmemLimit - fixed) / stage;
   if (nst > static_cast<size_t>(kDlMaxStages)) nst = kDlMaxStages;
@@ -518,15 +685,15 @@ bool decode_layer_plan(const bigrig_expert_layout& L, int k, int E, int G, DlPla
   return true;
 }
 
-template <int BITS, int SDT, int NCH, int CW>
+template <int BITS, int SDT>
 int dl_launch(const DecodeLayerArgs& args, size_t smem, int G, cudaStream_t s) {
-  auto kern = decode_layer_kernel<BITS, SDT, NCH, CW>;
+  auto kern = decode_layer_kernel<BITS, SDT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return set_error(BIGRIG_ERR_CUDA, "decode_layer: cannot reserve %zu bytes of smem", smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
-  cfg.blockDim = dim3((CW + 1) * 32);
+  cfg.blockDim = dim3((kDlCW + 1) * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -539,12 +706,6 @@ int dl_launch(const DecodeLayerArgs& args, size_t smem, int G, cudaStream_t s) {
   return check_launch("decode_layer_kernel");
 }
 
-template <int BITS, int SDT>
-int dl_shape(const DecodeLayerArgs& args, const DlPlan& p, int G, cudaStream_t s) {
-  if (p.nch == 2) return dl_launch<BITS, SDT, 2, 16>(args, p.smem, G, s);
-  return dl_launch<BITS, SDT, 4, 8>(args, p.smem, G, s);
-}
-
 }  // namespace
 
 bool decode_layer_fits(const bigrig_expert_layout& L, int k, int E) {
@@ -555,7 +716,7 @@ bool decode_layer_fits(const bigrig_expert_layout& L, int k, int E) {
 int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, int E, int k,
                         int mode, int norm, const int32_t* g2s, const void* slab,
                         const bigrig_expert_layout& L, const void* residual, void* out,
-                        int32_t* idx_out, float* sc_out, void* h, void* tagged, uint32_t* sync,
+                        int32_t* idx_out, float* sc_out, void* h, void* tagged, void* arrivals,
                         int32_t* err, cudaStream_t s) {
   const int G = sm_count_dl();
   DlPlan p;
@@ -574,7 +735,7 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
   a.sc_out = sc_out;
   a.h = static_cast<uint16_t*>(h);
   a.tagged = static_cast<unsigned long long*>(tagged);
-  a.sync = sync;
+  a.arrivals = static_cast<unsigned long long*>(arrivals);
   a.err = err;
   a.E = E;
   a.k = k;
@@ -584,10 +745,10 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
   a.nstages = p.nstages;
   a.seg_per_item = p.seg_per_item;
   a.max_tiles = p.max_tiles;
-  if (L.bits == 4 && L.scale_dtype == BIGRIG_F16) return dl_shape<4, BIGRIG_F16>(a, p, G, s);
-  if (L.bits == 4 && L.scale_dtype == BIGRIG_BF16) return dl_shape<4, BIGRIG_BF16>(a, p, G, s);
-  if (L.bits == 8 && L.scale_dtype == BIGRIG_F16) return dl_shape<8, BIGRIG_F16>(a, p, G, s);
-  if (L.bits == 8 && L.scale_dtype == BIGRIG_BF16) return dl_shape<8, BIGRIG_BF16>(a, p, G, s);
+  if (L.bits == 4 && L.scale_dtype == BIGRIG_F16) return dl_launch<4, BIGRIG_F16>(a, p.smem, G, s);
+  if (L.bits == 4 && L.scale_dtype == BIGRIG_BF16) return dl_launch<4, BIGRIG_BF16>(a, p.smem, G, s);
+  if (L.bits == 8 && L.scale_dtype == BIGRIG_F16) return dl_launch<8, BIGRIG_F16>(a, p.smem, G, s);
+  if (L.bits == 8 && L.scale_dtype == BIGRIG_BF16) return dl_launch<8, BIGRIG_BF16>(a, p.smem, G, s);
   return set_error(BIGRIG_ERR_UNSUPPORTED, "decode_layer: bits=%d scale_dtype=%d", L.bits, L.scale_dtype);
 }
 

@@ -1,9 +1,12 @@
 """The persistent one-token decode kernel (one cooperative launch per MoE layer).
 
-It must give the three-kernel chain's bits exactly -- outputs, indices and scores -- at
-the full layer sizes of every family it runs, with and without the residual, for 4- and
-8-bit codes, one to eight routed experts and a missing slot; leave its flag and barrier
-words back at zero after every call; and replay the same bits from a CUDA graph.
+Its routing must be the three-kernel chain's bit for bit (indices and scores); its
+output, computed on the tensor cores in another summation order, must meet the expert
+parity bar against the chain and against exact fp32 weights in plain torch -- at the full
+layer sizes of every family it runs, with and without the residual, for 4- and 8-bit
+codes, one to eight routed experts and a missing slot.  It must give the same bits on
+every call (its flag words carry over between launches), count no error and no wait
+timeout, and replay the same bits from a CUDA graph.
 """
 import numpy as np
 import pytest
@@ -79,13 +82,13 @@ def test_persistent_equals_chain(cuda, name):
         assert n1["route"] == n0["route"]
     words = _words(ws)
     assert words[0] == 0 and words[1] == 0, words      # no errors, no wait timed out
-    assert words[4] == 0 and words[5] == 0, words      # router and barrier counts reset
     cout, cidx, csc = _run("chain", name, L, slab, g2s, x, gw, gb, ws)
     cout_r, _, _ = _run("chain", name, L, slab, g2s, x, gw, gb, ws, residual=x)
     assert torch.equal(idx, cidx) and torch.equal(sc, csc)
     assert torch.equal(idx_r, cidx) and torch.equal(sc_r, csc)
-    assert torch.equal(out, cout)
-    assert torch.equal(out_r, cout_r)
+    long = max(L.hidden, L.inter) >= 4096
+    assert_close(out.float().cpu().numpy(), cout.float().cpu().numpy(), long_reduction=long)
+    assert_close(out_r.float().cpu().numpy(), cout_r.float().cpu().numpy(), long_reduction=long)
     # consecutive calls reuse the same flag words: the same bits every time
     for _ in range(3):
         again, _, _ = _run("auto", name, L, slab, g2s, x, gw, gb, ws)
@@ -115,12 +118,12 @@ def test_persistent_missing_slot(cuda):
     out, _, _ = _run("auto", name, L, slab, holes, x, gw, gb, ws)
     assert ws.errors() > 0
     cout, _, _ = _run("chain", name, L, slab, holes, x, gw, gb, ws)
-    assert torch.equal(out, cout)
+    assert_close(out.float().cpu().numpy(), cout.float().cpu().numpy())
     full, _, _ = _run("auto", name, L, slab, g2s, x, gw, gb, ws)
     assert not torch.equal(out, full)
     ws.errors()
     words = _words(ws)
-    assert words[1] == 0 and words[4] == 0 and words[5] == 0, words
+    assert words[1] == 0, words
 
 
 def test_persistent_graph_replay(cuda):
@@ -156,4 +159,4 @@ def test_persistent_graph_replay(cuda):
         assert torch.equal(hs[4], want)
     del graph
     words = _words(ws)
-    assert words[0] == 0 and words[1] == 0 and words[4] == 0 and words[5] == 0, words
+    assert words[0] == 0 and words[1] == 0, words
