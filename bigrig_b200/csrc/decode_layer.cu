@@ -15,10 +15,11 @@
 //            slots from a copy of g2s staged at start
 //   gate/up  items of (routed expert, 8 features), dealt round-robin to CTAs and
 //            streamed by the producer through a ring of bulk copies with full / empty
-//            mbarriers.  A pair of consumer warps takes an item, each warp half of the
-//            hidden dimension, on the tensor cores: warp-level bf16 MMAs (m16n8k16)
-//            whose 16 rows are the item's 8 gate and 8 up rows, A converted in
-//            registers from the codes to exact bf16 integers q, B the token.
+//            mbarriers.  Every consumer warp takes its 1/16 of the hidden dimension of
+//            each item as the item lands, on the tensor cores: warp-level bf16 MMAs
+//            (m16n8k16) whose 16 rows are the item's 8 gate and 8 up rows, A converted
+//            in registers from the codes to exact bf16 integers q, B the token; the last
+//            warp to finish an item adds the 16 partials in warp order and writes h.
 //   barrier  grid-wide, consumer threads only (the producer is already streaming the
 //            down-projection weights into the ring)
 //   down     items of (16 hidden features, a group of routed experts), a pair of warps
@@ -39,10 +40,13 @@
 #include "gemv_common.cuh"
 #include "routing.cuh"
 
-// Phase-boundary hook (thread 0 of each CTA); empty in the library, defined by
-// instrumented builds that record per-CTA timestamps.
+// Phase-boundary hooks (DL_STAMP: thread 0 of each CTA; DL_WSTAMP: lane 0 of each warp);
+// empty in the library, defined by instrumented builds that record timestamps.
 #ifndef DL_STAMP
 #define DL_STAMP(i)
+#endif
+#ifndef DL_WSTAMP
+#define DL_WSTAMP(i)
 #endif
 
 namespace bigrig {
@@ -52,7 +56,6 @@ constexpr int kDlFeatDown = 16;          // hidden features of a down tile (the 
 constexpr int kDlRouterPerCta = 4;       // experts whose logits one CTA computes
 constexpr int kDlMaxStages = 12;
 constexpr int kDlCW = 16;                // consumer warps
-constexpr int kDlPairs = kDlCW / 2;
 constexpr int kDlGroup = 64;             // quantisation group size the kernel is built for
 constexpr uint32_t kDlSpinLimit = 1u << 22;
 
@@ -72,7 +75,7 @@ struct DecodeLayerArgs {
   unsigned long long* arrivals;  // grid-barrier arrivals over all launches
   int32_t* err;
   int E, k, mode, norm;
-  int stage_bytes, nstages, seg_per_item, max_tiles;
+  int stage_bytes, nstages, seg_per_item, max_tiles, max_items, ksplit;
 };
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
@@ -165,6 +168,36 @@ __device__ __forceinline__ void slot_k(int t, int s, int pair, int& k_lo, int& k
   }
 }
 
+// Most k-blocks of the hidden dimension one consumer warp owns in the gate/up phase (its
+// B fragments live in registers): 16 warps x this covers H = 4096.
+template <int BITS>
+constexpr int kDlMaxSliceBlocks = BITS == 4 ? 2 : 4;
+
+// One k-block of 16 rows against B fragments held in registers: gate rows g from wg,
+// up rows g+8 from wu (the lane's 16-byte chunk of each).
+template <int BITS>
+__device__ __forceinline__ void mma_block(float* d, float* dh, const uint4 wg, const uint4 wu,
+                                          const uint2* b) {
+  using KB = KBlock<BITS>;
+  const uint32_t gw[4] = {wg.x, wg.y, wg.z, wg.w};
+  const uint32_t uw[4] = {wu.x, wu.y, wu.z, wu.w};
+#pragma unroll
+  for (int s = 0; s < KB::STEPS; ++s) {
+    if constexpr (BITS == 4) {
+      const uint32_t G = gw[s >> 1], U = uw[s >> 1];
+      const int sh = 8 * (s & 1);
+      mma_bf16_16816(d, nibble_pair(G >> sh), nibble_pair(U >> sh), nibble_pair(G >> (sh + 4)),
+                     nibble_pair(U >> (sh + 4)), b[s].x, b[s].y);
+    } else {
+      const uint32_t G = gw[s], U = uw[s];
+      mma_bf16_16816(d, nibble_pair(G), nibble_pair(U), nibble_pair(G >> 8), nibble_pair(U >> 8),
+                     b[s].x, b[s].y);
+      mma_bf16_16816(dh, nibble_pair(G >> 4), nibble_pair(U >> 4), nibble_pair(G >> 12),
+                     nibble_pair(U >> 12), b[s].x, b[s].y);
+    }
+  }
+}
+
 // nr rows of length K (row r at src + r * K) re-laid as B fragments: row r's (b0, b1) of
 // k-step s of k-block blk for lane t at perm[r * rstride + (blk * STEPS + s) * 4 + t], plus
 // the fp32 sum of each group of 64 at gsum[r * (K / 64) + group] (eight lanes per group,
@@ -214,18 +247,19 @@ __device__ __forceinline__ void build_bperm(const uint16_t* __restrict__ src, in
   }
 }
 
-// One warp's share of an MMA GEMV over k-blocks [blk0, blk1) of rows whose codes start at
-// rows_g (rows g) and, when TWO, rows_u (rows g+8; otherwise those rows are zero).  Scales / biases of
-// row r, group G at sc[r * ng + G] / bi[r * ng + G] (rows g: sc_g / bi_g, rows g+8: sc_u /
-// bi_u).  Returns the lane's fp32 partial sums of rows g (pg) and g+8 (pu) over its
-// groups; the caller adds the four lanes of a row.
-template <int BITS, int SDT, bool TWO>
-__device__ __forceinline__ void mma_rows(const uint8_t* rows_g, const uint8_t* rows_u, int pitch,
-                                         const uint16_t* sc_g, const uint16_t* bi_g,
-                                         const uint16_t* sc_u, const uint16_t* bi_u, int ng,
-                                         const uint2* __restrict__ bperm,
-                                         const float* __restrict__ gsum, int blk0, int blk1,
-                                         float& pg, float& pu) {
+// One warp's share of an MMA GEMV over k-blocks [blk0, blk1) of 16 rows whose codes start
+// at rows_g (rows g) and rows_u (rows g+8).  Scales / biases of row r, group G at
+// sc[r * ng + G] / bi[r * ng + G] (rows g: sc_g / bi_g, rows g+8: sc_u / bi_u).  Returns
+// the lane's fp32 partial sums of rows g (x) and g+8 (y) over its groups; the caller adds
+// the four lanes of a row.  Not inlined: the gate/up and the down phase run the same
+// instructions, so the second finds them in the instruction cache.
+template <int BITS, int SDT>
+__device__ __noinline__ float2 mma_rows(const uint8_t* rows_g, const uint8_t* rows_u, int pitch,
+                                        const uint16_t* sc_g, const uint16_t* bi_g,
+                                        const uint16_t* sc_u, const uint16_t* bi_u, int ng,
+                                        const uint2* __restrict__ bperm,
+                                        const float* __restrict__ gsum, int blk0, int blk1) {
+  constexpr bool TWO = true;
   using KB = KBlock<BITS>;
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const uint8_t* rg = rows_g + g * pitch + 16 * t;
@@ -233,8 +267,7 @@ __device__ __forceinline__ void mma_rows(const uint8_t* rows_g, const uint8_t* r
   float d[4] = {0.f, 0.f, 0.f, 0.f};
   float dh[4] = {0.f, 0.f, 0.f, 0.f};            // 8-bit: high-nibble sums
   int wstart = blk0 * KB::GROUPS;                // first group of the open column window
-  pg = 0.f;
-  pu = 0.f;
+  float pg = 0.f, pu = 0.f;
   auto flush = [&](int wend) {
     // columns 2t, 2t+1 of the window [wstart, wend)
 #pragma unroll
@@ -287,6 +320,7 @@ __device__ __forceinline__ void mma_rows(const uint8_t* rows_g, const uint8_t* r
     const int gnext = (blk + 1) * KB::GROUPS;
     if (gnext - wstart >= 8 || blk + 1 == blk1) flush(min(gnext, ng));
   }
+  return make_float2(pg, pu);
 }
 
 template <int BITS, int SDT>
@@ -296,32 +330,47 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
   constexpr int ND = kDlFeatDown;
   constexpr int CW = kDlCW;
   constexpr int CT = CW * 32;              // consumer threads
+  constexpr int MAXNB = kDlMaxSliceBlocks<BITS>;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float s_lg[kMaxExperts];
+  __shared__ __align__(16) float s_lg[kMaxExperts];
   __shared__ int32_t s_g2s[kMaxExperts];
   __shared__ int32_t s_idx[32], s_slot[32];
   __shared__ float s_sc[32], s_rank_lg[32];
   __shared__ unsigned long long s_epoch;
-  __shared__ float2 s_pair[2][kDlPairs][NF];
+  __shared__ float s_resid[2 * kDlFeatDown];     // the combine's residual values
   const bigrig_expert_layout& L = a.L;
   const int H = L.hidden, I = L.inter, E = a.E, k = a.k;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
   const bool producer = warp == CW;
   const int G = gridDim.x, cta = blockIdx.x;
   const int pitch_h = H * BITS / 8, pitch_i = I * BITS / 8;
   const int gh = H / kDlGroup, gi = I / kDlGroup;
   const int nblk_h = (gh + KB::GROUPS - 1) / KB::GROUPS, nblk_i = (gi + KB::GROUPS - 1) / KB::GROUPS;
   const int nst = a.nstages, stage_bytes = a.stage_bytes;
+  const int ksplit = a.ksplit;                   // warps per routed expert in the down phase
+
+  const int tiles_g = I / NF;
+  const int n_items = k * tiles_g;
+  const int my_items = cta < n_items ? (n_items - 1 - cta) / G + 1 : 0;
+  const int tiles_d = H / ND;
+  const int my_tiles = cta < tiles_d ? (tiles_d - 1 - cta) / G + 1 : 0;
+  const int spi = a.seg_per_item;
+  const int ipt = (k + spi - 1) / spi;           // down items per tile
+  const int n_down = my_tiles * ipt;
+  const int item_bytes = 2 * NF * pitch_h + 4 * NF * gh * 2;
+  const int seg_bytes = ND * pitch_i + 2 * ND * gi * 2;
 
   SmemCarve sc(smem);
-  uint64_t* bars = sc.take<uint64_t>((2 * kDlMaxStages + 3) * 8);
+  uint64_t* bars = sc.take<uint64_t>((2 * kDlMaxStages + 4) * 8);
   uint16_t* xraw = sc.take<uint16_t>(static_cast<size_t>(H) * 2);
   uint2* xperm = sc.take<uint2>(static_cast<size_t>(nblk_h) * KB::STEPS * 4 * 8);
   float* xgs = sc.take<float>(static_cast<size_t>(gh) * 4);
   uint16_t* hraw = sc.take<uint16_t>(static_cast<size_t>(k) * I * 2);
   uint2* hperm = sc.take<uint2>(static_cast<size_t>(k) * nblk_i * KB::STEPS * 4 * 8);
   float* hgs = sc.take<float>(static_cast<size_t>(k) * gi * 4);
-  float* ybuf = sc.take<float>(static_cast<size_t>(a.max_tiles) * k * ND * 4);
+  float2* gpart = sc.take<float2>(static_cast<size_t>(a.max_items) * CW * NF * 8);
+  float2* dpart = sc.take<float2>(static_cast<size_t>(a.max_tiles) * k * ksplit * 8 * 8);
   uint8_t* ring = sc.take<uint8_t>(static_cast<size_t>(nst) * stage_bytes);
   uint16_t* wr = reinterpret_cast<uint16_t*>(ring);     // router rows, before any item
   uint64_t* full = bars;
@@ -329,6 +378,7 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
   uint64_t* bar_x = bars + 2 * kDlMaxStages;
   uint64_t* bar_r = bar_x + 1;
   uint64_t* bar_h = bar_x + 2;
+  uint64_t* bar_s = bar_x + 3;                   // scores written (for the combine)
   DL_STAMP(0);
 
   // ---------------------------------------------------------------- start
@@ -341,6 +391,7 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
     bar_init(bar_x, 1);
     bar_init(bar_r, 1);
     bar_init(bar_h, 1);
+    bar_init(bar_s, 1);
     bar_expect_tx(bar_x, H * 2);
     bulk_g2s(xraw, a.x, H * 2, bar_x);
     if (n_mine > 0) {
@@ -356,6 +407,7 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
     if (lane == 0) s_epoch = ld_acquire_u64(a.arrivals) / static_cast<unsigned long long>(G);
     for (int e = lane; e < E; e += 32) s_g2s[e] = a.g2s ? a.g2s[e] : e;
   }
+  if (threadIdx.x < 32) s_idx[threadIdx.x] = -1;
   __syncthreads();
   const unsigned long long epoch = s_epoch;
   const unsigned long long tag = ((epoch + 1ull) & 0xffffffffull) << 32;
@@ -389,19 +441,11 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
   __syncthreads();                               // router rows read: the ring is free
   DL_STAMP(1);
 
-  const int tiles_g = I / NF;
-  const int n_items = k * tiles_g;
-  const int my_items = cta < n_items ? (n_items - 1 - cta) / G + 1 : 0;
-  const int tiles_d = H / ND;
-  const int my_tiles = cta < tiles_d ? (tiles_d - 1 - cta) / G + 1 : 0;
-  const int spi = a.seg_per_item;
-  const int ipt = (k + spi - 1) / spi;           // down items per tile
-  const int n_down = my_tiles * ipt;
-  const int item_bytes = 2 * NF * pitch_h + 4 * NF * gh * 2;
-  const int seg_bytes = ND * pitch_i + 2 * ND * gi * 2;
-
+  // ---------------------------------------------------------------- routing
+  // the producer collects the E tagged logits; every consumer thread then ranks (logit
+  // descending, expert id ascending -- topk_warp's order) a share of them: 8 threads per
+  // candidate, each counting the candidates above it among E/8 others
   if (producer) {
-    // ------------------------------------------------------------ routing
     uint32_t need = 0;
     for (int e = lane, i = 0; e < E; e += 32, ++i) need |= 1u << i;
     for (uint32_t n = 0; need; ++n) {
@@ -424,119 +468,239 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
       }
     }
     __syncwarp();
-    const int per = (E + 31) / 32;
-#define BIGRIG_TK(N) \
-  if (per == N) topk_rank_warp<N>(s_lg, E, k, a.mode, a.norm, s_idx, s_sc, s_rank_lg);
-    BIGRIG_TK(1) BIGRIG_TK(2) BIGRIG_TK(3) BIGRIG_TK(4)
-    BIGRIG_TK(5) BIGRIG_TK(6) BIGRIG_TK(7) BIGRIG_TK(8)
-#undef BIGRIG_TK
-    if (lane < k) {
-      const int e = s_idx[lane];
-      const int slot = (e >= 0 && e < E) ? s_g2s[e] : -1;
-      s_slot[lane] = slot;
-      if (cta == 0) {
-        a.idx_out[lane] = e;
-        a.sc_out[lane] = s_sc[lane];
-        if (slot < 0) atomicAdd(a.err, 1);
-      }
-    }
-    __syncwarp();
-    DL_STAMP(2);
-    // ------------------------------------------------------------ stream the ring
-    if (lane == 0) {
-      const uint64_t once = l2_evict_first();   // expert weights: read once per token
-      for (int q = 0; q < my_items + n_down; ++q) {
-        const int b = q % nst;
-        if (q >= nst) stage_wait(empty + b, ((q / nst) - 1) & 1, a.err);
-        uint8_t* dst = ring + static_cast<size_t>(b) * stage_bytes;
-        if (q < my_items) {
-          const int it = cta + q * G;
-          const int s = it / tiles_g, f0 = (it - s * tiles_g) * NF;
-          const int slot = s_slot[s];
-          bar_expect_tx(full + b, slot >= 0 ? static_cast<uint32_t>(item_bytes) : 0u);
-          if (slot < 0) continue;
-          const uint8_t* base = a.slab + static_cast<int64_t>(slot) * L.slot_stride;
-          uint16_t* sb = reinterpret_cast<uint16_t*>(dst + 2 * NF * pitch_h);
-          for (int m = 0; m < 2; ++m) {
-            bulk_g2s_hint(dst + m * NF * pitch_h,
-                          base + L.weight_off[m] + static_cast<int64_t>(f0) * pitch_h, NF * pitch_h,
-                          full + b, once);
-            bulk_g2s_hint(sb + (2 * m) * NF * gh,
-                          base + L.scales_off[m] + static_cast<int64_t>(f0) * gh * 2, NF * gh * 2,
-                          full + b, once);
-            bulk_g2s_hint(sb + (2 * m + 1) * NF * gh,
-                          base + L.biases_off[m] + static_cast<int64_t>(f0) * gh * 2, NF * gh * 2,
-                          full + b, once);
-          }
-        } else {
-          const int d = q - my_items;
-          const int f0 = (cta + (d / ipt) * G) * ND;
-          const int s0 = (d % ipt) * spi, s1 = min(k, s0 + spi);
-          uint32_t bytes = 0;
-          for (int s = s0; s < s1; ++s) bytes += s_slot[s] >= 0 ? seg_bytes : 0;
-          bar_expect_tx(full + b, bytes);
-          for (int s = s0; s < s1; ++s) {
-            if (s_slot[s] < 0) continue;
-            const uint8_t* base = a.slab + static_cast<int64_t>(s_slot[s]) * L.slot_stride;
-            uint8_t* dd = dst + static_cast<size_t>(s - s0) * seg_bytes;
-            uint16_t* sb = reinterpret_cast<uint16_t*>(dd + ND * pitch_i);
-            bulk_g2s_hint(dd, base + L.weight_off[2] + static_cast<int64_t>(f0) * pitch_i,
-                          ND * pitch_i, full + b, once);
-            bulk_g2s_hint(sb, base + L.scales_off[2] + static_cast<int64_t>(f0) * gi * 2,
-                          ND * gi * 2, full + b, once);
-            bulk_g2s_hint(sb + ND * gi, base + L.biases_off[2] + static_cast<int64_t>(f0) * gi * 2,
-                          ND * gi * 2, full + b, once);
-          }
+    DL_STAMP(8);
+  } else {
+    build_bperm<BITS>(xraw, H, 1, xperm, 0, xgs, threadIdx.x, CT);
+  }
+  __syncthreads();                               // logits in s_lg
+  if (!producer) {
+    const int per_cand = (E + 7) / 8;
+    for (int c0 = 0; c0 < E; c0 += CT / 8) {
+      const int c = c0 + (threadIdx.x >> 3), part = threadIdx.x & 7;
+      int r = 0;
+      float v = 0.f;
+      if (c < E) {
+        v = s_lg[c];
+        const int u0 = part * per_cand, u1 = min(E, u0 + per_cand);
+        for (int u = u0; u < u1; ++u) {
+          const float w = s_lg[u];
+          r += (w > v) || (w == v && u < c);
         }
       }
+      r += __shfl_xor_sync(0xffffffffu, r, 1);
+      r += __shfl_xor_sync(0xffffffffu, r, 2);
+      r += __shfl_xor_sync(0xffffffffu, r, 4);
+      if (c < E && part == 0 && v == v && r < k) {   // NaN logits are never selected
+        s_idx[r] = c;
+        s_rank_lg[r] = v;
+      }
     }
+  }
+  __syncthreads();                               // ranks in s_idx / s_rank_lg
+
+  if (producer) {
+    DL_STAMP(9);
+    if (lane < k) {
+      const int e = s_idx[lane];
+      s_slot[lane] = (e >= 0 && e < E) ? s_g2s[e] : -1;
+    }
+    __syncwarp();
+    // ------------------------------------------------------------ stream the ring
+    // the first stages go out at once; then the scores (needed only by the combine);
+    // then the rest as stages free up
+    const int total = my_items + n_down;
+    const int first = min(nst, total);
+    const uint64_t once = l2_evict_first();     // expert weights: read once per token
+    // one ring stage: lane 0 arms the barrier, then lane c issues copy c of the stage
+    // (a gate/up item has 6: codes, scales, biases of gate and up; a down item 3 per
+    // expert), so the address arithmetic of the copies runs side by side
+    auto issue = [&](int q) {
+      const int b = q % nst;
+      if (q >= nst) stage_wait(empty + b, ((q / nst) - 1) & 1, a.err);
+      if (q < 16) DL_WSTAMP(16 + q);
+      uint8_t* dst = ring + static_cast<size_t>(b) * stage_bytes;
+      if (q < my_items) {
+        const int it = cta + q * G;
+        const int s = it / tiles_g, f0 = (it - s * tiles_g) * NF;
+        const int slot = s_slot[s];
+        if (lane == 0) bar_expect_tx(full + b, slot >= 0 ? static_cast<uint32_t>(item_bytes) : 0u);
+        __syncwarp();
+        if (slot >= 0 && lane < 6) {
+          const uint8_t* base = a.slab + static_cast<int64_t>(slot) * L.slot_stride;
+          const int m = lane / 3, part = lane % 3;   // projection; codes / scales / biases
+          const uint8_t* src;
+          uint8_t* d;
+          uint32_t bytes;
+          if (part == 0) {
+            src = base + L.weight_off[m] + static_cast<int64_t>(f0) * pitch_h;
+            d = dst + m * NF * pitch_h;
+            bytes = NF * pitch_h;
+          } else {
+            const int64_t off = part == 1 ? L.scales_off[m] : L.biases_off[m];
+            src = base + off + static_cast<int64_t>(f0) * gh * 2;
+            d = dst + 2 * NF * pitch_h + (2 * m + part - 1) * NF * gh * 2;
+            bytes = NF * gh * 2;
+          }
+          bulk_g2s_hint(d, src, bytes, full + b, once);
+        }
+      } else {
+        const int d = q - my_items;
+        const int f0 = (cta + (d / ipt) * G) * ND;
+        const int s0 = (d % ipt) * spi, s1 = min(k, s0 + spi);
+        uint32_t bytes = 0;
+        for (int s = s0; s < s1; ++s) bytes += s_slot[s] >= 0 ? seg_bytes : 0;
+        if (lane == 0) bar_expect_tx(full + b, bytes);
+        __syncwarp();
+        for (int c = lane; c < 3 * (s1 - s0); c += 32) {
+          const int s = s0 + c / 3, part = c % 3;
+          if (s_slot[s] < 0) continue;
+          const uint8_t* base = a.slab + static_cast<int64_t>(s_slot[s]) * L.slot_stride;
+          uint8_t* dd = dst + static_cast<size_t>(s - s0) * seg_bytes;
+          if (part == 0)
+            bulk_g2s_hint(dd, base + L.weight_off[2] + static_cast<int64_t>(f0) * pitch_i,
+                          ND * pitch_i, full + b, once);
+          else
+            bulk_g2s_hint(dd + ND * pitch_i + (part - 1) * ND * gi * 2,
+                          base + (part == 1 ? L.scales_off[2] : L.biases_off[2]) +
+                              static_cast<int64_t>(f0) * gi * 2,
+                          ND * gi * 2, full + b, once);
+        }
+      }
+      __syncwarp();
+    };
+    for (int q = 0; q < first; ++q) issue(q);
+    DL_STAMP(2);
+    // scores: topk_warp's formulas and reductions over the same values in the same lanes
+    {
+      const int per = (E + 31) / 32;
+      float mx = -INFINITY;
+      for (int i = 0; i < per; ++i)
+        if (i * 32 + lane < E) mx = fmaxf(mx, s_lg[i * 32 + lane]);
+      mx = warp_max(mx);
+      const int my_idx = lane < k ? s_idx[lane] : -1;
+      const float my_logit = (lane < k && my_idx >= 0) ? s_rank_lg[lane] : -INFINITY;
+      const float first_logit = s_idx[0] >= 0 ? s_rank_lg[0] : -INFINITY;
+      float sv = 0.f;
+      if (a.mode == BIGRIG_SOFTMAX_TOPK) {
+        float denom = 0.f;
+        for (int i = 0; i < per; ++i)
+          if (i * 32 + lane < E) denom += expf(s_lg[i * 32 + lane] - mx);
+        denom = warp_sum(denom);
+        sv = (lane < k) ? expf(my_logit - mx) / denom : 0.f;
+        if (a.norm) sv = sv / warp_sum(sv);
+      } else {
+        const float ex = (lane < k) ? expf(my_logit - first_logit) : 0.f;
+        sv = ex / warp_sum(ex);
+      }
+      if (lane < k) {
+        s_sc[lane] = sv;
+        if (cta == 0) {
+          a.idx_out[lane] = my_idx;
+          a.sc_out[lane] = sv;
+          if (s_slot[lane] < 0) atomicAdd(a.err, 1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) bar_arrive(bar_s);
+    }
+    for (int q = first; q < total; ++q) issue(q);
+    DL_STAMP(13);
     return;                                      // consumers wait for every stage it filled
   }
 
-  // ---------------------------------------------------------------- consumers: x as B
-  build_bperm<BITS>(xraw, H, 1, xperm, 0, xgs, threadIdx.x, CT);
-  named_sync(1, CT);
+  // the combine's residual, fetched now (into shared memory, so the load completes
+  // here) so that its latency hides behind the layer
+  if (a.residual && threadIdx.x < my_tiles * ND) {
+    const int tl = threadIdx.x / ND, f = threadIdx.x % ND;
+    s_resid[threadIdx.x] = bf16_bits_to_f32(a.residual[(cta + tl * G) * ND + f]);
+  }
 
   // ---------------------------------------------------------------- gate/up
-  // pair p = warp / 2 takes items j with j % 8 == p; warp half hh takes k-blocks
-  // [hh * half, ...) of the hidden dimension
-  const int pair = warp >> 1, hh = warp & 1;
-  const int half_blk = (nblk_h + 1) / 2;
-  const int kb0 = hh * half_blk, kb1 = min(nblk_h, kb0 + half_blk);
+  // consumer warp w owns k-blocks [kb0, kb1) of the hidden dimension in every item; its B
+  // fragments (the token) stay in registers for all items.  Per item it leaves the partial
+  // sums of the 8 gate and 8 up rows over its blocks; they are added after the last item.
+  const int kb0 = warp * nblk_h / CW, kb1 = (warp + 1) * nblk_h / CW;
+  const int nb = kb1 - kb0;
+  uint2 breg[MAXNB][KB::STEPS];
+#pragma unroll
+  for (int bi = 0; bi < MAXNB; ++bi) {
+    const int blk = kb0 + bi;
+    const int g_lane = blk * KB::GROUPS + (BITS == 4 ? (t >> 1) : 0);
+    const bool use = bi < nb && g_lane < gh && g == g_lane - kb0 * KB::GROUPS;
+#pragma unroll
+    for (int s = 0; s < KB::STEPS; ++s)
+      breg[bi][s] = use ? xperm[(blk * KB::STEPS + s) * 4 + t] : make_uint2(0u, 0u);
+  }
+  // the lane's two accumulator columns: groups kb0*GROUPS + 2t + {0, 1}
+  const int gend = min(kb1 * KB::GROUPS, gh);
+  int gcol[2];
+  float xg[2];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    gcol[c] = kb0 * KB::GROUPS + 2 * t + c;
+    xg[c] = gcol[c] < gend ? xgs[gcol[c]] : 0.f;
+  }
+  const uint8_t* goff = nullptr;                 // this lane's code bytes in a stage
   for (int j = 0; j < my_items; ++j) {
     const int b = j % nst;
     const bool landed = stage_wait(full + b, (j / nst) & 1, a.err);
     if (j == 0) DL_STAMP(3);
-    if (j % kDlPairs == pair) {
-      const int it = cta + j * G;
-      const int s = it / tiles_g, f0 = (it - s * tiles_g) * NF;
-      const bool have = s_slot[s] >= 0 && landed && xok;
-      const uint8_t* st = ring + static_cast<size_t>(b) * stage_bytes;
-      const uint16_t* sb = reinterpret_cast<const uint16_t*>(st + 2 * NF * pitch_h);
-      float pg = 0.f, pu = 0.f;
-      if (have)
-        mma_rows<BITS, SDT, true>(st, st + NF * pitch_h, pitch_h, sb, sb + NF * gh, sb + 2 * NF * gh,
-                            sb + 3 * NF * gh, gh, xperm, xgs, kb0, kb1, pg, pu);
-      pg += __shfl_xor_sync(0xffffffffu, pg, 1);
-      pu += __shfl_xor_sync(0xffffffffu, pu, 1);
-      pg += __shfl_xor_sync(0xffffffffu, pg, 2);
-      pu += __shfl_xor_sync(0xffffffffu, pu, 2);
-      __syncwarp();
-      if (lane == 0) bar_arrive(empty + b);     // stage b read by this warp
-      const int buf = (j / kDlPairs) & 1;
-      if (hh == 1 && (lane & 3) == 0) s_pair[buf][pair][lane >> 2] = make_float2(pg, pu);
-      named_sync(2 + pair, 64);
-      if (hh == 0 && (lane & 3) == 0) {
-        const float2 o = s_pair[buf][pair][lane >> 2];
-        const float gv = pg + o.x, uv = pu + o.y;
-        a.h[static_cast<size_t>(s) * I + f0 + (lane >> 2)] = have ? f32_to_bf16_bits(silu_f32(gv) * uv) : 0;
+    if (j == 0) DL_WSTAMP(0);
+    const int it = cta + j * G;
+    const int s = it / tiles_g;
+    const bool have = s_slot[s] >= 0 && landed && xok;
+    const uint8_t* st = ring + static_cast<size_t>(b) * stage_bytes;
+    goff = st + g * pitch_h + 16 * t + kb0 * KB::BYTES;
+    const uint16_t* sb = reinterpret_cast<const uint16_t*>(st + 2 * NF * pitch_h);
+    float pg = 0.f, pu = 0.f;
+    if (have && nb > 0) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f}, dh[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int bi = 0; bi < MAXNB; ++bi) {
+        if (bi < nb) {
+          const uint4 wg = *reinterpret_cast<const uint4*>(goff + bi * KB::BYTES);
+          const uint4 wu = *reinterpret_cast<const uint4*>(goff + NF * pitch_h + bi * KB::BYTES);
+          mma_block<BITS>(d, dh, wg, wu, breg[bi]);
+        }
       }
-    } else {
-      __syncwarp();
-      if (lane == 0) bar_arrive(empty + b);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        if (gcol[c] < gend) {
+          const int G0 = gcol[c];
+          const float vg = BITS == 4 ? d[c] : fmaf(16.f, dh[c], d[c]);
+          const float vu = BITS == 4 ? d[2 + c] : fmaf(16.f, dh[2 + c], d[2 + c]);
+          pg = fmaf(half_to_f32<SDT>(sb[(0 * NF + g) * gh + G0]), vg,
+                    fmaf(half_to_f32<SDT>(sb[(1 * NF + g) * gh + G0]), xg[c], pg));
+          pu = fmaf(half_to_f32<SDT>(sb[(2 * NF + g) * gh + G0]), vu,
+                    fmaf(half_to_f32<SDT>(sb[(3 * NF + g) * gh + G0]), xg[c], pu));
+        }
+      }
     }
+    pg += __shfl_xor_sync(0xffffffffu, pg, 1);
+    pu += __shfl_xor_sync(0xffffffffu, pu, 1);
+    pg += __shfl_xor_sync(0xffffffffu, pg, 2);
+    pu += __shfl_xor_sync(0xffffffffu, pu, 2);
+    if (t == 0) gpart[(j * CW + warp) * NF + g] = make_float2(pg, pu);
+    __syncwarp();
+    if (lane == 0) bar_arrive(empty + b);        // stage b read by this warp
   }
   DL_STAMP(4);
+  DL_WSTAMP(1);
+  named_sync(1, CT);
+  // h = bf16(silu(gate) * up), the 16 partials of each row added in warp order
+  for (int i = threadIdx.x; i < my_items * NF; i += CT) {
+    const int j = i / NF, f = i - j * NF;
+    const int it = cta + j * G;
+    const int s = it / tiles_g, f0 = (it - s * tiles_g) * NF;
+    float gv = 0.f, uv = 0.f;
+    for (int w = 0; w < CW; ++w) {
+      const float2 o = gpart[(j * CW + w) * NF + f];
+      gv += o.x;
+      uv += o.y;
+    }
+    a.h[static_cast<size_t>(s) * I + f0 + f] = s_slot[s] >= 0 ? f32_to_bf16_bits(silu_f32(gv) * uv) : 0;
+  }
+  DL_STAMP(10);
 
   // ---------------------------------------------------------------- grid barrier
   named_sync(1, CT);
@@ -570,58 +734,61 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
   build_bperm<BITS>(hraw, I, k, hperm, hstride, hgs, threadIdx.x, CT);
   named_sync(1, CT);
   DL_STAMP(6);
-  // a down item holds spi experts; warps 2m, 2m+1 of a team of 2*spi take expert m of the
-  // item, each half of the intermediate dimension; teams take items round-robin
-  const int team = 2 * spi;
-  const int dteams = CW / team;
-  const int dteam = warp / team, dseg = (warp % team) >> 1;
-  const int dhalf_blk = (nblk_i + 1) / 2;
-  const int db0 = hh * dhalf_blk, db1 = min(nblk_i, db0 + dhalf_blk);
+  // warp w takes routed expert s = w / ksplit (and s + CW / ksplit, ...) over k-blocks
+  // [ks * nblk_i / ksplit, ...) of the intermediate dimension, ks = w % ksplit, in every
+  // down tile of the CTA
+  const int ks = warp % ksplit;
+  const int db0 = ks * nblk_i / ksplit, db1 = (ks + 1) * nblk_i / ksplit;
   for (int d = 0; d < n_down; ++d) {
     const int q = my_items + d;
     const int b = q % nst;
     const bool landed = stage_wait(full + b, (q / nst) & 1, a.err) && hok;
-    if (dteam < dteams && d % dteams == dteam) {
-      const int tl = d / ipt;
-      const int s = (d % ipt) * spi + dseg;
-      if (s < k) {
-        const bool have = s_slot[s] >= 0 && landed;
-        const uint8_t* wc = ring + static_cast<size_t>(b) * stage_bytes + static_cast<size_t>(dseg) * seg_bytes;
-        const uint16_t* sb = reinterpret_cast<const uint16_t*>(wc + ND * pitch_i);
-        float p0 = 0.f, p8 = 0.f;
-        if (have)
-          mma_rows<BITS, SDT, true>(wc, wc + 8 * pitch_i, pitch_i, sb, sb + ND * gi, sb + 8 * gi,
-                                    sb + ND * gi + 8 * gi, gi, hperm + static_cast<size_t>(s) * hstride,
-                                    hgs + s * gi, db0, db1, p0, p8);
-        p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
-        p8 += __shfl_xor_sync(0xffffffffu, p8, 1);
-        p0 += __shfl_xor_sync(0xffffffffu, p0, 2);
-        p8 += __shfl_xor_sync(0xffffffffu, p8, 2);
-        __syncwarp();
-        if (lane == 0) bar_arrive(empty + b);
-        const int buf = (d / dteams) & 1;
-        if (hh == 1 && (lane & 3) == 0) s_pair[buf][pair][lane >> 2] = make_float2(p0, p8);
-        named_sync(2 + pair, 64);
-        if (hh == 0 && (lane & 3) == 0) {
-          const float2 o = s_pair[buf][pair][lane >> 2];
-          float* yb = ybuf + (tl * k + s) * ND;
-          yb[lane >> 2] = have ? bf16_round(p0 + o.x) : 0.f;
-          yb[8 + (lane >> 2)] = have ? bf16_round(p8 + o.y) : 0.f;
-        }
-        continue;
-      }
+    if (d == n_down - 1) DL_STAMP(14);
+    if (d < 8) DL_WSTAMP(8 + d);
+    const int tl = d / ipt;
+    const int s0 = (d % ipt) * spi, s1 = min(k, s0 + spi);
+    for (int s = warp / ksplit; s < k; s += CW / ksplit) {
+      if (s < s0 || s >= s1) continue;
+      const bool have = s_slot[s] >= 0 && landed && db0 < db1;
+      const uint8_t* wc = ring + static_cast<size_t>(b) * stage_bytes + static_cast<size_t>(s - s0) * seg_bytes;
+      const uint16_t* sb = reinterpret_cast<const uint16_t*>(wc + ND * pitch_i);
+      float2 p = make_float2(0.f, 0.f);
+      DL_WSTAMP(2);
+      if (have)
+        p = mma_rows<BITS, SDT>(wc, wc + 8 * pitch_i, pitch_i, sb, sb + ND * gi, sb + 8 * gi,
+                                sb + ND * gi + 8 * gi, gi, hperm + static_cast<size_t>(s) * hstride,
+                                hgs + s * gi, db0, db1);
+      p.x += __shfl_xor_sync(0xffffffffu, p.x, 1);
+      p.y += __shfl_xor_sync(0xffffffffu, p.y, 1);
+      p.x += __shfl_xor_sync(0xffffffffu, p.x, 2);
+      p.y += __shfl_xor_sync(0xffffffffu, p.y, 2);
+      if (t == 0) dpart[((tl * k + s) * ksplit + ks) * 8 + g] = p;   // features g and g + 8
+      DL_WSTAMP(3);
     }
     __syncwarp();
     if (lane == 0) bar_arrive(empty + b);
   }
+  DL_STAMP(11);
+  DL_WSTAMP(4);
   named_sync(1, CT);
-  // combine in rank order, plus the residual
+  DL_STAMP(12);
+  // combine in rank order, plus the residual; y of a routed expert is its k-split
+  // partials added in order and rounded to bf16
+  const bool scores = stage_wait(bar_s, 0, a.err);
   if (threadIdx.x < my_tiles * ND) {
     const int tl = threadIdx.x / ND, f = threadIdx.x % ND;
     const int o = (cta + tl * G) * ND + f;
     float acc = 0.f;
-    for (int r = 0; r < k; ++r) acc = acc + s_sc[r] * ybuf[(tl * k + r) * ND + f];
-    if (a.residual) acc = bf16_bits_to_f32(a.residual[o]) + bf16_round(acc);
+    for (int r = 0; r < k; ++r) {
+      float y = 0.f;
+      for (int q = 0; q < ksplit; ++q) {
+        const float2 pp = dpart[((tl * k + r) * ksplit + q) * 8 + (f & 7)];
+        y += f < 8 ? pp.x : pp.y;
+      }
+      y = s_slot[r] >= 0 ? bf16_round(y) : 0.f;
+      acc = acc + (scores ? s_sc[r] : 0.f) * y;
+    }
+    if (a.residual) acc = s_resid[threadIdx.x] + bf16_round(acc);
     a.out[o] = f32_to_bf16_bits(acc);
   }
   DL_STAMP(7);
@@ -630,7 +797,9 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
 // ------------------------------------------------------------------ launcher
 namespace {
 
-constexpr size_t kDlSmemLimit = 220 * 1024;
+// dynamic shared memory: the 227 KB a block may hold, less the kernel's static arrays
+// (routing state) and a margin
+constexpr size_t kDlSmemLimit = 222 * 1024;
 
 int sm_count_dl() {
   static int sms = 0;
@@ -644,19 +813,22 @@ int sm_count_dl() {
 }
 
 struct DlPlan {
-  int stage_bytes, nstages, seg_per_item, max_tiles;
+  int stage_bytes, nstages, seg_per_item, max_tiles, max_items, ksplit;
   size_t smem;
 };
 
 // The persistent kernel's plan for a layer, or false when it cannot run it: more than
-// 32 routed experts, a quantisation group other than 64, a layer whose fixed shared
-// memory leaves no room for a ring of two stages.
+// 32 routed experts, a quantisation group other than 64, a hidden dimension wider than
+// 16 warps' register-held slices, a layer whose fixed shared memory leaves no room for a
+// ring of two stages.
 bool decode_layer_plan(const bigrig_expert_layout& L, int k, int E, int G, DlPlan* p) {
   if (G <= 0 || k > 32 || E > kMaxExperts || L.group_size != kDlGroup) return false;
-  if (L.hidden % kDlGroup || L.inter % kDlGroup) return false;
+  if (L.hidden % kDlGroup || L.inter % kDlGroup || L.hidden % kDlFeatDown) return false;
   const int kb_k = L.bits == 4 ? 128 : 64, steps = L.bits == 4 ? 8 : 4;
+  const int max_slice = L.bits == 4 ? kDlMaxSliceBlocks<4> : kDlMaxSliceBlocks<8>;
   const size_t gh = L.hidden / kDlGroup, gi = L.inter / kDlGroup;
   const size_t nblk_h = (L.hidden + kb_k - 1) / kb_k, nblk_i = (L.inter + kb_k - 1) / kb_k;
+  if (nblk_h > static_cast<size_t>(kDlCW) * max_slice) return false;
   const size_t ph = static_cast<size_t>(L.hidden) * L.bits / 8;
   const size_t pi = static_cast<size_t>(L.inter) * L.bits / 8;
   const size_t item = 2 * kDlFeat * ph + 4 * kDlFeat * gh * 2;
@@ -664,16 +836,20 @@ bool decode_layer_plan(const bigrig_expert_layout& L, int k, int E, int G, DlPla
   const size_t stage = item > seg ? item : seg;
   int spi = static_cast<int>(stage / seg);
   if (spi > k) spi = k;
-  if (spi > kDlCW / 2) spi = kDlCW / 2;
-  if (L.hidden % kDlFeatDown) return false;
+  int ksplit = 1;
+  while (ksplit * 2 * k <= kDlCW) ksplit *= 2;   // warps per routed expert in the down phase
   const int tiles_d = L.hidden / kDlFeatDown;
+  const int n_items = k * (L.inter / kDlFeat);
   p->max_tiles = (tiles_d + G - 1) / G;
-  const size_t fixed = round128((2 * kDlMaxStages + 3) * 8) + round128(L.hidden * 2) +
+  p->max_items = (n_items + G - 1) / G;
+  p->ksplit = ksplit;
+  const size_t fixed = round128((2 * kDlMaxStages + 4) * 8) + round128(L.hidden * 2) +
                        round128(nblk_h * steps * 4 * 8) + round128(gh * 4) +
                        round128(static_cast<size_t>(k) * L.inter * 2) +
                        round128(static_cast<size_t>(k) * nblk_i * steps * 4 * 8) +
                        round128(static_cast<size_t>(k) * gi * 4) +
-                       round128(static_cast<size_t>(p->max_tiles) * k * kDlFeatDown * 4);
+                       round128(static_cast<size_t>(p->max_items) * kDlCW * kDlFeat * 8) +
+                       round128(static_cast<size_t>(p->max_tiles) * k * ksplit * 8 * 8);
   if (fixed >= kDlSmemLimit) return false;
   size_t nst = (kDlSmemLimit - fixed) / stage;
   if (nst > static_cast<size_t>(kDlMaxStages)) nst = kDlMaxStages;
@@ -745,6 +921,8 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
   a.nstages = p.nstages;
   a.seg_per_item = p.seg_per_item;
   a.max_tiles = p.max_tiles;
+  a.max_items = p.max_items;
+  a.ksplit = p.ksplit;
   if (L.bits == 4 && L.scale_dtype == BIGRIG_F16) return dl_launch<4, BIGRIG_F16>(a, p.smem, G, s);
   if (L.bits == 4 && L.scale_dtype == BIGRIG_BF16) return dl_launch<4, BIGRIG_BF16>(a, p.smem, G, s);
   if (L.bits == 8 && L.scale_dtype == BIGRIG_F16) return dl_launch<8, BIGRIG_F16>(a, p.smem, G, s);

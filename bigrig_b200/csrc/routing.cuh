@@ -73,8 +73,8 @@ __device__ __forceinline__ void topk_warp(Load load, int E, int k, int mode, int
 // ascending) order is counted directly against all E logits, the k best are scattered to
 // their ranks, and the scores come from the same formulas and reductions as topk_warp, so
 // indices and scores are bit-identical to it.  NaN logits are never selected (as in
-// topk_warp); a rank no finite logit fills keeps idx -1.  `rank_lg` is 32 floats of
-// shared scratch.
+// topk_warp); a rank no finite logit fills keeps idx -1.  `lg` is 16-byte aligned shared
+// memory with room for a multiple of 4 entries; `rank_lg` is 32 floats of shared scratch.
 template <int PER_LANE>
 __device__ __forceinline__ void topk_rank_warp(const float* lg, int E, int k, int mode,
                                                int norm_topk, int32_t* idx, float* sc,
@@ -99,19 +99,31 @@ __device__ __forceinline__ void topk_rank_warp(const float* lg, int E, int k, in
     denom = warp_sum(denom);
   }
   __syncwarp();
+  // ranks: every candidate against all E logits, four per shared-memory load (lg is
+  // 16-byte aligned; the tail past E is skipped by index)
+  int rank[PER_LANE];
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) rank[i] = 0;
+#pragma unroll 2
+  for (int u0 = 0; u0 < E; u0 += 4) {
+    const float4 w4 = *reinterpret_cast<const float4*>(lg + u0);
+    const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int u = u0 + q;
+#pragma unroll
+      for (int i = 0; i < PER_LANE; ++i) {
+        const int e = i * 32 + lane;
+        rank[i] += u < E && ((w[q] > v[i]) || (w[q] == v[i] && u < e));
+      }
+    }
+  }
 #pragma unroll
   for (int i = 0; i < PER_LANE; ++i) {
     const int e = i * 32 + lane;
-    if (e < E && v[i] == v[i]) {
-      int r = 0;
-      for (int u = 0; u < E; ++u) {
-        const float w = lg[u];
-        r += (w > v[i]) || (w == v[i] && u < e);
-      }
-      if (r < k) {
-        idx[r] = e;
-        rank_lg[r] = v[i];
-      }
+    if (e < E && v[i] == v[i] && rank[i] < k) {
+      idx[rank[i]] = e;
+      rank_lg[rank[i]] = v[i];
     }
   }
   __syncwarp();

@@ -147,9 +147,17 @@ def test_missing_slot_is_reported_not_read(cuda):
     assert ws.errors() == 0
 
 
+@pytest.fixture
+def chain_path():
+    """One-token moe_layer calls on the three-kernel chain (not the persistent kernel)."""
+    prev = _lib.set_path("chain")
+    yield
+    _lib.set_path(prev)
+
+
 @pytest.mark.parametrize("T,k,E,mode", [(1, 8, 64, "softmax_topk"), (2, 8, 128, "softmax_topk"),
                                         (4, 4, 128, "topk_softmax"), (16, 2, 8, "topk_softmax")])
-def test_fused_decode_layer_is_bit_identical(cuda, T, k, E, mode):
+def test_fused_decode_layer_is_bit_identical(cuda, T, k, E, mode, chain_path):
     """The fused three-kernel decode chain (route, gate_up, down+combine) computes exactly
     what the separate kernels compute, with and without the residual."""
     rng = np.random.default_rng(T * 100 + E)
