@@ -114,14 +114,32 @@ class Clocks:
                 "samples": len(sm)}
 
 
+def _traffic() -> dict:
+    """DRAM bytes per launch (read + write) of the profiled kernels, from the ncu summary
+    committed in profiles/traffic.txt ("<kernel> <bytes>" lines)."""
+    out = {}
+    tpath = os.path.join(ROOT, "profiles", "traffic.txt")
+    if os.path.exists(tpath):
+        for line in open(tpath):
+            parts = line.split()
+            if len(parts) >= 2 and not line.startswith("#"):
+                try:
+                    out[parts[0]] = int(float(parts[1]))
+                except ValueError:
+                    pass
+    return out
+
+
 # ------------------------------------------------------------------ model
-def build_model(device, seed: int, experts=None):
+def build_model(device, seed: int, experts=None, layers=None):
     """Router weights (replicated on every rank) and a pinned host store holding the
     given global expert ids of every layer (all of them by default)."""
     from bigrig_b200.block import fill_store, make_blocks
     from bigrig_b200.fetch import HostExpertStore
     from bigrig_b200.formats import bytes_per_expert, make_spec
-    c = CFG
+    c = dict(CFG)
+    if layers is not None:
+        c["layers"] = layers
     blocks = make_blocks(c["layers"], c["hidden"], c["inter"], c["experts"], c["top_k"],
                          c["family"], c["bits"], c["group_size"], c["scale_dtype"], True,
                          seed=seed, device=device)
@@ -238,6 +256,9 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="decode only (for profiling)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="MoE layers of the stack (default: the config's 16; fewer only to keep "
+                         "a profiler capture small -- such a run is not a bench line)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -259,9 +280,11 @@ def main() -> None:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     _lib.load(build_if_stale=False)
-    c = CFG
+    c = dict(CFG)
+    if args.layers is not None:
+        c["layers"] = args.layers
     if world == 1:
-        blocks, store = build_model(dev, seed=0)
+        blocks, store = build_model(dev, seed=0, layers=c["layers"])
         handle = attach(blocks, store, c["capacity"], policy=c["policy"], warm="auto", device=dev)
         stack = blocks
     else:
@@ -272,7 +295,7 @@ def main() -> None:
         from bigrig_b200.stream import ExpertPool, StreamHandle, StreamingSwitchGLU
         ep = ExpertParallel(c["experts"])
         lo, hi = ep.local_range()
-        blocks, store = build_model(dev, seed=0, experts=range(lo, hi))
+        blocks, store = build_model(dev, seed=0, experts=range(lo, hi), layers=c["layers"])
         pools, mods = [], []
         for b in blocks:
             pool = ExpertPool(b.layer, None, hi - lo, min(c["capacity"], hi - lo), b.spec,
@@ -310,10 +333,12 @@ def main() -> None:
                 b.padded = False             # prompt chunks exchange exact row counts
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("prefill")
         e0.record()
         layered.prefill(layers, layered.chunks(prompt, c["prefill_chunk"]),
                         layer_scope=handle.prefill_layer)
         e1.record()
+        torch.cuda.nvtx.range_pop()
         barrier()
         pf_ms = max_over_ranks(e0.elapsed_time(e1))
         extras["prefill_tok_s"] = world * c["prompt"] / (pf_ms / 1e3)
@@ -334,10 +359,12 @@ def main() -> None:
     clocks = Clocks(local)
     clocks.start()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("decode")
     t0.record()
     for i in range(K):
         stack_step(stack, tokens[W + i])
     t1.record()
+    torch.cuda.nvtx.range_pop()
     barrier()
     clk = clocks.stop()
     _lib.timing_enable([])
@@ -393,11 +420,13 @@ def main() -> None:
             graph.replay()
         barrier()
         r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("resident_decode")
         r0.record()
         for i in range(K):
             xin.copy_(tokens[W + i])
             graph.replay()
         r1.record()
+        torch.cuda.nvtx.range_pop()
         barrier()
         rms = max_over_ranks(r0.elapsed_time(r1))
         res_tok_s = K / (rms / 1e3)
@@ -423,13 +452,17 @@ def main() -> None:
     gu_avg_ms = gu_ms / max(1, gu_n)
     gu_bytes = gate_up_bytes(1, c["top_k"])
     achieved = gu_bytes / (gu_avg_ms / 1e3) / 1e9 if gu_n else None
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "traffic.txt")
-    if os.path.exists(tpath):
-        for line in open(tpath):
-            parts = line.split()
-            if len(parts) >= 2 and parts[0] == "gemv_gate_up_kernel":
-                traffic = int(float(parts[1]))
+    traffic = _traffic().get("gemv_gate_up_kernel")
+    if "moe_layer_hbm_gbs" in extras:
+        # the persistent one-token layer kernel of the resident decode: algorithmic bytes of
+        # a layer over the graph's time per layer (which includes the launch gap)
+        extras["resident_roofline"] = {
+            "kernel": "decode_layer_kernel", "bound": "hbm",
+            "achieved": extras["moe_layer_hbm_gbs"], "peak": hbm_peak, "unit": "GB/s",
+            "frac": extras["moe_layer_hbm_gbs"] / hbm_peak, "peak_kind": peak_kind,
+            "traffic": _traffic().get("decode_layer_kernel"),
+            "bytes_per_launch": extras["moe_layer_bytes"],
+            "avg_launch_ms": extras["resident_ms_per_token"] / c["layers"]}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K,

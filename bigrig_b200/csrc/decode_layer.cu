@@ -511,9 +511,9 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
     const int total = my_items + n_down;
     const int first = min(nst, total);
     const uint64_t once = l2_evict_first();     // expert weights: read once per token
-    // one ring stage: lane 0 arms the barrier, then lane c issues copy c of the stage
-    // (a gate/up item has 6: codes, scales, biases of gate and up; a down item 3 per
-    // expert), so the address arithmetic of the copies runs side by side
+    // one ring stage: lane 0 arms the barrier and issues its copies (a gate/up item has
+    // 6: codes, scales, biases of gate and up; a down item 3 per expert) -- one lane
+    // feeds the copy engine faster than several taking turns
     auto issue = [&](int q) {
       const int b = q % nst;
       if (q >= nst) stage_wait(empty + b, ((q / nst) - 1) & 1, a.err);
@@ -525,9 +525,9 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
         const int slot = s_slot[s];
         if (lane == 0) bar_expect_tx(full + b, slot >= 0 ? static_cast<uint32_t>(item_bytes) : 0u);
         __syncwarp();
-        if (slot >= 0 && lane < 6) {
+        if (slot >= 0 && lane == 0) for (int c = 0; c < 6; ++c) {
           const uint8_t* base = a.slab + static_cast<int64_t>(slot) * L.slot_stride;
-          const int m = lane / 3, part = lane % 3;   // projection; codes / scales / biases
+          const int m = c / 3, part = c % 3;         // projection; codes / scales / biases
           const uint8_t* src;
           uint8_t* d;
           uint32_t bytes;
@@ -551,7 +551,7 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
         for (int s = s0; s < s1; ++s) bytes += s_slot[s] >= 0 ? seg_bytes : 0;
         if (lane == 0) bar_expect_tx(full + b, bytes);
         __syncwarp();
-        for (int c = lane; c < 3 * (s1 - s0); c += 32) {
+        for (int c = 0; lane == 0 && c < 3 * (s1 - s0); ++c) {
           const int s = s0 + c / 3, part = c % 3;
           if (s_slot[s] < 0) continue;
           const uint8_t* base = a.slab + static_cast<int64_t>(s_slot[s]) * L.slot_stride;
