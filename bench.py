@@ -487,7 +487,8 @@ def main() -> None:
                          "bytes_per_launch": gu_bytes, "avg_launch_ms": gu_avg_ms,
                          "timed_launches": gu_n},
             "pool": {"miss_rate": st["miss_rate"], "hits": st["hits"], "misses": st["misses"],
-                     "admit_gb": st["admit_gb"], "sync_seconds": st["sync_seconds"]},
+                     "admit_gb": st["admit_gb"], "sync_seconds": st["sync_seconds"],
+                     "stage_issued": st.get("stage_issued"), "stage_hits": st.get("stage_hits")},
             "clocks": clk,
             "cpu_baseline": cpu,
             **extras,

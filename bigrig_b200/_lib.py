@@ -27,7 +27,7 @@ EXPORTS = (
     "bigrig_dequant", "bigrig_router_logits", "bigrig_router_topk", "bigrig_moe_permute",
     "bigrig_switch_glu", "bigrig_combine", "bigrig_moe_forward", "bigrig_workspace_errors",
     "bigrig_timing_enable", "bigrig_timing_read", "bigrig_launch_counts", "bigrig_kernel_name",
-    "bigrig_set_path", "bigrig_moe_layer", "bigrig_switch_glu_noalloc",
+    "bigrig_set_path", "bigrig_moe_layer", "bigrig_switch_glu_noalloc", "bigrig_copy_regions",
 )
 NOALLOC_SCRATCH_BYTES = 4 << 20
 KERNELS = {"router_logits": 0, "router_topk": 1, "permute": 2, "gate_up": 3, "down": 4,
@@ -71,6 +71,7 @@ _SIG = {
     "bigrig_moe_forward": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _P,
                                ctypes.POINTER(ExpertLayout), _P, _P, _P, _P, ctypes.c_size_t, _P]),
     "bigrig_workspace_errors": (_I, [_P, _P, _P]),
+    "bigrig_copy_regions": (_I, [_P, _P, _P, _I, _P]),
     "bigrig_timing_enable": (_I, [_I]),
     "bigrig_timing_read": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
     "bigrig_launch_counts": (_I, [ctypes.POINTER(ctypes.c_int64)]),

@@ -108,6 +108,12 @@ class MoEBlock:
                                       workspace=sw.workspace)
             pool.mark_read()
             return out
+        if (pool is not None and x.shape[0] == 1 and hasattr(sw, "decode_layer")
+                and not getattr(sw, "bypass", False)):
+            # one decode token over a capped pool: route, make resident, then the whole
+            # layer in one library call
+            return sw.decode_layer(x, self.gate_w, self.gate_b, self.top_k, mode, norm,
+                                   residual=residual)
         idx, scores = self.route(x)
         y = sw(x, idx)
         return ops.combine(y, scores, residual=residual)

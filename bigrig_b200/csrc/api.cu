@@ -450,6 +450,21 @@ const char* bigrig_kernel_name(int kernel_id) {
   return (kernel_id >= 0 && kernel_id < BIGRIG_K_COUNT) ? kKernelNames[kernel_id] : "";
 }
 
+int bigrig_copy_regions(void* const* dst, const void* const* src, const size_t* bytes, int n,
+                        void* stream) {
+  if (n < 0 || (n > 0 && (!dst || !src || !bytes)))
+    return set_error(BIGRIG_ERR_INVALID, "copy_regions: n=%d or NULL arrays", n);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int i = 0; i < n; ++i) {
+    if (bytes[i] == 0) continue;
+    if (!dst[i] || !src[i]) return set_error(BIGRIG_ERR_INVALID, "copy_regions: NULL pointer %d", i);
+    const cudaError_t rc = cudaMemcpyAsync(dst[i], src[i], bytes[i], cudaMemcpyDefault, s);
+    if (rc != cudaSuccess)
+      return set_error(BIGRIG_ERR_CUDA, "copy_regions: copy %d: %s", i, cudaGetErrorString(rc));
+  }
+  return BIGRIG_OK;
+}
+
 int bigrig_workspace_errors(void* workspace, int32_t* out, void* stream) {
   if (!workspace || !out) return set_error(BIGRIG_ERR_INVALID, "workspace_errors: NULL pointer");
   const cudaStream_t s = static_cast<cudaStream_t>(stream);

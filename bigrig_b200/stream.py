@@ -39,6 +39,19 @@ from . import ops
 from .formats import PROJECTIONS, bytes_per_expert, layout_from_spec
 from .pool import _policy_factory
 
+# Most experts a layer copies to the GPU on the previous layer's prediction -- the router's
+# top-k, as in the reference (stream.py:1723-1726).
+STAGE_MAX = 8
+# Whether a layer stages the next layer's predicted experts (pinned host -> HBM staging
+# buffers, on the copy stream, behind its own misses) while its experts compute.  The
+# reference keeps this off (stream.py:1731-1758): on unified memory the staging copy
+# contended with the expert reads.  On a discrete GPU it runs over PCIe beside the HBM-bound
+# compute; the next layer's own router, evaluated in the same two launches as this layer's
+# routing, names about 92 % of the next layer's misses (95 % of what it stages is used, on
+# the synthetic OLMoE stack), and the copies leave the critical path: capped decode 202 ->
+# 213 tok/s.  On by default; BIGRIG_STAGE=0 turns it off.
+STAGING = os.environ.get("BIGRIG_STAGE", "1") != "0"
+
 
 def projections_of(spec: dict) -> tuple:
     """The projections this layer's experts carry, in packed byte order (stream.py:66-68)."""
@@ -102,9 +115,10 @@ class ExpertPool:
         self.admit_seconds = 0.0
         self.admit_bytes = 0
         self.stage_pred = None
-        self.stage = {}
+        self.stage = {}            # expert id -> its bytes in a staging buffer, ready to admit
         self.stage_issued = 0
         self.stage_hits = 0
+        self._stage_buf = None     # [STAGE_MAX, bytes_per_expert] in HBM, made on first use
         self.zero_copy_admits = 0
         self.evicts = 0
         self.views = bool(views)
@@ -114,11 +128,13 @@ class ExpertPool:
         self._copy_stream = copy_stream
         self._copies_done = None     # event: this pool's queued admissions have landed
         self._reads_done = None      # event: the last kernel that read the slab has finished
+        self._bpe = bytes_per_expert(spec)
+        self._batch = None           # slot writes collected by ensure(), issued in one call
 
     # -- construction -------------------------------------------------------
     @property
     def bytes_per_expert(self) -> int:
-        return bytes_per_expert(self.spec)
+        return self._bpe
 
     def build(self):
         """Allocate the HBM slab.  The model's (E, ...) expert tensors, if ``sg`` holds
@@ -225,6 +241,73 @@ class ExpertPool:
         with torch.cuda.stream(self._copy_stream):
             return src.to(self.device, non_blocking=src.is_pinned())
 
+    def stage_experts(self, items) -> int:
+        """stage_expert for several (expert, blob) pairs with one library call issuing the
+        copies; returns how many were staged."""
+        picked = []
+        for e, blob in items:
+            e = int(e)
+            if self.g2s[e] >= 0 or e in self.stage or len(self.stage) + len(picked) >= STAGE_MAX:
+                continue
+            if any(e == p for p, _ in picked):
+                continue
+            src = _as_u8(blob)
+            if src.numel() != self.bytes_per_expert:
+                raise ValueError(f"expert {e}: manifest accounts for {self.bytes_per_expert} "
+                                 f"bytes but the region is {src.numel()}.")
+            picked.append((e, src))
+        if not picked:
+            return 0
+        if self.device.type != "cuda":
+            for e, src in picked:
+                self.stage_expert(e, src)
+            return len(picked)
+        if self._stage_buf is None:
+            self._stage_buf = torch.empty((STAGE_MAX, self.bytes_per_expert), dtype=torch.uint8,
+                                          device=self.device)
+        import ctypes
+        from . import _lib
+        base = len(self.stage)
+        dsts = [self._stage_buf[base + i] for i in range(len(picked))]
+        n = len(picked)
+        dst = (ctypes.c_void_p * n)(*[d.data_ptr() for d in dsts])
+        src = (ctypes.c_void_p * n)(*[t.data_ptr() for _, t in picked])
+        size = (ctypes.c_size_t * n)(*[self.bytes_per_expert] * n)
+        # the copy stream orders these writes after the previous token's admissions that
+        # read the same buffers
+        _lib.check(_lib.load().bigrig_copy_regions(
+            dst, src, size, n, ctypes.c_void_p(self._copy_stream.cuda_stream)), "copy_regions")
+        for (e, _), d in zip(picked, dsts):
+            self.stage[e] = d
+        self.stage_issued += n
+        return n
+
+    def stage_expert(self, e: int, blob) -> bool:
+        """Copy expert e's bytes (pinned host) into a staging buffer ahead of its admission,
+        on the copy stream; ``ensure`` admits a staged expert with a device-to-device copy.
+        Returns False when there is nothing to do (resident, already staged, buffers full)."""
+        e = int(e)
+        if self.g2s[e] >= 0 or e in self.stage or len(self.stage) >= STAGE_MAX:
+            return False
+        src = _as_u8(blob)
+        if src.numel() != self.bytes_per_expert:
+            raise ValueError(f"expert {e}: manifest accounts for {self.bytes_per_expert} bytes "
+                             f"but the region is {src.numel()}.")
+        if self._stage_buf is None:
+            self._stage_buf = torch.empty((STAGE_MAX, self.bytes_per_expert), dtype=torch.uint8,
+                                          device=self.device)
+        dst = self._stage_buf[len(self.stage)]
+        if self.device.type == "cuda":
+            # the copy stream orders this write after the previous token's admission that
+            # read the same buffer
+            with torch.cuda.stream(self._copy_stream):
+                dst.copy_(src, non_blocking=src.is_pinned())
+        else:
+            dst.copy_(src)
+        self.stage[e] = dst
+        self.stage_issued += 1
+        return True
+
     def admit_arrays(self, e: int, arrays, protect=(), _t0=None) -> int:
         """Place bytes (host or device) into a slot; bookkeeping as admit (stream.py:757-780)."""
         if _t0 is None:
@@ -249,6 +332,9 @@ class ExpertPool:
         if self.device.type != "cuda":
             dst.copy_(src.reshape(-1))
             return
+        if self._batch is not None:
+            self._batch.append((dst, src.reshape(-1)))
+            return
         cs = self._copy_stream
         if self._reads_done is not None:
             cs.wait_event(self._reads_done)     # a kernel may still be reading this slot
@@ -260,6 +346,37 @@ class ExpertPool:
             self._copies_done = torch.cuda.Event()
         self._copies_done.record(cs)
         self.admit_bytes += n
+
+    def _begin_writes(self) -> None:
+        """Collect the slot writes of the admissions that follow (one decode step's)."""
+        if self.device.type == "cuda":
+            self._batch = []
+
+    def _flush_writes(self) -> None:
+        """Issue the collected slot writes on the copy stream: one wait on the slab's last
+        reader, one library call with a cudaMemcpyAsync per slot, one completion event."""
+        batch, self._batch = self._batch, None
+        if not batch:
+            return
+        import ctypes
+        from . import _lib
+        cs = self._copy_stream
+        if self._reads_done is not None:
+            cs.wait_event(self._reads_done)     # a kernel may still be reading these slots
+        n = len(batch)
+        dst = (ctypes.c_void_p * n)(*[d.data_ptr() for d, _ in batch])
+        src = (ctypes.c_void_p * n)(*[t.data_ptr() for _, t in batch])
+        size = (ctypes.c_size_t * n)(*[d.numel() for d, _ in batch])
+        _lib.check(_lib.load().bigrig_copy_regions(dst, src, size, n,
+                                                   ctypes.c_void_p(cs.cuda_stream)),
+                   "copy_regions")
+        for _, t in batch:
+            if t.device.type == "cuda":
+                t.record_stream(cs)
+        if self._copies_done is None:
+            self._copies_done = torch.cuda.Event()
+        self._copies_done.record(cs)
+        self.admit_bytes += sum(d.numel() for d, _ in batch)
 
     def ready(self, stream: torch.cuda.Stream | None = None) -> None:
         """Order ``stream`` (default: current) after every admission queued so far.
@@ -294,17 +411,31 @@ class ExpertPool:
         return self.capacity == self.n_experts and self._resident == self.n_experts
 
     def g2s_device(self) -> torch.Tensor:
-        """The expert->slot table on the device, re-uploaded only when residency changed."""
+        """The expert->slot table on the device, re-uploaded only when residency changed
+        (from a small ring of pinned host buffers, each reused once its last upload ran)."""
         if self._g2s_dirty or self._g2s_dev is None:
-            t = torch.from_numpy(self.g2s.copy())
-            if self._g2s_dev is None:
-                self._g2s_dev = t.to(self.device)
-            elif self.device.type == "cuda":
-                # pinned staging from torch's caching host allocator, which keeps the
-                # block alive until the asynchronous copy has consumed it
-                self._g2s_dev.copy_(t.pin_memory(), non_blocking=True)
+            if self._g2s_dev is None or self.device.type != "cuda":
+                t = torch.from_numpy(self.g2s.copy())
+                if self._g2s_dev is None:
+                    self._g2s_dev = t.to(self.device)
+                else:
+                    self._g2s_dev.copy_(t)
             else:
-                self._g2s_dev.copy_(t)
+                ring = getattr(self, "_g2s_ring", None)
+                if ring is None:
+                    ring = self._g2s_ring = [
+                        [torch.empty(self.n_experts, dtype=torch.int32).pin_memory(), None]
+                        for _ in range(4)]
+                    self._g2s_i = 0
+                slot = ring[self._g2s_i]
+                self._g2s_i = (self._g2s_i + 1) % len(ring)
+                if slot[1] is not None:
+                    slot[1].synchronize()
+                else:
+                    slot[1] = torch.cuda.Event()
+                slot[0].numpy()[:] = self.g2s
+                self._g2s_dev.copy_(slot[0], non_blocking=True)
+                slot[1].record()
             self._g2s_dirty = False
         return self._g2s_dev
 
@@ -393,19 +524,124 @@ class StreamingSwitchGLU:
                     f"token evicts an expert it is still using.")
             staged = [int(e) for e in need if int(e) in pool.stage]
             cold = [int(e) for e in need if int(e) not in pool.stage]
-            for e in staged:
-                pool.admit_arrays(e, pool.stage[e], protect=uniq)
-                pool.stage_hits += 1
-            if cold:
-                t0 = time.perf_counter()
-                blobs = self._fetch([(pool.layer, e) for e in cold])
-                self.fetch_seconds += time.perf_counter() - t0
-                for e in cold:
-                    b = blobs[(pool.layer, e)]
-                    self.fetch_bytes += pool.bytes_per_expert
-                    pool.admit(e, b, protect=uniq)
+            pool._begin_writes()
+            try:
+                for e in staged:
+                    pool.admit_arrays(e, pool.stage[e], protect=uniq)
+                    pool.stage_hits += 1
+                if cold:
+                    t0 = time.perf_counter()
+                    blobs = self._fetch([(pool.layer, e) for e in cold])
+                    self.fetch_seconds += time.perf_counter() - t0
+                    for e in cold:
+                        b = blobs[(pool.layer, e)]
+                        self.fetch_bytes += pool.bytes_per_expert
+                        pool.admit(e, b, protect=uniq)
+            finally:
+                pool._flush_writes()
         pool.stage = {}
         return pool.g2s[gi]
+
+    def _readback(self, x2: torch.Tensor, indices: torch.Tensor, k: int):
+        """The routing on the host (the step's synchronisation point, stream.py:1447-1450),
+        plus -- when staging is on -- the next layer's own router's top experts for this
+        token, computed on the device and read back in the same synchronisation
+        (stream.py:1428-1440)."""
+        nxt = self._next
+        if (STAGING and nxt is not None and self._next_gate is not None and x2.shape[0] == 1
+                and not nxt.full):
+            gw, gb = self._next_gate
+            nk = min(STAGE_MAX, nxt.n_experts)
+            pidx, _ = ops.router_topk(ops.router_logits(x2, gw, gb), nk)
+            both = torch.cat([indices.reshape(1, k).to(torch.int32), pidx.reshape(1, nk)], dim=1)
+            t0 = time.perf_counter()
+            host = both.to("cpu").numpy().astype(np.int64)
+            self.sync_seconds += time.perf_counter() - t0
+            return host[:, :k], host[0, k:]
+        t0 = time.perf_counter()
+        gi = indices.reshape(-1, k).to("cpu").numpy().astype(np.int64)
+        self.sync_seconds += time.perf_counter() - t0
+        return gi, None
+
+    def decode_layer(self, x: torch.Tensor, gate_w: torch.Tensor, gate_b: torch.Tensor | None,
+                     k: int, mode: str, norm_topk: bool,
+                     residual: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode token through the whole MoE block over this pool: the router's top-k
+        is computed and read back (with, when staging is on, the next layer's prediction
+        from the same two launches: one logits call over both routers' weights and one top-k
+        over the two rows), made resident, then one library call computes router, experts
+        and combine (``bigrig_moe_layer``, whose routing is bit-identical to the one read
+        back).  Returns out [1, H] = residual + sum_j score * y."""
+        pool = self._pool
+        H = x.shape[-1]
+        if k > pool.capacity:
+            raise ValueError(
+                f"layer {pool.layer}: top-k is {k} but the pool holds {pool.capacity}. A single "
+                f"token cannot be served, so no capacity below top-k is ever valid.")
+        x2 = x.reshape(-1, H)
+        if x2.dtype != torch.bfloat16:
+            x2 = x2.to(torch.bfloat16)
+        x2 = x2.contiguous()
+        nxt = self._next
+        E = pool.n_experts
+        pred = None
+        if (STAGING and nxt is not None and self._next_gate is not None and not nxt.full
+                and nxt.n_experts == E and k <= E):
+            w2, b2 = self._route_pair(gate_w, gate_b)
+            idx2, _ = ops.router_topk(ops.router_logits(x2, w2, b2).reshape(2, E), k, mode, norm_topk)
+            t0 = time.perf_counter()
+            host = idx2.to("cpu").numpy().astype(np.int64)        # the host readback
+            self.sync_seconds += time.perf_counter() - t0
+            gi, pred = host[:1], host[1]
+        else:
+            idx, _ = ops.router_topk(ops.router_logits(x2, gate_w, gate_b), k, mode, norm_topk)
+            t0 = time.perf_counter()
+            gi = idx.to("cpu").numpy().astype(np.int64)           # the host readback
+            self.sync_seconds += time.perf_counter() - t0
+        self._count_routing(gi.reshape(-1))
+        self.ensure(gi)
+        pool.ready()
+        scratch = getattr(self, "_layer_scratch", None)
+        if scratch is None or scratch[0].shape[1] != k or scratch[0].device != x2.device:
+            scratch = self._layer_scratch = (
+                torch.empty(1, k, dtype=torch.int32, device=x2.device),
+                torch.empty(1, k, dtype=torch.float32, device=x2.device))
+        out, _, _ = ops.moe_layer(x2, gate_w, gate_b, k, pool.slab, pool.layout, pool.n_experts,
+                                  mode, norm_topk, g2s=pool.g2s_device(), residual=residual,
+                                  indices=scratch[0], scores=scratch[1], workspace=self.workspace)
+        pool.mark_read()
+        if pred is not None:
+            self._speculate(pred)
+        return out
+
+    def _route_pair(self, gate_w: torch.Tensor, gate_b: torch.Tensor | None):
+        """This layer's and the next layer's router weights stacked [2E, H] (and biases),
+        built once."""
+        key = (gate_w.data_ptr(), None if gate_b is None else gate_b.data_ptr())
+        if getattr(self, "_pair_key", None) != key:
+            ngw, ngb = self._next_gate
+            E = gate_w.shape[0]
+            dev = gate_w.device
+            zb = torch.zeros(E, dtype=torch.float32, device=dev)
+            self._pair_w = torch.cat([gate_w, ngw]).contiguous()
+            self._pair_b = torch.cat([gate_b if gate_b is not None else zb,
+                                      ngb if ngb is not None else zb]).contiguous()
+            self._pair_key = key
+        return self._pair_w, self._pair_b
+
+    def _speculate(self, predicted) -> None:
+        """Stage the experts the next layer is likely to want while this layer computes
+        (stream.py:1036-1072): those not resident in the next pool, at most STAGE_MAX, copied
+        from pinned host DRAM behind this layer's own admissions.  Nothing here can change an
+        answer: the next layer's ``ensure`` still admits exactly what its router selected, a
+        staged one by a device-to-device copy and any other from the host."""
+        nxt = self._next
+        want = [int(e) for e in predicted if nxt.g2s[int(e)] < 0 and int(e) not in nxt.stage]
+        want = want[:max(0, STAGE_MAX - len(nxt.stage))]
+        if not want:
+            return
+        blobs = self._fetch([(nxt.layer, e) for e in want])
+        self.pred_issued += nxt.stage_experts([(e, blobs[(nxt.layer, e)]) for e in want])
 
     def _fetch(self, keys) -> dict:
         local = getattr(self._fetcher, "fetch_local", None)
@@ -448,14 +684,16 @@ class StreamingSwitchGLU:
             raise ValueError(
                 f"layer {pool.layer}: top-k is {k} but the pool holds {pool.capacity}. A single "
                 f"token cannot be served, so no capacity below top-k is ever valid.")
-        t0 = time.perf_counter()
-        gi = indices.reshape(-1, k).to("cpu").numpy().astype(np.int64)   # the host readback
-        self.sync_seconds += time.perf_counter() - t0
+        gi, pred = self._readback(x2, indices, k)
         self._count_routing(gi.reshape(-1))
         if len(np.unique(gi)) <= pool.capacity:
             self.ensure(gi)
             idx2 = indices.reshape(-1, k).to(torch.int32).contiguous()
             y = self._run(x2, idx2, pool.g2s_device())
+            if pred is not None:
+                # after this layer's kernels are queued: the host work of staging overlaps
+                # them instead of delaying their launch
+                self._speculate(pred)
             return y.reshape(*lead, k, H)
         # More distinct experts than slots: expert-sorted spans of <= C experts, each made
         # resident and computed before the next span may evict it (stream.py:1509-1561).
@@ -612,6 +850,7 @@ class StreamHandle:
     def reset_stats(self):
         for p in self.pools:
             p.hits = p.misses = 0
+            p.stage_issued = p.stage_hits = 0
             p.admit_seconds = 0.0
             p.admit_bytes = 0
         for m in self.mods:
@@ -624,6 +863,8 @@ class StreamHandle:
         """Release every slab explicitly (stream.py:2160-2191)."""
         for p in self.pools:
             p.slab = None
+            p._stage_buf = None
+            p.stage = {}
             p._built = False
         for m in self.mods:
             m._pool = None
@@ -644,6 +885,11 @@ def attach(blocks, store, capacity, policy: str = "lfuda", full_layers=(), warm=
     """
     full = set(full_layers or ())
     pools, mods = [], []
+    dev = torch.device(device) if device is not None else (
+        torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else None)
+    # one copy stream for every layer: a layer's staging of the next layer's experts queues
+    # behind its own admissions, and the next layer's admission from staging behind both
+    copy_stream = torch.cuda.Stream(device=dev) if dev is not None and dev.type == "cuda" else None
     for blk in blocks:
         E = blk.n_experts
         if blk.layer in full:
@@ -653,11 +899,18 @@ def attach(blocks, store, capacity, policy: str = "lfuda", full_layers=(), warm=
                 else int(capacity)
         C = max(1, min(E, C))
         pool = ExpertPool(blk.layer, None, E, C, blk.spec, policy=policy, quant=blk.quant,
-                          device=device).build()
+                          device=device, copy_stream=copy_stream).build()
         mod = StreamingSwitchGLU(pool, store)
         blk.switch = mod
         pools.append(pool)
         mods.append(mod)
+    # every streamed layer knows the next one's router (stream.py:1895-1911)
+    for j, mod in enumerate(mods[:-1]):
+        gw = getattr(blocks[j + 1], "gate_w", None)
+        if gw is not None:
+            mod._next = pools[j + 1]
+            mod._next_gate = (gw, getattr(blocks[j + 1], "gate_b", None))
+            mod._pred_m = STAGE_MAX
     h = StreamHandle(blocks, pools, mods, store, full_layers=sorted(full))
     h.warm(warm if warm is not True else "auto")
     for m in mods:

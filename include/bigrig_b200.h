@@ -197,6 +197,14 @@ BIGRIG_API int bigrig_moe_layer(const void* x, const void* gate_w, const float* 
  * with a synchronous read on `stream`; resets it to 0.  For tests and debugging. */
 BIGRIG_API int bigrig_workspace_errors(void* workspace, int32_t* out, void* stream);
 
+/* n asynchronous copies on `stream`, one cudaMemcpyAsync each: dst[i] <- src[i], bytes[i]
+ * (host or device pointers; pinned host sources stay asynchronous).  The pool's admissions
+ * of one step in a single call -- replaces the per-expert slot writes of ExpertPool.admit /
+ * admit_arrays (stream.py:692-705, 757-780) so that a decode step pays one host call per
+ * layer instead of one per expert. */
+BIGRIG_API int bigrig_copy_regions(void* const* dst, const void* const* src, const size_t* bytes,
+                                   int n, void* stream);
+
 /* bigrig_switch_glu for callers that cannot allocate device memory when they call: a
  * process whose device memory is carved up once at start-up by another allocator, or a
  * caller in a latency-critical loop where cudaMalloc (which synchronises the device) is
