@@ -60,6 +60,17 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def _bf16_sustained():
+    """The sustained bf16 tensor peak (a kernel timed inside a long step), TFLOP/s."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"]), "measured sustained"
+    return 1400.0, "fallback sustained"
+
+
 # ------------------------------------------------------------------ clocks
 class Clocks:
     """nvidia-smi sampling every 200 ms while the timed region runs."""
@@ -167,15 +178,6 @@ def algorithmic_layer_bytes(T: int, distinct: int) -> int:
     bpe = bytes_per_expert(make_spec(c["hidden"], c["inter"], c["bits"], c["group_size"],
                                      c["scale_dtype"]))
     return distinct * bpe + c["experts"] * c["hidden"] * 2 + T * c["hidden"] * 2 * 2
-
-
-def gate_up_bytes(T: int, distinct: int) -> int:
-    """Algorithmic bytes of one gemv_gate_up launch: the routed experts' gate and up codes,
-    scales and biases, the x rows in and the h rows out."""
-    c = CFG
-    H, I = c["hidden"], c["inter"]
-    per = 2 * (I * H * c["bits"] // 8 + 2 * I * (H // c["group_size"]) * 2)
-    return distinct * per + T * H * 2 + T * c["top_k"] * I * 2
 
 
 # ------------------------------------------------------------------ CPU restatement
@@ -355,7 +357,7 @@ def main() -> None:
     handle.reset_stats()
     barrier()
     counts0 = _lib.launch_counts()
-    _lib.timing_enable(["gate_up"])
+    _lib.timing_enable(["decode_layer"])
     clocks = Clocks(local)
     clocks.start()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -369,7 +371,7 @@ def main() -> None:
     clk = clocks.stop()
     _lib.timing_enable([])
     counts1 = _lib.launch_counts()
-    gu_ms, gu_n = _lib.timing_read("gate_up")
+    gu_ms, gu_n = _lib.timing_read("decode_layer")
     ms = max_over_ranks(t0.elapsed_time(t1))
     value = world * K / (ms / 1e3)
     st = handle.stats()
@@ -439,6 +441,37 @@ def main() -> None:
         extras["resident_ms_per_token"] = rms / K
         del graph, yout
 
+        # ---- resident prefill: the same prompt, layer-major, every expert in HBM -- the
+        # tcgen05 grouped GEMM with nothing to fetch; its kernels timed with CUDA events
+        res_layers = [(lambda h, b=b: b(h, residual=h)) for b in blocks]
+        layered.prefill(res_layers, layered.chunks(prompt[:c["prefill_chunk"]], c["prefill_chunk"]))
+        barrier()
+        _lib.timing_enable(["gemm_gate_up", "gemm_down"])
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("resident_prefill")
+        p0.record()
+        layered.prefill(res_layers, layered.chunks(prompt, c["prefill_chunk"]))
+        p1.record()
+        torch.cuda.nvtx.range_pop()
+        barrier()
+        _lib.timing_enable([])
+        gu_ms_p, _ = _lib.timing_read("gemm_gate_up")
+        dn_ms_p, _ = _lib.timing_read("gemm_down")
+        rp_ms = max_over_ranks(p0.elapsed_time(p1))
+        flops = 6.0 * c["prompt"] * c["top_k"] * c["hidden"] * c["inter"] * c["layers"]
+        gemm_s = (gu_ms_p + dn_ms_p) / 1e3
+        bf16_peak, bf16_kind = _bf16_sustained()
+        extras["resident_prefill_tok_s"] = world * c["prompt"] / (rp_ms / 1e3)
+        extras["prefill_gemm"] = {
+            "kernel": "grouped_gemm_kernel", "bound": "tensor",
+            "achieved": flops / gemm_s / 1e12 if gemm_s > 0 else None, "unit": "TFLOP/s",
+            "peak": bf16_peak, "peak_kind": bf16_kind,
+            "frac": (flops / gemm_s / 1e12) / bf16_peak if gemm_s > 0 else None,
+            "flops": flops, "gemm_ms": gemm_s * 1e3, "prefill_ms": rp_ms,
+            "note": "6 x prompt x top_k x hidden x inter x layers over the gate/up + down "
+                    "GEMM launch time of a 2048-token layer-major prefill with every expert "
+                    "resident"}
+
     # ---- CPU restatement on rank 0 at N=1 (bounded sample)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -450,9 +483,9 @@ def main() -> None:
 
     hbm_peak, _, peak_kind = _peaks()
     gu_avg_ms = gu_ms / max(1, gu_n)
-    gu_bytes = gate_up_bytes(1, c["top_k"])
+    gu_bytes = algorithmic_layer_bytes(1, c["top_k"])
     achieved = gu_bytes / (gu_avg_ms / 1e3) / 1e9 if gu_n else None
-    traffic = _traffic().get("gemv_gate_up_kernel")
+    traffic = _traffic().get("decode_layer_kernel")
     if "moe_layer_hbm_gbs" in extras:
         # the persistent one-token layer kernel of the resident decode: algorithmic bytes of
         # a layer over the graph's time per layer (which includes the launch gap)
@@ -480,7 +513,7 @@ def main() -> None:
             "e2e": e2e,
             "gpu_launches": launches,
             "launches_by_kernel": {k: counts1[k] - counts0[k] for k in counts1},
-            "roofline": {"kernel": "gemv_gate_up_kernel", "bound": "hbm", "achieved": achieved,
+            "roofline": {"kernel": "decode_layer_kernel", "bound": "hbm", "achieved": achieved,
                          "peak": hbm_peak, "unit": "GB/s",
                          "frac": (achieved / hbm_peak) if achieved else None,
                          "peak_kind": peak_kind, "traffic": traffic,
