@@ -442,35 +442,48 @@ def main() -> None:
         del graph, yout
 
         # ---- resident prefill: the same prompt, layer-major, every expert in HBM -- the
-        # tcgen05 grouped GEMM with nothing to fetch; its kernels timed with CUDA events
+        # tcgen05 grouped GEMM with nothing to fetch; its kernels timed with CUDA events.
+        # Twice: in the reference's 512-token chunks, and token-wise (every chunk of a
+        # layer in one call: the same rows and results, all of an expert's rows at once).
         res_layers = [(lambda h, b=b: b(h, residual=h)) for b in blocks]
-        layered.prefill(res_layers, layered.chunks(prompt[:c["prefill_chunk"]], c["prefill_chunk"]))
-        barrier()
-        _lib.timing_enable(["gemm_gate_up", "gemm_down"])
-        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.nvtx.range_push("resident_prefill")
-        p0.record()
-        layered.prefill(res_layers, layered.chunks(prompt, c["prefill_chunk"]))
-        p1.record()
-        torch.cuda.nvtx.range_pop()
-        barrier()
-        _lib.timing_enable([])
-        gu_ms_p, _ = _lib.timing_read("gemm_gate_up")
-        dn_ms_p, _ = _lib.timing_read("gemm_down")
-        rp_ms = max_over_ranks(p0.elapsed_time(p1))
         flops = 6.0 * c["prompt"] * c["top_k"] * c["hidden"] * c["inter"] * c["layers"]
-        gemm_s = (gu_ms_p + dn_ms_p) / 1e3
         bf16_peak, bf16_kind = _bf16_sustained()
+
+        def resident_prefill(token_wise):
+            for _ in range(2):
+                layered.prefill(res_layers, layered.chunks(prompt, c["prefill_chunk"]),
+                                token_wise=token_wise)
+            barrier()
+            _lib.timing_enable(["gemm_gate_up", "gemm_down"])
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.nvtx.range_push("resident_prefill_tw" if token_wise else "resident_prefill")
+            p0.record()
+            layered.prefill(res_layers, layered.chunks(prompt, c["prefill_chunk"]),
+                            token_wise=token_wise)
+            p1.record()
+            torch.cuda.nvtx.range_pop()
+            barrier()
+            _lib.timing_enable([])
+            gu_ms_p, _ = _lib.timing_read("gemm_gate_up")
+            dn_ms_p, _ = _lib.timing_read("gemm_down")
+            rp_ms = max_over_ranks(p0.elapsed_time(p1))
+            gemm_s = max_over_ranks(gu_ms_p + dn_ms_p) / 1e3
+            achieved = flops / gemm_s / 1e12 if gemm_s > 0 else None
+            return rp_ms, {
+                "kernel": "grouped_gemm_kernel", "bound": "tensor",
+                "achieved": achieved, "unit": "TFLOP/s", "peak": bf16_peak, "peak_kind": bf16_kind,
+                "frac": achieved / bf16_peak if achieved else None,
+                "flops": flops, "gemm_ms": gemm_s * 1e3, "prefill_ms": rp_ms,
+                "gate_up_ms": gu_ms_p, "down_ms": dn_ms_p,
+                "note": "6 x prompt x top_k x hidden x inter x layers over the gate/up + down "
+                        "GEMM launch time of a 2048-token layer-major prefill with every expert "
+                        "resident, " + ("token-wise (one call per layer)" if token_wise else
+                                        f"in chunks of {c['prefill_chunk']}")}
+
+        rp_ms, extras["prefill_gemm"] = resident_prefill(False)
         extras["resident_prefill_tok_s"] = world * c["prompt"] / (rp_ms / 1e3)
-        extras["prefill_gemm"] = {
-            "kernel": "grouped_gemm_kernel", "bound": "tensor",
-            "achieved": flops / gemm_s / 1e12 if gemm_s > 0 else None, "unit": "TFLOP/s",
-            "peak": bf16_peak, "peak_kind": bf16_kind,
-            "frac": (flops / gemm_s / 1e12) / bf16_peak if gemm_s > 0 else None,
-            "flops": flops, "gemm_ms": gemm_s * 1e3, "prefill_ms": rp_ms,
-            "note": "6 x prompt x top_k x hidden x inter x layers over the gate/up + down "
-                    "GEMM launch time of a 2048-token layer-major prefill with every expert "
-                    "resident"}
+        rp_tw, extras["prefill_gemm_token_wise"] = resident_prefill(True)
+        extras["resident_prefill_token_wise_tok_s"] = world * c["prompt"] / (rp_tw / 1e3)
 
     # ---- CPU restatement on rank 0 at N=1 (bounded sample)
     cpu = None

@@ -98,6 +98,7 @@ struct Workspace {
   int32_t* seg_start;
   int32_t* num_seg;
   uint16_t* h;        // [P, I] bf16, expert-sorted rows
+  uint16_t* xp;       // [P, H] the grouped GEMM's token operand: x rows in expert order
   uint16_t* y;        // [P, H] bf16, (token, k) order (moe_forward only)
   int32_t* indices;   // [P] (moe_forward when the caller passes none)
   float* scores;      // [P]
@@ -125,6 +126,7 @@ size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Wor
   ws.seg_start = static_cast<int32_t*>(take((E + 1) * sizeof(int32_t)));
   ws.num_seg = static_cast<int32_t*>(take(sizeof(int32_t)));
   ws.h = static_cast<uint16_t*>(take(P * L.inter * sizeof(uint16_t)));
+  ws.xp = static_cast<uint16_t*>(take(P * L.hidden * sizeof(uint16_t)));
   ws.y = static_cast<uint16_t*>(take(P * L.hidden * sizeof(uint16_t)));
   ws.indices = static_cast<int32_t*>(take(P * sizeof(int32_t)));
   ws.scores = static_cast<float*>(take(P * sizeof(float)));
@@ -229,9 +231,9 @@ int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, c
   const bool gemm = path == BIGRIG_PATH_GEMM ||
                     ((path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_CHAIN) && P >= g_gemm_min_rows.load() * (P < E ? P : E));
   if (gemm) {
-    const int bn = gemm_token_tile(T, k, E);
-    if (int rc = launch_gemm_gate_up(x, rv, slab, L, ws.h, bn, s)) return rc;
-    return launch_gemm_down(ws.h, rv, slab, L, y, bn, s);
+    const int mean = gemm_mean_rows(T, k, E);
+    if (int rc = launch_gemm_gate_up(x, rv, slab, L, ws.h, ws.xp, T, mean, s)) return rc;
+    return launch_gemm_down(ws.h, rv, slab, L, y, mean, s);
   }
   if (int rc = launch_gemv_gate_up(x, rv, slab, L, ws.h, s)) return rc;
   return launch_gemv_down(ws.h, rv, slab, L, y, s);

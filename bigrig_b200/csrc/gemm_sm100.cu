@@ -10,34 +10,46 @@
 //
 // Swap-AB: D[feature, token] = W[feature, K] . X[token, K]^T, so the expert's
 // output features fill the 128-row M of the MMA and the few tokens an expert gets
-// are the N dimension (a multiple of 16 up to 256).  Both operands are K-major
-// bf16 tiles of 64 K-elements in 128-byte-swizzled shared memory, one swizzle
-// atom per 8 rows, so each of the four K=16 MMAs of a stage starts 32 bytes
-// further into the atom.
+// are the N dimension (a multiple of 16 up to 256).  The weight operand A is
+// dequantised into tensor memory (one row per TMEM lane); the token operand B is a
+// K-major tile of 64 K-elements in 128-byte-swizzled shared memory, so each of the
+// four K=16 MMAs of an iteration starts 32 bytes further into the swizzle atom.
 //
-// Warp roles in a CTA of 288 threads, persistent over (expert, feature tile,
-// token tile) work items:
-//   warps 0-7  producers: load codes, scales, biases, dequantise
-//              w = bf16(f32(scale) * q + f32(bias)) in registers and store the A
-//              tile; gather the routed token rows (B tile); fence the generic
-//              proxy against the async proxy; arrive on the stage's full barrier.
-//              Warps 0-3 then run the epilogue from TMEM (lane quarter = warp).
-//   warp 8     MMA issuer: one elected lane waits for a full stage, issues
-//              tcgen05.mma, and commits the stage back to its empty barrier and
-//              the finished tile to the accumulator barrier.
-// Every mbarrier wait is bounded: past the limit the CTA records an error,
-// raises a shared abort flag so every other wait returns at once, drains the
-// MMAs it issued, frees its TMEM and returns.
+// Warp roles in a CTA of 448 threads, persistent over (expert, feature tile, token
+// slice) work items:
+//   warp 13    loader: one lane issues every copy -- a tile's scale and bias blocks
+//              (one bulk copy each, they are contiguous), the codes as TMA boxes of
+//              128 rows x 128 bytes (four 4-bit or two 8-bit iterations per box) and
+//              the token rows as one TMA box per iteration -- each completing on its
+//              ring slot's mbarrier by transaction count.
+//   warps 0-7  producers: dequantise their row's codes from the swizzled box into
+//              registers (w = OT(s * q + b), OT the operand type) and write them to
+//              the A slot in TMEM with tcgen05.st; arrive on the slot's full barrier.
+//   warp 12    MMA issuer: one lane waits for an A slot and a B slot, issues
+//              tcgen05.mma (A from TMEM, B from shared memory), and commits both
+//              slots back to their empty barriers and a finished tile to its
+//              accumulator barrier.
+//   warps 8-11 epilogue: TMEM accumulators -> silu(gate) * up (h, expert-sorted
+//              rows) or the down output scattered to (token, k) order.
+// Every mbarrier wait is bounded: past the limit the CTA records an error, raises
+// a shared abort flag so every other wait returns at once, drains the MMAs it
+// issued and the copies in flight, frees its TMEM and returns.
+#include <cuda.h>
+
 #include "gemv_common.cuh"
 
 namespace bigrig {
 namespace sm100 {
 
 constexpr int kProducerWarps = 8;
-constexpr int kThreads = (kProducerWarps + 1) * 32;
+constexpr int kProducerThreads = kProducerWarps * 32;
+static_assert(kProducerThreads == 256, "one producer thread per A-tile row and matrix");
+constexpr int kEpilogueWarps = 8;          // two per TMEM lane quarter
+constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
+constexpr int kLoaderWarp = kMmaWarp + 1;
+constexpr int kThreads = (kLoaderWarp + 1) * 32;
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;                 // one 128-byte swizzle atom of bf16 per row
-constexpr int kATile = kBlockM * kBlockK * 2;
 constexpr uint32_t kSpinLimit = 1u << 22;   // a few seconds of polling before giving up
 
 // ------------------------------------------------------------------ PTX helpers
@@ -114,21 +126,24 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16: bf16 x bf16 -> f32, both operands K-major.
-__host__ __device__ constexpr uint32_t instr_desc(int M, int N) {
+// Instruction descriptor, kind::f16: f16 x f16 or bf16 x bf16 -> f32, both K-major.
+__host__ __device__ constexpr uint32_t instr_desc(int M, int N, int ot = BIGRIG_BF16) {
+  const uint32_t fmt = ot == BIGRIG_F16 ? 0u : 1u;  // 0 f16, 1 bf16 (A and B alike)
   return (1u << 4)                                   // D format f32
-         | (1u << 7)                                 // A format bf16
-         | (1u << 10)                                // B format bf16
+         | (fmt << 7)                                // A format
+         | (fmt << 10)                               // B format
          | (static_cast<uint32_t>(N >> 3) << 17)     // N
          | (static_cast<uint32_t>(M >> 4) << 24);    // M
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
-                                         uint32_t accumulate) {
+// A from tensor memory (128 lanes = rows, K in 32-bit columns of operand pairs), B from
+// a shared-memory descriptor.
+__device__ __forceinline__ void mma_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t db,
+                                           uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -136,6 +151,23 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                    smem_u32(bar))
                : "memory");
 }
+
+// 32 lanes x 16 columns of 32 bits from TMEM (this warp's lane quarter), not waited for.
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// silu(g) = g / (1 + e^-g) with the fast exponential and division: h is rounded to a
+// 16-bit type right after, far above their error.
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 // 32 lanes x 8 columns of fp32 from TMEM (this warp's lane quarter).
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
@@ -166,73 +198,314 @@ __device__ __forceinline__ uint32_t swz(int r, int j) {
 // (tile chunks jbase..jbase+3); 8-bit: 16 codes -> 32 bytes (jbase, jbase+1).
 // w = bf16(fma(s, q, b)) with q recovered exactly through the 2^23 mantissa trick and
 // the scale pre-divided by the code field's power of 16 (or 256), which is exact.
-template <int BITS>
-__device__ __forceinline__ void dequant_chunk(uint8_t* tile, int row, int jbase, uint4 w, float s,
-                                              float b) {
-  constexpr float M = 8388608.f;
-  constexpr uint32_t E23 = 0x4B000000u;
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Packed-pair arithmetic in the operand type OT (BIGRIG_F16 or BIGRIG_BF16), one rounding.
+template <int OT>
+__device__ __forceinline__ uint32_t x2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (OT == BIGRIG_F16) asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+template <int OT>
+__device__ __forceinline__ uint32_t x2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  if constexpr (OT == BIGRIG_F16) asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  else asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Tensor-core operand type of a format: the 4-bit path computes in the scale dtype (as
+// the reference's fp16 and bf16 models do); the 8-bit path in bf16.
+__host__ __device__ constexpr int operand_type(int bits, int sdt) {
+  return bits == 4 && sdt == BIGRIG_F16 ? BIGRIG_F16 : BIGRIG_BF16;
+}
+
+// K order inside every 8-element block of the 4-bit path's operands: slot 2i holds
+// element i and slot 2i+1 element i+4, so that one mask of a 32-bit code word yields
+// the pair of codes (i, i+4).  A dot product over K is unchanged when both operands
+// carry the same order; the token operand is permuted to match.
+__host__ __device__ constexpr int k8_slot(int i) { return i < 4 ? 2 * i : 2 * (i - 4) + 1; }
+
+// 4-bit: one 16-byte chunk (32 codes) of a row -> 16 words of OT pairs (o[0..15], K
+// order as k8_slot says).  The pair 0x6400 | n (fp16) or 0x4300 | n (bf16) is the value
+// 1024 + n or 128 + n exactly; subtracting the base leaves q exactly, and one packed fma
+// gives w = OT(s * q + b) with a single rounding, s and b being the format's own scale
+// and bias (exact in OT).
+template <int OT>
+__device__ __forceinline__ void dequant_chunk4(uint4 w, uint32_t s2, uint32_t b2, uint32_t* o) {
+  constexpr uint32_t base = OT == BIGRIG_F16 ? 0x64006400u : 0x43004300u, m = 0x000F000Fu;
   const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-  if constexpr (BITS == 4) {
-    const float s1 = s * 0.0625f, s2 = s * 0.00390625f, s3 = s * 0.000244140625f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {          // word i: codes 8i..8i+7 -> 16 bytes of bf16
-      const uint32_t lo = ws[i], hi = ws[i] >> 16;
-      const float q0 = __uint_as_float((lo & 0x000Fu) | E23) - M;
-      const float q1 = __uint_as_float((lo & 0x00F0u) | E23) - M;
-      const float q2 = __uint_as_float((lo & 0x0F00u) | E23) - M;
-      const float q3 = __uint_as_float((lo & 0xF000u) | E23) - M;
-      const float q4 = __uint_as_float((hi & 0x000Fu) | E23) - M;
-      const float q5 = __uint_as_float((hi & 0x00F0u) | E23) - M;
-      const float q6 = __uint_as_float((hi & 0x0F00u) | E23) - M;
-      const float q7 = __uint_as_float((hi & 0xF000u) | E23) - M;
-      uint4 o;
-      o.x = pack_bf16x2(fmaf(s, q0, b), fmaf(s1, q1, b));
-      o.y = pack_bf16x2(fmaf(s2, q2, b), fmaf(s3, q3, b));
-      o.z = pack_bf16x2(fmaf(s, q4, b), fmaf(s1, q5, b));
-      o.w = pack_bf16x2(fmaf(s2, q6, b), fmaf(s3, q7, b));
-      *reinterpret_cast<uint4*>(tile + swz(row, jbase + i)) = o;
-    }
-  } else {
-    const float s1 = s * 0.00390625f;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {          // words 2i, 2i+1: 8 codes -> 16 bytes
-      const uint32_t a = ws[2 * i], c = ws[2 * i + 1];
-      uint4 o;
-      o.x = pack_bf16x2(fmaf(s, __uint_as_float((a & 0x00FFu) | E23) - M, b),
-                        fmaf(s1, __uint_as_float((a & 0xFF00u) | E23) - M, b));
-      o.y = pack_bf16x2(fmaf(s, __uint_as_float(((a >> 16) & 0x00FFu) | E23) - M, b),
-                        fmaf(s1, __uint_as_float(((a >> 16) & 0xFF00u) | E23) - M, b));
-      o.z = pack_bf16x2(fmaf(s, __uint_as_float((c & 0x00FFu) | E23) - M, b),
-                        fmaf(s1, __uint_as_float((c & 0xFF00u) | E23) - M, b));
-      o.w = pack_bf16x2(fmaf(s, __uint_as_float(((c >> 16) & 0x00FFu) | E23) - M, b),
-                        fmaf(s1, __uint_as_float(((c >> 16) & 0xFF00u) | E23) - M, b));
-      *reinterpret_cast<uint4*>(tile + swz(row, jbase + i)) = o;
-    }
+  for (int i = 0; i < 4; ++i) {            // word i: codes 8i..8i+7 -> words 4i..4i+3
+    const uint32_t c = ws[i];
+    o[4 * i + 0] = x2_fma<OT>(x2_sub<OT>((c & m) | base, base), s2, b2);
+    o[4 * i + 1] = x2_fma<OT>(x2_sub<OT>(((c >> 4) & m) | base, base), s2, b2);
+    o[4 * i + 2] = x2_fma<OT>(x2_sub<OT>(((c >> 8) & m) | base, base), s2, b2);
+    o[4 * i + 3] = x2_fma<OT>(x2_sub<OT>(((c >> 12) & m) | base, base), s2, b2);
   }
 }
 
+// 8-bit: one 16-byte chunk (16 codes) -> 8 words of bf16 pairs, natural K order.
+// w = bf16(fma(s, q, b)) in fp32, q recovered exactly through the 2^23 mantissa trick
+// with the scale pre-divided by 256 for the high byte (exact).
+__device__ __forceinline__ void dequant_chunk8(uint4 w, float s, float b, uint32_t* o) {
+  constexpr float M = 8388608.f;
+  constexpr uint32_t E23 = 0x4B000000u;
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  const float s1 = s * 0.00390625f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {            // word i: codes 4i..4i+3 -> words 2i, 2i+1
+    const uint32_t a = ws[i];
+    o[2 * i] = pack_bf16x2(fmaf(s, __uint_as_float((a & 0x00FFu) | E23) - M, b),
+                           fmaf(s1, __uint_as_float((a & 0xFF00u) | E23) - M, b));
+    o[2 * i + 1] = pack_bf16x2(fmaf(s, __uint_as_float(((a >> 16) & 0x00FFu) | E23) - M, b),
+                               fmaf(s1, __uint_as_float(((a >> 16) & 0xFF00u) | E23) - M, b));
+  }
+}
+
+// 32 lanes x N 32-bit columns into TMEM (this warp's lane quarter), N = 16 or 32.
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t* v) {
+  if constexpr (N == 16) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+  } else {
+    static_assert(N == 32, "tmem_st: 16 or 32 columns");
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+        "%29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+        "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+        "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+  }
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// fp32 pair -> fp16 pair, saturating at the largest finite fp16 (no infinities).
+__device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// xs[p] = x[order[p] / k] for the P expert-sorted pairs: the gate/up token operand as
+// contiguous rows for its TMA boxes.  The 4-bit path also takes it to the operand type
+// OT (bf16 -> fp16 is exact inside the fp16 range and saturates outside it) and to the
+// k8_slot order inside every 8-element block.
+template <int OT, bool K8>
+__global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ order,
+                                   int k, int P, int chunks_per_row, uint4* __restrict__ xs) {
+  const int64_t n = static_cast<int64_t>(P) * chunks_per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int p = static_cast<int>(i / chunks_per_row), c = static_cast<int>(i % chunks_per_row);
+    uint4 v = x[static_cast<int64_t>(order[p] / k) * chunks_per_row + c];
+    if constexpr (OT == BIGRIG_F16) {
+      uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        w[j] = pack_f16x2_sat(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
+    }
+    if constexpr (K8) {
+      uint4 o;
+      o.x = __byte_perm(v.x, v.z, 0x5410);   // (e0, e4)
+      o.y = __byte_perm(v.x, v.z, 0x7632);   // (e1, e5)
+      o.z = __byte_perm(v.y, v.w, 0x5410);   // (e2, e6)
+      o.w = __byte_perm(v.y, v.w, 0x7632);   // (e3, e7)
+      v = o;
+    }
+    xs[i] = v;
+  }
+}
+
+// ------------------------------------------------------------------ TMA
+// Tiled tensor loads (no multicast) into this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], "
+      "[%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tm, int x, int y, int z,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], "
+      "[%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t lds16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// ------------------------------------------------------------------ pipeline shape
+// Rings (shared memory unless noted):
+//   codes : RS slots of NMAT TMA boxes, 128 rows x 128 bytes each (F iterations of
+//           one row's codes), 128-byte swizzled
+//   B     : SB slots of BN token rows x 64 operands, 128-byte swizzled (one iteration)
+//   scales: NSB per-tile buffers of the tile's scale and bias blocks (NMAT x 2 x 128
+//           rows x K / group_size)
+//   A     : (TMEM) SA slots of NMAT dequantised 128 x 64 tiles, one row per TMEM lane,
+//           written by the producers with tcgen05.st and read by the MMA from tensor
+//           memory, so the weights never make a round trip through shared memory
+// The accumulators take the TMEM columns after the A slots.  RS, SB and NSB are
+// chosen at launch (the scale buffer's size depends on K).
+//
+// Producer thread mapping: warp w owns TMEM lane quarter w % 4, i.e. rows
+// 32 (w % 4) + lane of the tile; gate/up warps 0-3 take the gate rows and 4-7 the up
+// rows (every code chunk of the row), down warps 0-3 the first and 4-7 the second half
+// of each row's code chunks of an iteration.
+template <int MODE, int BN, int BITS>
+struct GemmShape {
+  static constexpr int NMAT = MODE == 0 ? 2 : 1;
+  static constexpr int ROW_BYTES = kBlockK * BITS / 8;            // one row's codes per iteration
+  static constexpr int F = 128 / ROW_BYTES;                       // iterations per code box
+  static constexpr int CPI = ROW_BYTES / 16;                      // 16-byte chunks per iteration
+  static constexpr int JT = MODE == 0 ? CPI : CPI / 2;            // chunks per thread
+  static constexpr int WPC = 64 / BITS;                           // A words per code chunk
+  static constexpr int AW = JT * WPC;                             // A words per thread
+  static constexpr int CODE_BOX = kBlockM * 128;
+  static constexpr int CODE_SLOT = NMAT * CODE_BOX;
+  static constexpr int B_BYTES = BN * kBlockK * 2;
+  // TMEM: SA A slots of NMAT x 32 columns, then NBUF accumulators of NMAT x BN columns.
+  // Two accumulators (the epilogue drains one while the MMA fills the other) with 3
+  // or 2 A slots where they fit, else one accumulator.
+  static constexpr int ACC_COLS = NMAT * BN;
+  static constexpr int SA_MAX = MODE == 0 ? 3 : 4;
+  static constexpr int SA = SA_MAX * NMAT * 32 + 2 * ACC_COLS <= 512 ? SA_MAX
+                          : 2 * NMAT * 32 + 2 * ACC_COLS <= 512 ? 2 : SA_MAX;
+  static constexpr int A_COLS = SA * NMAT * 32;
+  static constexpr int NBUF = A_COLS + 2 * ACC_COLS <= 512 ? 2 : 1;  // accumulator buffers
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int kMeta = 2048;                              // barriers, flags, tile prefix
+  static constexpr int kLimit = 227 * 1024;
+  static constexpr size_t smem(int rs, int sb, int nsb, int sc_bytes) {
+    return 1024 + static_cast<size_t>(rs) * CODE_SLOT + static_cast<size_t>(sb) * B_BYTES +
+           static_cast<size_t>(nsb) * sc_bytes + kMeta;
+  }
+  static_assert(A_COLS + NBUF * ACC_COLS <= TMEM_COLS, "grouped_gemm: TMEM columns");
+  static_assert(JT >= 1 && (AW == 16 || AW == 32), "grouped_gemm: mapping");
+};
+
+struct GemmRings {
+  int rs, sb, nsb, sc_bytes;
+};
+
+// A work item: one 128-feature tile of one expert against one slice of its rows.  A
+// segment of R rows is cut into ceil(R / BN) equal slices (multiples of 16), so a
+// segment just over BN rows gets two half-size MMAs instead of a full and a sliver.
+struct GemmTile {
+  int slot, row0, m0, n0, rows, local;
+};
+
+__device__ __forceinline__ GemmTile gemm_tile(const RouteView& rv, const int* tile_start, int nseg,
+                                              int m_tiles, int BN, int tile) {
+  int lo = 0, hi = nseg - 1;                 // last segment whose start <= tile
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tile_start[mid] <= tile) lo = mid; else hi = mid - 1;
+  }
+  GemmTile t;
+  int R;
+  t.local = tile - tile_start[lo];
+  t.slot = segment_slot(rv, lo, t.row0, R);
+  const int nt = (R + BN - 1) / BN;
+  const int rpt = (((R + nt - 1) / nt) + 15) & ~15;
+  const int mt = t.local / nt, ni = t.local - mt * nt;
+  t.m0 = mt * kBlockM;
+  t.n0 = ni * rpt;
+  t.rows = min(rpt, R - t.n0);
+  return t;
+}
+
+// Ring cursor: slot index and the parity of its current use.
+struct Ring {
+  int slot = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++slot == n) { slot = 0; phase ^= 1u; }
+  }
+};
+
+// ------------------------------------------------------------------ phase timing
+// Tuning builds only (-DBIGRIG_GEMM_PROFILE): one producer lane, one epilogue lane,
+// the MMA lane and the loader lane add clock64 spans per phase into g_gemm_prof (read
+// and cleared through bigrig_gemm_prof_read).  A normal build compiles none of it.
+#ifdef BIGRIG_GEMM_PROFILE
+__device__ unsigned long long g_gemm_prof[64];      // [MODE][32]
+#define GG_T(v) const long long v = clock64()
+#define GG_ADD(i, v) (prof[i] += clock64() - (v))
+#define GG_INC(i) (prof[i] += 1)
+#else
+#define GG_T(v)
+#define GG_ADD(i, v)
+#define GG_INC(i)
+#endif
+
 // ------------------------------------------------------------------ the kernel
 // MODE 0: gate/up (two weight matrices, output h); MODE 1: down (one matrix, output y).
-template <int MODE, int BN, int BITS, int SDT, int STAGES>
+// tm_code0/1: the codes of projection gate/up (MODE 0) or down (tm_code0, MODE 1) over
+// the slab as [slot][row][byte]; tm_act: the token operand [P rows][K] (expert-sorted).
+template <int MODE, int BN, int BITS, int SDT>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
-    const uint16_t* __restrict__ act,   // MODE 0: x [T, H]; MODE 1: h [P, I] (sorted rows)
-    RouteView rv, const uint8_t* __restrict__ slab, bigrig_expert_layout L,
+    const __grid_constant__ CUtensorMap tm_code0, const __grid_constant__ CUtensorMap tm_code1,
+    const __grid_constant__ CUtensorMap tm_act, RouteView rv, const uint8_t* __restrict__ slab,
+    bigrig_expert_layout L, GemmRings rg,
     uint16_t* __restrict__ out) {       // MODE 0: h [P, I]; MODE 1: y [P, H] ((token, k) order)
-  constexpr int NMAT = MODE == 0 ? 2 : 1;
-  constexpr int BTILE = BN * kBlockK * 2;
-  constexpr int STAGE_BYTES = NMAT * kATile + BTILE;
-  constexpr int TMEM_COLS = (NMAT * BN) <= 32 ? 32 : (NMAT * BN) <= 64 ? 64 : (NMAT * BN) <= 128 ? 128 : (NMAT * BN) <= 256 ? 256 : 512;
-  constexpr int CHUNKS_PER_ROW = kBlockK * BITS / 128;        // 16-byte code chunks per row per stage
-  constexpr int CODES_PER_CHUNK = 128 / BITS;
+  using G = GemmShape<MODE, BN, BITS>;
+  constexpr int NMAT = G::NMAT, JT = G::JT, NBUF = G::NBUF, WPC = G::WPC, F = G::F, CPI = G::CPI;
+  constexpr int SA = G::SA;
+  constexpr int OT = operand_type(BITS, SDT);
+  const int RS = rg.rs, SB = rg.sb, NSB = rg.nsb;
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* tiles = smem;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* accum_full = empty_bar + STAGES;
-  uint64_t* accum_empty = accum_full + 1;
-  uint64_t* drain_bar = accum_empty + 1;
+  // 1024-byte aligned by an offset from the shared array itself, so that every pointer
+  // below stays in the shared address space (plain LDS/STS, no generic addressing)
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* code_ring = smem;
+  uint8_t* b_ring = code_ring + RS * G::CODE_SLOT;
+  uint8_t* sc_ring = b_ring + SB * G::B_BYTES;
+  uint64_t* code_full = reinterpret_cast<uint64_t*>(sc_ring + NSB * rg.sc_bytes);
+  uint64_t* code_empty = code_full + RS;
+  uint64_t* b_full = code_empty + RS;
+  uint64_t* b_empty = b_full + SB;
+  uint64_t* sc_full = b_empty + SB;
+  uint64_t* sc_empty = sc_full + 2;
+  uint64_t* a_full = sc_empty + 2;
+  uint64_t* a_empty = a_full + SA;
+  uint64_t* acc_full = a_empty + SA;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain_bar = acc_empty + 2;
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_s + 1);
   int* tile_start = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_base_s + 2));  // [S+1]
@@ -242,177 +515,306 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   const int NF = MODE == 0 ? L.inter : L.hidden;       // output features
   const int m_tiles = (NF + kBlockM - 1) / kBlockM;
   const int k_iters = K / kBlockK;
+  const int gpitch = K / L.group_size;
   const int nseg = min(min(*rv.num_seg, rv.s_max), kMaxExperts);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&full_bar[i], kProducerWarps * 32);
-      mbar_init(&empty_bar[i], 1);
+    for (int i = 0; i < RS; ++i) {
+      mbar_init(&code_full[i], 1);
+      mbar_init(&code_empty[i], kProducerWarps);
     }
-    mbar_init(accum_full, 1);
-    mbar_init(accum_empty, 4);
+    for (int i = 0; i < SB; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sc_full[i], 1);
+      mbar_init(&sc_empty[i], kProducerWarps);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpilogueWarps);
+    }
+    for (int i = 0; i < SA; ++i) {
+      mbar_init(&a_full[i], kProducerWarps);
+      mbar_init(&a_empty[i], 1);
+    }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // tile prefix over segments: segment s owns m_tiles * ceil(R_s / BN) work items
-  if (warp == 0) {
-    if (lane == 0) {
-      int acc = 0;
-      for (int s = 0; s < nseg; ++s) {
-        tile_start[s] = acc;
-        int row0, R;
-        segment_slot(rv, s, row0, R);      // R = 0 for inconsistent metadata: no tiles
-        acc += m_tiles * ((R + BN - 1) / BN);
-      }
-      tile_start[nseg] = acc;
+  if (warp == 0 && lane == 0) {
+    int acc = 0;
+    for (int s = 0; s < nseg; ++s) {
+      tile_start[s] = acc;
+      int row0, R;
+      segment_slot(rv, s, row0, R);        // R = 0 for inconsistent metadata: no tiles
+      acc += m_tiles * ((R + BN - 1) / BN);
     }
+    tile_start[nseg] = acc;
   }
-  if (warp == kProducerWarps) tmem_alloc(tmem_base_s, TMEM_COLS);
+  if (warp == kMmaWarp) tmem_alloc(tmem_base_s, G::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base_s;
+  const uint32_t tmem_acc = tmem + G::A_COLS;          // accumulators after the A slots
   const int total = tile_start[nseg];
+  const int my_tiles = blockIdx.x < total ? (total - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int sc_half = kBlockM * gpitch * 2;            // one (mat, scale|bias) block in bytes
+#ifdef BIGRIG_GEMM_PROFILE
+  long long prof[32] = {};
+  GG_T(t_kernel);
+#endif
 
   if (warp < kProducerWarps) {
-    // ---------------------------------------------------------------- producers (+ epilogue)
-    const int ptid = threadIdx.x;             // 0..255
-    uint32_t stage = 0, phase = 0, accum_phase = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
-      int s = 0;
-      while (s + 1 < nseg && tile_start[s + 1] <= tile) ++s;
-      const int local = tile - tile_start[s];
-      int row0, R;
-      const int slot = segment_slot(rv, s, row0, R);
-      const int n_tiles = (R + BN - 1) / BN;
-      const int mt = local / n_tiles, nt = local - mt * n_tiles;
-      const int m0 = mt * kBlockM, n0 = nt * BN;
-      const bool valid_slot = slot >= 0;
-      if (!valid_slot && ptid == 0 && mt == 0 && nt == 0) atomicAdd(rv.err, 1);
-      const uint8_t* base = slab + static_cast<int64_t>(valid_slot ? slot : 0) * L.slot_stride;
-      const int64_t code_pitch = static_cast<int64_t>(K) * BITS / 8;
-      const int gpitch = K / L.group_size;
-      // token rows of this tile this thread gathers (B operand): chunk c = ptid + 256*i
+    // ---------------------------------------------------------------- producers
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;                      // tile row = TMEM lane
+    const int mat = MODE == 0 ? half : 0;
+    const int chalf = MODE == 0 ? 0 : half * JT;            // first chunk of the iteration
+    const uint32_t code_base = smem_u32(code_ring) + mat * G::CODE_BOX + r * 128;
+    const uint32_t sc_base = smem_u32(sc_ring) + (mat * 2) * sc_half + r * gpitch * 2;
+    // this thread's A columns: slot s at s * NMAT * 32 + mat * 32 + chalf * WPC, lane r
+    const uint32_t a_taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + mat * 32 + chalf * WPC;
+    Ring cr, ar;
+    bool ok = true;
+    for (int j = 0; j < my_tiles && ok; ++j) {
+      const int sb = j % NSB;
+      GG_T(t7);
+      if (!mbar_wait(&sc_full[sb], (j / NSB) & 1, abort_flag, rv.err, 1)) break;
+      GG_ADD(7, t7);
+      const uint32_t s_addr = sc_base + sb * rg.sc_bytes, b_addr = s_addr + sc_half;
       for (int kit = 0; kit < k_iters; ++kit) {
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, rv.err, 1)) break;
-        uint8_t* st = tiles + stage * STAGE_BYTES;
-        const int k0 = kit * kBlockK;
-        const int grp = k0 / L.group_size;
-        // A tiles: NMAT x 128 rows x CHUNKS_PER_ROW chunks
-        for (int job = ptid; job < NMAT * kBlockM * CHUNKS_PER_ROW; job += kProducerWarps * 32) {
-          const int mat = job / (kBlockM * CHUNKS_PER_ROW);
-          const int rem = job - mat * kBlockM * CHUNKS_PER_ROW;
-          const int r = rem / CHUNKS_PER_ROW, ch = rem - r * CHUNKS_PER_ROW;
-          const int f = m0 + r;
-          const int proj = MODE == 0 ? mat : 2;
-          uint8_t* atile = st + mat * kATile;
-          const int jbase = ch * (CODES_PER_CHUNK * 2 / 16);
-          if (f < NF && valid_slot) {
-            const uint8_t* codes = base + L.weight_off[proj] + f * code_pitch + (k0 * BITS / 8) + ch * 16;
-            const uint4 w = ld_stream_v4(codes);
-            const uint16_t* sc = reinterpret_cast<const uint16_t*>(base + L.scales_off[proj]);
-            const uint16_t* bi = reinterpret_cast<const uint16_t*>(base + L.biases_off[proj]);
-            const float sv = half_to_f32<SDT>(ld_nc_u16(sc + static_cast<int64_t>(f) * gpitch + grp));
-            const float bv = half_to_f32<SDT>(ld_nc_u16(bi + static_cast<int64_t>(f) * gpitch + grp));
-            dequant_chunk<BITS>(atile, r, jbase, w, sv, bv);
-          } else {
+        const int sub = kit % F;
+        if (sub == 0) {
+          GG_T(t0);
+          if (!mbar_wait(&code_full[cr.slot], cr.phase, abort_flag, rv.err, 2)) { ok = false; break; }
+          GG_ADD(0, t0);
+        }
+        GG_T(t2);
+        const int grp = kit * kBlockK / L.group_size;
+        const uint32_t sh = lds16(s_addr + grp * 2), bh = lds16(b_addr + grp * 2);
+        const uint32_t cb = code_base + cr.slot * G::CODE_SLOT;
+        uint4 w[JT];
 #pragma unroll
-            for (int j = 0; j < CODES_PER_CHUNK * 2 / 16; ++j)
-              *reinterpret_cast<uint4*>(atile + swz(r, jbase + j)) = make_uint4(0, 0, 0, 0);
-          }
+        for (int c = 0; c < JT; ++c) w[c] = lds128(cb + (((sub * CPI + chalf + c) ^ (r & 7)) << 4));
+        uint32_t av[G::AW];
+        if constexpr (BITS == 4) {           // operands in the scale dtype itself
+          const uint32_t s2 = sh * 0x10001u, b2 = bh * 0x10001u;
+#pragma unroll
+          for (int c = 0; c < JT; ++c) dequant_chunk4<OT>(w[c], s2, b2, av + c * WPC);
+        } else {
+          const float sv = half_to_f32<SDT>(static_cast<uint16_t>(sh));
+          const float bv = half_to_f32<SDT>(static_cast<uint16_t>(bh));
+#pragma unroll
+          for (int c = 0; c < JT; ++c) dequant_chunk8(w[c], sv, bv, av + c * WPC);
         }
-        // B tile: BN token rows x 8 chunks of 16 bytes
-        uint8_t* btile = st + NMAT * kATile;
-        for (int c = ptid; c < BN * 8; c += kProducerWarps * 32) {
-          const int r = c >> 3, j = c & 7;
-          uint4 v = make_uint4(0, 0, 0, 0);
-          if (n0 + r < R) {
-            const int p = row0 + n0 + r;
-            const int64_t src_row = MODE == 0 ? (rv.order[p] / rv.k) : p;
-            v = *reinterpret_cast<const uint4*>(act + src_row * K + k0 + j * 8);
-          }
-          *reinterpret_cast<uint4*>(btile + swz(r, j)) = v;
+        GG_ADD(2, t2);
+        if (sub == F - 1 || kit == k_iters - 1) {  // this warp is done with the code box
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&code_empty[cr.slot]);
+          cr.next(RS);
         }
-        fence_proxy_async();               // generic-proxy stores -> visible to the tensor core
-        mbar_arrive(&full_bar[stage]);
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
-      }
-      if (*abort_flag) break;
-      // ---------------------------------------------------------------- epilogue (warps 0-3)
-      if (warp < 4) {
-        if (!mbar_wait(accum_full, accum_phase, abort_flag, rv.err, 2)) break;
+        GG_T(t1);
+        if (!mbar_wait(&a_empty[ar.slot], ar.phase ^ 1, abort_flag, rv.err, 3)) { ok = false; break; }
         tc_fence_after();
-        const int f = m0 + warp * 32 + lane;
-        const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-        for (int j0 = 0; j0 < BN; j0 += 8) {
-          if (n0 + j0 >= R) break;
-          float a[8], u[8];
-          tmem_ld8(lane_addr + j0, a);
-          if (MODE == 0) tmem_ld8(lane_addr + BN + j0, u);
+        GG_ADD(1, t1);
+        GG_T(t3);
+        tmem_st<G::AW>(a_taddr + ar.slot * (NMAT * 32), av);
+        tmem_wait_st();
+        tc_fence_before();                    // TMEM stores -> the MMA after the barrier
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[ar.slot]);
+        ar.next(SA);
+        GG_ADD(3, t3);
+        GG_INC(6);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sc_empty[sb]);
+    }
+  } else if (warp < kMmaWarp) {
+    // ---------------------------------------------------------------- epilogue (warps 8-15)
+    // warp 8 + e drains TMEM lane quarter e % 4 (features m0 + 32 (e % 4) + lane) and the
+    // 16-column groups of token columns g with g % 2 == e / 4
+    const int eq = warp & 3, eh = (warp - kProducerWarps) >> 2;
+    for (int j = 0; j < my_tiles; ++j) {
+      const GemmTile t = gemm_tile(rv, tile_start, nseg, m_tiles, BN, blockIdx.x + j * gridDim.x);
+      const int buf = NBUF == 2 ? (j & 1) : 0, use = NBUF == 2 ? (j >> 1) : j;
+      GG_T(t8);
+      if (!mbar_wait(&acc_full[buf], use & 1, abort_flag, rv.err, 4)) break;
+      GG_ADD(8, t8);
+      GG_T(t9);
+      tc_fence_after();
+      const int f = t.m0 + eq * 32 + lane;
+      const bool fok = f < NF;
+      // the 4-bit down pass reads h as its K-permuted token operand
+      const int fcol = BITS == 4 && MODE == 0 ? (f & ~7) | k8_slot(f & 7) : f;
+      const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(eq * 32) << 16) + buf * G::ACC_COLS;
+      const int prow = t.row0 + t.n0;            // sorted row of token column 0
+      // MODE 1 scatters column c to output row order[prow + c]: lanes 0-15 hold the 16
+      // rows of a column group, loaded one group ahead
+      int ord_next = 0;
+      if (MODE == 1 && eh * 16 + lane < t.rows && lane < 16) ord_next = rv.order[prow + eh * 16 + lane];
+      for (int j0 = eh * 16; j0 < t.rows; j0 += 32) {
+        uint32_t a[16], u[16];
+        tmem_ld16_nowait(lane_addr + j0, a);
+        if (MODE == 0) tmem_ld16_nowait(lane_addr + BN + j0, u);
+        const int ord = ord_next;
+        if (MODE == 1 && j0 + 32 + lane < t.rows && lane < 16) ord_next = rv.order[prow + j0 + 32 + lane];
+        tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int row = n0 + j0 + i;
-            if (row < R && f < NF && valid_slot) {
-              const int p = row0 + row;
-              if (MODE == 0) {
-                out[static_cast<int64_t>(p) * NF + f] = f32_to_bf16_bits(silu_f32(a[i]) * u[i]);
-              } else {
-                out[static_cast<int64_t>(rv.order[p]) * NF + f] = f32_to_bf16_bits(a[i]);
-              }
-            } else if (row < R && f < NF) {
-              const int p = row0 + row;
-              const int64_t o = MODE == 0 ? static_cast<int64_t>(p) : rv.order[p];
-              out[o * NF + f] = 0;
+        for (int i = 0; i < 16; ++i) {
+          const int o = MODE == 1 ? __shfl_sync(0xffffffffu, ord, i) : 0;
+          if (j0 + i < t.rows && fok) {
+            if (MODE == 0) {
+              const float hv = silu_fast(__uint_as_float(a[i])) * __uint_as_float(u[i]);
+              out[static_cast<int64_t>(prow + j0 + i) * NF + fcol] =
+                  t.slot < 0 ? uint16_t(0)
+                  : OT == BIGRIG_F16 ? f32_to_f16_bits(fminf(fmaxf(hv, -65504.f), 65504.f))
+                                     : f32_to_bf16_bits(hv);
+            } else {
+              out[static_cast<int64_t>(o) * NF + f] =
+                  t.slot >= 0 ? f32_to_bf16_bits(__uint_as_float(a[i])) : uint16_t(0);
             }
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(accum_empty);
-        accum_phase ^= 1;
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      GG_ADD(9, t9);
+      GG_INC(10);
     }
-  } else {
-    // ---------------------------------------------------------------- MMA issuer (warp 8)
-    uint32_t stage = 0, phase = 0, accum_phase = 0;
-    constexpr uint32_t idesc = instr_desc(kBlockM, BN);
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
-      // the previous tile's epilogue must have drained the accumulators
-      if (!mbar_wait(accum_empty, accum_phase ^ 1, abort_flag, rv.err, 3)) break;
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------------------------------------- MMA issuer (warp 12)
+    Ring ar, br;
+    for (int j = 0; j < my_tiles && !*abort_flag; ++j) {
+      const GemmTile t = gemm_tile(rv, tile_start, nseg, m_tiles, BN, blockIdx.x + j * gridDim.x);
+      const uint32_t idesc = instr_desc(kBlockM, (t.rows + 15) & ~15, OT);
+      const int buf = NBUF == 2 ? (j & 1) : 0, use = NBUF == 2 ? (j >> 1) : j;
+      // the epilogue must have drained this accumulator buffer's previous tile
+      GG_T(t11);
+      if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, rv.err, 5)) break;
+      GG_ADD(11, t11);
       tc_fence_after();
+      const uint32_t acc = tmem_acc + buf * G::ACC_COLS;
+      bool ok = true;
       for (int kit = 0; kit < k_iters; ++kit) {
-        if (!mbar_wait(&full_bar[stage], phase, abort_flag, rv.err, 4)) break;
+        GG_T(t12);
+        if (!mbar_wait(&a_full[ar.slot], ar.phase, abort_flag, rv.err, 6) ||
+            !mbar_wait(&b_full[br.slot], br.phase, abort_flag, rv.err, 7)) { ok = false; break; }
+        GG_ADD(12, t12);
+        GG_T(t13);
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t st = smem_u32(tiles + stage * STAGE_BYTES);
-          const uint32_t bst = st + NMAT * kATile;
+          const uint32_t ast = tmem + ar.slot * (NMAT * 32);
+          const uint32_t bst = smem_u32(b_ring + br.slot * G::B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < kBlockK / 16; ++kk) {
             const uint64_t db = smem_desc(bst + kk * 32);
 #pragma unroll
-            for (int mat = 0; mat < NMAT; ++mat) {
-              const uint64_t da = smem_desc(st + mat * kATile + kk * 32);
-              mma_bf16(tmem + mat * BN, da, db, idesc, (kit > 0 || kk > 0) ? 1u : 0u);
-            }
+            for (int m = 0; m < NMAT; ++m)
+              mma_tmem_a(acc + m * BN, ast + m * 32 + kk * 8, db, idesc, (kit > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(&empty_bar[stage]);
-          if (kit == k_iters - 1) mma_commit(accum_full);
+          mma_commit(&a_empty[ar.slot]);
+          mma_commit(&b_empty[br.slot]);
+          if (kit == k_iters - 1) mma_commit(&acc_full[buf]);
         }
         __syncwarp();
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        ar.next(SA);
+        br.next(SB);
+        GG_ADD(13, t13);
       }
-      if (*abort_flag) break;
-      accum_phase ^= 1;
+      if (!ok) break;
     }
+  } else if (lane == 0) {
+    // ---------------------------------------------------------------- loader (warp 13, one lane)
+    Ring cr, br;
+    int ns = 0, nc = 0, nb = 0;                       // scale tiles, code boxes, B boxes issued
+    const int64_t s_off0 = MODE == 1 ? L.scales_off[2] : L.scales_off[0];
+    const int64_t b_off0 = MODE == 1 ? L.biases_off[2] : L.biases_off[0];
+    for (int j = 0; j < my_tiles; ++j) {
+      const GemmTile t = gemm_tile(rv, tile_start, nseg, m_tiles, BN, blockIdx.x + j * gridDim.x);
+      if (t.slot < 0 && t.local == 0) atomicAdd(rv.err, 1);
+      const int slot = t.slot >= 0 ? t.slot : 0;     // a missing expert's tiles read slot 0;
+                                                     // the epilogue writes zeros for them
+      const uint8_t* base = slab + static_cast<int64_t>(slot) * L.slot_stride;
+      // this tile's scale and bias blocks: rows [m0, m0 + rows) are contiguous
+      const int sb = j % NSB;
+      GG_T(t16);
+      if (!mbar_wait(&sc_empty[sb], ((j / NSB) & 1) ^ 1, abort_flag, rv.err, 8)) break;
+      GG_ADD(16, t16);
+      const uint32_t rows = static_cast<uint32_t>(min(kBlockM, NF - t.m0));
+      const uint32_t blk = rows * gpitch * 2;          // a multiple of 128: rows % 64 == 0
+      bar_expect_tx(&sc_full[sb], NMAT * 2 * blk);
+      ++ns;
+      uint8_t* sdst = sc_ring + sb * rg.sc_bytes;
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m) {
+        const int64_t so = (MODE == 1 ? s_off0 : m ? L.scales_off[1] : s_off0) + int64_t(t.m0) * gpitch * 2;
+        const int64_t bo = (MODE == 1 ? b_off0 : m ? L.biases_off[1] : b_off0) + int64_t(t.m0) * gpitch * 2;
+        bulk_g2s(sdst + (m * 2) * sc_half, base + so, blk, &sc_full[sb]);
+        bulk_g2s(sdst + (m * 2 + 1) * sc_half, base + bo, blk, &sc_full[sb]);
+      }
+      bool ok = true;
+      for (int kit = 0; kit < k_iters && ok; ++kit) {
+        if (kit % F == 0) {
+          GG_T(t17);
+          if (!mbar_wait(&code_empty[cr.slot], cr.phase ^ 1, abort_flag, rv.err, 9)) { ok = false; break; }
+          GG_ADD(17, t17);
+          bar_expect_tx(&code_full[cr.slot], NMAT * G::CODE_BOX);
+          const uint32_t dst = smem_u32(code_ring + cr.slot * G::CODE_SLOT);
+          const int x = kit * G::ROW_BYTES;
+          tma_load_3d(dst, &tm_code0, x, t.m0, slot, smem_u32(&code_full[cr.slot]));
+          if (NMAT == 2)
+            tma_load_3d(dst + G::CODE_BOX, &tm_code1, x, t.m0, slot, smem_u32(&code_full[cr.slot]));
+          cr.next(RS);
+          ++nc;
+        }
+        GG_T(t18);
+        if (!mbar_wait(&b_empty[br.slot], br.phase ^ 1, abort_flag, rv.err, 10)) { ok = false; break; }
+        GG_ADD(18, t18);
+        bar_expect_tx(&b_full[br.slot], G::B_BYTES);
+        tma_load_2d(smem_u32(b_ring + br.slot * G::B_BYTES), &tm_act, kit * kBlockK, t.row0 + t.n0,
+                    smem_u32(&b_full[br.slot]));
+        br.next(SB);
+        ++nb;
+        GG_INC(19);
+      }
+      if (!ok) break;
+    }
+    // every copy issued must land before the CTA's shared memory goes away (after an
+    // abort its consumers may never have waited for it): wait for the last use of each
+    // slot, bounded
+    auto drain = [&](uint64_t* bars, int n_issued, int n_slots) {
+      for (int f = max(0, n_issued - n_slots); f < n_issued; ++f) {
+        uint32_t n = 0;
+        while (!mbar_try_wait(&bars[f % n_slots], (f / n_slots) & 1) && ++n < kSpinLimit) {
+        }
+      }
+    };
+    drain(sc_full, ns, NSB);
+    drain(code_full, nc, RS);
+    drain(b_full, nb, SB);
   }
 
+#ifdef BIGRIG_GEMM_PROFILE
+  GG_ADD(15, t_kernel);
+  if (threadIdx.x == 0 || threadIdx.x == kProducerThreads || threadIdx.x == kMmaWarp * 32 ||
+      threadIdx.x == kLoaderWarp * 32) {
+    unsigned long long* g = g_gemm_prof + MODE * 32;
+    for (int i = 0; i < 32; ++i)       // the four roles fill disjoint phase slots
+      if (prof[i] && i != 15) atomicAdd(&g[i], static_cast<unsigned long long>(prof[i]));
+    if (threadIdx.x == 0) atomicAdd(&g[15], static_cast<unsigned long long>(prof[15]));
+    if (threadIdx.x == 0) atomicAdd(&g[31], 1ull);
+  }
+#endif
   // drain: every MMA this CTA issued must complete before TMEM is released.  On the
   // normal path the epilogue already waited for them; after an abort they may still
   // be in flight, so the issuing thread commits once more and waits (bounded).
   tc_fence_before();
   __syncthreads();
-  if (warp == kProducerWarps) {
+  if (warp == kMmaWarp) {
     if (*abort_flag) {
       if (lane == 0) mma_commit(drain_bar);
       __syncwarp();
@@ -421,26 +823,83 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       }
     }
     tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tmem_dealloc(tmem, G::TMEM_COLS);
   }
 }
 
 // ------------------------------------------------------------------ launchers
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// A tiled map of `rank` dimensions (innermost first), 128-byte swizzle, zero fill.
+static bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, cuuint32_t rank, const void* base,
+                       const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, dt, rank, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Slots a code map may address: the slab's extent is not passed in, and a TMA box only
+// touches the slot it is given.
+constexpr cuuint64_t kMapSlots = 1u << 16;
+
 template <int MODE, int BN, int BITS, int SDT>
 static int launch_one(const void* act, const RouteView& rv, const void* slab,
                       const bigrig_expert_layout& L, void* out, cudaStream_t s, int sms) {
-  constexpr int STAGES = MODE == 0 ? (BN <= 128 ? 4 : 3) : (BN <= 128 ? 6 : 4);
-  constexpr int NMAT = MODE == 0 ? 2 : 1;
-  constexpr int STAGE_BYTES = NMAT * kATile + BN * kBlockK * 2;
-  const size_t smem = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * STAGES * 8 + 24 + 16 +
-                      (kMaxExperts + 1) * sizeof(int);
-  auto kern = grouped_gemm_kernel<MODE, BN, BITS, SDT, STAGES>;
+  using G = GemmShape<MODE, BN, BITS>;
+  const int K = MODE == 0 ? L.hidden : L.inter, NF = MODE == 0 ? L.inter : L.hidden;
+  const int gpitch = K / L.group_size;
+  GemmRings rg{0, 0, 0, (G::NMAT * 2 * kBlockM * gpitch * 2 + 127) & ~127};
+  static const int prefs[][3] = {{3, 4, 2}, {2, 4, 2}, {2, 3, 2}, {3, 4, 1}, {2, 4, 1}, {2, 3, 1}, {2, 2, 1}};
+  for (const auto& c : prefs)
+    if (G::smem(c[0], c[1], c[2], rg.sc_bytes) <= static_cast<size_t>(G::kLimit)) {
+      rg.rs = c[0]; rg.sb = c[1]; rg.nsb = c[2];
+      break;
+    }
+  if (!rg.rs)
+    return set_error(BIGRIG_ERR_UNSUPPORTED, "grouped_gemm: K=%d needs more shared memory than a CTA has", K);
+  const size_t smem = G::smem(rg.rs, rg.sb, rg.nsb, rg.sc_bytes);
+
+  CUtensorMap tm[3];
+  const int projs[2] = {MODE == 0 ? 0 : 2, MODE == 0 ? 1 : 2};
+  for (int i = 0; i < 2; ++i) {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(K) * BITS / 8, static_cast<cuuint64_t>(NF), kMapSlots};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K) * BITS / 8, static_cast<cuuint64_t>(L.slot_stride)};
+    const cuuint32_t box[3] = {128, kBlockM, 1};
+    if (!encode_map(&tm[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3,
+                    static_cast<const uint8_t*>(slab) + L.weight_off[projs[i]], dims, strides, box))
+      return set_error(BIGRIG_ERR_CUDA, "grouped_gemm: cannot encode the code tensor map");
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rv.P)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+    const cuuint32_t box[2] = {kBlockK, BN};
+    if (!encode_map(&tm[2], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, act, dims, strides, box))
+      return set_error(BIGRIG_ERR_CUDA, "grouped_gemm: cannot encode the token tensor map");
+  }
+  auto kern = grouped_gemm_kernel<MODE, BN, BITS, SDT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return set_error(BIGRIG_ERR_CUDA, "grouped_gemm: cannot reserve %zu bytes of smem", smem);
   TimedLaunch tl(MODE == 0 ? BIGRIG_K_GEMM_GATE_UP : BIGRIG_K_GEMM_DOWN, s);
-  kern<<<sms, kThreads, smem, s>>>(static_cast<const uint16_t*>(act), rv,
-                                   static_cast<const uint8_t*>(slab), L,
+  kern<<<sms, kThreads, smem, s>>>(tm[0], tm[1], tm[2], rv, static_cast<const uint8_t*>(slab), L, rg,
                                    static_cast<uint16_t*>(out));
   return check_launch(MODE == 0 ? "grouped_gemm_gate_up" : "grouped_gemm_down");
 }
@@ -468,36 +927,75 @@ static int sm_count() {
   return n;
 }
 
-// Token tile: the smallest of 32/64/128/256 that covers the mean rows per expert.
-int gemm_token_tile(int T, int k, int E) {
-  const int mean = (T * k + E - 1) / E;
-  return mean <= 32 ? 32 : mean <= 64 ? 64 : mean <= 128 ? 128 : 256;
+// Mean rows per routed expert; each pass picks its token tile from it.
+int gemm_mean_rows(int T, int k, int E) { return (T * k + E - 1) / E; }
+
+// Token tile of a pass: the smallest offered that covers 1.25x the mean rows, so most
+// experts take one slice (or the fewest equal slices) per feature tile.  Gate/up tiles
+// stop at 160 columns (two accumulators of 2 x 160 plus the A slots fill TMEM), down
+// tiles at 256.
+static int pick_tile(int mean, const int* opts, int n) {
+  const int want = (mean * 5 + 3) / 4;
+  for (int i = 0; i < n; ++i)
+    if (opts[i] >= want) return opts[i];
+  return opts[n - 1];
 }
 
 int launch_gemm_gate_up(const void* x, const RouteView& rv, const void* slab,
-                        const bigrig_expert_layout& L, void* h, int bn, cudaStream_t s) {
+                        const bigrig_expert_layout& L, void* h, void* xs, int T, int mean_rows,
+                        cudaStream_t s) {
   if (L.group_size % sm100::kBlockK)
     return set_error(BIGRIG_ERR_UNSUPPORTED, "grouped_gemm: group_size must be a multiple of 64");
-  switch (bn) {
-    case 32: return sm100::dispatch_fmt<0, 32>(x, rv, slab, L, h, s, sm_count());
-    case 64: return sm100::dispatch_fmt<0, 64>(x, rv, slab, L, h, s, sm_count());
-    case 128: return sm100::dispatch_fmt<0, 128>(x, rv, slab, L, h, s, sm_count());
-    case 256: return sm100::dispatch_fmt<0, 256>(x, rv, slab, L, h, s, sm_count());
+  (void)T;
+  // the token operand as expert-sorted rows (and for 4-bit formats in the operand type
+  // and K order of the dequantised weights)
+  const int cpr = L.hidden / 8;
+  const int64_t n = static_cast<int64_t>(rv.P) * cpr;
+  if (n > 0) {
+    const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 8 * sm_count()));
+    const uint4* xv = static_cast<const uint4*>(x);
+    uint4* xsv = static_cast<uint4*>(xs);
+    if (L.bits == 4 && L.scale_dtype == BIGRIG_F16)
+      sm100::gather_rows_kernel<BIGRIG_F16, true><<<blocks, 256, 0, s>>>(xv, rv.order, rv.k, rv.P, cpr, xsv);
+    else if (L.bits == 4)
+      sm100::gather_rows_kernel<BIGRIG_BF16, true><<<blocks, 256, 0, s>>>(xv, rv.order, rv.k, rv.P, cpr, xsv);
+    else
+      sm100::gather_rows_kernel<BIGRIG_BF16, false><<<blocks, 256, 0, s>>>(xv, rv.order, rv.k, rv.P, cpr, xsv);
+    if (int rc = check_launch("gather_rows")) return rc;
   }
-  return set_error(BIGRIG_ERR_INVALID, "grouped_gemm: token tile %d", bn);
+  static const int opts[] = {32, 64, 96, 128, 160};
+  switch (pick_tile(mean_rows, opts, 5)) {
+    case 32: return sm100::dispatch_fmt<0, 32>(xs, rv, slab, L, h, s, sm_count());
+    case 64: return sm100::dispatch_fmt<0, 64>(xs, rv, slab, L, h, s, sm_count());
+    case 96: return sm100::dispatch_fmt<0, 96>(xs, rv, slab, L, h, s, sm_count());
+    case 128: return sm100::dispatch_fmt<0, 128>(xs, rv, slab, L, h, s, sm_count());
+    case 160: return sm100::dispatch_fmt<0, 160>(xs, rv, slab, L, h, s, sm_count());
+  }
+  return set_error(BIGRIG_ERR_INVALID, "grouped_gemm: mean rows %d", mean_rows);
 }
 
 int launch_gemm_down(const void* h, const RouteView& rv, const void* slab,
-                     const bigrig_expert_layout& L, void* y, int bn, cudaStream_t s) {
+                     const bigrig_expert_layout& L, void* y, int mean_rows, cudaStream_t s) {
   if (L.group_size % sm100::kBlockK)
     return set_error(BIGRIG_ERR_UNSUPPORTED, "grouped_gemm: group_size must be a multiple of 64");
-  switch (bn) {
+  static const int opts[] = {32, 64, 128, 256};
+  switch (pick_tile(mean_rows, opts, 4)) {
     case 32: return sm100::dispatch_fmt<1, 32>(h, rv, slab, L, y, s, sm_count());
     case 64: return sm100::dispatch_fmt<1, 64>(h, rv, slab, L, y, s, sm_count());
     case 128: return sm100::dispatch_fmt<1, 128>(h, rv, slab, L, y, s, sm_count());
     case 256: return sm100::dispatch_fmt<1, 256>(h, rv, slab, L, y, s, sm_count());
   }
-  return set_error(BIGRIG_ERR_INVALID, "grouped_gemm: token tile %d", bn);
+  return set_error(BIGRIG_ERR_INVALID, "grouped_gemm: mean rows %d", mean_rows);
 }
 
 }  // namespace bigrig
+
+#ifdef BIGRIG_GEMM_PROFILE
+extern "C" BIGRIG_API int bigrig_gemm_prof_read(unsigned long long* out) {
+  if (cudaMemcpyFromSymbol(out, bigrig::sm100::g_gemm_prof, sizeof(unsigned long long) * 64) !=
+      cudaSuccess)
+    return 1;
+  static const unsigned long long zero[64] = {};
+  return cudaMemcpyToSymbol(bigrig::sm100::g_gemm_prof, zero, sizeof(zero)) != cudaSuccess;
+}
+#endif

@@ -76,11 +76,16 @@ int launch_gemv_gate_up(const void* x, const RouteView& rv, const void* slab,
                         const bigrig_expert_layout& L, void* h, cudaStream_t s);
 int launch_gemv_down(const void* h, const RouteView& rv, const void* slab,
                      const bigrig_expert_layout& L, void* y, cudaStream_t s);
-int gemm_token_tile(int T, int k, int E);
+int gemm_mean_rows(int T, int k, int E);  // mean rows per routed expert (token tile input)
+// x [T, H] bf16; xs [P, H] scratch for the token operand: x's rows in expert-sorted
+// order (for 4-bit formats in the K order and operand type of the dequantised weights,
+// fp16 for fp16-scaled formats).  4-bit h rows come out in that K order and type, and
+// launch_gemm_down expects them so.
 int launch_gemm_gate_up(const void* x, const RouteView& rv, const void* slab,
-                        const bigrig_expert_layout& L, void* h, int bn, cudaStream_t s);
+                        const bigrig_expert_layout& L, void* h, void* xs, int T, int mean_rows,
+                        cudaStream_t s);
 int launch_gemm_down(const void* h, const RouteView& rv, const void* slab,
-                     const bigrig_expert_layout& L, void* y, int bn, cudaStream_t s);
+                     const bigrig_expert_layout& L, void* y, int mean_rows, cudaStream_t s);
 bool decode_layer_fits(const bigrig_expert_layout& L, int k, int E);
 int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, int E, int k,
                         int mode, int norm, const int32_t* g2s, const void* slab,

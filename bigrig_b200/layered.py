@@ -27,13 +27,29 @@ def chunks(x, step: int) -> list:
     return [x[i:i + step] for i in range(0, x.shape[0], step)]
 
 
-def prefill(layers, hidden: list, layer_scope=None, progress=None) -> list:
-    """Run every chunk of ``hidden`` through ``layers`` layer by layer; returns the chunks."""
+def prefill(layers, hidden: list, layer_scope=None, progress=None, token_wise: bool = False) -> list:
+    """Run every chunk of ``hidden`` through ``layers`` layer by layer; returns the chunks.
+
+    ``token_wise``: the caller vouches that every layer treats each token on its own (an
+    MoE stack without attention), so a layer runs once over all chunks' tokens stacked
+    and the result is cut back into the same chunks.  The rows and every token's result
+    are those of the chunked loop; the expert GEMMs get all the prompt's rows of an
+    expert at once instead of one chunk's share."""
     hidden = list(hidden)
     n = len(layers)
     if not hidden or n == 0:
         return hidden
-    total = sum(h.shape[0] for h in hidden)
+    sizes = [h.shape[0] for h in hidden]
+    total = sum(sizes)
+    if token_wise and len(hidden) > 1:
+        import torch
+        stacked = torch.cat(hidden)
+        for li, layer in enumerate(layers):
+            with layer_scope(li) if layer_scope is not None else contextlib.nullcontext():
+                stacked = layer(stacked)
+            if progress is not None:
+                progress(total * (li + 1) // n, total)
+        return list(torch.split(stacked, sizes))
     for li, layer in enumerate(layers):
         with layer_scope(li) if layer_scope is not None else contextlib.nullcontext():
             for j in range(len(hidden)):

@@ -12,7 +12,8 @@ Rounding points: gate and up stay in fp32 (the accumulator), the activation
 ``h = silu(gate) * up`` is stored as bf16 (the input dtype of the down
 projection), and the output is bf16.  ``intermediate="bf16"`` also rounds gate
 and up to bf16 (a model whose projections emit bf16), ``"f32"`` keeps h in fp32
-too; all three agree within the 1e-2 relative / 2e-3 absolute tolerance of the
+too, ``"h_f16"`` stores h as fp16 (an fp16 model's down-projection input); all
+agree within the 1e-2 relative / 2e-3 absolute tolerance of the
 parity tests on typical rows.  The default is the one the kernels implement:
 rounding gate/up before the SiLU lets a one-ulp flip of a large gate value move a
 whole output row, which no reduction order can reproduce bit for bit.
@@ -21,9 +22,14 @@ from __future__ import annotations
 
 import numpy as np
 
-from .affine import bf16_round, dequantize_f32
+from .affine import bf16_round, dequantize_f32, f32_to_half_bits, half_bits_to_f32
 
 PROJ = ("gate_proj", "up_proj", "down_proj")
+
+
+def f16_round(a) -> np.ndarray:
+    """fp32 values rounded through fp16 and back (round to nearest even)."""
+    return half_bits_to_f32(f32_to_half_bits(np.asarray(a, dtype=np.float32), "float16"), "float16")
 
 
 def silu(g: np.ndarray) -> np.ndarray:
@@ -37,23 +43,27 @@ def expert_weights_f32(expert: dict, group_size: int, bits: int, scale_dtype: st
 
     ``weight_round="bf16"`` rounds each dequantised weight to bf16 once, as a
     multi-row quantized matmul does when it dequantises a weight tile into the
-    activation dtype before the matrix product; None keeps the exact fp32 value,
-    as the one-row (GEMV) form ``s * sum(q x) + b * sum(x)`` effectively uses."""
+    activation dtype before the matrix product; ``"f16"`` rounds it to fp16 once (the
+    ``mx.dequantize`` value of an fp16-scaled format, the operand of an fp16 model's
+    matrix product); None keeps the exact fp32 value, as the one-row (GEMV) form
+    ``s * sum(q x) + b * sum(x)`` effectively uses."""
     out = {p: dequantize_f32(*expert[p], group_size, bits, scale_dtype) for p in PROJ}
     if weight_round == "bf16":
         out = {p: bf16_round(w) for p, w in out.items()}
+    elif weight_round == "f16":
+        out = {p: f16_round(w) for p, w in out.items()}
     elif weight_round is not None:
-        raise ValueError(f"weight_round must be None or 'bf16', got {weight_round!r}")
+        raise ValueError(f"weight_round must be None, 'bf16' or 'f16', got {weight_round!r}")
     return out
 
 
 def expert_forward(x: np.ndarray, w: dict, intermediate: str = "h_bf16") -> np.ndarray:
     """x fp32 [R, H] (values of a bf16 tensor) -> y fp32 [R, H] (values of bf16)."""
-    if intermediate not in ("h_bf16", "bf16", "f32"):
-        raise ValueError(f"intermediate must be h_bf16, bf16 or f32, got {intermediate!r}")
+    if intermediate not in ("h_bf16", "h_f16", "bf16", "f32"):
+        raise ValueError(f"intermediate must be h_bf16, h_f16, bf16 or f32, got {intermediate!r}")
     keep = lambda a: a.astype(np.float32)  # noqa: E731
     rnd_gu = bf16_round if intermediate == "bf16" else keep
-    rnd_h = keep if intermediate == "f32" else bf16_round
+    rnd_h = keep if intermediate == "f32" else f16_round if intermediate == "h_f16" else bf16_round
     up = rnd_gu(x @ w["up_proj"].T)
     gate = rnd_gu(x @ w["gate_proj"].T)
     h = rnd_h(silu(gate) * up)

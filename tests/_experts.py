@@ -48,8 +48,15 @@ class Layer:
             self._w[key] = moe.expert_weights_f32(self.q[e], 64, self.bits, self.sd, weight_round)
         return self._w[key]
 
-    def oracle_switch(self, x_f32, idx, weight_round=None):
-        return moe.switch_glu(x_f32, idx, lambda e: self.weights(e, weight_round))
+    def oracle_switch(self, x_f32, idx, weight_round=None, intermediate="h_bf16"):
+        return moe.switch_glu(x_f32, idx, lambda e: self.weights(e, weight_round), intermediate)
+
+    def gemm_rounding(self):
+        """(weight_round, intermediate) of the grouped GEMM for this format: 4-bit experts
+        compute in their scale dtype (fp16 weights and h for fp16 scales), 8-bit in bf16."""
+        if self.bits == 4 and self.sd == "float16":
+            return "f16", "h_f16"
+        return "bf16", "h_bf16"
 
 
 def bf16_tensor(a: np.ndarray, device="cuda") -> torch.Tensor:

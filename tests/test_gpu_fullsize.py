@@ -3,7 +3,7 @@
 The numpy restatement is too slow for 128 full-size experts, so the reference
 here is built from pieces already pinned bit for bit against it: the dequant
 kernel (test_gpu_kernels) feeds a plain torch fp32 computation with the same
-bf16 rounding points.  Size-independent properties ride along: a token's outputs
+rounding points.  Size-independent properties ride along: a token's outputs
 do not depend on the batch around it (bit for bit), and the permutation is a
 stable sort at the largest prefill size.
 """
@@ -58,21 +58,25 @@ def _dequant_f32(slab, L, slot, proj):
     return (q * s[..., None] + b[..., None]).reshape(rows, cols)
 
 
-def _reference(slab, L, x, idx, bf16_weights=False):
-    """y[t, j] in fp32 torch from exact dequantised weights (rounded once to bf16 for the
-    tensor-core path), with the kernels' rounding points: gate/up fp32, h and y bf16."""
+def _reference(slab, L, x, idx, gemm=False):
+    """y[t, j] in fp32 torch from exact dequantised weights, with the kernels' rounding
+    points: gate/up fp32, h and y bf16.  For the tensor-core path (``gemm``) each weight
+    is rounded once to the operand type -- fp16 for fp16-scaled 4-bit formats, bf16
+    otherwise -- and h is stored in that type."""
     T, k = idx.shape
     y = torch.empty(T, k, L.hidden, dtype=torch.float32, device=x.device)
     xf = x.float()
+    ot = torch.float16 if L.bits == 4 and L.scale_dtype == "float16" else torch.bfloat16
+    hdt = ot if gemm else torch.bfloat16
     for e in torch.unique(idx).tolist():
         w = [_dequant_f32(slab, L, e, p) for p in range(3)]
-        if bf16_weights:
-            w = [t.bfloat16().float() for t in w]
+        if gemm:
+            w = [t.to(ot).float() for t in w]
         rows = (idx == e).nonzero()
         xe = xf[rows[:, 0]]
         gate = xe @ w[0].T
         up = xe @ w[1].T
-        h = (torch.nn.functional.silu(gate) * up).bfloat16().float()
+        h = (torch.nn.functional.silu(gate) * up).to(hdt).float()
         y[rows[:, 0], rows[:, 1]] = (h @ w[2].T).bfloat16().float()
     return y
 
@@ -99,7 +103,7 @@ def test_full_size_layer(cuda, name, T, path):
     prev = _lib.set_path(path)
     try:
         y = ops.switch_glu(x, idx, slab, L, E)
-        ref = _reference(slab, L, x, idx, bf16_weights=(path == "gemm"))
+        ref = _reference(slab, L, x, idx, gemm=(path == "gemm"))
         assert_close(y.float().cpu().numpy(), ref.cpu().numpy(),
                      long_reduction=path == "gemm" or max(H, I) >= 4096)
         if path == "gemv":

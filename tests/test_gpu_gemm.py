@@ -1,6 +1,7 @@
 """The tcgen05 grouped GEMM (prefill path) against the restatement of a multi-row
-quantized matmul: weights dequantised into bf16 tiles, fp32 accumulation, bf16
-rounding of gate/up, the activation and the output."""
+quantized matmul: weights dequantised into operand tiles (fp16 for fp16-scaled 4-bit
+formats, as mx.dequantize gives them; bf16 otherwise), fp32 accumulation, the
+activation h stored in the same type, bf16 output."""
 import numpy as np
 import pytest
 import torch
@@ -47,7 +48,8 @@ def test_gemm_matches_oracle(cuda, path, H, I, E, k, bits, sd, T):
                        g2s=L.g2s)
     torch.cuda.synchronize()
     assert _lib.launch_counts()["gemm_gate_up"] == n0 + 1, "the GEMM path did not run"
-    assert_close(to_f32(y), L.oracle_switch(x, idx, weight_round="bf16"))
+    wr, inter = L.gemm_rounding()
+    assert_close(to_f32(y), L.oracle_switch(x, idx, weight_round=wr, intermediate=inter))
 
 
 def test_gemm_agrees_with_gemv(cuda):
@@ -76,3 +78,33 @@ def test_gemm_batch_invariance(cuda, path):
     y = ops.switch_glu(xt, it, L.slab, L.layout, E)
     y2 = ops.switch_glu(xt.flip(0).contiguous(), it.flip(0).contiguous(), L.slab, L.layout, E)
     assert torch.equal(y, y2.flip(0))
+
+
+def test_token_wise_prefill_matches_chunked(cuda):
+    """A resident MoE stack prefilled layer-major in chunks and token-wise (each layer once
+    over every chunk's tokens) gives the same bits: routing, the grouped GEMM's columns and
+    the combine are all per token."""
+    from bigrig_b200 import layered, stream
+    from bigrig_b200.block import fill_store, make_blocks
+    from bigrig_b200.fetch import HostExpertStore
+    from bigrig_b200.formats import bytes_per_expert, make_spec
+    LAYERS, H, I, E, K = 2, 1024, 512, 32, 8
+    blocks = make_blocks(LAYERS, H, I, E, K, "olmoe", 4, 64, "float16", True, seed=5,
+                         device=cuda)
+    spec = make_spec(H, I, 4, 64, "float16")
+    store = HostExpertStore({li: (E, bytes_per_expert(spec)) for li in range(LAYERS)})
+    fill_store(store, LAYERS, H, I, E, 4, 64, "float16", seed=6, device=cuda)
+    handle = stream.attach(blocks, store, E, policy="lfuda", warm="auto", device=cuda)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(1)
+    prompt = (torch.randn(600, H, generator=g, device=cuda) * 0.5).bfloat16()
+    layers = [(lambda h, b=b: b(h, residual=h)) for b in blocks]
+    n0 = _lib.launch_counts()["gemm_gate_up"]
+    chunked = layered.prefill(layers, layered.chunks(prompt, 128))
+    tw = layered.prefill(layers, layered.chunks(prompt, 128), token_wise=True)
+    torch.cuda.synchronize()
+    assert _lib.launch_counts()["gemm_gate_up"] == n0 + LAYERS * 5 + LAYERS
+    del handle
+    assert [c.shape[0] for c in tw] == [128, 128, 128, 128, 88]
+    for a, b in zip(chunked, tw):
+        assert torch.equal(a, b)
