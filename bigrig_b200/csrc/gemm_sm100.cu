@@ -15,21 +15,22 @@
 // K-major tile of 64 K-elements in 128-byte-swizzled shared memory, so each of the
 // four K=16 MMAs of an iteration starts 32 bytes further into the swizzle atom.
 //
-// Warp roles in a CTA of 448 threads, persistent over (expert, feature tile, token
+// Warp roles in a CTA of 576 threads, persistent over (expert, feature tile, token
 // slice) work items:
-//   warp 13    loader: one lane issues every copy -- a tile's scale and bias blocks
+//   warp 17    loader: one lane issues every copy -- a tile's scale and bias blocks
 //              (one bulk copy each, they are contiguous), the codes as TMA boxes of
 //              128 rows x 128 bytes (four 4-bit or two 8-bit iterations per box) and
 //              the token rows as one TMA box per iteration -- each completing on its
 //              ring slot's mbarrier by transaction count.
 //   warps 0-7  producers: dequantise their row's codes from the swizzled box into
 //              registers (w = OT(s * q + b), OT the operand type) and write them to
-//              the A slot in TMEM with tcgen05.st; arrive on the slot's full barrier.
-//   warp 12    MMA issuer: one lane waits for an A slot and a B slot, issues
-//              tcgen05.mma (A from TMEM, B from shared memory), and commits both
-//              slots back to their empty barriers and a finished tile to its
-//              accumulator barrier.
-//   warps 8-11 epilogue: TMEM accumulators -> silu(gate) * up (h, expert-sorted
+//              the A slot in TMEM with tcgen05.st; warp 0 also waits for the slot's
+//              token rows; all arrive on the slot's hardware named barrier.
+//   warp 16    MMA issuer: syncs on the slot's named barrier, one lane issues
+//              tcgen05.mma (A from TMEM, B from shared memory) and commits the slot
+//              back to its empty barrier and a finished tile to its accumulator
+//              barrier.
+//   warps 8-15 epilogue: TMEM accumulators -> silu(gate) * up (h, expert-sorted
 //              rows) or the down output scattered to (token, k) order.
 // Every mbarrier wait is bounded: past the limit the CTA records an error, raises
 // a shared abort flag so every other wait returns at once, drains the MMAs it
@@ -48,6 +49,12 @@ constexpr int kEpilogueWarps = 8;          // two per TMEM lane quarter
 constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
 constexpr int kLoaderWarp = kMmaWarp + 1;
 constexpr int kThreads = (kLoaderWarp + 1) * 32;
+// A-slot handoff producers -> MMA warp: hardware named barrier kReadyBar0 + slot, which
+// the producer warps arrive on and the MMA warp syncs on (the issuing warp touches no
+// shared memory to learn that a slot is ready; every shared-memory access it makes holds
+// up its next tcgen05.mma by hundreds of cycles under tensor load)
+constexpr int kReadyBar0 = 1;
+constexpr int kReadyCount = (kProducerWarps + 1) * 32;
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;                 // one 128-byte swizzle atom of bf16 per row
 constexpr uint32_t kSpinLimit = 1u << 22;   // a few seconds of polling before giving up
@@ -76,11 +83,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to ~1 us while the phase is
+// incomplete (it returns as soon as the phase completes): waiting warps stop competing
+// for issue slots with the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on phase `parity`.  Returns false when the CTA is aborting.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int32_t* err, int where) {
   uint32_t n = 0;
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity)) {
     if (*abort_flag) return false;
     if (++n > kSpinLimit) {
       *abort_flag = 1;
@@ -90,6 +110,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
   }
   return true;
+}
+
+// mbar_wait with the reason it returned: 0 the phase completed, 1 the CTA is aborting
+// (another role raised the flag), 2 this wait ran out (it raised the flag).
+__device__ __forceinline__ int mbar_wait_why(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                             int32_t* err, int where) {
+  uint32_t n = 0;
+  while (!mbar_try_wait_sleep(bar, parity)) {
+    if (*abort_flag) return 1;
+    if (++n > kSpinLimit) {
+      *abort_flag = 1;
+      if (err) atomicAdd(err + 1, 1);
+      if (err) atomicExch(err + 2, where);
+      return 2;
+    }
+  }
+  return 0;
+}
+
+// Bounded wait that does not give up on the abort flag (catch-up arrivals after an abort).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t n = 0; n < kSpinLimit; ++n)
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+  return false;
 }
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -152,6 +196,14 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
+__device__ __forceinline__ void nb_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void nb_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // 32 lanes x 16 columns of 32 bits from TMEM (this warp's lane quarter), not waited for.
 __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -164,6 +216,13 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t* r) {
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// fp32 -> bf16 bits, round to nearest even (the hardware conversion).
+__device__ __forceinline__ uint16_t bf16_rn(float f) {
+  uint16_t b;
+  asm("{ .reg .b16 h; cvt.rn.bf16.f32 h, %1; mov.b16 %0, h; }" : "=h"(b) : "f"(f));
+  return b;
+}
 
 // silu(g) = g / (1 + e^-g) with the fast exponential and division: h is rounded to a
 // 16-bit type right after, far above their error.
@@ -247,6 +306,9 @@ __host__ __device__ constexpr int k8_slot(int i) { return i < 4 ? 2 * i : 2 * (i
 // 1024 + n or 128 + n exactly; subtracting the base leaves q exactly, and one packed fma
 // gives w = OT(s * q + b) with a single rounding, s and b being the format's own scale
 // and bias (exact in OT).
+//
+// fp16 takes the odd nibbles without a shift: 0x6400 | (n << 4) is 1024 + 16 n, and
+// fma(v, 1/16, -64) = n exactly (fp16 has the mantissa bits to hold 16 n; bf16 does not).
 template <int OT>
 __device__ __forceinline__ void dequant_chunk4(uint4 w, uint32_t s2, uint32_t b2, uint32_t* o) {
   constexpr uint32_t base = OT == BIGRIG_F16 ? 0x64006400u : 0x43004300u, m = 0x000F000Fu;
@@ -254,10 +316,19 @@ __device__ __forceinline__ void dequant_chunk4(uint4 w, uint32_t s2, uint32_t b2
 #pragma unroll
   for (int i = 0; i < 4; ++i) {            // word i: codes 8i..8i+7 -> words 4i..4i+3
     const uint32_t c = ws[i];
-    o[4 * i + 0] = x2_fma<OT>(x2_sub<OT>((c & m) | base, base), s2, b2);
-    o[4 * i + 1] = x2_fma<OT>(x2_sub<OT>(((c >> 4) & m) | base, base), s2, b2);
-    o[4 * i + 2] = x2_fma<OT>(x2_sub<OT>(((c >> 8) & m) | base, base), s2, b2);
-    o[4 * i + 3] = x2_fma<OT>(x2_sub<OT>(((c >> 12) & m) | base, base), s2, b2);
+    if constexpr (OT == BIGRIG_F16) {
+      constexpr uint32_t m_hi = 0x00F000F0u, sixteenth = 0x2C002C00u, neg64 = 0xD400D400u;
+      const uint32_t c8 = c >> 8;
+      o[4 * i + 0] = x2_fma<OT>(x2_sub<OT>((c & m) | base, base), s2, b2);
+      o[4 * i + 1] = x2_fma<OT>(x2_fma<OT>((c & m_hi) | base, sixteenth, neg64), s2, b2);
+      o[4 * i + 2] = x2_fma<OT>(x2_sub<OT>((c8 & m) | base, base), s2, b2);
+      o[4 * i + 3] = x2_fma<OT>(x2_fma<OT>((c8 & m_hi) | base, sixteenth, neg64), s2, b2);
+    } else {
+      o[4 * i + 0] = x2_fma<OT>(x2_sub<OT>((c & m) | base, base), s2, b2);
+      o[4 * i + 1] = x2_fma<OT>(x2_sub<OT>(((c >> 4) & m) | base, base), s2, b2);
+      o[4 * i + 2] = x2_fma<OT>(x2_sub<OT>(((c >> 8) & m) | base, base), s2, b2);
+      o[4 * i + 3] = x2_fma<OT>(x2_sub<OT>(((c >> 12) & m) | base, base), s2, b2);
+    }
   }
 }
 
@@ -372,14 +443,15 @@ __device__ __forceinline__ uint32_t lds16(uint32_t addr) {
 // Rings (shared memory unless noted):
 //   codes : RS slots of NMAT TMA boxes, 128 rows x 128 bytes each (F iterations of
 //           one row's codes), 128-byte swizzled
-//   B     : SB slots of BN token rows x 64 operands, 128-byte swizzled (one iteration)
+//   B     : SA slots of BN token rows x 64 operands, 128-byte swizzled (one iteration)
 //   scales: NSB per-tile buffers of the tile's scale and bias blocks (NMAT x 2 x 128
 //           rows x K / group_size)
 //   A     : (TMEM) SA slots of NMAT dequantised 128 x 64 tiles, one row per TMEM lane,
 //           written by the producers with tcgen05.st and read by the MMA from tensor
 //           memory, so the weights never make a round trip through shared memory
-// The accumulators take the TMEM columns after the A slots.  RS, SB and NSB are
-// chosen at launch (the scale buffer's size depends on K).
+// An A slot and the B slot of the same index form one ring slot: one MMA commit per
+// iteration frees both.  The accumulators take the TMEM columns after the A slots.  RS
+// and NSB are chosen at launch (the scale buffer's size depends on K).
 //
 // Producer thread mapping: warp w owns TMEM lane quarter w % 4, i.e. rows
 // 32 (w % 4) + lane of the tile; gate/up warps 0-3 take the gate rows and 4-7 the up
@@ -428,25 +500,26 @@ struct GemmTile {
   int slot, row0, m0, n0, rows, local;
 };
 
-__device__ __forceinline__ GemmTile gemm_tile(const RouteView& rv, const int* tile_start, int nseg,
-                                              int m_tiles, int BN, int tile) {
-  int lo = 0, hi = nseg - 1;                 // last segment whose start <= tile
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (tile_start[mid] <= tile) lo = mid; else hi = mid - 1;
+// A CTA's work items come in increasing order, so each role walks the segments forward
+// instead of searching the tile prefix for every item.
+struct TileWalker {
+  int seg = 0;
+  __device__ __forceinline__ GemmTile at(const RouteView& rv, const int* tile_start, int nseg,
+                                         int m_tiles, int BN, int tile) {
+    while (seg + 1 < nseg && tile_start[seg + 1] <= tile) ++seg;
+    GemmTile t;
+    int R;
+    t.local = tile - tile_start[seg];
+    t.slot = segment_slot(rv, seg, t.row0, R);
+    const int nt = (R + BN - 1) / BN;
+    const int rpt = (((R + nt - 1) / nt) + 15) & ~15;
+    const int mt = t.local / nt, ni = t.local - mt * nt;
+    t.m0 = mt * kBlockM;
+    t.n0 = ni * rpt;
+    t.rows = min(rpt, R - t.n0);
+    return t;
   }
-  GemmTile t;
-  int R;
-  t.local = tile - tile_start[lo];
-  t.slot = segment_slot(rv, lo, t.row0, R);
-  const int nt = (R + BN - 1) / BN;
-  const int rpt = (((R + nt - 1) / nt) + 15) & ~15;
-  const int mt = t.local / nt, ni = t.local - mt * nt;
-  t.m0 = mt * kBlockM;
-  t.n0 = ni * rpt;
-  t.rows = min(rpt, R - t.n0);
-  return t;
-}
+};
 
 // Ring cursor: slot index and the parity of its current use.
 struct Ring {
@@ -484,9 +557,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     uint16_t* __restrict__ out) {       // MODE 0: h [P, I]; MODE 1: y [P, H] ((token, k) order)
   using G = GemmShape<MODE, BN, BITS>;
   constexpr int NMAT = G::NMAT, JT = G::JT, NBUF = G::NBUF, WPC = G::WPC, F = G::F, CPI = G::CPI;
-  constexpr int SA = G::SA;
+  constexpr int S = G::SA;               // slots: an A slot in TMEM and a B slot in smem
   constexpr int OT = operand_type(BITS, SDT);
-  const int RS = rg.rs, SB = rg.sb, NSB = rg.nsb;
+  const int RS = rg.rs, NSB = rg.nsb;
 
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned by an offset from the shared array itself, so that every pointer
@@ -494,21 +567,20 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* code_ring = smem;
   uint8_t* b_ring = code_ring + RS * G::CODE_SLOT;
-  uint8_t* sc_ring = b_ring + SB * G::B_BYTES;
+  uint8_t* sc_ring = b_ring + S * G::B_BYTES;
   uint64_t* code_full = reinterpret_cast<uint64_t*>(sc_ring + NSB * rg.sc_bytes);
   uint64_t* code_empty = code_full + RS;
   uint64_t* b_full = code_empty + RS;
-  uint64_t* b_empty = b_full + SB;
-  uint64_t* sc_full = b_empty + SB;
+  uint64_t* s_empty = b_full + S;        // slot free again: its MMAs completed (one commit)
+  uint64_t* sc_full = s_empty + S;
   uint64_t* sc_empty = sc_full + 2;
-  uint64_t* a_full = sc_empty + 2;
-  uint64_t* a_empty = a_full + SA;
-  uint64_t* acc_full = a_empty + SA;
+  uint64_t* acc_full = sc_empty + 2;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain_bar = acc_empty + 2;
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  int* tile_rows = reinterpret_cast<int*>(drain_bar + 1);  // [8] token columns of tile j at j % 8
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(tile_rows + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_s + 1);
-  int* tile_start = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_base_s + 2));  // [S+1]
+  int* tile_start = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_base_s + 2));  // [nseg+1]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = MODE == 0 ? L.hidden : L.inter;        // reduction length
@@ -523,19 +595,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       mbar_init(&code_full[i], 1);
       mbar_init(&code_empty[i], kProducerWarps);
     }
-    for (int i = 0; i < SB; ++i) {
+    for (int i = 0; i < S; ++i) {
       mbar_init(&b_full[i], 1);
-      mbar_init(&b_empty[i], 1);
+      mbar_init(&s_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sc_full[i], 1);
       mbar_init(&sc_empty[i], kProducerWarps);
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], kEpilogueWarps);
-    }
-    for (int i = 0; i < SA; ++i) {
-      mbar_init(&a_full[i], kProducerWarps);
-      mbar_init(&a_empty[i], 1);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -576,58 +644,129 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     const uint32_t sc_base = smem_u32(sc_ring) + (mat * 2) * sc_half + r * gpitch * 2;
     // this thread's A columns: slot s at s * NMAT * 32 + mat * 32 + chalf * WPC, lane r
     const uint32_t a_taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + mat * 32 + chalf * WPC;
+    // a row's scales start 16-byte aligned when K / group_size is a multiple of 8: then
+    // eight groups come in one 16-byte read (lanes are rows gpitch * 2 bytes apart, so
+    // per-group 2-byte reads would pile onto two banks)
+    const bool s_vec = (gpitch & 7) == 0;
+    const int ipg = L.group_size / kBlockK;                 // iterations per scale group
     Ring cr, ar;
     bool ok = true;
+    // Every iteration of a tile gets exactly one arrival on its slot's named barrier from
+    // every producer warp, on the way out too.  The MMA warp checks the abort flag once
+    // per tile, so a warp that gives up (a bounded wait ran out, or another role aborted:
+    // the flag is set either way) keeps arriving to the end of its tile, each arrival
+    // after the slot's previous use completed -- never two on one barrier phase.  If a
+    // slot wait itself ran out, the MMAs are stuck: one last arrival, unthrottled (the MMA
+    // warp already took the slot's previous phase), and no more.
+    auto bail = [&](int kit, bool throttle_first) {
+      for (int q = kit; q < k_iters; ++q) {
+        if ((q > kit || throttle_first) &&
+            !__all_sync(0xffffffffu, mbar_wait_bounded(&s_empty[ar.slot], ar.phase ^ 1)))
+          break;
+        __syncwarp();
+        nb_arrive(kReadyBar0 + ar.slot, kReadyCount);
+        ar.next(S);
+        if (!throttle_first && q == kit) break;
+      }
+      ok = false;
+    };
     for (int j = 0; j < my_tiles && ok; ++j) {
       const int sb = j % NSB;
       GG_T(t7);
-      if (!mbar_wait(&sc_full[sb], (j / NSB) & 1, abort_flag, rv.err, 1)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sc_full[sb], (j / NSB) & 1, abort_flag, rv.err, 1))) {
+        bail(0, true);
+        break;
+      }
       GG_ADD(7, t7);
       const uint32_t s_addr = sc_base + sb * rg.sc_bytes, b_addr = s_addr + sc_half;
-      for (int kit = 0; kit < k_iters; ++kit) {
-        const int sub = kit % F;
-        if (sub == 0) {
-          GG_T(t0);
-          if (!mbar_wait(&code_full[cr.slot], cr.phase, abort_flag, rv.err, 2)) { ok = false; break; }
-          GG_ADD(0, t0);
+      uint4 s8 = make_uint4(0, 0, 0, 0), b8 = s8;
+      // group of the current iteration, counted without a division: a group spans
+      // ipg = group_size / 64 iterations
+      int grp = 0, gleft = ipg;
+      for (int kit0 = 0; kit0 < k_iters && ok; kit0 += F) {
+        // this thread's codes of all F iterations of the box, read at once; the box is
+        // handed back to the loader right away
+        GG_T(t0);
+        if (!__all_sync(0xffffffffu, mbar_wait(&code_full[cr.slot], cr.phase, abort_flag, rv.err, 2))) {
+          bail(kit0, true);
+          break;
         }
-        GG_T(t2);
-        const int grp = kit * kBlockK / L.group_size;
-        const uint32_t sh = lds16(s_addr + grp * 2), bh = lds16(b_addr + grp * 2);
+        GG_ADD(0, t0);
         const uint32_t cb = code_base + cr.slot * G::CODE_SLOT;
-        uint4 w[JT];
+        uint4 wb[F][JT];
+        uint32_t landed = 0;
 #pragma unroll
-        for (int c = 0; c < JT; ++c) w[c] = lds128(cb + (((sub * CPI + chalf + c) ^ (r & 7)) << 4));
-        uint32_t av[G::AW];
-        if constexpr (BITS == 4) {           // operands in the scale dtype itself
-          const uint32_t s2 = sh * 0x10001u, b2 = bh * 0x10001u;
+        for (int sub = 0; sub < F; ++sub)
 #pragma unroll
-          for (int c = 0; c < JT; ++c) dequant_chunk4<OT>(w[c], s2, b2, av + c * WPC);
-        } else {
-          const float sv = half_to_f32<SDT>(static_cast<uint16_t>(sh));
-          const float bv = half_to_f32<SDT>(static_cast<uint16_t>(bh));
-#pragma unroll
-          for (int c = 0; c < JT; ++c) dequant_chunk8(w[c], sv, bv, av + c * WPC);
-        }
-        GG_ADD(2, t2);
-        if (sub == F - 1 || kit == k_iters - 1) {  // this warp is done with the code box
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&code_empty[cr.slot]);
-          cr.next(RS);
-        }
-        GG_T(t1);
-        if (!mbar_wait(&a_empty[ar.slot], ar.phase ^ 1, abort_flag, rv.err, 3)) { ok = false; break; }
-        tc_fence_after();
-        GG_ADD(1, t1);
-        GG_T(t3);
-        tmem_st<G::AW>(a_taddr + ar.slot * (NMAT * 32), av);
-        tmem_wait_st();
-        tc_fence_before();                    // TMEM stores -> the MMA after the barrier
+          for (int c = 0; c < JT; ++c) {
+            wb[sub][c] = lds128(cb + (((sub * CPI + chalf + c) ^ (r & 7)) << 4));
+            landed ^= wb[sub][c].w;
+          }
+        // the loads must have returned before the box goes back to the loader (its next
+        // TMA box overwrites it): an instruction reading every load's result makes the
+        // warp wait for all of them
+        asm volatile("" ::"r"(landed));
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[ar.slot]);
-        ar.next(SA);
-        GG_ADD(3, t3);
-        GG_INC(6);
+        if (lane == 0) mbar_arrive(&code_empty[cr.slot]);
+        cr.next(RS);
+#pragma unroll
+        for (int sub = 0; sub < F; ++sub) {
+          if (kit0 + sub >= k_iters || !ok) break;
+          GG_T(t2);
+          uint32_t sh, bh;
+          if (s_vec) {
+            if ((grp & 7) == 0 && gleft == ipg) {   // first iteration of a block of 8 groups
+              s8 = lds128(s_addr + (grp >> 3) * 16);
+              b8 = lds128(b_addr + (grp >> 3) * 16);
+            }
+            const int wi = (grp >> 1) & 3, hs = (grp & 1) * 16;
+            sh = ((wi == 0 ? s8.x : wi == 1 ? s8.y : wi == 2 ? s8.z : s8.w) >> hs) & 0xFFFFu;
+            bh = ((wi == 0 ? b8.x : wi == 1 ? b8.y : wi == 2 ? b8.z : b8.w) >> hs) & 0xFFFFu;
+          } else {
+            sh = lds16(s_addr + grp * 2);
+            bh = lds16(b_addr + grp * 2);
+          }
+          if (--gleft == 0) { ++grp; gleft = ipg; }
+          uint32_t av[G::AW];
+          if constexpr (BITS == 4) {           // operands in the scale dtype itself
+            const uint32_t s2 = sh * 0x10001u, b2 = bh * 0x10001u;
+#pragma unroll
+            for (int c = 0; c < JT; ++c) dequant_chunk4<OT>(wb[sub][c], s2, b2, av + c * WPC);
+          } else {
+            const float sv = half_to_f32<SDT>(static_cast<uint16_t>(sh));
+            const float bv = half_to_f32<SDT>(static_cast<uint16_t>(bh));
+#pragma unroll
+            for (int c = 0; c < JT; ++c) dequant_chunk8(wb[sub][c], sv, bv, av + c * WPC);
+          }
+          GG_ADD(2, t2);
+          GG_T(t1);
+          const int why = mbar_wait_why(&s_empty[ar.slot], ar.phase ^ 1, abort_flag, rv.err, 3);
+          if (__any_sync(0xffffffffu, why != 0)) {
+            // ran out: the MMAs are stuck, one last arrival; aborted: catch up, throttled
+            bail(kit0 + sub, !__any_sync(0xffffffffu, why == 2));
+            break;
+          }
+          tc_fence_after();
+          GG_ADD(1, t1);
+          GG_T(t3);
+          tmem_st<G::AW>(a_taddr + ar.slot * (NMAT * 32), av);
+          tmem_wait_st();
+          tc_fence_before();                  // TMEM stores -> the MMA after the barrier
+          // warp 0 also sees this iteration's token rows land, so a completed handoff
+          // means both operands are in place
+          bool bok = true;
+          if (warp == 0) bok = __all_sync(0xffffffffu, mbar_wait(&b_full[ar.slot], ar.phase, abort_flag, rv.err, 11));
+          __syncwarp();
+          nb_arrive(kReadyBar0 + ar.slot, kReadyCount);
+          ar.next(S);
+          GG_ADD(3, t3);
+          GG_INC(6);
+          if (!bok) {                         // arrived for this iteration: catch up after it
+            if (kit0 + sub + 1 < k_iters) bail(kit0 + sub + 1, true);
+            ok = false;
+            break;
+          }
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sc_empty[sb]);
@@ -637,8 +776,9 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     // warp 8 + e drains TMEM lane quarter e % 4 (features m0 + 32 (e % 4) + lane) and the
     // 16-column groups of token columns g with g % 2 == e / 4
     const int eq = warp & 3, eh = (warp - kProducerWarps) >> 2;
+    TileWalker tw;
     for (int j = 0; j < my_tiles; ++j) {
-      const GemmTile t = gemm_tile(rv, tile_start, nseg, m_tiles, BN, blockIdx.x + j * gridDim.x);
+      const GemmTile t = tw.at(rv, tile_start, nseg, m_tiles, BN, blockIdx.x + j * gridDim.x);
       const int buf = NBUF == 2 ? (j & 1) : 0, use = NBUF == 2 ? (j >> 1) : j;
       GG_T(t8);
       if (!mbar_wait(&acc_full[buf], use & 1, abort_flag, rv.err, 4)) break;
@@ -655,60 +795,96 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       // rows of a column group, loaded one group ahead
       int ord_next = 0;
       if (MODE == 1 && eh * 16 + lane < t.rows && lane < 16) ord_next = rv.order[prow + eh * 16 + lane];
-      for (int j0 = eh * 16; j0 < t.rows; j0 += 32) {
-        uint32_t a[16], u[16];
-        tmem_ld16_nowait(lane_addr + j0, a);
-        if (MODE == 0) tmem_ld16_nowait(lane_addr + BN + j0, u);
-        const int ord = ord_next;
-        if (MODE == 1 && j0 + 32 + lane < t.rows && lane < 16) ord_next = rv.order[prow + j0 + 32 + lane];
-        tmem_ld_wait();
+      if constexpr (MODE == 0) {
+        // gate/up: h for all of this warp's column groups first, kept as packed 16-bit
+        // pairs in registers, so that the accumulator goes back to the MMA before any
+        // global store (with one accumulator buffer the next tile's MMAs wait for it)
+        constexpr int NG = (BN / 16 + 1) / 2;   // 16-column groups per warp (every other)
+        uint32_t hp[NG * 8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int o = MODE == 1 ? __shfl_sync(0xffffffffu, ord, i) : 0;
-          if (j0 + i < t.rows && fok) {
-            if (MODE == 0) {
-              const float hv = silu_fast(__uint_as_float(a[i])) * __uint_as_float(u[i]);
-              out[static_cast<int64_t>(prow + j0 + i) * NF + fcol] =
-                  t.slot < 0 ? uint16_t(0)
-                  : OT == BIGRIG_F16 ? f32_to_f16_bits(fminf(fmaxf(hv, -65504.f), 65504.f))
-                                     : f32_to_bf16_bits(hv);
-            } else {
-              out[static_cast<int64_t>(o) * NF + f] =
-                  t.slot >= 0 ? f32_to_bf16_bits(__uint_as_float(a[i])) : uint16_t(0);
+        for (int gi = 0; gi < NG; ++gi) {
+          const int j0 = (eh + 2 * gi) * 16;
+          if (j0 < t.rows) {
+            uint32_t a[16], u[16];
+            tmem_ld16_nowait(lane_addr + j0, a);
+            tmem_ld16_nowait(lane_addr + BN + j0, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+              const float h0 = silu_fast(__uint_as_float(a[i])) * __uint_as_float(u[i]);
+              const float h1 = silu_fast(__uint_as_float(a[i + 1])) * __uint_as_float(u[i + 1]);
+              hp[gi * 8 + i / 2] = OT == BIGRIG_F16 ? pack_f16x2_sat(h0, h1) : pack_bf16x2(h0, h1);
             }
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+#pragma unroll
+        for (int gi = 0; gi < NG; ++gi) {
+          const int j0 = (eh + 2 * gi) * 16;
+          if (j0 < t.rows && fok) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              if (j0 + i < t.rows)
+                out[static_cast<int64_t>(prow + j0 + i) * NF + fcol] =
+                    t.slot < 0 ? uint16_t(0) : static_cast<uint16_t>(hp[gi * 8 + i / 2] >> ((i & 1) * 16));
+            }
+          }
+        }
+      } else {
+        for (int j0 = eh * 16; j0 < t.rows; j0 += 32) {
+          uint32_t a[16];
+          tmem_ld16_nowait(lane_addr + j0, a);
+          const int ord = ord_next;
+          if (j0 + 32 + lane < t.rows && lane < 16) ord_next = rv.order[prow + j0 + 32 + lane];
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int o = __shfl_sync(0xffffffffu, ord, i);
+            if (j0 + i < t.rows && fok)
+              out[static_cast<int64_t>(o) * NF + f] = t.slot >= 0 ? bf16_rn(__uint_as_float(a[i])) : uint16_t(0);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
       GG_ADD(9, t9);
       GG_INC(10);
     }
   } else if (warp == kMmaWarp) {
-    // ---------------------------------------------------------------- MMA issuer (warp 12)
-    Ring ar, br;
-    for (int j = 0; j < my_tiles && !*abort_flag; ++j) {
-      const GemmTile t = gemm_tile(rv, tile_start, nseg, m_tiles, BN, blockIdx.x + j * gridDim.x);
-      const uint32_t idesc = instr_desc(kBlockM, (t.rows + 15) & ~15, OT);
+    // ---------------------------------------------------------------- MMA issuer (warp 16)
+    // Touches shared memory only once per tile (the accumulator wait, the abort flag and
+    // the next tile's width): each access holds up the next tcgen05.mma by hundreds of
+    // cycles under tensor load.
+    const volatile int* rows_ring = tile_rows;
+    Ring ar;
+    int rows = 0;                             // token columns of the current tile
+    for (int j = 0; j < my_tiles; ++j) {
       const int buf = NBUF == 2 ? (j & 1) : 0, use = NBUF == 2 ? (j >> 1) : j;
       // the epilogue must have drained this accumulator buffer's previous tile
       GG_T(t11);
       if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, rv.err, 5)) break;
       GG_ADD(11, t11);
+      if (*abort_flag) break;                 // once per tile: a producer that gave up
+                                              // keeps arriving to the end of its tile
       tc_fence_after();
       const uint32_t acc = tmem_acc + buf * G::ACC_COLS;
-      bool ok = true;
+      uint32_t idesc = 0;
       for (int kit = 0; kit < k_iters; ++kit) {
         GG_T(t12);
-        if (!mbar_wait(&a_full[ar.slot], ar.phase, abort_flag, rv.err, 6) ||
-            !mbar_wait(&b_full[br.slot], br.phase, abort_flag, rv.err, 7)) { ok = false; break; }
+        nb_sync(kReadyBar0 + ar.slot, kReadyCount);   // A slot and token rows in place
         GG_ADD(12, t12);
         GG_T(t13);
+        if (kit == 0) {
+          if (j == 0) rows = rows_ring[0];    // posted before the first token rows
+          idesc = instr_desc(kBlockM, (rows + 15) & ~15, OT);
+        }
         tc_fence_after();
         if (lane == 0) {
           const uint32_t ast = tmem + ar.slot * (NMAT * 32);
-          const uint32_t bst = smem_u32(b_ring + br.slot * G::B_BYTES);
+          const uint32_t bst = smem_u32(b_ring + ar.slot * G::B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < kBlockK / 16; ++kk) {
             const uint64_t db = smem_desc(bst + kk * 32);
@@ -716,25 +892,32 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
             for (int m = 0; m < NMAT; ++m)
               mma_tmem_a(acc + m * BN, ast + m * 32 + kk * 8, db, idesc, (kit > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(&a_empty[ar.slot]);
-          mma_commit(&b_empty[br.slot]);
+          mma_commit(&s_empty[ar.slot]);      // A and B slot free once these MMAs are done
           if (kit == k_iters - 1) mma_commit(&acc_full[buf]);
         }
         __syncwarp();
-        ar.next(SA);
-        br.next(SB);
+        ar.next(S);
         GG_ADD(13, t13);
+        // the next tile's width, read with this tile's last MMAs already queued (the
+        // loader posted it before this iteration's token rows)
+        if (kit == k_iters - 1 && j + 1 < my_tiles) rows = rows_ring[(j + 1) & 7];
       }
-      if (!ok) break;
     }
   } else if (lane == 0) {
-    // ---------------------------------------------------------------- loader (warp 13, one lane)
-    Ring cr, br;
+    // ---------------------------------------------------------------- loader (warp 17, one lane)
+    Ring cr, sr;
+    TileWalker tw;
     int ns = 0, nc = 0, nb = 0;                       // scale tiles, code boxes, B boxes issued
     const int64_t s_off0 = MODE == 1 ? L.scales_off[2] : L.scales_off[0];
     const int64_t b_off0 = MODE == 1 ? L.biases_off[2] : L.biases_off[0];
+    GemmTile t{};
+    if (my_tiles > 0) {
+      t = tw.at(rv, tile_start, nseg, m_tiles, BN, blockIdx.x);
+      tile_rows[0] = t.rows;
+    }
     for (int j = 0; j < my_tiles; ++j) {
-      const GemmTile t = gemm_tile(rv, tile_start, nseg, m_tiles, BN, blockIdx.x + j * gridDim.x);
+      GemmTile tn{};
+      if (j + 1 < my_tiles) tn = tw.at(rv, tile_start, nseg, m_tiles, BN, blockIdx.x + (j + 1) * gridDim.x);
       if (t.slot < 0 && t.local == 0) atomicAdd(rv.err, 1);
       const int slot = t.slot >= 0 ? t.slot : 0;     // a missing expert's tiles read slot 0;
                                                      // the epilogue writes zeros for them
@@ -771,17 +954,21 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
           cr.next(RS);
           ++nc;
         }
+        // the next tile's width goes out before this tile's last token rows: the MMA lane
+        // reads it after the handoff of that iteration
+        if (kit == k_iters - 1 && j + 1 < my_tiles) tile_rows[(j + 1) & 7] = tn.rows;
         GG_T(t18);
-        if (!mbar_wait(&b_empty[br.slot], br.phase ^ 1, abort_flag, rv.err, 10)) { ok = false; break; }
+        if (!mbar_wait(&s_empty[sr.slot], sr.phase ^ 1, abort_flag, rv.err, 10)) { ok = false; break; }
         GG_ADD(18, t18);
-        bar_expect_tx(&b_full[br.slot], G::B_BYTES);
-        tma_load_2d(smem_u32(b_ring + br.slot * G::B_BYTES), &tm_act, kit * kBlockK, t.row0 + t.n0,
-                    smem_u32(&b_full[br.slot]));
-        br.next(SB);
+        bar_expect_tx(&b_full[sr.slot], G::B_BYTES);
+        tma_load_2d(smem_u32(b_ring + sr.slot * G::B_BYTES), &tm_act, kit * kBlockK, t.row0 + t.n0,
+                    smem_u32(&b_full[sr.slot]));
+        sr.next(S);
         ++nb;
         GG_INC(19);
       }
       if (!ok) break;
+      t = tn;
     }
     // every copy issued must land before the CTA's shared memory goes away (after an
     // abort its consumers may never have waited for it): wait for the last use of each
@@ -795,7 +982,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     };
     drain(sc_full, ns, NSB);
     drain(code_full, nc, RS);
-    drain(b_full, nb, SB);
+    drain(b_full, nb, S);
   }
 
 #ifdef BIGRIG_GEMM_PROFILE
@@ -866,11 +1053,11 @@ static int launch_one(const void* act, const RouteView& rv, const void* slab,
   using G = GemmShape<MODE, BN, BITS>;
   const int K = MODE == 0 ? L.hidden : L.inter, NF = MODE == 0 ? L.inter : L.hidden;
   const int gpitch = K / L.group_size;
-  GemmRings rg{0, 0, 0, (G::NMAT * 2 * kBlockM * gpitch * 2 + 127) & ~127};
-  static const int prefs[][3] = {{3, 4, 2}, {2, 4, 2}, {2, 3, 2}, {3, 4, 1}, {2, 4, 1}, {2, 3, 1}, {2, 2, 1}};
+  GemmRings rg{0, G::SA, 0, (G::NMAT * 2 * kBlockM * gpitch * 2 + 127) & ~127};
+  static const int prefs[][2] = {{3, 2}, {2, 2}, {3, 1}, {2, 1}};   // (code slots, scale buffers)
   for (const auto& c : prefs)
-    if (G::smem(c[0], c[1], c[2], rg.sc_bytes) <= static_cast<size_t>(G::kLimit)) {
-      rg.rs = c[0]; rg.sb = c[1]; rg.nsb = c[2];
+    if (G::smem(c[0], G::SA, c[1], rg.sc_bytes) <= static_cast<size_t>(G::kLimit)) {
+      rg.rs = c[0]; rg.nsb = c[1];
       break;
     }
   if (!rg.rs)
@@ -931,9 +1118,9 @@ static int sm_count() {
 int gemm_mean_rows(int T, int k, int E) { return (T * k + E - 1) / E; }
 
 // Token tile of a pass: the smallest offered that covers 1.25x the mean rows, so most
-// experts take one slice (or the fewest equal slices) per feature tile.  Gate/up tiles
-// stop at 160 columns (two accumulators of 2 x 160 plus the A slots fill TMEM), down
-// tiles at 256.
+// experts take one slice (or the fewest equal slices) per feature tile.  Tiles stop at
+// 160 columns: gate/up's one accumulator of 2 x 160 plus the A slots fill TMEM, and
+// down keeps two accumulators (the epilogue of one tile overlaps the next one's MMAs).
 static int pick_tile(int mean, const int* opts, int n) {
   const int want = (mean * 5 + 3) / 4;
   for (int i = 0; i < n; ++i)
@@ -978,12 +1165,12 @@ int launch_gemm_down(const void* h, const RouteView& rv, const void* slab,
                      const bigrig_expert_layout& L, void* y, int mean_rows, cudaStream_t s) {
   if (L.group_size % sm100::kBlockK)
     return set_error(BIGRIG_ERR_UNSUPPORTED, "grouped_gemm: group_size must be a multiple of 64");
-  static const int opts[] = {32, 64, 128, 256};
+  static const int opts[] = {32, 64, 128, 160};
   switch (pick_tile(mean_rows, opts, 4)) {
     case 32: return sm100::dispatch_fmt<1, 32>(h, rv, slab, L, y, s, sm_count());
     case 64: return sm100::dispatch_fmt<1, 64>(h, rv, slab, L, y, s, sm_count());
     case 128: return sm100::dispatch_fmt<1, 128>(h, rv, slab, L, y, s, sm_count());
-    case 256: return sm100::dispatch_fmt<1, 256>(h, rv, slab, L, y, s, sm_count());
+    case 160: return sm100::dispatch_fmt<1, 160>(h, rv, slab, L, y, s, sm_count());
   }
   return set_error(BIGRIG_ERR_INVALID, "grouped_gemm: mean rows %d", mean_rows);
 }
