@@ -460,23 +460,29 @@ __device__ __forceinline__ uint32_t lds16(uint32_t addr) {
 template <int MODE, int BN, int BITS>
 struct GemmShape {
   static constexpr int NMAT = MODE == 0 ? 2 : 1;
-  static constexpr int ROW_BYTES = kBlockK * BITS / 8;            // one row's codes per iteration
-  static constexpr int F = 128 / ROW_BYTES;                       // iterations per code box
-  static constexpr int CPI = ROW_BYTES / 16;                      // 16-byte chunks per iteration
-  static constexpr int JT = MODE == 0 ? CPI : CPI / 2;            // chunks per thread
+  // K-steps of 64 per iteration (one slot, one handoff, one commit): the down pass has
+  // one matrix, so it takes two steps to give each handoff eight MMAs like gate/up
+  static constexpr int KS = MODE == 0 ? 1 : 2;
+  static constexpr int ROW_BYTES = kBlockK * BITS / 8;            // one row's codes per step
+  static constexpr int F = 128 / ROW_BYTES;                       // steps per code box
+  static constexpr int IPB = F / KS;                              // iterations per code box
+  static constexpr int CPI = ROW_BYTES / 16;                      // 16-byte chunks per step
+  static constexpr int JT = CPI;                                  // chunks per thread and step
   static constexpr int WPC = 64 / BITS;                           // A words per code chunk
-  static constexpr int AW = JT * WPC;                             // A words per thread
+  static constexpr int AW = JT * WPC;                             // A words per thread (32)
+  static constexpr int SLOT_COLS = NMAT * KS * 32;                // TMEM columns of an A slot
   static constexpr int CODE_BOX = kBlockM * 128;
   static constexpr int CODE_SLOT = NMAT * CODE_BOX;
-  static constexpr int B_BYTES = BN * kBlockK * 2;
-  // TMEM: SA A slots of NMAT x 32 columns, then NBUF accumulators of NMAT x BN columns.
-  // Two accumulators (the epilogue drains one while the MMA fills the other) with 3
-  // or 2 A slots where they fit, else one accumulator.
+  static constexpr int B_BOX = BN * kBlockK * 2;                  // one step's token rows
+  static constexpr int B_BYTES = KS * B_BOX;
+  // TMEM: SA A slots, then NBUF accumulators of NMAT x BN columns.  Two accumulators (the
+  // epilogue drains one while the MMA fills the other) with as many A slots as fit (up
+  // to 4, at least 2), else one accumulator and 3 slots.
   static constexpr int ACC_COLS = NMAT * BN;
-  static constexpr int SA_MAX = MODE == 0 ? 3 : 4;
-  static constexpr int SA = SA_MAX * NMAT * 32 + 2 * ACC_COLS <= 512 ? SA_MAX
-                          : 2 * NMAT * 32 + 2 * ACC_COLS <= 512 ? 2 : SA_MAX;
-  static constexpr int A_COLS = SA * NMAT * 32;
+  static constexpr int SA = 4 * SLOT_COLS + 2 * ACC_COLS <= 512 ? 4
+                          : 3 * SLOT_COLS + 2 * ACC_COLS <= 512 ? 3
+                          : 2 * SLOT_COLS + 2 * ACC_COLS <= 512 ? 2 : 3;
+  static constexpr int A_COLS = SA * SLOT_COLS;
   static constexpr int NBUF = A_COLS + 2 * ACC_COLS <= 512 ? 2 : 1;  // accumulator buffers
   static constexpr int TMEM_COLS = 512;
   static constexpr int kMeta = 2048;                              // barriers, flags, tile prefix
@@ -486,7 +492,7 @@ struct GemmShape {
            static_cast<size_t>(nsb) * sc_bytes + kMeta;
   }
   static_assert(A_COLS + NBUF * ACC_COLS <= TMEM_COLS, "grouped_gemm: TMEM columns");
-  static_assert(JT >= 1 && (AW == 16 || AW == 32), "grouped_gemm: mapping");
+  static_assert(AW == 32 && F % KS == 0, "grouped_gemm: mapping");
 };
 
 struct GemmRings {
@@ -557,6 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     uint16_t* __restrict__ out) {       // MODE 0: h [P, I]; MODE 1: y [P, H] ((token, k) order)
   using G = GemmShape<MODE, BN, BITS>;
   constexpr int NMAT = G::NMAT, JT = G::JT, NBUF = G::NBUF, WPC = G::WPC, F = G::F, CPI = G::CPI;
+  constexpr int KS = G::KS, IPB = G::IPB;
   constexpr int S = G::SA;               // slots: an A slot in TMEM and a B slot in smem
   constexpr int OT = operand_type(BITS, SDT);
   const int RS = rg.rs, NSB = rg.nsb;
@@ -586,7 +593,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   const int K = MODE == 0 ? L.hidden : L.inter;        // reduction length
   const int NF = MODE == 0 ? L.inter : L.hidden;       // output features
   const int m_tiles = (NF + kBlockM - 1) / kBlockM;
-  const int k_iters = K / kBlockK;
+  const int k_steps = K / kBlockK;                     // 64-element K steps
+  const int k_iters = (k_steps + KS - 1) / KS;         // iterations (slots) per tile
   const int gpitch = K / L.group_size;
   const int nseg = min(min(*rv.num_seg, rv.s_max), kMaxExperts);
 
@@ -638,12 +646,12 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     // ---------------------------------------------------------------- producers
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;                      // tile row = TMEM lane
-    const int mat = MODE == 0 ? half : 0;
-    const int chalf = MODE == 0 ? 0 : half * JT;            // first chunk of the iteration
+    const int mat = MODE == 0 ? half : 0;                   // gate/up: the matrix
+    const int ts = MODE == 0 ? 0 : half;                    // down: the step of the iteration
     const uint32_t code_base = smem_u32(code_ring) + mat * G::CODE_BOX + r * 128;
     const uint32_t sc_base = smem_u32(sc_ring) + (mat * 2) * sc_half + r * gpitch * 2;
-    // this thread's A columns: slot s at s * NMAT * 32 + mat * 32 + chalf * WPC, lane r
-    const uint32_t a_taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + mat * 32 + chalf * WPC;
+    // this thread's A columns: slot s at s * SLOT_COLS + mat * KS * 32 + ts * 32, lane r
+    const uint32_t a_taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + mat * KS * 32 + ts * 32;
     // a row's scales start 16-byte aligned when K / group_size is a multiple of 8: then
     // eight groups come in one 16-byte read (lanes are rows gpitch * 2 bytes apart, so
     // per-group 2-byte reads would pile onto two banks)
@@ -680,27 +688,25 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       GG_ADD(7, t7);
       const uint32_t s_addr = sc_base + sb * rg.sc_bytes, b_addr = s_addr + sc_half;
       uint4 s8 = make_uint4(0, 0, 0, 0), b8 = s8;
-      // group of the current iteration, counted without a division: a group spans
-      // ipg = group_size / 64 iterations
-      int grp = 0, gleft = ipg;
-      for (int kit0 = 0; kit0 < k_iters && ok; kit0 += F) {
-        // this thread's codes of all F iterations of the box, read at once; the box is
-        // handed back to the loader right away
+      int cur8 = -1;                          // block of 8 groups held in s8 / b8
+      for (int kit0 = 0; kit0 < k_steps && ok; kit0 += F) {
+        // this thread's codes of its steps of the box's IPB iterations, read at once;
+        // the box is handed back to the loader right away
         GG_T(t0);
         if (!__all_sync(0xffffffffu, mbar_wait(&code_full[cr.slot], cr.phase, abort_flag, rv.err, 2))) {
-          bail(kit0, true);
+          bail(kit0 / KS, true);
           break;
         }
         GG_ADD(0, t0);
         const uint32_t cb = code_base + cr.slot * G::CODE_SLOT;
-        uint4 wb[F][JT];
+        uint4 wb[IPB][JT];
         uint32_t landed = 0;
 #pragma unroll
-        for (int sub = 0; sub < F; ++sub)
+        for (int ib = 0; ib < IPB; ++ib)
 #pragma unroll
           for (int c = 0; c < JT; ++c) {
-            wb[sub][c] = lds128(cb + (((sub * CPI + chalf + c) ^ (r & 7)) << 4));
-            landed ^= wb[sub][c].w;
+            wb[ib][c] = lds128(cb + ((((ib * KS + ts) * CPI + c) ^ (r & 7)) << 4));
+            landed ^= wb[ib][c].w;
           }
         // the loads must have returned before the box goes back to the loader (its next
         // TMA box overwrites it): an instruction reading every load's result makes the
@@ -710,47 +716,55 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         if (lane == 0) mbar_arrive(&code_empty[cr.slot]);
         cr.next(RS);
 #pragma unroll
-        for (int sub = 0; sub < F; ++sub) {
-          if (kit0 + sub >= k_iters || !ok) break;
+        for (int ib = 0; ib < IPB; ++ib) {
+          const int it_step = kit0 + ib * KS;       // first step of this iteration
+          if (it_step >= k_steps || !ok) break;
+          const int kstep = it_step + ts;           // this thread's step
+          const bool have = kstep < k_steps;        // (an odd last step has no partner)
           GG_T(t2);
-          uint32_t sh, bh;
-          if (s_vec) {
-            if ((grp & 7) == 0 && gleft == ipg) {   // first iteration of a block of 8 groups
-              s8 = lds128(s_addr + (grp >> 3) * 16);
-              b8 = lds128(b_addr + (grp >> 3) * 16);
-            }
-            const int wi = (grp >> 1) & 3, hs = (grp & 1) * 16;
-            sh = ((wi == 0 ? s8.x : wi == 1 ? s8.y : wi == 2 ? s8.z : s8.w) >> hs) & 0xFFFFu;
-            bh = ((wi == 0 ? b8.x : wi == 1 ? b8.y : wi == 2 ? b8.z : b8.w) >> hs) & 0xFFFFu;
-          } else {
-            sh = lds16(s_addr + grp * 2);
-            bh = lds16(b_addr + grp * 2);
-          }
-          if (--gleft == 0) { ++grp; gleft = ipg; }
           uint32_t av[G::AW];
-          if constexpr (BITS == 4) {           // operands in the scale dtype itself
-            const uint32_t s2 = sh * 0x10001u, b2 = bh * 0x10001u;
+          if (have) {
+            const int grp = ipg == 1 ? kstep : kstep / ipg;
+            uint32_t sh, bh;
+            if (s_vec) {
+              if ((grp >> 3) != cur8) {
+                cur8 = grp >> 3;
+                s8 = lds128(s_addr + cur8 * 16);
+                b8 = lds128(b_addr + cur8 * 16);
+              }
+              const int wi = (grp >> 1) & 3, hs = (grp & 1) * 16;
+              sh = ((wi == 0 ? s8.x : wi == 1 ? s8.y : wi == 2 ? s8.z : s8.w) >> hs) & 0xFFFFu;
+              bh = ((wi == 0 ? b8.x : wi == 1 ? b8.y : wi == 2 ? b8.z : b8.w) >> hs) & 0xFFFFu;
+            } else {
+              sh = lds16(s_addr + grp * 2);
+              bh = lds16(b_addr + grp * 2);
+            }
+            if constexpr (BITS == 4) {         // operands in the scale dtype itself
+              const uint32_t s2 = sh * 0x10001u, b2 = bh * 0x10001u;
 #pragma unroll
-            for (int c = 0; c < JT; ++c) dequant_chunk4<OT>(wb[sub][c], s2, b2, av + c * WPC);
-          } else {
-            const float sv = half_to_f32<SDT>(static_cast<uint16_t>(sh));
-            const float bv = half_to_f32<SDT>(static_cast<uint16_t>(bh));
+              for (int c = 0; c < JT; ++c) dequant_chunk4<OT>(wb[ib][c], s2, b2, av + c * WPC);
+            } else {
+              const float sv = half_to_f32<SDT>(static_cast<uint16_t>(sh));
+              const float bv = half_to_f32<SDT>(static_cast<uint16_t>(bh));
 #pragma unroll
-            for (int c = 0; c < JT; ++c) dequant_chunk8(wb[sub][c], sv, bv, av + c * WPC);
+              for (int c = 0; c < JT; ++c) dequant_chunk8(wb[ib][c], sv, bv, av + c * WPC);
+            }
           }
           GG_ADD(2, t2);
           GG_T(t1);
           const int why = mbar_wait_why(&s_empty[ar.slot], ar.phase ^ 1, abort_flag, rv.err, 3);
           if (__any_sync(0xffffffffu, why != 0)) {
             // ran out: the MMAs are stuck, one last arrival; aborted: catch up, throttled
-            bail(kit0 + sub, !__any_sync(0xffffffffu, why == 2));
+            bail(it_step / KS, !__any_sync(0xffffffffu, why == 2));
             break;
           }
           tc_fence_after();
           GG_ADD(1, t1);
           GG_T(t3);
-          tmem_st<G::AW>(a_taddr + ar.slot * (NMAT * 32), av);
-          tmem_wait_st();
+          if (have) {
+            tmem_st<G::AW>(a_taddr + ar.slot * G::SLOT_COLS, av);
+            tmem_wait_st();
+          }
           tc_fence_before();                  // TMEM stores -> the MMA after the barrier
           // warp 0 also sees this iteration's token rows land, so a completed handoff
           // means both operands are in place
@@ -762,7 +776,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
           GG_ADD(3, t3);
           GG_INC(6);
           if (!bok) {                         // arrived for this iteration: catch up after it
-            if (kit0 + sub + 1 < k_iters) bail(kit0 + sub + 1, true);
+            if (it_step / KS + 1 < k_iters) bail(it_step / KS + 1, true);
             ok = false;
             break;
           }
@@ -883,14 +897,21 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t ast = tmem + ar.slot * (NMAT * 32);
+          const uint32_t ast = tmem + ar.slot * G::SLOT_COLS;
           const uint32_t bst = smem_u32(b_ring + ar.slot * G::B_BYTES);
+          const int steps = min(KS, k_steps - kit * KS);
 #pragma unroll
-          for (int kk = 0; kk < kBlockK / 16; ++kk) {
-            const uint64_t db = smem_desc(bst + kk * 32);
+          for (int st = 0; st < KS; ++st) {
+            if (st < steps) {
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m)
-              mma_tmem_a(acc + m * BN, ast + m * 32 + kk * 8, db, idesc, (kit > 0 || kk > 0) ? 1u : 0u);
+              for (int kk = 0; kk < kBlockK / 16; ++kk) {
+                const uint64_t db = smem_desc(bst + st * G::B_BOX + kk * 32);
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+                  mma_tmem_a(acc + m * BN, ast + m * KS * 32 + st * 32 + kk * 8, db, idesc,
+                             (kit > 0 || st > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
           }
           mma_commit(&s_empty[ar.slot]);      // A and B slot free once these MMAs are done
           if (kit == k_iters - 1) mma_commit(&acc_full[buf]);
@@ -941,13 +962,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       }
       bool ok = true;
       for (int kit = 0; kit < k_iters && ok; ++kit) {
-        if (kit % F == 0) {
+        if ((kit * KS) % F == 0) {
           GG_T(t17);
           if (!mbar_wait(&code_empty[cr.slot], cr.phase ^ 1, abort_flag, rv.err, 9)) { ok = false; break; }
           GG_ADD(17, t17);
           bar_expect_tx(&code_full[cr.slot], NMAT * G::CODE_BOX);
           const uint32_t dst = smem_u32(code_ring + cr.slot * G::CODE_SLOT);
-          const int x = kit * G::ROW_BYTES;
+          const int x = kit * KS * G::ROW_BYTES;
           tma_load_3d(dst, &tm_code0, x, t.m0, slot, smem_u32(&code_full[cr.slot]));
           if (NMAT == 2)
             tma_load_3d(dst + G::CODE_BOX, &tm_code1, x, t.m0, slot, smem_u32(&code_full[cr.slot]));
@@ -960,9 +981,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         GG_T(t18);
         if (!mbar_wait(&s_empty[sr.slot], sr.phase ^ 1, abort_flag, rv.err, 10)) { ok = false; break; }
         GG_ADD(18, t18);
-        bar_expect_tx(&b_full[sr.slot], G::B_BYTES);
-        tma_load_2d(smem_u32(b_ring + sr.slot * G::B_BYTES), &tm_act, kit * kBlockK, t.row0 + t.n0,
-                    smem_u32(&b_full[sr.slot]));
+        const int steps = min(KS, k_steps - kit * KS);
+        bar_expect_tx(&b_full[sr.slot], steps * G::B_BOX);
+        for (int st = 0; st < steps; ++st)
+          tma_load_2d(smem_u32(b_ring + sr.slot * G::B_BYTES + st * G::B_BOX), &tm_act,
+                      (kit * KS + st) * kBlockK, t.row0 + t.n0, smem_u32(&b_full[sr.slot]));
         sr.next(S);
         ++nb;
         GG_INC(19);
@@ -1043,6 +1066,10 @@ static bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, cuuint32_t rank, 
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// launch_one's answer when the rings for this token tile and K do not fit in shared
+// memory (not an error: a smaller tile may fit).
+constexpr int kNoFit = 1 << 20;
+
 // Slots a code map may address: the slab's extent is not passed in, and a TMA box only
 // touches the slot it is given.
 constexpr cuuint64_t kMapSlots = 1u << 16;
@@ -1060,8 +1087,7 @@ static int launch_one(const void* act, const RouteView& rv, const void* slab,
       rg.rs = c[0]; rg.nsb = c[1];
       break;
     }
-  if (!rg.rs)
-    return set_error(BIGRIG_ERR_UNSUPPORTED, "grouped_gemm: K=%d needs more shared memory than a CTA has", K);
+  if (!rg.rs) return kNoFit;                          // the caller tries a smaller token tile
   const size_t smem = G::smem(rg.rs, rg.sb, rg.nsb, rg.sc_bytes);
 
   CUtensorMap tm[3];
@@ -1077,7 +1103,7 @@ static int launch_one(const void* act, const RouteView& rv, const void* slab,
   {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rv.P)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-    const cuuint32_t box[2] = {kBlockK, BN};
+    const cuuint32_t box[2] = {kBlockK, BN};         // one step's rows (G::B_BOX bytes)
     if (!encode_map(&tm[2], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, act, dims, strides, box))
       return set_error(BIGRIG_ERR_CUDA, "grouped_gemm: cannot encode the token tensor map");
   }
@@ -1121,11 +1147,13 @@ int gemm_mean_rows(int T, int k, int E) { return (T * k + E - 1) / E; }
 // experts take one slice (or the fewest equal slices) per feature tile.  Tiles stop at
 // 160 columns: gate/up's one accumulator of 2 x 160 plus the A slots fill TMEM, and
 // down keeps two accumulators (the epilogue of one tile overlaps the next one's MMAs).
+// When the rings of that tile do not fit in shared memory for this K (large K means
+// large per-tile scale blocks), the next smaller tile is used.
 static int pick_tile(int mean, const int* opts, int n) {
   const int want = (mean * 5 + 3) / 4;
   for (int i = 0; i < n; ++i)
-    if (opts[i] >= want) return opts[i];
-  return opts[n - 1];
+    if (opts[i] >= want) return i;
+  return n - 1;
 }
 
 int launch_gemm_gate_up(const void* x, const RouteView& rv, const void* slab,
@@ -1151,14 +1179,19 @@ int launch_gemm_gate_up(const void* x, const RouteView& rv, const void* slab,
     if (int rc = check_launch("gather_rows")) return rc;
   }
   static const int opts[] = {32, 64, 96, 128, 160};
-  switch (pick_tile(mean_rows, opts, 5)) {
-    case 32: return sm100::dispatch_fmt<0, 32>(xs, rv, slab, L, h, s, sm_count());
-    case 64: return sm100::dispatch_fmt<0, 64>(xs, rv, slab, L, h, s, sm_count());
-    case 96: return sm100::dispatch_fmt<0, 96>(xs, rv, slab, L, h, s, sm_count());
-    case 128: return sm100::dispatch_fmt<0, 128>(xs, rv, slab, L, h, s, sm_count());
-    case 160: return sm100::dispatch_fmt<0, 160>(xs, rv, slab, L, h, s, sm_count());
+  for (int i = pick_tile(mean_rows, opts, 5); i >= 0; --i) {
+    int rc = sm100::kNoFit;
+    switch (opts[i]) {
+      case 32: rc = sm100::dispatch_fmt<0, 32>(xs, rv, slab, L, h, s, sm_count()); break;
+      case 64: rc = sm100::dispatch_fmt<0, 64>(xs, rv, slab, L, h, s, sm_count()); break;
+      case 96: rc = sm100::dispatch_fmt<0, 96>(xs, rv, slab, L, h, s, sm_count()); break;
+      case 128: rc = sm100::dispatch_fmt<0, 128>(xs, rv, slab, L, h, s, sm_count()); break;
+      case 160: rc = sm100::dispatch_fmt<0, 160>(xs, rv, slab, L, h, s, sm_count()); break;
+    }
+    if (rc != sm100::kNoFit) return rc;
   }
-  return set_error(BIGRIG_ERR_INVALID, "grouped_gemm: mean rows %d", mean_rows);
+  return set_error(BIGRIG_ERR_UNSUPPORTED, "grouped_gemm: hidden=%d needs more shared memory than a CTA has",
+                   L.hidden);
 }
 
 int launch_gemm_down(const void* h, const RouteView& rv, const void* slab,
@@ -1166,13 +1199,18 @@ int launch_gemm_down(const void* h, const RouteView& rv, const void* slab,
   if (L.group_size % sm100::kBlockK)
     return set_error(BIGRIG_ERR_UNSUPPORTED, "grouped_gemm: group_size must be a multiple of 64");
   static const int opts[] = {32, 64, 128, 160};
-  switch (pick_tile(mean_rows, opts, 4)) {
-    case 32: return sm100::dispatch_fmt<1, 32>(h, rv, slab, L, y, s, sm_count());
-    case 64: return sm100::dispatch_fmt<1, 64>(h, rv, slab, L, y, s, sm_count());
-    case 128: return sm100::dispatch_fmt<1, 128>(h, rv, slab, L, y, s, sm_count());
-    case 160: return sm100::dispatch_fmt<1, 160>(h, rv, slab, L, y, s, sm_count());
+  for (int i = pick_tile(mean_rows, opts, 4); i >= 0; --i) {
+    int rc = sm100::kNoFit;
+    switch (opts[i]) {
+      case 32: rc = sm100::dispatch_fmt<1, 32>(h, rv, slab, L, y, s, sm_count()); break;
+      case 64: rc = sm100::dispatch_fmt<1, 64>(h, rv, slab, L, y, s, sm_count()); break;
+      case 128: rc = sm100::dispatch_fmt<1, 128>(h, rv, slab, L, y, s, sm_count()); break;
+      case 160: rc = sm100::dispatch_fmt<1, 160>(h, rv, slab, L, y, s, sm_count()); break;
+    }
+    if (rc != sm100::kNoFit) return rc;
   }
-  return set_error(BIGRIG_ERR_INVALID, "grouped_gemm: mean rows %d", mean_rows);
+  return set_error(BIGRIG_ERR_UNSUPPORTED, "grouped_gemm: inter=%d needs more shared memory than a CTA has",
+                   L.inter);
 }
 
 }  // namespace bigrig
