@@ -333,19 +333,33 @@ def main() -> None:
         if world > 1:
             for b in stack:
                 b.padded = False             # prompt chunks exchange exact row counts
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.nvtx.range_push("prefill")
-        e0.record()
-        layered.prefill(layers, layered.chunks(prompt, c["prefill_chunk"]),
+
+        def capped_prefill(token_wise, name):
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.nvtx.range_push(name)
+            e0.record()
+            layered.prefill(layers, layered.chunks(prompt, c["prefill_chunk"]),
+                            layer_scope=handle.prefill_layer, token_wise=token_wise)
+            e1.record()
+            torch.cuda.nvtx.range_pop()
+            barrier()
+            return max_over_ranks(e0.elapsed_time(e1))
+
+        # a one-chunk pass first: library set-up (workspaces, tensor maps) outside the timing
+        layered.prefill(layers, layered.chunks(prompt[:c["prefill_chunk"]], c["prefill_chunk"]),
                         layer_scope=handle.prefill_layer)
-        e1.record()
-        torch.cuda.nvtx.range_pop()
-        barrier()
-        pf_ms = max_over_ranks(e0.elapsed_time(e1))
+        pf_ms = capped_prefill(True, "prefill")
+        pfc_ms = capped_prefill(False, "prefill_chunked")
         extras["prefill_tok_s"] = world * c["prompt"] / (pf_ms / 1e3)
-        extras["prefill_note"] = ("2048-token prompt, layer-major in chunks of 512, expert-sorted "
-                                  "spans through the capped pools, tcgen05 grouped GEMM")
+        extras["prefill_chunked_tok_s"] = world * c["prompt"] / (pfc_ms / 1e3)
+        extras["prefill_note"] = ("2048-token prompt, layer-major through the capped pools: "
+                                  "prefill_tok_s token-wise (each layer once over the whole "
+                                  "prompt, so every expert crosses PCIe once per layer), "
+                                  "prefill_chunked_tok_s in the reference's chunks of 512 (a "
+                                  "layer's experts cycle through the pool once per chunk); "
+                                  "expert-sorted spans of <= capacity experts, tcgen05 grouped "
+                                  "GEMM")
         if world > 1:
             for b in stack:
                 b.padded = b.switch._sync_free

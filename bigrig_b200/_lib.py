@@ -27,7 +27,7 @@ EXPORTS = (
     "bigrig_dequant", "bigrig_router_logits", "bigrig_router_topk", "bigrig_moe_permute",
     "bigrig_switch_glu", "bigrig_combine", "bigrig_moe_forward", "bigrig_workspace_errors",
     "bigrig_timing_enable", "bigrig_timing_read", "bigrig_launch_counts", "bigrig_kernel_name",
-    "bigrig_set_path", "bigrig_moe_layer", "bigrig_switch_glu_noalloc", "bigrig_copy_regions",
+    "bigrig_set_path", "bigrig_get_path", "bigrig_moe_layer", "bigrig_switch_glu_noalloc", "bigrig_copy_regions",
 )
 NOALLOC_SCRATCH_BYTES = 4 << 20
 KERNELS = {"router_logits": 0, "router_topk": 1, "permute": 2, "gate_up": 3, "down": 4,
@@ -77,6 +77,7 @@ _SIG = {
     "bigrig_launch_counts": (_I, [ctypes.POINTER(ctypes.c_int64)]),
     "bigrig_kernel_name": (ctypes.c_char_p, [_I]),
     "bigrig_set_path": (_I, [_I, _I]),
+    "bigrig_get_path": (_I, [_P, _P]),
     "bigrig_moe_layer": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, ctypes.POINTER(ExpertLayout),
                               _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     "bigrig_switch_glu_noalloc": (_I, [_P, _P, _I, _I, _I, _P, _P, ctypes.POINTER(ExpertLayout),
@@ -156,6 +157,13 @@ def timing_read(kernel: str) -> tuple:
     check(load().bigrig_timing_read(KERNELS[kernel], ctypes.byref(ms), ctypes.byref(n)),
           "timing_read")
     return float(ms.value), int(n.value)
+
+
+def get_path() -> tuple:
+    """(mode, gemm_min_rows) as set_path last set them."""
+    mode, rows = ctypes.c_int(0), ctypes.c_int(0)
+    check(load().bigrig_get_path(ctypes.byref(mode), ctypes.byref(rows)), "get_path")
+    return {v: k for k, v in PATHS.items()}[mode.value], int(rows.value)
 
 
 def set_path(mode: str = "auto", gemm_min_rows: int = 8) -> str:

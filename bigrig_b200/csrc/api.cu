@@ -410,6 +410,12 @@ int bigrig_set_path(int mode, int gemm_min_rows) {
   return prev;
 }
 
+int bigrig_get_path(int* mode, int* gemm_min_rows) {
+  if (mode) *mode = g_path.load();
+  if (gemm_min_rows) *gemm_min_rows = g_gemm_min_rows.load();
+  return BIGRIG_OK;
+}
+
 int bigrig_timing_enable(int mask) {
   g_timing_on.store(mask);
   return BIGRIG_OK;

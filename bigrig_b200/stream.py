@@ -35,7 +35,7 @@ import time
 import numpy as np
 import torch
 
-from . import ops
+from . import _lib, ops
 from .formats import PROJECTIONS, bytes_per_expert, layout_from_spec
 from .pool import _policy_factory
 
@@ -704,14 +704,42 @@ class StreamingSwitchGLU:
         tok = order // k
         rank = order % k
         y = torch.empty(pe.shape[0], H, dtype=torch.bfloat16, device=x2.device)
+        spans = _pair_chunks(spe, pool.capacity)
+        # Each span's experts renumbered 0..U-1 (sorted pairs: the rank among the span's
+        # distinct experts) with a span-local expert->slot table, so that the expert GEMM
+        # sees U experts sharing the span's rows -- its token tile follows the real rows per
+        # expert -- instead of all E.  Host tables for every span go up in one copy.
+        local = np.empty(spe.shape[0], dtype=np.int32)
+        n_loc = []
+        for lo, hi in spans:
+            uniq, inv = np.unique(spe[lo:hi], return_inverse=True)
+            local[lo:hi] = inv
+            n_loc.append(len(uniq))
         order_dev = torch.from_numpy(order).to(x2.device)
         tok_dev = torch.from_numpy(tok).to(x2.device)
-        spe_dev = torch.from_numpy(spe.astype(np.int32)).to(x2.device)
-        for lo, hi in _pair_chunks(spe, pool.capacity):
-            self.ensure(spe[lo:hi], ranks=rank[lo:hi])
-            rows = x2.index_select(0, tok_dev[lo:hi]).contiguous()
-            part = self._run(rows, spe_dev[lo:hi].reshape(-1, 1).contiguous(), pool.g2s_device())
-            y.index_copy_(0, order_dev[lo:hi], part.reshape(hi - lo, H))
+        local_dev = torch.from_numpy(local).to(x2.device)
+        # The expert kernel is the one the whole call would take (decided on its pairs and
+        # all E experts), forced for every span: both kernels are batch-invariant, so the
+        # spans then give the whole call's bits (a span's own size could pick the other).
+        mode, min_rows = _lib.get_path()
+        forced = None
+        if mode in ("auto", "chain"):
+            P, E = pe.shape[0], pool.n_experts
+            forced = "gemm" if P >= min_rows * min(P, E) else "gemv"
+            _lib.set_path(forced, min_rows)
+        try:
+            for (lo, hi), u in zip(spans, n_loc):
+                self.ensure(spe[lo:hi], ranks=rank[lo:hi])
+                g2s_loc = torch.from_numpy(pool.g2s[np.unique(spe[lo:hi])].astype(np.int32)).to(x2.device)
+                rows = x2.index_select(0, tok_dev[lo:hi]).contiguous()
+                pool.ready()
+                part = ops.switch_glu(rows, local_dev[lo:hi].reshape(-1, 1).contiguous(), pool.slab,
+                                      pool.layout, u, g2s=g2s_loc, workspace=self.workspace)
+                pool.mark_read()
+                y.index_copy_(0, order_dev[lo:hi], part.reshape(hi - lo, H))
+        finally:
+            if forced is not None:
+                _lib.set_path(mode, min_rows)
         return y.reshape(*lead, k, H)
 
     # -- prefill holding / read-ahead (stream.py:1174-1235) ----------------------

@@ -162,6 +162,9 @@ BIGRIG_API int bigrig_moe_forward(const void* x, const void* logits, int logits_
 #define BIGRIG_PATH_CHAIN 3
 BIGRIG_API int bigrig_set_path(int mode, int gemm_min_rows);
 
+/* The current path mode and gemm_min_rows (either pointer may be NULL); 0. */
+BIGRIG_API int bigrig_get_path(int* mode, int* gemm_min_rows);
+
 /* CUDA-event timing of this library's kernel launches, off by default.  `mask`
  * selects kernel ids (bit i = id i); each selected launch is bracketed by two
  * events on its own stream (do not enable it while a stream is being captured
