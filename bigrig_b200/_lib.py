@@ -167,8 +167,9 @@ def get_path() -> tuple:
 
 
 def set_path(mode: str = "auto", gemm_min_rows: int = 8) -> str:
-    """Choose the expert kernels: "auto" (GEMV for decode-sized calls, the tcgen05 grouped
-    GEMM once the mean rows per routed expert reaches ``gemm_min_rows``, one-token
+    """Choose the expert kernels: "auto" (GEMV for calls of at most 32 routed pairs, the
+    tcgen05 grouped GEMM above that or once the mean rows per routed expert reaches
+    ``gemm_min_rows``, one-token
     ``moe_layer`` calls as one persistent kernel), "gemv" or "gemm" (force one expert
     path), or "chain" ("auto" with one-token layers on the three-kernel chain).  Returns
     the previous mode."""

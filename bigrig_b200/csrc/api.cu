@@ -60,6 +60,7 @@ const char* kKernelNames[BIGRIG_K_COUNT] = {
     "route_kernel",         "down_combine_kernel", "decode_layer_kernel"};
 std::atomic<int> g_path{BIGRIG_PATH_AUTO};
 std::atomic<int> g_gemm_min_rows{8};
+constexpr int kDecodePairs = 32;     // routed pairs the fused decode chain / GEMV path takes
 }  // namespace
 
 TimedLaunch::TimedLaunch(int kernel_id, cudaStream_t s) : id_(kernel_id), s_(s), start_(nullptr) {
@@ -202,7 +203,7 @@ RouteView route_view(const Workspace& ws, const int32_t* g2s, int T, int k, int 
 // Decode-sized calls take the fused three-kernel chain.
 bool fused_decode(int T, int k, const bigrig_expert_layout& L) {
   const int path = g_path.load();
-  return path != BIGRIG_PATH_GEMM && T * k <= 32 &&
+  return path != BIGRIG_PATH_GEMM && T * k <= kDecodePairs &&
          down_combine_smem(T * k, L) <= 200 * 1024;
 }
 
@@ -228,8 +229,12 @@ int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, c
     return rc;
   const RouteView rv = route_view(ws, g2s, T, k, E);
   const int path = g_path.load();
+  // The tensor-core GEMM once a call has more pairs than the decode chain takes (its
+  // dequant streams weights far faster than the GEMV's passes over an expert's rows, even
+  // at 16-column MMAs), or when the mean rows per routed expert reaches gemm_min_rows.
   const bool gemm = path == BIGRIG_PATH_GEMM ||
-                    ((path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_CHAIN) && P >= g_gemm_min_rows.load() * (P < E ? P : E));
+                    ((path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_CHAIN) &&
+                     (P > kDecodePairs || P >= g_gemm_min_rows.load() * (P < E ? P : E)));
   if (gemm) {
     const int mean = gemm_mean_rows(T, k, E);
     if (int rc = launch_gemm_gate_up(x, rv, slab, L, ws.h, ws.xp, T, mean, s)) return rc;

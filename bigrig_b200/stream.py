@@ -718,14 +718,14 @@ class StreamingSwitchGLU:
         order_dev = torch.from_numpy(order).to(x2.device)
         tok_dev = torch.from_numpy(tok).to(x2.device)
         local_dev = torch.from_numpy(local).to(x2.device)
-        # The expert kernel is the one the whole call would take (decided on its pairs and
-        # all E experts), forced for every span: both kernels are batch-invariant, so the
+        # The expert kernel is the one the whole call would take (the library's rule on its
+        # pairs and all E experts: the GEMM beyond 32 pairs), forced for every span: both kernels are batch-invariant, so the
         # spans then give the whole call's bits (a span's own size could pick the other).
         mode, min_rows = _lib.get_path()
         forced = None
         if mode in ("auto", "chain"):
             P, E = pe.shape[0], pool.n_experts
-            forced = "gemm" if P >= min_rows * min(P, E) else "gemv"
+            forced = "gemm" if P > 32 or P >= min_rows * min(P, E) else "gemv"
             _lib.set_path(forced, min_rows)
         try:
             for (lo, hi), u in zip(spans, n_loc):

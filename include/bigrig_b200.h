@@ -149,9 +149,9 @@ BIGRIG_API int bigrig_moe_forward(const void* x, const void* logits, int logits_
 #define BIGRIG_K_COUNT 12
 
 /* Which expert kernels bigrig_switch_glu / bigrig_moe_forward / bigrig_moe_layer use:
- * BIGRIG_PATH_AUTO picks the grouped GEMV when an expert gets few rows (decode)
- * and the tcgen05 grouped GEMM when the mean rows per routed expert reaches
- * `gemm_min_rows`, and runs a one-token bigrig_moe_layer as one persistent kernel;
+ * BIGRIG_PATH_AUTO picks the grouped GEMV for calls of at most 32 routed pairs (decode)
+ * and the tcgen05 grouped GEMM above that or when the mean rows per routed expert
+ * reaches `gemm_min_rows`, and runs a one-token bigrig_moe_layer as one persistent kernel;
  * BIGRIG_PATH_GEMV and BIGRIG_PATH_GEMM force one expert path; BIGRIG_PATH_CHAIN is
  * AUTO with one-token layers on the three-kernel chain instead of the persistent
  * kernel (the two give bit-identical results).  Process-wide; returns the previous
