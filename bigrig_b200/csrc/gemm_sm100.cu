@@ -474,7 +474,7 @@ struct GemmShape {
   static constexpr int CODE_BOX = kBlockM * 128;
   static constexpr int CODE_SLOT = NMAT * CODE_BOX;
   static constexpr int B_BOX = BN * kBlockK * 2;                  // one step's token rows
-  static constexpr int B_BYTES = KS * B_BOX;
+  static constexpr int B_BYTES = KS * B_BOX;                      // one token-row slot
   // TMEM: SA A slots, then NBUF accumulators of NMAT x BN columns.  Two accumulators (the
   // epilogue drains one while the MMA fills the other) with as many A slots as fit (up
   // to 4, at least 2), else one accumulator and 3 slots.
@@ -491,6 +491,11 @@ struct GemmShape {
     return 1024 + static_cast<size_t>(rs) * CODE_SLOT + static_cast<size_t>(sb) * B_BYTES +
            static_cast<size_t>(nsb) * sc_bytes + kMeta;
   }
+  // Token-row slots: the A slots' ring (one commit frees both) once a step carries enough
+  // MMA work to cover a TMA load's latency; small tiles (a few rows per expert, decode
+  // batches) get their own deeper ring of small slots and a second commit per step.
+  static constexpr int SB = BN <= 32 ? 12 : BN <= 64 ? 8 : SA;
+  static constexpr bool SPLIT_B = SB != SA;
   static_assert(A_COLS + NBUF * ACC_COLS <= TMEM_COLS, "grouped_gemm: TMEM columns");
   static_assert(AW == 32 && F % KS == 0, "grouped_gemm: mapping");
 };
@@ -574,12 +579,14 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* code_ring = smem;
   uint8_t* b_ring = code_ring + RS * G::CODE_SLOT;
-  uint8_t* sc_ring = b_ring + S * G::B_BYTES;
+  const int SB = G::SPLIT_B ? rg.sb : S;  // token-row slots (split rings: chosen at launch)
+  uint8_t* sc_ring = b_ring + SB * G::B_BYTES;
   uint64_t* code_full = reinterpret_cast<uint64_t*>(sc_ring + NSB * rg.sc_bytes);
   uint64_t* code_empty = code_full + RS;
-  uint64_t* b_full = code_empty + RS;
-  uint64_t* s_empty = b_full + S;        // slot free again: its MMAs completed (one commit)
-  uint64_t* sc_full = s_empty + S;
+  uint64_t* b_full = code_empty + RS;    // [G::SB]
+  uint64_t* s_empty = b_full + G::SB;    // A slot (and, unsplit, its B slot) free again
+  uint64_t* b_empty = s_empty + S;       // split rings only: token-row slot free again
+  uint64_t* sc_full = b_empty + G::SB;
   uint64_t* sc_empty = sc_full + 2;
   uint64_t* acc_full = sc_empty + 2;
   uint64_t* acc_empty = acc_full + 2;
@@ -603,10 +610,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       mbar_init(&code_full[i], 1);
       mbar_init(&code_empty[i], kProducerWarps);
     }
-    for (int i = 0; i < S; ++i) {
+    for (int i = 0; i < SB; ++i) {
       mbar_init(&b_full[i], 1);
-      mbar_init(&s_empty[i], 1);
+      mbar_init(&b_empty[i], 1);
     }
+    for (int i = 0; i < S; ++i) mbar_init(&s_empty[i], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sc_full[i], 1);
       mbar_init(&sc_empty[i], kProducerWarps);
@@ -657,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     // per-group 2-byte reads would pile onto two banks)
     const bool s_vec = (gpitch & 7) == 0;
     const int ipg = L.group_size / kBlockK;                 // iterations per scale group
-    Ring cr, ar;
+    Ring cr, ar, br;                          // br: token-row slots (split rings only)
     bool ok = true;
     // Every iteration of a tile gets exactly one arrival on its slot's named barrier from
     // every producer warp, on the way out too.  The MMA warp checks the abort flag once
@@ -769,7 +777,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
           // warp 0 also sees this iteration's token rows land, so a completed handoff
           // means both operands are in place
           bool bok = true;
-          if (warp == 0) bok = __all_sync(0xffffffffu, mbar_wait(&b_full[ar.slot], ar.phase, abort_flag, rv.err, 11));
+          if (warp == 0) {
+            const Ring& bw = G::SPLIT_B ? br : ar;
+            bok = __all_sync(0xffffffffu, mbar_wait(&b_full[bw.slot], bw.phase, abort_flag, rv.err, 11));
+          }
+          if (G::SPLIT_B) br.next(SB);
           __syncwarp();
           nb_arrive(kReadyBar0 + ar.slot, kReadyCount);
           ar.next(S);
@@ -873,7 +885,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     // the next tile's width): each access holds up the next tcgen05.mma by hundreds of
     // cycles under tensor load.
     const volatile int* rows_ring = tile_rows;
-    Ring ar;
+    Ring ar, br;
     int rows = 0;                             // token columns of the current tile
     for (int j = 0; j < my_tiles; ++j) {
       const int buf = NBUF == 2 ? (j & 1) : 0, use = NBUF == 2 ? (j >> 1) : j;
@@ -898,7 +910,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         tc_fence_after();
         if (lane == 0) {
           const uint32_t ast = tmem + ar.slot * G::SLOT_COLS;
-          const uint32_t bst = smem_u32(b_ring + ar.slot * G::B_BYTES);
+          const uint32_t bst = smem_u32(b_ring + (G::SPLIT_B ? br.slot : ar.slot) * G::B_BYTES);
           const int steps = min(KS, k_steps - kit * KS);
 #pragma unroll
           for (int st = 0; st < KS; ++st) {
@@ -913,11 +925,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
               }
             }
           }
-          mma_commit(&s_empty[ar.slot]);      // A and B slot free once these MMAs are done
+          mma_commit(&s_empty[ar.slot]);      // A (and unsplit, B) slot free once these are done
+          if (G::SPLIT_B) mma_commit(&b_empty[br.slot]);
           if (kit == k_iters - 1) mma_commit(&acc_full[buf]);
         }
         __syncwarp();
         ar.next(S);
+        if (G::SPLIT_B) br.next(SB);
         GG_ADD(13, t13);
         // the next tile's width, read with this tile's last MMAs already queued (the
         // loader posted it before this iteration's token rows)
@@ -979,14 +993,15 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         // reads it after the handoff of that iteration
         if (kit == k_iters - 1 && j + 1 < my_tiles) tile_rows[(j + 1) & 7] = tn.rows;
         GG_T(t18);
-        if (!mbar_wait(&s_empty[sr.slot], sr.phase ^ 1, abort_flag, rv.err, 10)) { ok = false; break; }
+        if (!mbar_wait(G::SPLIT_B ? &b_empty[sr.slot] : &s_empty[sr.slot], sr.phase ^ 1, abort_flag,
+                       rv.err, 10)) { ok = false; break; }
         GG_ADD(18, t18);
         const int steps = min(KS, k_steps - kit * KS);
         bar_expect_tx(&b_full[sr.slot], steps * G::B_BOX);
         for (int st = 0; st < steps; ++st)
           tma_load_2d(smem_u32(b_ring + sr.slot * G::B_BYTES + st * G::B_BOX), &tm_act,
                       (kit * KS + st) * kBlockK, t.row0 + t.n0, smem_u32(&b_full[sr.slot]));
-        sr.next(S);
+        sr.next(SB);
         ++nb;
         GG_INC(19);
       }
@@ -1005,7 +1020,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
     };
     drain(sc_full, ns, NSB);
     drain(code_full, nc, RS);
-    drain(b_full, nb, S);
+    drain(b_full, nb, SB);
   }
 
 #ifdef BIGRIG_GEMM_PROFILE
@@ -1080,13 +1095,18 @@ static int launch_one(const void* act, const RouteView& rv, const void* slab,
   using G = GemmShape<MODE, BN, BITS>;
   const int K = MODE == 0 ? L.hidden : L.inter, NF = MODE == 0 ? L.inter : L.hidden;
   const int gpitch = K / L.group_size;
-  GemmRings rg{0, G::SA, 0, (G::NMAT * 2 * kBlockM * gpitch * 2 + 127) & ~127};
-  static const int prefs[][2] = {{3, 2}, {2, 2}, {3, 1}, {2, 1}};   // (code slots, scale buffers)
-  for (const auto& c : prefs)
-    if (G::smem(c[0], G::SA, c[1], rg.sc_bytes) <= static_cast<size_t>(G::kLimit)) {
-      rg.rs = c[0]; rg.nsb = c[1];
-      break;
-    }
+  GemmRings rg{0, 0, 0, (G::NMAT * 2 * kBlockM * gpitch * 2 + 127) & ~127};
+  // (code slots, scale buffers) from the most buffered; a split token-row ring as deep as
+  // fits beside them (at least 4), an unsplit one has the A slots' depth
+  static const int prefs[][2] = {{3, 2}, {2, 2}, {3, 1}, {2, 1}};
+  for (const auto& c : prefs) {
+    for (int sb = G::SB; sb >= (G::SPLIT_B ? 4 : G::SB); --sb)
+      if (G::smem(c[0], sb, c[1], rg.sc_bytes) <= static_cast<size_t>(G::kLimit)) {
+        rg.rs = c[0]; rg.sb = sb; rg.nsb = c[1];
+        break;
+      }
+    if (rg.rs) break;
+  }
   if (!rg.rs) return kNoFit;                          // the caller tries a smaller token tile
   const size_t smem = G::smem(rg.rs, rg.sb, rg.nsb, rg.sc_bytes);
 
