@@ -14,12 +14,13 @@
 //            (topk_rank_warp: the chain's indices and scores bit for bit) and reads the
 //            slots from a copy of g2s staged at start
 //   gate/up  items of (routed expert, 8 features), dealt round-robin to CTAs and
-//            streamed by the producer through a ring of bulk copies with full / empty
-//            mbarriers.  Every consumer warp takes its 1/16 of the hidden dimension of
-//            each item as the item lands, on the tensor cores: warp-level bf16 MMAs
-//            (m16n8k16) whose 16 rows are the item's 8 gate and 8 up rows, A converted
-//            in registers from the codes to exact bf16 integers q, B the token; the last
-//            warp to finish an item adds the 16 partials in warp order and writes h.
+//            streamed by the producer through a ring of tensor-map (or bulk) copies with
+//            full / empty mbarriers.  As an item lands, 8 or 16 consumer warps take their
+//            slices of its hidden dimension (with 8, the two halves of the consumers take
+//            alternate items), on the tensor cores: warp-level bf16 MMAs (m16n8k16)
+//            whose 16 rows are the item's 8 gate and 8 up rows, A converted in registers
+//            from the codes to exact bf16 integers q, B the token; after the last item
+//            the partials of every row are added in warp order and h written.
 //   barrier  grid-wide, consumer threads only (the producer is already streaming the
 //            down-projection weights into the ring)
 //   down     items of (16 hidden features, a group of routed experts), a pair of warps
@@ -37,6 +38,10 @@
 //
 // Every wait -- mbarriers, tagged logits, the grid barrier -- is bounded; a timeout
 // counts in the error words and the kernel carries on to its end.
+#include <cuda.h>
+
+#include <cstring>
+
 #include "gemv_common.cuh"
 #include "routing.cuh"
 
@@ -76,7 +81,37 @@ struct DecodeLayerArgs {
   int32_t* err;
   int E, k, mode, norm;
   int stage_bytes, nstages, seg_per_item, max_tiles, max_items, ksplit;
+  int seg_stride;             // bytes between a down item's expert segments in a stage
+  int wpi;                    // consumer warps per gate/up item (8 or 16)
+  int maps;                   // kDlMapGateUp | kDlMapDown: which copies go through tensor maps
 };
+
+// The copy engine takes one copy at a time, at a cost per copy that the small scale and
+// bias rows do not amortise.  Tensor maps over the slab fetch what the bulk path needs six
+// copies for in two (an item's gate and up codes in one box; its gate and up scales and
+// biases in another) and a down segment's scales and biases in one.
+constexpr int kDlMapGateUp = 1;
+constexpr int kDlMapDown = 2;
+
+__device__ __forceinline__ void tma4_g2s_hint(void* dst, const CUtensorMap* m, int c0, int c1, int c2,
+                                              int c3, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar)),
+      "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma5_g2s_hint(void* dst, const CUtensorMap* m, int c0, int c1, int c2,
+                                              int c3, int c4, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+      "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
   unsigned long long v;
@@ -186,8 +221,10 @@ __device__ __forceinline__ void mma_block(float* d, float* dh, const uint4 wg, c
     if constexpr (BITS == 4) {
       const uint32_t G = gw[s >> 1], U = uw[s >> 1];
       const int sh = 8 * (s & 1);
-      mma_bf16_16816(d, nibble_pair(G >> sh), nibble_pair(U >> sh), nibble_pair(G >> (sh + 4)),
-                     nibble_pair(U >> (sh + 4)), b[s].x, b[s].y);
+      // even and odd k-steps in two accumulators: two dependent MMA chains of half the
+      // length (the caller adds them)
+      mma_bf16_16816((s & 1) ? dh : d, nibble_pair(G >> sh), nibble_pair(U >> sh),
+                     nibble_pair(G >> (sh + 4)), nibble_pair(U >> (sh + 4)), b[s].x, b[s].y);
     } else {
       const uint32_t G = gw[s], U = uw[s];
       mma_bf16_16816(d, nibble_pair(G), nibble_pair(U), nibble_pair(G >> 8), nibble_pair(U >> 8),
@@ -265,7 +302,7 @@ __device__ __noinline__ float2 mma_rows(const uint8_t* rows_g, const uint8_t* ro
   const uint8_t* rg = rows_g + g * pitch + 16 * t;
   const uint8_t* ru = TWO ? rows_u + g * pitch + 16 * t : nullptr;
   float d[4] = {0.f, 0.f, 0.f, 0.f};
-  float dh[4] = {0.f, 0.f, 0.f, 0.f};            // 8-bit: high-nibble sums
+  float dh[4] = {0.f, 0.f, 0.f, 0.f};            // 8-bit: high-nibble sums; 4-bit: odd k-steps
   int wstart = blk0 * KB::GROUPS;                // first group of the open column window
   float pg = 0.f, pu = 0.f;
   auto flush = [&](int wend) {
@@ -274,8 +311,8 @@ __device__ __noinline__ float2 mma_rows(const uint8_t* rows_g, const uint8_t* ro
     for (int c = 0; c < 2; ++c) {
       const int G = wstart + 2 * t + c;
       if (G < wend) {
-        const float vg = BITS == 4 ? d[c] : fmaf(16.f, dh[c], d[c]);
-        const float vu = BITS == 4 ? d[2 + c] : fmaf(16.f, dh[2 + c], d[2 + c]);
+        const float vg = BITS == 4 ? d[c] + dh[c] : fmaf(16.f, dh[c], d[c]);
+        const float vu = BITS == 4 ? d[2 + c] + dh[2 + c] : fmaf(16.f, dh[2 + c], d[2 + c]);
         const float xs = gsum[G];
         pg = fmaf(half_to_f32<SDT>(sc_g[g * ng + G]), vg, fmaf(half_to_f32<SDT>(bi_g[g * ng + G]), xs, pg));
         if (TWO)
@@ -306,7 +343,7 @@ __device__ __noinline__ float2 mma_rows(const uint8_t* rows_g, const uint8_t* ro
         const int sh = 8 * (s & 1);
         const uint32_t a0 = nibble_pair(G >> sh), a2 = nibble_pair(G >> (sh + 4));
         const uint32_t a1 = TWO ? nibble_pair(U >> sh) : 0u, a3 = TWO ? nibble_pair(U >> (sh + 4)) : 0u;
-        mma_bf16_16816(d, a0, a1, a2, a3, b.x, b.y);
+        mma_bf16_16816((s & 1) ? dh : d, a0, a1, a2, a3, b.x, b.y);   // two chains, as mma_block
       } else {
         const uint32_t G = gw[s], U = uw[s];
         const uint32_t l0 = nibble_pair(G), l2 = nibble_pair(G >> 8);
@@ -324,14 +361,16 @@ __device__ __noinline__ float2 mma_rows(const uint8_t* rows_g, const uint8_t* ro
 }
 
 template <int BITS, int SDT>
-__global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(DecodeLayerArgs a) {
+__global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
+    DecodeLayerArgs a, const __grid_constant__ CUtensorMap tm_code,
+    const __grid_constant__ CUtensorMap tm_gsb, const __grid_constant__ CUtensorMap tm_dsb) {
   using KB = KBlock<BITS>;
   constexpr int NF = kDlFeat;
   constexpr int ND = kDlFeatDown;
   constexpr int CW = kDlCW;
   constexpr int CT = CW * 32;              // consumer threads
   constexpr int MAXNB = kDlMaxSliceBlocks<BITS>;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ __align__(16) float s_lg[kMaxExperts];
   __shared__ int32_t s_g2s[kMaxExperts];
   __shared__ int32_t s_idx[32], s_slot[32];
@@ -360,8 +399,11 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
   const int n_down = my_tiles * ipt;
   const int item_bytes = 2 * NF * pitch_h + 4 * NF * gh * 2;
   const int seg_bytes = ND * pitch_i + 2 * ND * gi * 2;
+  const int seg_stride = a.seg_stride;
 
-  SmemCarve sc(smem);
+  // tensor-map copies land at 128-byte aligned addresses: every carved buffer, the stage
+  // size and the segment stride are multiples of 128
+  SmemCarve sc(smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u));
   uint64_t* bars = sc.take<uint64_t>((2 * kDlMaxStages + 4) * 8);
   uint16_t* xraw = sc.take<uint16_t>(static_cast<size_t>(H) * 2);
   uint2* xperm = sc.take<uint2>(static_cast<size_t>(nblk_h) * KB::STEPS * 4 * 8);
@@ -405,6 +447,12 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
     // this launch's index: the barrier arrivals of all earlier launches over G (arrivals
     // of this launch that are already in add fewer than G)
     if (lane == 0) s_epoch = ld_acquire_u64(a.arrivals) / static_cast<unsigned long long>(G);
+    if (lane == 1 && (a.maps & kDlMapGateUp)) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_code)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_gsb)) : "memory");
+    }
+    if (lane == 2 && (a.maps & kDlMapDown))
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_dsb)) : "memory");
     for (int e = lane; e < E; e += 32) s_g2s[e] = a.g2s ? a.g2s[e] : e;
   }
   if (threadIdx.x < 32) s_idx[threadIdx.x] = -1;
@@ -511,9 +559,10 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
     const int total = my_items + n_down;
     const int first = min(nst, total);
     const uint64_t once = l2_evict_first();     // expert weights: read once per token
-    // one ring stage: lane 0 arms the barrier and issues its copies (a gate/up item has
-    // 6: codes, scales, biases of gate and up; a down item 3 per expert) -- one lane
-    // feeds the copy engine faster than several taking turns
+    // one ring stage: lane 0 arms the barrier, then the stage's copies go out in one warp
+    // instruction per kind, a lane per copy (a gate/up item is two tensor-map boxes or six
+    // bulk copies: codes, scales, biases of gate and up; a down item per routed expert
+    // its codes plus one box or two bulk copies of scales and biases)
     auto issue = [&](int q) {
       const int b = q % nst;
       if (q >= nst) stage_wait(empty + b, ((q / nst) - 1) & 1, a.err);
@@ -525,9 +574,14 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
         const int slot = s_slot[s];
         if (lane == 0) bar_expect_tx(full + b, slot >= 0 ? static_cast<uint32_t>(item_bytes) : 0u);
         __syncwarp();
-        if (slot >= 0 && lane == 0) for (int c = 0; c < 6; ++c) {
+        if (slot >= 0 && (a.maps & kDlMapGateUp)) {
+          // [proj][row][code bytes] and [proj][scales, biases][8-row block] boxes
+          if (lane == 0) tma4_g2s_hint(dst, &tm_code, 0, f0, 0, slot, full + b, once);
+          if (lane == 1)
+            tma5_g2s_hint(dst + 2 * NF * pitch_h, &tm_gsb, 0, f0 / NF, 0, 0, slot, full + b, once);
+        } else if (slot >= 0 && lane < 6) {
           const uint8_t* base = a.slab + static_cast<int64_t>(slot) * L.slot_stride;
-          const int m = c / 3, part = c % 3;         // projection; codes / scales / biases
+          const int m = lane / 3, part = lane % 3;   // projection; codes / scales / biases
           const uint8_t* src;
           uint8_t* d;
           uint32_t bytes;
@@ -551,14 +605,18 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
         for (int s = s0; s < s1; ++s) bytes += s_slot[s] >= 0 ? seg_bytes : 0;
         if (lane == 0) bar_expect_tx(full + b, bytes);
         __syncwarp();
-        for (int c = 0; lane == 0 && c < 3 * (s1 - s0); ++c) {
-          const int s = s0 + c / 3, part = c % 3;
-          if (s_slot[s] < 0) continue;
-          const uint8_t* base = a.slab + static_cast<int64_t>(s_slot[s]) * L.slot_stride;
-          uint8_t* dd = dst + static_cast<size_t>(s - s0) * seg_bytes;
+        const int per = (a.maps & kDlMapDown) ? 2 : 3;   // copies per routed expert
+        for (int c = lane; c < per * (s1 - s0); c += 32) {
+          const int s = s0 + c / per, part = c % per;
+          const int slot = s_slot[s];
+          if (slot < 0) continue;
+          const uint8_t* base = a.slab + static_cast<int64_t>(slot) * L.slot_stride;
+          uint8_t* dd = dst + static_cast<size_t>(s - s0) * seg_stride;
           if (part == 0)
             bulk_g2s_hint(dd, base + L.weight_off[2] + static_cast<int64_t>(f0) * pitch_i,
                           ND * pitch_i, full + b, once);
+          else if (per == 2)                           // [scales, biases][16-row block]
+            tma4_g2s_hint(dd + ND * pitch_i, &tm_dsb, 0, f0 / ND, 0, slot, full + b, once);
           else
             bulk_g2s_hint(dd + ND * pitch_i + (part - 1) * ND * gi * 2,
                           base + (part == 1 ? L.scales_off[2] : L.biases_off[2]) +
@@ -619,7 +677,12 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
   // consumer warp w owns k-blocks [kb0, kb1) of the hidden dimension in every item; its B
   // fragments (the token) stay in registers for all items.  Per item it leaves the partial
   // sums of the 8 gate and 8 up rows over its blocks; they are added after the last item.
-  const int kb0 = warp * nblk_h / CW, kb1 = (warp + 1) * nblk_h / CW;
+  // with 8 warps per item (when a warp's share of the hidden dimension fits its registers)
+  // the two halves of the consumers take alternate items: each warp runs twice the MMAs
+  // per item for half the items, half the per-item waits and reductions
+  const int wpi = a.wpi, ngrp = CW / wpi;
+  const int wl = warp % wpi, grp = warp / wpi;
+  const int kb0 = wl * nblk_h / wpi, kb1 = (wl + 1) * nblk_h / wpi;
   const int nb = kb1 - kb0;
   uint2 breg[MAXNB][KB::STEPS];
 #pragma unroll
@@ -646,6 +709,11 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
     const bool landed = stage_wait(full + b, (j / nst) & 1, a.err);
     if (j == 0) DL_STAMP(3);
     if (j == 0) DL_WSTAMP(0);
+    if (j % ngrp != grp) {                       // the other half's item: free the stage
+      __syncwarp();
+      if (lane == 0) bar_arrive(empty + b);
+      continue;
+    }
     const int it = cta + j * G;
     const int s = it / tiles_g;
     const bool have = s_slot[s] >= 0 && landed && xok;
@@ -667,8 +735,8 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
       for (int c = 0; c < 2; ++c) {
         if (gcol[c] < gend) {
           const int G0 = gcol[c];
-          const float vg = BITS == 4 ? d[c] : fmaf(16.f, dh[c], d[c]);
-          const float vu = BITS == 4 ? d[2 + c] : fmaf(16.f, dh[2 + c], d[2 + c]);
+          const float vg = BITS == 4 ? d[c] + dh[c] : fmaf(16.f, dh[c], d[c]);
+          const float vu = BITS == 4 ? d[2 + c] + dh[2 + c] : fmaf(16.f, dh[2 + c], d[2 + c]);
           pg = fmaf(half_to_f32<SDT>(sb[(0 * NF + g) * gh + G0]), vg,
                     fmaf(half_to_f32<SDT>(sb[(1 * NF + g) * gh + G0]), xg[c], pg));
           pu = fmaf(half_to_f32<SDT>(sb[(2 * NF + g) * gh + G0]), vu,
@@ -680,21 +748,21 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
     pu += __shfl_xor_sync(0xffffffffu, pu, 1);
     pg += __shfl_xor_sync(0xffffffffu, pg, 2);
     pu += __shfl_xor_sync(0xffffffffu, pu, 2);
-    if (t == 0) gpart[(j * CW + warp) * NF + g] = make_float2(pg, pu);
+    if (t == 0) gpart[(j * wpi + wl) * NF + g] = make_float2(pg, pu);
     __syncwarp();
     if (lane == 0) bar_arrive(empty + b);        // stage b read by this warp
   }
   DL_STAMP(4);
   DL_WSTAMP(1);
   named_sync(1, CT);
-  // h = bf16(silu(gate) * up), the 16 partials of each row added in warp order
+  // h = bf16(silu(gate) * up), the wpi partials of each row added in warp order
   for (int i = threadIdx.x; i < my_items * NF; i += CT) {
     const int j = i / NF, f = i - j * NF;
     const int it = cta + j * G;
     const int s = it / tiles_g, f0 = (it - s * tiles_g) * NF;
     float gv = 0.f, uv = 0.f;
-    for (int w = 0; w < CW; ++w) {
-      const float2 o = gpart[(j * CW + w) * NF + f];
+    for (int w = 0; w < wpi; ++w) {
+      const float2 o = gpart[(j * wpi + w) * NF + f];
       gv += o.x;
       uv += o.y;
     }
@@ -739,18 +807,28 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
   // down tile of the CTA
   const int ks = warp % ksplit;
   const int db0 = ks * nblk_i / ksplit, db1 = (ks + 1) * nblk_i / ksplit;
+  // When no down item refills a stage (n_down <= nst) nobody waits for the down stages to
+  // be released: a warp waits only on the stages holding its experts, so all warps start
+  // at once instead of walking the stages in order.  Otherwise every warp releases every
+  // down stage in order (the producer refills them).
+  const bool direct = n_down <= nst;
   for (int d = 0; d < n_down; ++d) {
+    const int tl = d / ipt;
+    const int s0 = (d % ipt) * spi, s1 = min(k, s0 + spi);
+    if (direct) {
+      bool mine = false;
+      for (int s = warp / ksplit; s < k; s += CW / ksplit) mine |= s >= s0 && s < s1;
+      if (!mine) continue;
+    }
     const int q = my_items + d;
     const int b = q % nst;
     const bool landed = stage_wait(full + b, (q / nst) & 1, a.err) && hok;
     if (d == n_down - 1) DL_STAMP(14);
     if (d < 8) DL_WSTAMP(8 + d);
-    const int tl = d / ipt;
-    const int s0 = (d % ipt) * spi, s1 = min(k, s0 + spi);
     for (int s = warp / ksplit; s < k; s += CW / ksplit) {
       if (s < s0 || s >= s1) continue;
       const bool have = s_slot[s] >= 0 && landed && db0 < db1;
-      const uint8_t* wc = ring + static_cast<size_t>(b) * stage_bytes + static_cast<size_t>(s - s0) * seg_bytes;
+      const uint8_t* wc = ring + static_cast<size_t>(b) * stage_bytes + static_cast<size_t>(s - s0) * seg_stride;
       const uint16_t* sb = reinterpret_cast<const uint16_t*>(wc + ND * pitch_i);
       float2 p = make_float2(0.f, 0.f);
       DL_WSTAMP(2);
@@ -766,7 +844,7 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(Decod
       DL_WSTAMP(3);
     }
     __syncwarp();
-    if (lane == 0) bar_arrive(empty + b);
+    if (!direct && lane == 0) bar_arrive(empty + b);
   }
   DL_STAMP(11);
   DL_WSTAMP(4);
@@ -813,7 +891,7 @@ int sm_count_dl() {
 }
 
 struct DlPlan {
-  int stage_bytes, nstages, seg_per_item, max_tiles, max_items, ksplit;
+  int stage_bytes, nstages, seg_per_item, max_tiles, max_items, ksplit, seg_stride, wpi;
   size_t smem;
 };
 
@@ -829,11 +907,12 @@ bool decode_layer_plan(const bigrig_expert_layout& L, int k, int E, int G, DlPla
   const size_t gh = L.hidden / kDlGroup, gi = L.inter / kDlGroup;
   const size_t nblk_h = (L.hidden + kb_k - 1) / kb_k, nblk_i = (L.inter + kb_k - 1) / kb_k;
   if (nblk_h > static_cast<size_t>(kDlCW) * max_slice) return false;
+  p->wpi = nblk_h <= static_cast<size_t>(kDlCW / 2) * max_slice ? kDlCW / 2 : kDlCW;
   const size_t ph = static_cast<size_t>(L.hidden) * L.bits / 8;
   const size_t pi = static_cast<size_t>(L.inter) * L.bits / 8;
   const size_t item = 2 * kDlFeat * ph + 4 * kDlFeat * gh * 2;
-  const size_t seg = kDlFeatDown * pi + 2 * kDlFeatDown * gi * 2;
-  const size_t stage = item > seg ? item : seg;
+  const size_t seg = round128(kDlFeatDown * pi + 2 * kDlFeatDown * gi * 2);
+  const size_t stage = round128(item > seg ? item : seg);
   int spi = static_cast<int>(stage / seg);
   if (spi > k) spi = k;
   int ksplit = 1;
@@ -843,7 +922,8 @@ bool decode_layer_plan(const bigrig_expert_layout& L, int k, int E, int G, DlPla
   p->max_tiles = (tiles_d + G - 1) / G;
   p->max_items = (n_items + G - 1) / G;
   p->ksplit = ksplit;
-  const size_t fixed = round128((2 * kDlMaxStages + 4) * 8) + round128(L.hidden * 2) +
+  // (the first 128 bytes: room to align the carve)
+  const size_t fixed = 128 + round128((2 * kDlMaxStages + 4) * 8) + round128(L.hidden * 2) +
                        round128(nblk_h * steps * 4 * 8) + round128(gh * 4) +
                        round128(static_cast<size_t>(k) * L.inter * 2) +
                        round128(static_cast<size_t>(k) * nblk_i * steps * 4 * 8) +
@@ -857,12 +937,95 @@ bool decode_layer_plan(const bigrig_expert_layout& L, int k, int E, int G, DlPla
   p->stage_bytes = static_cast<int>(stage);
   p->nstages = static_cast<int>(nst);
   p->seg_per_item = spi;
+  p->seg_stride = static_cast<int>(seg);
   p->smem = fixed + nst * stage;
   return true;
 }
 
+using DlEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+DlEncodeFn dl_encode_fn() {
+  static DlEncodeFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<DlEncodeFn>(p);
+  }
+  return fn;
+}
+
+// Slots a map may address: the slab's extent is not passed in, and a box only touches the
+// slot whose index it is given.
+constexpr cuuint64_t kDlMapSlots = 1u << 16;
+
+// A map of 8-byte elements over the slab, no swizzle, no fill.  False when the layout breaks
+// a rule of tiled maps (16-byte aligned base and strides, at most 256 elements per box side)
+// or the encoder refuses it.
+bool dl_encode(CUtensorMap* m, int rank, const uint8_t* base, const cuuint64_t* dims,
+               const cuuint64_t* strides, const cuuint32_t* box) {
+  DlEncodeFn fn = dl_encode_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  for (int i = 0; i < rank; ++i)
+    if (box[i] < 1 || box[i] > 256 || dims[i] < box[i]) return false;
+  for (int i = 0; i + 1 < rank; ++i)
+    if (strides[i] == 0 || (strides[i] & 15)) return false;
+  const cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, static_cast<cuuint32_t>(rank), const_cast<uint8_t*>(base),
+            dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The maps of a layer's slab (kDlMapGateUp / kDlMapDown of those it could build).
+//   code  [8-byte words of a row][row][gate, up][slot], box: an item's 8 rows of both
+//   gsb   [words of an 8-row block's scales][block][scales, biases][gate, up][slot]
+//   dsb   [words of a 16-row block of down scales][block][scales, biases][slot]
+// The slab keeps gate, up (and each projection's scales and biases) at fixed distances,
+// which is what lets one box span them.
+int dl_maps(const uint8_t* slab, const bigrig_expert_layout& L, CUtensorMap* code, CUtensorMap* gsb,
+            CUtensorMap* dsb) {
+  const int64_t ph = static_cast<int64_t>(L.hidden) * L.bits / 8;
+  const int64_t gh = L.hidden / L.group_size, gi = L.inter / L.group_size;
+  const int64_t pst = L.weight_off[1] - L.weight_off[0];
+  const int64_t kst = L.biases_off[0] - L.scales_off[0];
+  const int64_t dkst = L.biases_off[2] - L.scales_off[2];
+  int maps = 0;
+  if (ph % 8 == 0 && pst > 0 && kst > 0 && L.scales_off[1] - L.scales_off[0] == pst &&
+      L.biases_off[1] - L.biases_off[0] == pst && L.weight_off[0] % 16 == 0 &&
+      L.scales_off[0] % 16 == 0 && L.inter % kDlFeat == 0) {
+    const cuuint64_t cd[4] = {static_cast<cuuint64_t>(ph / 8), static_cast<cuuint64_t>(L.inter), 2, kDlMapSlots};
+    const cuuint64_t cs[3] = {static_cast<cuuint64_t>(ph), static_cast<cuuint64_t>(pst),
+                              static_cast<cuuint64_t>(L.slot_stride)};
+    const cuuint32_t cb[4] = {static_cast<cuuint32_t>(ph / 8), kDlFeat, 2, 1};
+    const int64_t blk = kDlFeat * gh * 2;            // an 8-row block's scales, bytes
+    const cuuint64_t sd[5] = {static_cast<cuuint64_t>(blk / 8), static_cast<cuuint64_t>(L.inter / kDlFeat), 2, 2,
+                              kDlMapSlots};
+    const cuuint64_t ss[4] = {static_cast<cuuint64_t>(blk), static_cast<cuuint64_t>(kst),
+                              static_cast<cuuint64_t>(pst), static_cast<cuuint64_t>(L.slot_stride)};
+    const cuuint32_t sb[5] = {static_cast<cuuint32_t>(blk / 8), 1, 2, 2, 1};
+    if (dl_encode(code, 4, slab + L.weight_off[0], cd, cs, cb) &&
+        dl_encode(gsb, 5, slab + L.scales_off[0], sd, ss, sb))
+      maps |= kDlMapGateUp;
+  }
+  if (dkst > 0 && L.scales_off[2] % 16 == 0 && L.hidden % kDlFeatDown == 0) {
+    const int64_t blk = kDlFeatDown * gi * 2;        // a 16-row block's scales, bytes
+    const cuuint64_t dd[4] = {static_cast<cuuint64_t>(blk / 8), static_cast<cuuint64_t>(L.hidden / kDlFeatDown), 2,
+                              kDlMapSlots};
+    const cuuint64_t ds[3] = {static_cast<cuuint64_t>(blk), static_cast<cuuint64_t>(dkst),
+                              static_cast<cuuint64_t>(L.slot_stride)};
+    const cuuint32_t db[4] = {static_cast<cuuint32_t>(blk / 8), 1, 2, 1};
+    if (dl_encode(dsb, 4, slab + L.scales_off[2], dd, ds, db)) maps |= kDlMapDown;
+  }
+  return maps;
+}
+
 template <int BITS, int SDT>
-int dl_launch(const DecodeLayerArgs& args, size_t smem, int G, cudaStream_t s) {
+int dl_launch(const DecodeLayerArgs& args, const CUtensorMap& tm_code, const CUtensorMap& tm_gsb,
+              const CUtensorMap& tm_dsb, size_t smem, int G, cudaStream_t s) {
   auto kern = decode_layer_kernel<BITS, SDT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
@@ -878,7 +1041,7 @@ int dl_launch(const DecodeLayerArgs& args, size_t smem, int G, cudaStream_t s) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   TimedLaunch tl(BIGRIG_K_DECODE_LAYER, s);
-  cudaLaunchKernelEx(&cfg, kern, args);
+  cudaLaunchKernelEx(&cfg, kern, args, tm_code, tm_gsb, tm_dsb);
   return check_launch("decode_layer_kernel");
 }
 
@@ -923,10 +1086,21 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
   a.max_tiles = p.max_tiles;
   a.max_items = p.max_items;
   a.ksplit = p.ksplit;
-  if (L.bits == 4 && L.scale_dtype == BIGRIG_F16) return dl_launch<4, BIGRIG_F16>(a, p.smem, G, s);
-  if (L.bits == 4 && L.scale_dtype == BIGRIG_BF16) return dl_launch<4, BIGRIG_BF16>(a, p.smem, G, s);
-  if (L.bits == 8 && L.scale_dtype == BIGRIG_F16) return dl_launch<8, BIGRIG_F16>(a, p.smem, G, s);
-  if (L.bits == 8 && L.scale_dtype == BIGRIG_BF16) return dl_launch<8, BIGRIG_BF16>(a, p.smem, G, s);
+  a.seg_stride = p.seg_stride;
+  a.wpi = p.wpi;
+  CUtensorMap tm_code, tm_gsb, tm_dsb;
+  memset(&tm_code, 0, sizeof(tm_code));
+  memset(&tm_gsb, 0, sizeof(tm_gsb));
+  memset(&tm_dsb, 0, sizeof(tm_dsb));
+  a.maps = dl_maps(a.slab, L, &tm_code, &tm_gsb, &tm_dsb);
+  if (L.bits == 4 && L.scale_dtype == BIGRIG_F16)
+    return dl_launch<4, BIGRIG_F16>(a, tm_code, tm_gsb, tm_dsb, p.smem, G, s);
+  if (L.bits == 4 && L.scale_dtype == BIGRIG_BF16)
+    return dl_launch<4, BIGRIG_BF16>(a, tm_code, tm_gsb, tm_dsb, p.smem, G, s);
+  if (L.bits == 8 && L.scale_dtype == BIGRIG_F16)
+    return dl_launch<8, BIGRIG_F16>(a, tm_code, tm_gsb, tm_dsb, p.smem, G, s);
+  if (L.bits == 8 && L.scale_dtype == BIGRIG_BF16)
+    return dl_launch<8, BIGRIG_BF16>(a, tm_code, tm_gsb, tm_dsb, p.smem, G, s);
   return set_error(BIGRIG_ERR_UNSUPPORTED, "decode_layer: bits=%d scale_dtype=%d", L.bits, L.scale_dtype);
 }
 
