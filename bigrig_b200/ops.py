@@ -33,8 +33,13 @@ def _require_cuda(name: str, t: torch.Tensor, dtype=None) -> None:
         raise ValueError(f"{name} must be contiguous")
 
 
+_raw_stream = torch._C._cuda_getCurrentRawStream
+
+
 def _stream(t: torch.Tensor) -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+    """The caller's current CUDA stream on ``t``'s device (the raw handle: a decode step makes
+    several of these calls per layer, and building a torch Stream object for each shows)."""
+    return ctypes.c_void_p(_raw_stream(t.get_device()))
 
 
 _layout_cache: dict = {}
@@ -94,8 +99,16 @@ def default_workspace(device) -> Workspace:
         return ws
 
 
+_ws_bytes: dict = {}
+
+
 def workspace_bytes(T: int, k: int, n_experts: int, layout: Layout) -> int:
-    return int(_lib.load().bigrig_moe_workspace_bytes(T, k, n_experts, ctypes.byref(c_layout(layout))))
+    key = (T, k, n_experts, layout)
+    n = _ws_bytes.get(key)
+    if n is None:
+        n = _ws_bytes[key] = int(_lib.load().bigrig_moe_workspace_bytes(
+            T, k, n_experts, ctypes.byref(c_layout(layout))))
+    return n
 
 
 # ------------------------------------------------------------------ entry points
@@ -111,15 +124,22 @@ def dequant(slab: torch.Tensor, layout: Layout, slot: int, proj: int) -> torch.T
     return out
 
 
-def router_logits(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
-    """fp32 logits[T, E] = x[T, H] . w[E, H]^T (+ bias[E]); x and w bf16."""
+def router_logits(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 logits[T, E] = x[T, H] . w[E, H]^T (+ bias[E]); x and w bf16.  ``out``, when
+    given, is a contiguous fp32 tensor of T*E elements."""
     _require_cuda("x", x, torch.bfloat16)
     _require_cuda("w", w, torch.bfloat16)
     if bias is not None:
         _require_cuda("bias", bias, torch.float32)
     T, H = x.shape
     E = w.shape[0]
-    out = torch.empty(T, E, dtype=torch.float32, device=x.device)
+    if out is None:
+        out = torch.empty(T, E, dtype=torch.float32, device=x.device)
+    else:
+        _require_cuda("out", out, torch.float32)
+        if out.numel() != T * E:
+            raise ValueError(f"out holds {out.numel()} logits, the call makes {T * E}")
     _lib.check(_lib.load().bigrig_router_logits(_vp(x), _vp(w), _vp(bias), _vp(out), T, H, E,
                                                 _stream(x)), "router_logits")
     return out

@@ -370,8 +370,11 @@ class ExpertPool:
         _lib.check(_lib.load().bigrig_copy_regions(dst, src, size, n,
                                                    ctypes.c_void_p(cs.cuda_stream)),
                    "copy_regions")
+        stage = self._stage_buf
         for _, t in batch:
-            if t.device.type == "cuda":
+            # device sources other than the pool's own staging buffers (which live as long
+            # as the pool) must outlive the copy
+            if t.device.type == "cuda" and (stage is None or t._base is not stage):
                 t.record_stream(cs)
         if self._copies_done is None:
             self._copies_done = torch.cuda.Event()
@@ -386,14 +389,22 @@ class ExpertPool:
         if self._copies_done is not None and self.device.type == "cuda":
             if torch.cuda.is_current_stream_capturing():
                 return
-            (stream or torch.cuda.current_stream(self.device)).wait_event(self._copies_done)
+            (stream or torch.cuda.current_stream(self._dev_index())).wait_event(self._copies_done)
 
     def mark_read(self, stream: torch.cuda.Stream | None = None) -> None:
         """Record that kernels reading the slab were queued on ``stream`` (default: current)."""
         if self.device.type == "cuda" and not torch.cuda.is_current_stream_capturing():
             if self._reads_done is None:
                 self._reads_done = torch.cuda.Event()
-            self._reads_done.record(stream or torch.cuda.current_stream(self.device))
+            self._reads_done.record(stream or torch.cuda.current_stream(self._dev_index()))
+
+    def _dev_index(self) -> int:
+        """The slab's CUDA device as an int (a device object costs a lookup per call)."""
+        i = getattr(self, "_dev_i", None)
+        if i is None:
+            i = self._dev_i = (self.device.index if self.device.index is not None
+                               else torch.cuda.current_device())
+        return i
 
     def settle(self) -> None:
         """Wait for every queued admission and kernel read; afterwards the pool's tables
@@ -585,18 +596,24 @@ class StreamingSwitchGLU:
         nxt = self._next
         E = pool.n_experts
         pred = None
+        rs = self._route_scratch(x2.device, E, k)
         if (STAGING and nxt is not None and self._next_gate is not None and not nxt.full
                 and nxt.n_experts == E and k <= E):
             w2, b2 = self._route_pair(gate_w, gate_b)
-            idx2, _ = ops.router_topk(ops.router_logits(x2, w2, b2).reshape(2, E), k, mode, norm_topk)
+            ops.router_logits(x2, w2, b2, out=rs[0])
+            ops.router_topk(rs[0].view(2, E), k, mode, norm_topk, indices=rs[1], scores=rs[2])
             t0 = time.perf_counter()
-            host = idx2.to("cpu").numpy().astype(np.int64)        # the host readback
+            rs[3].copy_(rs[1])                                    # the host readback
+            host = rs[3].numpy().astype(np.int64)
             self.sync_seconds += time.perf_counter() - t0
             gi, pred = host[:1], host[1]
         else:
-            idx, _ = ops.router_topk(ops.router_logits(x2, gate_w, gate_b), k, mode, norm_topk)
+            ops.router_logits(x2, gate_w, gate_b, out=rs[0][:E])
+            ops.router_topk(rs[0][:E].view(1, E), k, mode, norm_topk, indices=rs[1][:1],
+                            scores=rs[2][:1])
             t0 = time.perf_counter()
-            gi = idx.to("cpu").numpy().astype(np.int64)           # the host readback
+            rs[3][:1].copy_(rs[1][:1])                            # the host readback
+            gi = rs[3][:1].numpy().astype(np.int64)
             self.sync_seconds += time.perf_counter() - t0
         self._count_routing(gi.reshape(-1))
         self.ensure(gi)
@@ -613,6 +630,18 @@ class StreamingSwitchGLU:
         if pred is not None:
             self._speculate(pred)
         return out
+
+    def _route_scratch(self, device, E: int, k: int):
+        """Per-layer routing buffers of the one-token path, made once: logits fp32 [2E] (this
+        layer's and the next router's), indices int32 [2, k], scores fp32 [2, k] on the
+        device, and a pinned int32 [2, k] host copy for the readback."""
+        rs = getattr(self, "_rs", None)
+        if rs is None or rs[0].numel() != 2 * E or rs[1].shape[1] != k or rs[0].device != device:
+            rs = self._rs = (torch.empty(2 * E, dtype=torch.float32, device=device),
+                             torch.empty(2, k, dtype=torch.int32, device=device),
+                             torch.empty(2, k, dtype=torch.float32, device=device),
+                             torch.empty(2, k, dtype=torch.int32).pin_memory())
+        return rs
 
     def _route_pair(self, gate_w: torch.Tensor, gate_b: torch.Tensor | None):
         """This layer's and the next layer's router weights stacked [2E, H] (and biases),
