@@ -43,10 +43,25 @@ def _stream(t: torch.Tensor) -> ctypes.c_void_p:
 
 
 _layout_cache: dict = {}
+_layout_by_id: dict = {}
+_stream_objs: dict = {}
+
+
+def current_stream(device_index: int) -> torch.cuda.Stream:
+    """torch's current stream on a device, the object looked up by its raw handle (building
+    a Stream object per call costs several microseconds; a decode step needs a few per layer)."""
+    raw = _raw_stream(device_index)
+    s = _stream_objs.get((device_index, raw))
+    if s is None:
+        s = _stream_objs[(device_index, raw)] = torch.cuda.current_stream(device_index)
+    return s
 
 
 def c_layout(L: Layout) -> _lib.ExpertLayout:
     """The ctypes struct of a Layout (cached; checked once by the library)."""
+    hit = _layout_by_id.get(id(L))
+    if hit is not None and hit[0] is L:
+        return hit[1]
     c = _layout_cache.get(L)
     if c is None:
         c = _lib.ExpertLayout()
@@ -58,6 +73,7 @@ def c_layout(L: Layout) -> _lib.ExpertLayout:
                                                                  L.biases_off[i])
         _lib.check(_lib.load().bigrig_check_layout(ctypes.byref(c)), "layout")
         _layout_cache[L] = c
+    _layout_by_id[id(L)] = (L, c)
     return c
 
 

@@ -389,14 +389,14 @@ class ExpertPool:
         if self._copies_done is not None and self.device.type == "cuda":
             if torch.cuda.is_current_stream_capturing():
                 return
-            (stream or torch.cuda.current_stream(self._dev_index())).wait_event(self._copies_done)
+            (stream or ops.current_stream(self._dev_index())).wait_event(self._copies_done)
 
     def mark_read(self, stream: torch.cuda.Stream | None = None) -> None:
         """Record that kernels reading the slab were queued on ``stream`` (default: current)."""
         if self.device.type == "cuda" and not torch.cuda.is_current_stream_capturing():
             if self._reads_done is None:
                 self._reads_done = torch.cuda.Event()
-            self._reads_done.record(stream or torch.cuda.current_stream(self._dev_index()))
+            self._reads_done.record(stream or ops.current_stream(self._dev_index()))
 
     def _dev_index(self) -> int:
         """The slab's CUDA device as an int (a device object costs a lookup per call)."""
@@ -446,7 +446,7 @@ class ExpertPool:
                     slot[1] = torch.cuda.Event()
                 slot[0].numpy()[:] = self.g2s
                 self._g2s_dev.copy_(slot[0], non_blocking=True)
-                slot[1].record()
+                slot[1].record(ops.current_stream(self._dev_index()))
             self._g2s_dirty = False
         return self._g2s_dev
 
