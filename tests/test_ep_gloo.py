@@ -1,4 +1,4 @@
-"""Expert-parallel dispatch/combine across 2 CPU ranks over gloo.
+"""Expert-parallel dispatch/combine across 2 and 4 CPU ranks over gloo.
 
 The expert computation is a stand-in (each expert scales its rows by its global id
 + 1), so the test checks the exchange itself: every pair reaches the rank owning
@@ -50,20 +50,31 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("padded", [True, False])
-@pytest.mark.parametrize("T", [1, 5])
-def test_dispatch_combine_two_ranks(padded, T):
+def _run_ranks(world, T, padded):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, T, padded, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, T, padded, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=120)
+        p.join(timeout=180)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    res = dict(q.get(timeout=10) for _ in range(2))
+    res = dict(q.get(timeout=10) for _ in range(world))
     assert max(res.values()) < 1e-5, res
+
+
+@pytest.mark.parametrize("padded", [True, False])
+@pytest.mark.parametrize("T", [1, 5])
+def test_dispatch_combine_two_ranks(padded, T):
+    _run_ranks(2, T, padded)
+
+
+@pytest.mark.parametrize("padded", [True, False])
+def test_dispatch_combine_four_ranks(padded):
+    """Two experts per rank, as bench.py's expert-parallel run places OLMoE's 64 on 4 GPUs
+    in proportion: pairs cross to three peers and back."""
+    _run_ranks(4, 5, padded)
 
 
 def test_plan_groups_pairs_stably_by_owner():
