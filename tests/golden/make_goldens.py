@@ -1,9 +1,8 @@
 """Generate the golden fixtures of tests/golden/ from the reference's own Python code.
 
-Run in a container that has the BigRig tree (read-only) at $BIGRIG_REF
-(default /root/reference):
+Run where the BigRig tree is readable, with its path in $BIGRIG_REF:
 
-    python tests/golden/make_goldens.py
+    BIGRIG_REF=<path to the BigRig tree> python tests/golden/make_goldens.py
 
 What it writes (all small, committed; nothing at test time reads the reference):
 
@@ -32,7 +31,7 @@ import types
 
 import numpy as np
 
-REF = os.environ.get("BIGRIG_REF", "/root/reference")
+REF = os.environ.get("BIGRIG_REF", "")
 HERE = os.path.dirname(os.path.abspath(__file__))
 POLICIES = ["lru", "wlfu", "lfuda", "s3fifo", "arc", "lirs", "gaterank", "coact"]
 CAPACITIES = [8, 16, 32, 64]
@@ -209,6 +208,8 @@ def manifest_fixture() -> dict:
 
 
 def main() -> None:
+    if not REF or not os.path.isdir(REF):
+        raise SystemExit("set BIGRIG_REF to the BigRig tree (the reference's source)")
     sys.path.insert(0, REF)
     with open(os.path.join(HERE, "manifest_golden.json"), "w") as f:
         json.dump(manifest_fixture(), f, indent=1)
