@@ -27,6 +27,7 @@ block applies the router weights (stream.py:1523-1525).
 from __future__ import annotations
 
 import contextlib
+import ctypes
 import inspect
 import json
 import os
@@ -60,6 +61,12 @@ def projections_of(spec: dict) -> tuple:
 
 def is_gated(projections) -> bool:
     return "gate_proj" in tuple(projections)
+
+
+def _call(rc: int, what: str) -> None:
+    """A library status code: raise on anything but BIGRIG_OK."""
+    if rc:
+        _lib.check(rc, what)
 
 
 def _as_u8(blob) -> torch.Tensor:
@@ -597,20 +604,35 @@ class StreamingSwitchGLU:
         E = pool.n_experts
         pred = None
         rs = self._route_scratch(x2.device, E, k)
+        if not x2.is_cuda:
+            ops._require_cuda("x", x2, torch.bfloat16)
+        mcode = ops._MODES.get(mode)
+        if mcode is None:
+            raise ValueError(f"mode must be one of {tuple(ops._MODES)}, got {mode!r}")
+        lib = _lib.load()
+        dev = x2.get_device()
+        st = ops._raw_stream(dev)
+        self._check_weights(gate_w, gate_b)
+        # the library called directly: every pointer here is a buffer of this layer's, checked
+        # once, and x2 is bf16, contiguous and on the device (made so above)
         if (STAGING and nxt is not None and self._next_gate is not None and not nxt.full
                 and nxt.n_experts == E and k <= E):
             w2, b2 = self._route_pair(gate_w, gate_b)
-            ops.router_logits(x2, w2, b2, out=rs[0])
-            ops.router_topk(rs[0].view(2, E), k, mode, norm_topk, indices=rs[1], scores=rs[2])
+            _call(lib.bigrig_router_logits(x2.data_ptr(), w2.data_ptr(), b2.data_ptr(), rs[4], 1,
+                                           H, 2 * E, st), "router_logits")
+            _call(lib.bigrig_router_topk(rs[4], _lib.F32, 2, E, k, mcode, int(norm_topk), rs[5],
+                                         rs[6], st), "router_topk")
             t0 = time.perf_counter()
             rs[3].copy_(rs[1])                                    # the host readback
             host = rs[3].numpy().astype(np.int64)
             self.sync_seconds += time.perf_counter() - t0
             gi, pred = host[:1], host[1]
         else:
-            ops.router_logits(x2, gate_w, gate_b, out=rs[0][:E])
-            ops.router_topk(rs[0][:E].view(1, E), k, mode, norm_topk, indices=rs[1][:1],
-                            scores=rs[2][:1])
+            _call(lib.bigrig_router_logits(x2.data_ptr(), gate_w.data_ptr(),
+                                           0 if gate_b is None else gate_b.data_ptr(), rs[4], 1,
+                                           H, E, st), "router_logits")
+            _call(lib.bigrig_router_topk(rs[4], _lib.F32, 1, E, k, mcode, int(norm_topk), rs[5],
+                                         rs[6], st), "router_topk")
             t0 = time.perf_counter()
             rs[3][:1].copy_(rs[1][:1])                            # the host readback
             gi = rs[3][:1].numpy().astype(np.int64)
@@ -618,14 +640,19 @@ class StreamingSwitchGLU:
         self._count_routing(gi.reshape(-1))
         self.ensure(gi)
         pool.ready()
-        scratch = getattr(self, "_layer_scratch", None)
-        if scratch is None or scratch[0].shape[1] != k or scratch[0].device != x2.device:
-            scratch = self._layer_scratch = (
-                torch.empty(1, k, dtype=torch.int32, device=x2.device),
-                torch.empty(1, k, dtype=torch.float32, device=x2.device))
-        out, _, _ = ops.moe_layer(x2, gate_w, gate_b, k, pool.slab, pool.layout, pool.n_experts,
-                                  mode, norm_topk, g2s=pool.g2s_device(), residual=residual,
-                                  indices=scratch[0], scores=scratch[1], workspace=self.workspace)
+        if residual is not None and not (residual.is_cuda and residual.dtype == torch.bfloat16
+                                         and residual.is_contiguous()
+                                         and residual.numel() == H):
+            ops._require_cuda("residual", residual, torch.bfloat16)
+            raise ValueError(f"residual holds {residual.numel()} values, the layer makes {H}")
+        ws = self.workspace or ops.default_workspace(x2.device)
+        buf = ws.reserve(ops.workspace_bytes(1, k, E, pool.layout))
+        out = torch.empty(1, H, dtype=torch.bfloat16, device=x2.device)
+        _call(lib.bigrig_moe_layer(
+            x2.data_ptr(), gate_w.data_ptr(), 0 if gate_b is None else gate_b.data_ptr(), 1, E, k,
+            mcode, int(norm_topk), pool.g2s_device().data_ptr(), pool.slab.data_ptr(),
+            self._layout_ptr(), 0 if residual is None else residual.data_ptr(), out.data_ptr(),
+            rs[5], rs[6], buf.data_ptr(), buf.numel(), st), "moe_layer")
         pool.mark_read()
         if pred is not None:
             self._speculate(pred)
@@ -634,14 +661,33 @@ class StreamingSwitchGLU:
     def _route_scratch(self, device, E: int, k: int):
         """Per-layer routing buffers of the one-token path, made once: logits fp32 [2E] (this
         layer's and the next router's), indices int32 [2, k], scores fp32 [2, k] on the
-        device, and a pinned int32 [2, k] host copy for the readback."""
+        device, a pinned int32 [2, k] host copy for the readback, and the three device
+        buffers' addresses."""
         rs = getattr(self, "_rs", None)
         if rs is None or rs[0].numel() != 2 * E or rs[1].shape[1] != k or rs[0].device != device:
-            rs = self._rs = (torch.empty(2 * E, dtype=torch.float32, device=device),
-                             torch.empty(2, k, dtype=torch.int32, device=device),
-                             torch.empty(2, k, dtype=torch.float32, device=device),
-                             torch.empty(2, k, dtype=torch.int32).pin_memory())
+            t = (torch.empty(2 * E, dtype=torch.float32, device=device),
+                 torch.empty(2, k, dtype=torch.int32, device=device),
+                 torch.empty(2, k, dtype=torch.float32, device=device),
+                 torch.empty(2, k, dtype=torch.int32).pin_memory())
+            rs = self._rs = t + (t[0].data_ptr(), t[1].data_ptr(), t[2].data_ptr())
         return rs
+
+    def _check_weights(self, gate_w: torch.Tensor, gate_b: torch.Tensor | None) -> None:
+        """The router's weights as the library wants them, checked once per pair of tensors."""
+        key = (id(gate_w), gate_w.data_ptr(), None if gate_b is None else (id(gate_b), gate_b.data_ptr()))
+        if getattr(self, "_checked", None) != key:
+            ops._require_cuda("gate_w", gate_w, torch.bfloat16)
+            if gate_b is not None:
+                ops._require_cuda("gate_b", gate_b, torch.float32)
+            ops._require_cuda("slab", self._pool.slab, torch.uint8)
+            self._checked = key
+
+    def _layout_ptr(self):
+        """A ctypes pointer to this pool's layout struct (checked by the library once)."""
+        lp = getattr(self, "_lp", None)
+        if lp is None or lp[0] is not self._pool.layout:
+            lp = self._lp = (self._pool.layout, ctypes.pointer(ops.c_layout(self._pool.layout)))
+        return lp[1]
 
     def _route_pair(self, gate_w: torch.Tensor, gate_b: torch.Tensor | None):
         """This layer's and the next layer's router weights stacked [2E, H] (and biases),
