@@ -1,19 +1,31 @@
-"""ARC, adaptive replacement cache (bigrig_engine/policies/arc.py:52-129).
+"""ARC, adaptive replacement: a recency list, a frequency list and their ghost lists.
 
-Two resident lists, T1 (seen once) and T2 (seen again), each least recent
-first, and their ghost lists B1/B2 of evicted ids.  A hit promotes T1 -> T2 or
-refreshes T2.  A miss that finds its id in B1 grows the target size ``p`` of
-T1 by max(1, |B2|/|B1|) (capped at c) and lands in T2; one in B2 shrinks ``p``
-by max(1, |B1|/|B2|) (floored at 0) and lands in T2; a new id lands in T1.
-The victim is the oldest of T1 when T1 exceeds ``p`` (or T2 is empty), else the
-oldest of T2.  Ghosts keep |T1|+|B1| <= c and the four lists <= 2c, oldest ghost
-dropped first (B2 before B1 for the second bound).
+Decision rule (bigrig_engine/policies/arc.py:52-129).  Lists, each ordered from its
+least recent entry: T1 (held, used once), T2 (held, used again), B1 and B2 (ids
+evicted from T1 and T2).  ``p`` is T1's target length, between 0 and the capacity c.
+
+* admission of a B1 ghost raises ``p`` by max(1, |B2| / max(1, |B1|)) (at most c)
+  and puts the expert at T2's tail; of a B2 ghost lowers ``p`` by
+  max(1, |B1| / max(1, |B2|)) (at least 0) and puts it at T2's tail; any other
+  expert goes to T1's tail;
+* a use moves the expert to T2's tail (from T1, from within T2, or from nowhere);
+* the victim is T1's oldest when T1 is longer than ``p`` or T2 is empty, else T2's
+  oldest;
+* an eviction moves the expert from T1 to B1's tail or from T2 to B2's tail;
+* after admissions and evictions the ghosts are trimmed, oldest first: B1 while
+  |T1| + |B1| > c, then B2 (or B1 when B2 is empty) while all four exceed 2c.
+
+State: per expert a list code and the clock value at which it entered that list;
+a list's oldest entry is its member with the smallest entry clock.
 """
 from __future__ import annotations
 
-from collections import OrderedDict
+import numpy as np
 
 from ..pool import Policy
+from ._columns import Columns, first_by
+
+OUT, T1, T2, B1, B2 = 0, 1, 2, 3, 4
 
 
 class ARC(Policy):
@@ -23,64 +35,72 @@ class ARC(Policy):
         super().__init__(capacity, n_experts)
         self.c = capacity
         self.p = 0.0
-        self.t1: OrderedDict = OrderedDict()
-        self.t2: OrderedDict = OrderedDict()
-        self.b1: OrderedDict = OrderedDict()
-        self.b2: OrderedDict = OrderedDict()
+        self.clock = 0
+        self.size = [0, 0, 0, 0, 0]          # entries per list code
+        self.col = Columns(n_experts, where=(np.int8, OUT), entered=(np.int64, 0))
 
-    def _bound_ghosts(self) -> None:
-        while self.b1 and len(self.t1) + len(self.b1) > self.c:
-            self.b1.popitem(last=False)
-        while len(self.t1) + len(self.t2) + len(self.b1) + len(self.b2) > 2 * self.c:
-            if self.b2:
-                self.b2.popitem(last=False)
-            elif self.b1:
-                self.b1.popitem(last=False)
+    def _put(self, e: int, lst: int) -> None:
+        """Move e to the tail of ``lst`` (OUT removes it from every list)."""
+        c = self.col
+        self.size[int(c.where[e])] -= 1
+        self.size[lst] += 1
+        c.where[e] = lst
+        self.clock += 1
+        c.entered[e] = self.clock
+
+    def _oldest(self, lst: int) -> int:
+        return first_by(self.col.where == lst, self.col.entered)
+
+    def _trim_ghosts(self) -> None:
+        s = self.size
+        while s[B1] and s[T1] + s[B1] > self.c:
+            self._put(self._oldest(B1), OUT)
+        while s[T1] + s[T2] + s[B1] + s[B2] > 2 * self.c:
+            if s[B2]:
+                self._put(self._oldest(B2), OUT)
+            elif s[B1]:
+                self._put(self._oldest(B1), OUT)
             else:
                 break
 
     def admit(self, e, rank=0):
-        if e in self.b1:
-            self.p = min(float(self.c), self.p + max(1.0, len(self.b2) / max(1, len(self.b1))))
-            del self.b1[e]
-            self.t2[e] = None
-        elif e in self.b2:
-            self.p = max(0.0, self.p - max(1.0, len(self.b1) / max(1, len(self.b2))))
-            del self.b2[e]
-            self.t2[e] = None
+        e = int(e)
+        self.col.fit(e)
+        w = int(self.col.where[e])
+        s = self.size
+        if w == B1:
+            self.p = min(float(self.c), self.p + max(1.0, s[B2] / max(1, s[B1])))
+            self._put(e, T2)
+        elif w == B2:
+            self.p = max(0.0, self.p - max(1.0, s[B1] / max(1, s[B2])))
+            self._put(e, T2)
         else:
-            self.t1.pop(e, None)
-            self.t2.pop(e, None)
-            self.t1[e] = None
-        self._bound_ghosts()
+            self._put(e, T1)
+        self._trim_ghosts()
 
     def touch(self, e, rank=0):
-        if e in self.t1:
-            del self.t1[e]
-            self.t2[e] = None
-        elif e in self.t2:
-            self.t2.move_to_end(e)
-        else:
-            self.t2[e] = None
-
-    @staticmethod
-    def _oldest(od) -> int:
-        for e in od:
-            return e
-        return -1
+        e = int(e)
+        self.col.fit(e)
+        self._put(e, T2)
 
     def victim(self):
-        if self.t1 and (len(self.t1) > self.p or not self.t2):
-            return self._oldest(self.t1)
-        if self.t2:
-            return self._oldest(self.t2)
-        return self._oldest(self.t1)
+        s = self.size
+        if s[T1] and (s[T1] > self.p or not s[T2]):
+            return self._oldest(T1)
+        if s[T2]:
+            return self._oldest(T2)
+        return -1
 
     def evicted(self, e):
-        if e in self.t1:
-            del self.t1[e]
-            self.b1[e] = None
-        elif e in self.t2:
-            del self.t2[e]
-            self.b2[e] = None
-        self._bound_ghosts()
+        e = int(e)
+        self.col.fit(e)
+        w = int(self.col.where[e])
+        if w == T1:
+            self._put(e, B1)
+        elif w == T2:
+            self._put(e, B2)
+        self._trim_ghosts()
+
+
+def factory(capacity, n_experts):
+    return ARC(capacity, n_experts)

@@ -1,35 +1,40 @@
-"""GateRank: recency plus a bonus for the router's rank (bigrig_engine/policies/gaterank.py:102-165).
+"""GateRank: recency with a bonus for a high router rank.
 
-Each use sets an expert's priority to ``tick + boost * w(rank)`` (kept at least
-its previous priority when ``monotone``); the victim is the resident expert with
-the lowest priority, ties to the lower id.  ``w`` is one of ``linear`` (k-1-r)/(k-1)
-with k = ``param`` (default 8), ``inv`` 1/(1+r), or ``geom`` param**r.  Priorities
-live in a lazily invalidated heap, rebuilt when stale entries pile up.
+Decision rule (bigrig_engine/policies/gaterank.py:102-165, defaults ``boost=16``,
+``shape="linear"``, ``param=8``, ``monotone=True``): the n-th use of the cache
+gives the used expert the priority ``n + boost * w(rank)``, or its previous
+priority if that is higher and ``monotone`` is set; the victim is the tracked
+expert of lowest priority, ties to the lowest expert id; an evicted expert is
+forgotten.  Rank weights ``w``:
+
+* ``linear``: (k - 1 - r) / (k - 1) with k = ``param`` (1 when k <= 1), at least 0;
+* ``inv``: 1 / (1 + r);
+* ``geom``: ``param`` ** r.
+
+State: a priority column and a tracked flag per expert; the victim is a masked
+argmin over the priority column.
 """
 from __future__ import annotations
 
-import heapq
+import numpy as np
 
 from ..pool import Policy
+from ._columns import Columns, first_by
 
 
-def _w_inv(r: int) -> float:
-    return 1.0 / (1.0 + r)
-
-
-def _w_geom(gamma: float):
-    return lambda r: gamma ** r
-
-
-def _w_linear(k: int):
-    def f(r: int) -> float:
+def rank_weight(shape: str, param: float):
+    """The rank-weight function ``w(r)`` for ``shape`` and its parameter."""
+    if shape == "inv":
+        return lambda r: 1.0 / (1.0 + r)
+    if shape == "geom":
+        g = param
+        return lambda r: g ** r
+    if shape == "linear":
+        k = int(param)
         if k <= 1:
-            return 1.0
-        return max(0.0, (k - 1 - r) / (k - 1))
-    return f
-
-
-SHAPES = {"inv": lambda p: _w_inv, "geom": lambda p: _w_geom(p), "linear": lambda p: _w_linear(int(p))}
+            return lambda r: 1.0
+        return lambda r: max(0.0, (k - 1 - r) / (k - 1))
+    raise ValueError(f"rank-weight shape must be linear, inv or geom, got {shape!r}")
 
 
 class GateRank(Policy):
@@ -40,48 +45,41 @@ class GateRank(Policy):
         super().__init__(capacity, n_experts)
         self.boost = float(boost)
         self.monotone = bool(monotone)
-        self.w = SHAPES[shape](param)
-        self.tick = 0
-        self.key: dict = {}
-        self.heap: list = []
-        self._limit = 4 * max(1, capacity) + 16
+        self.weight = rank_weight(shape, param)
+        self.clock = 0
+        self.col = Columns(n_experts, prio=(np.float64, 0.0), tracked=(np.bool_, False))
 
     def _use(self, e: int, rank: int) -> None:
-        self.tick += 1
-        k = self.tick + self.boost * self.w(rank)
-        if self.monotone:
-            old = self.key.get(e)
-            if old is not None and old > k:
-                k = old
-        self.key[e] = k
-        heapq.heappush(self.heap, (k, e))
-        if len(self.heap) > self._limit:
-            self.heap = [(v, x) for x, v in self.key.items()]
-            heapq.heapify(self.heap)
+        c = self.col
+        c.fit(e)
+        self.clock += 1
+        p = self.clock + self.boost * self.weight(rank)
+        if self.monotone and c.tracked[e] and float(c.prio[e]) > p:
+            p = float(c.prio[e])
+        c.prio[e] = p
+        c.tracked[e] = True
 
     def admit(self, e, rank=0):
-        self._use(e, rank)
+        self._use(int(e), rank)
 
     def touch(self, e, rank=0):
-        self._use(e, rank)
+        self._use(int(e), rank)
 
     def victim(self):
-        while self.heap:
-            k, e = self.heap[0]
-            if self.key.get(e) != k:
-                heapq.heappop(self.heap)
-                continue
-            return e
-        return -1
+        return first_by(self.col.tracked, self.col.prio)
 
     def evicted(self, e):
-        self.key.pop(e, None)
+        e = int(e)
+        if e < self.col.tracked.shape[0]:
+            self.col.tracked[e] = False
 
 
 def make(boost: float = 16.0, shape: str = "linear", param: float = 8, monotone: bool = True):
-    """A ``factory(capacity, n_experts)`` with GateRank's parameters bound."""
+    """A ``factory(capacity, n_experts)`` building GateRank with these parameters."""
     return lambda capacity, n_experts: GateRank(capacity, n_experts, boost=boost, shape=shape,
                                                 param=param, monotone=monotone)
 
 
-gaterank = make()
+def gaterank(capacity, n_experts):
+    """The shipped configuration."""
+    return GateRank(capacity, n_experts)

@@ -1,17 +1,28 @@
-"""LFUDA: LFU with dynamic aging, the shipped default (bigrig_engine/policies/lfuda.py:67-173).
+"""LFUDA, frequency with dynamic aging: the engine's default expert-cache policy.
 
-Every use re-anchors an expert's key to the cache age: ``key = L + count``,
-with ``count`` saturating at ``fcap`` (12).  The victim is the resident expert
-with the smallest key, ties to the least recently used.  An eviction raises
-``L`` to the victim's key (never lowers it) and, with ``keep_ghost``, keeps the
-victim's count multiplied by ``ghost_decay`` (0.5) so a returning expert is not
-a stranger.  ``rank_weight`` > 0 credits a use at router rank r with
-1 + rank_weight / (1 + r) instead of 1.  ``victim(exclude=...)`` skips experts
-the caller is still using, so the pool never has to report a false eviction.
+Decision rule (bigrig_engine/policies/lfuda.py:67-173, defaults ``rank_weight=0``,
+``keep_ghost=True``, ``fcap=12``, ``ghost_decay=0.5``):
+
+* a use of expert e adds a credit (1, or 1 + rank_weight / (1 + rank) when rank
+  weighting is on) to e's frequency, saturating at ``fcap``, and sets e's priority
+  to ``age + frequency``;
+* the victim is the held expert of lowest priority, ties to the one used longest
+  ago; ``victim(exclude=...)`` never names an excluded expert;
+* an eviction raises ``age`` to the victim's priority if that is higher, and
+  keeps the victim's frequency scaled by ``ghost_decay`` (``keep_ghost``) or
+  forgets it.
+
+State: four per-expert columns (frequency, priority, use clock, held flag) and
+the scalar age.  Priorities and frequencies are float64 and updated with the
+same operations in the same order as the rule above states, so the victims, and
+the miss counts on a replayed trace, are the reference's.
 """
 from __future__ import annotations
 
+import numpy as np
+
 from ..pool import Policy
+from ._columns import Columns, first_by
 
 
 class LFUDA(Policy):
@@ -22,60 +33,73 @@ class LFUDA(Policy):
         super().__init__(capacity, n_experts)
         self.rank_weight = float(rank_weight)
         self.keep_ghost = bool(keep_ghost)
-        self.fcap = fcap
+        self.fcap = None if fcap is None else float(fcap)
         self.ghost_decay = float(ghost_decay)
-        self.L = 0.0          # cache age: the largest key evicted so far
-        self.cnt: dict = {}   # expert -> frequency credit (kept across evictions as a ghost)
-        self.key: dict = {}   # resident expert -> L at last use + credit
-        self.last: dict = {}  # expert -> tick of last use (tie-break)
-        self.resident: set = set()
-        self.tick = 0
+        self.age = 0.0
+        self.clock = 0
+        self.col = Columns(n_experts, freq=(np.float64, 0.0), prio=(np.float64, 0.0),
+                           used_at=(np.int64, 0), held=(np.bool_, False),
+                           has_prio=(np.bool_, False))
+
+    def _credit(self, rank: int) -> float:
+        if self.rank_weight == 0.0:
+            return 1.0
+        return 1.0 + self.rank_weight / (1.0 + rank)
 
     def _use(self, e: int, rank: int) -> None:
-        self.tick += 1
-        self.last[e] = self.tick
-        credit = 1.0 if self.rank_weight == 0.0 else 1.0 + self.rank_weight / (1.0 + rank)
-        c = self.cnt.get(e, 0.0) + credit
-        if self.fcap is not None and c > self.fcap:
-            c = self.fcap
-        self.cnt[e] = c
-        self.key[e] = self.L + c
+        c = self.col
+        c.fit(e)
+        self.clock += 1
+        c.used_at[e] = self.clock
+        f = float(c.freq[e]) + self._credit(rank)
+        if self.fcap is not None and f > self.fcap:
+            f = self.fcap
+        c.freq[e] = f
+        c.prio[e] = self.age + f
+        c.has_prio[e] = True
 
     def admit(self, e, rank=0):
-        self.resident.add(e)
+        e = int(e)
+        self.col.fit(e)
+        self.col.held[e] = True
         if not self.keep_ghost:
-            self.cnt.pop(e, None)
+            self.col.freq[e] = 0.0
         self._use(e, rank)
 
     def touch(self, e, rank=0):
-        self._use(e, rank)
+        self._use(int(e), rank)
 
     def victim(self, exclude=()):
-        cands = self.resident if not exclude else self.resident.difference(exclude)
-        if not cands:
-            return -1
-        return min(cands, key=lambda x: (self.key.get(x, 0.0), self.last.get(x, 0)))
+        c = self.col
+        mask = c.held
+        if exclude:
+            mask = mask.copy()
+            for x in exclude:
+                if 0 <= int(x) < mask.shape[0]:
+                    mask[int(x)] = False
+        return first_by(mask, c.prio, c.used_at)
 
     def evicted(self, e):
-        k = self.key.pop(e, self.L)
-        if k > self.L:
-            self.L = k
-        self.resident.discard(e)
+        e = int(e)
+        c = self.col
+        c.fit(e)
+        p = float(c.prio[e]) if c.has_prio[e] else self.age
+        c.has_prio[e] = False
+        if p > self.age:
+            self.age = p
+        c.held[e] = False
         if not self.keep_ghost:
-            self.cnt.pop(e, None)
-            self.last.pop(e, None)
+            c.freq[e] = 0.0
+            c.used_at[e] = 0
         elif self.ghost_decay != 1.0:
-            self.cnt[e] = self.cnt.get(e, 0.0) * self.ghost_decay
+            c.freq[e] = float(c.freq[e]) * self.ghost_decay
+
+    @property
+    def L(self) -> float:
+        """The cache age under its conventional name."""
+        return self.age
 
 
-class TextbookLFUDA(LFUDA):
-    """Uncapped count dropped on eviction: aging alone (kept for comparison)."""
-    name = "lfuda_textbook"
-
-    def __init__(self, capacity, n_experts):
-        super().__init__(capacity, n_experts, keep_ghost=False, fcap=None, ghost_decay=1.0)
-
-
-def factory(**kw):
-    """``factory(**params)`` -> ``f(capacity, n_experts)`` with LFUDA's parameters bound."""
-    return lambda capacity, n_experts: LFUDA(capacity, n_experts, **kw)
+def factory(**params):
+    """``factory(**params)`` -> ``f(capacity, n_experts)`` building LFUDA with those parameters."""
+    return lambda capacity, n_experts: LFUDA(capacity, n_experts, **params)

@@ -1,103 +1,148 @@
-"""S3-FIFO (bigrig_engine/policies/s3fifo.py:42-144).
+"""S3-FIFO: a small probationary FIFO, a main FIFO and a ghost FIFO of recent rejects.
 
-A small FIFO S (target 10% of capacity) quarantines new experts, a main FIFO M
-holds proven ones, and a ghost FIFO (capacity entries) remembers ids evicted
-from S.  A hit bumps a frequency capped at 3.  Admission puts a ghost id
-straight into M, anything else into S.  Eviction: while S holds at least its
-target, pop S's head -- promoted to M's tail (frequency reset) if it was hit more
-than once, else evicted and remembered as a ghost; otherwise pop M's head --
-re-queued with frequency - 1 if it was hit, else evicted.
+Decision rule (bigrig_engine/policies/s3fifo.py:42-144; small queue target 10 %
+of capacity, frequency capped at 3, promotion above 1 use, ghost length equal to
+the capacity):
+
+* admission places a ghost straight into the main queue, anything else into the
+  small queue, with frequency 0 (an expert already queued is left alone);
+* a use raises the frequency by one, up to the cap;
+* ``victim()`` works the queues until it frees someone.  While the small queue
+  holds at least its target (or the main queue is empty) its head leaves it: with
+  frequency above 1 it moves to the main queue's tail with frequency 0, otherwise
+  it is the victim and becomes the newest ghost (the oldest ghost is forgotten
+  once the ghosts exceed their length).  Otherwise the main queue's head leaves
+  it: with a positive frequency it re-enters at the tail one lower, otherwise it
+  is the victim;
+* ``evicted(e)`` drops e from whichever queue still holds it.
+
+State: per expert a queue code (none / small / main), the clock value at which it
+entered its queue, a frequency, and a ghost clock (0 = not a ghost).  A queue's
+head is its member with the smallest entry clock.
 """
 from __future__ import annotations
 
-from collections import OrderedDict, deque
+import numpy as np
 
 from ..pool import Policy
+from ._columns import Columns, first_by
+
+NONE, SMALL, MAIN = 0, 1, 2
 
 
 class S3FIFO(Policy):
     name = "s3fifo"
 
-    S_RATIO = 0.10
-    FREQ_MAX = 3
-    PROMOTE_THRESHOLD = 1
-    GHOST_RATIO = 1.0
+    SMALL_SHARE = 0.10
+    FREQ_CAP = 3
+    PROMOTE_ABOVE = 1
+    GHOST_SHARE = 1.0
 
     def __init__(self, capacity, n_experts):
         super().__init__(capacity, n_experts)
-        self.s_target = max(1, int(round(self.S_RATIO * capacity)))
-        self.ghost_max = max(1, int(round(self.GHOST_RATIO * capacity)))
-        self.small: deque = deque()
-        self.main: deque = deque()
-        self.in_small: set = set()
-        self.in_main: set = set()
-        self.freq: dict = {}
-        self.ghost: OrderedDict = OrderedDict()
+        self.small_target = max(1, int(round(self.SMALL_SHARE * capacity)))
+        self.ghost_len = max(1, int(round(self.GHOST_SHARE * capacity)))
+        self.clock = 0
+        self.n_small = 0
+        self.n_main = 0
+        self.n_ghost = 0
+        self.col = Columns(n_experts, queue=(np.int8, NONE), entered=(np.int64, 0),
+                           freq=(np.int64, 0), ghost_at=(np.int64, 0))
+
+    def _enqueue(self, e: int, q: int) -> None:
+        self.clock += 1
+        self.col.queue[e] = q
+        self.col.entered[e] = self.clock
+        if q == SMALL:
+            self.n_small += 1
+        else:
+            self.n_main += 1
+
+    def _dequeue(self, e: int) -> None:
+        q = self.col.queue[e]
+        if q == SMALL:
+            self.n_small -= 1
+        elif q == MAIN:
+            self.n_main -= 1
+        self.col.queue[e] = NONE
+
+    def _head(self, q: int) -> int:
+        return first_by(self.col.queue == q, self.col.entered)
+
+    def _remember(self, e: int) -> None:
+        c = self.col
+        if c.ghost_at[e] == 0:
+            self.n_ghost += 1
+        self.clock += 1
+        c.ghost_at[e] = self.clock
+        while self.n_ghost > self.ghost_len:
+            g = first_by(c.ghost_at > 0, c.ghost_at)
+            c.ghost_at[g] = 0
+            self.n_ghost -= 1
 
     def admit(self, e, rank=0):
-        if e in self.in_small or e in self.in_main:
+        e = int(e)
+        c = self.col
+        c.fit(e)
+        if c.queue[e] != NONE:
             return
-        self.freq[e] = 0
-        if e in self.ghost:
-            del self.ghost[e]
-            self.main.append(e)
-            self.in_main.add(e)
+        c.freq[e] = 0
+        if c.ghost_at[e] > 0:
+            c.ghost_at[e] = 0
+            self.n_ghost -= 1
+            self._enqueue(e, MAIN)
         else:
-            self.small.append(e)
-            self.in_small.add(e)
+            self._enqueue(e, SMALL)
 
     def touch(self, e, rank=0):
-        f = self.freq.get(e, 0)
-        if f < self.FREQ_MAX:
-            self.freq[e] = f + 1
+        e = int(e)
+        c = self.col
+        c.fit(e)
+        if c.freq[e] < self.FREQ_CAP:
+            c.freq[e] += 1
 
-    def _from_small(self):
-        e = self.small.popleft()
-        self.in_small.discard(e)
-        if self.freq.get(e, 0) > self.PROMOTE_THRESHOLD:
-            self.freq[e] = 0
-            self.main.append(e)
-            self.in_main.add(e)
-            return None
-        self.freq.pop(e, None)
-        self.ghost[e] = None
-        self.ghost.move_to_end(e)
-        while len(self.ghost) > self.ghost_max:
-            self.ghost.popitem(last=False)
+    def _leave_small(self) -> int:
+        """Move the small queue's head on; return it if it is the victim, else -1."""
+        c = self.col
+        e = self._head(SMALL)
+        self._dequeue(e)
+        if c.freq[e] > self.PROMOTE_ABOVE:
+            c.freq[e] = 0
+            self._enqueue(e, MAIN)
+            return -1
+        c.freq[e] = 0
+        self._remember(e)
         return e
 
-    def _from_main(self):
-        e = self.main.popleft()
-        f = self.freq.get(e, 0)
-        if f > 0:
-            self.freq[e] = f - 1
-            self.main.append(e)
-            return None
-        self.in_main.discard(e)
-        self.freq.pop(e, None)
+    def _leave_main(self) -> int:
+        """Move the main queue's head on; return it if it is the victim, else -1."""
+        c = self.col
+        e = self._head(MAIN)
+        self._dequeue(e)
+        if c.freq[e] > 0:
+            c.freq[e] -= 1
+            self._enqueue(e, MAIN)
+            return -1
+        c.freq[e] = 0
         return e
 
     def victim(self):
-        while self.small or self.main:
-            if self.small and len(self.small) >= self.s_target:
-                v = self._from_small()
-            elif self.main:
-                v = self._from_main()
+        while self.n_small or self.n_main:
+            if self.n_small and (self.n_small >= self.small_target or not self.n_main):
+                v = self._leave_small()
             else:
-                v = self._from_small()
-            if v is not None:
+                v = self._leave_main()
+            if v >= 0:
                 return v
         return -1
 
     def evicted(self, e):
-        self.in_small.discard(e)
-        self.in_main.discard(e)
-        self.freq.pop(e, None)
-        for q in (self.small, self.main):
-            try:
-                q.remove(e)
-            except ValueError:
-                pass
+        e = int(e)
+        c = self.col
+        c.fit(e)
+        if c.queue[e] != NONE:
+            self._dequeue(e)
+        c.freq[e] = 0
 
 
 def factory(capacity, n_experts):

@@ -130,7 +130,7 @@ _BUILTIN = {"lru": LRU, "windowed_lfu": WindowedLFU, "wlfu": WindowedLFU}
 def available_policies() -> list:
     import pkgutil
     from . import policies as _pk
-    mods = {m.name for m in pkgutil.iter_modules(_pk.__path__)}
+    mods = {m.name for m in pkgutil.iter_modules(_pk.__path__) if not m.name.startswith("_")}
     return sorted(mods | set(_BUILTIN))
 
 
@@ -141,15 +141,22 @@ def _policy_factory(name: str, capacity: int, n_experts: int):
     configuration three ways, tried in this order: a module-level callable named
     like the module, a ``factory`` that is either ``factory(capacity, n_experts)``
     or ``factory(**kw) -> factory``, or failing both its own policy class.
+    A dotted name (``package.module``) resolves the same way from that module, so
+    any policy module written against the contract plugs in without living here.
     Unknown names raise ImportError listing what exists.
     """
     if name in _BUILTIN:
         return _BUILTIN[name]
+    if name.startswith("_"):
+        raise ImportError(f"no policy named {name!r}. Available: "
+                          f"{', '.join(available_policies())}")
+    path = name if "." in name else f"{__package__}.policies.{name}"
     try:
-        mod = importlib.import_module(f"{__package__}.policies.{name}")
+        mod = importlib.import_module(path)
     except ModuleNotFoundError:
         raise ImportError(f"no policy named {name!r}. Available: "
                           f"{', '.join(available_policies())}") from None
+    name = name.rsplit(".", 1)[-1]
 
     def works(f) -> bool:
         try:
@@ -288,7 +295,7 @@ def select_policy(tag: str, capacity: int, candidates=None, layers: int = 2,
     """Score candidate policies on a trace against the LRU and Belady bounds and pick the
     one that closes most of the gap (bigrig_engine/pool.py:219-249)."""
     import numpy as np
-    names = candidates or ["lfuda", "s3fifo", "gaterank", "lirs", "arc", "coact"]
+    names = candidates or [n for n in available_policies() if n not in _BUILTIN]
     idx, _ = load_trace(tag)
     E = n_experts or int(idx.max()) + 1
     streams = [requests(idx, l) for l in range(min(layers, idx.shape[0]))]

@@ -28,7 +28,6 @@ from __future__ import annotations
 
 import contextlib
 import ctypes
-import inspect
 import json
 import os
 import time
@@ -38,7 +37,7 @@ import torch
 
 from . import _lib, ops
 from .formats import PROJECTIONS, bytes_per_expert, layout_from_spec
-from .pool import _policy_factory
+from .residency import SlotTable
 
 # Most experts a layer copies to the GPU on the previous layer's prediction -- the router's
 # top-k, as in the reference (stream.py:1723-1726).
@@ -78,8 +77,8 @@ def _as_u8(blob) -> torch.Tensor:
     return torch.from_numpy(np.frombuffer(blob, dtype=np.uint8).copy())
 
 
-class ExpertPool:
-    """C slots of one layer's experts in HBM, plus the tables saying which expert is where.
+class ExpertPool(SlotTable):
+    """C slots of one layer's experts in HBM; the residency tables come from ``SlotTable``.
 
     Same constructor, methods, counters and exceptions as the reference
     (stream.py:501-810).  ``views`` is accepted for interface compatibility: on a
@@ -89,54 +88,32 @@ class ExpertPool:
     def __init__(self, layer: int, sg, n_experts: int, capacity: int, spec: dict,
                  policy: str = "lfuda", quant: dict | None = None, views: bool = False,
                  device=None, copy_stream: torch.cuda.Stream | None = None):
-        if not 1 <= capacity <= n_experts:
-            raise ValueError(
-                f"capacity must be in [1, {n_experts}], got {capacity}. A pool larger than the "
-                f"expert count wastes memory; a pool of zero cannot serve any token.")
-        self.layer, self.sg, self.n_experts, self.capacity = layer, sg, n_experts, capacity
-        self.spec = spec
+        super().__init__(layer, n_experts, capacity, policy)
+        self.sg, self.spec, self.views = sg, spec, bool(views)
         self.projections = projections_of(spec)
         self.gated = is_gated(self.projections)
         self.spec_quant = dict(quant or {"bits": 4, "group_size": 64, "mode": "affine"})
         self.layout = layout_from_spec(spec, self.spec_quant)
-        self.device = torch.device(device) if device is not None else (
-            torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
-            else torch.device("cpu"))
-        self.policy = _policy_factory(policy, capacity, n_experts)(capacity, n_experts)
-        try:
-            self._policy_excludes = "exclude" in inspect.signature(self.policy.victim).parameters
-        except (TypeError, ValueError):
-            self._policy_excludes = False
-        self._slot_tick = np.zeros(capacity, dtype=np.int64)
-        self._tick = 0
-        self.g2s = np.full(n_experts, -1, dtype=np.int32)
-        self.s2g = np.full(capacity, -1, dtype=np.int32)
-        self._g2s_dev = None
-        self._g2s_dirty = True
-        self._free = list(range(capacity))
-        self._resident = 0
-        self.hits = 0
-        self.misses = 0
-        self.uses = np.zeros(n_experts, dtype=np.int64)
-        self.admits = 0
-        self.admit_seconds = 0.0
-        self.admit_bytes = 0
-        self.stage_pred = None
-        self.stage = {}            # expert id -> its bytes in a staging buffer, ready to admit
-        self.stage_issued = 0
-        self.stage_hits = 0
-        self._stage_buf = None     # [STAGE_MAX, bytes_per_expert] in HBM, made on first use
-        self.zero_copy_admits = 0
-        self.evicts = 0
-        self.views = bool(views)
+        self._bpe = bytes_per_expert(spec)
+        if device is None:
+            device = (torch.device("cuda", torch.cuda.current_device())
+                      if torch.cuda.is_available() else "cpu")
+        self.device = torch.device(device)
+        # the HBM side: the slab, its copy stream and the two events ordering copies and reads
         self.slab: torch.Tensor | None = None
         self._built = False
-        self._pending_rank: dict = {}
         self._copy_stream = copy_stream
         self._copies_done = None     # event: this pool's queued admissions have landed
         self._reads_done = None      # event: the last kernel that read the slab has finished
-        self._bpe = bytes_per_expert(spec)
         self._batch = None           # slot writes collected by ensure(), issued in one call
+        self._g2s_dev = None
+        self.admit_seconds = 0.0
+        self.admit_bytes = 0
+        # staging: experts the previous layer predicted for this one, copied ahead of need
+        self.stage_pred = None
+        self.stage = {}              # expert id -> its bytes in a staging buffer
+        self._stage_buf = None       # [STAGE_MAX, bytes_per_expert] in HBM, made on first use
+        self.stage_issued = self.stage_hits = self.zero_copy_admits = 0
 
     # -- construction -------------------------------------------------------
     @property
@@ -171,68 +148,17 @@ class ExpertPool:
 
     views_of = expert_arrays
 
-    def slot_of(self, e: int) -> int:
-        return int(self.g2s[e])
-
-    # -- residency ----------------------------------------------------------
-    def touch(self, experts, ranks=None) -> list:
-        """Record a request for each expert; return those not resident (stream.py:622-642)."""
-        need, nrank = [], []
-        ranks = list(ranks) if ranks is not None else [0] * len(experts)
-        for e, r in zip(experts, ranks):
-            e, r = int(e), int(r)
-            self.uses[e] += 1
-            if self.g2s[e] >= 0:
-                self.hits += 1
-                self.policy.touch(e, r)
-            else:
-                self.misses += 1
-                need.append(e)
-                nrank.append(r)
-        self._pending_rank = dict(zip(need, nrank))
-        return need
-
-    def _victim(self, protect=()) -> int:
-        """Free a slot, telling the policy only about real evictions (stream.py:644-690)."""
-        if self._free:
-            return self._free.pop()
-        protect = {int(x) for x in protect}
-        v = self.policy.victim(exclude=protect) if self._policy_excludes else self.policy.victim()
-        ev = int(v) if v is not None and v >= 0 and v not in protect and self.g2s[v] >= 0 else -1
-        if ev < 0:
-            best, best_t = -1, None
-            for slot in range(self.capacity):
-                g = int(self.s2g[slot])
-                if g < 0 or g in protect:
-                    continue
-                if best_t is None or self._slot_tick[slot] < best_t:
-                    best, best_t = g, self._slot_tick[slot]
-            ev = best
-        if ev < 0:
-            raise RuntimeError(
-                f"layer {self.layer}: every one of {self.capacity} slots holds an expert this "
-                f"step still needs. Capacity must be at least top-k.")
-        slot = int(self.g2s[ev])
-        if hasattr(self.policy, "evicted"):
-            self.policy.evicted(ev)
-        self.g2s[ev] = -1
-        self.s2g[slot] = -1
-        self._resident -= 1
-        self._g2s_dirty = True
-        self.evicts += 1
-        return slot
-
     def admit(self, e: int, blob, protect=()) -> int:
         """Copy expert e's packed bytes into a slot and return the slot (stream.py:692-705)."""
-        if not self._built:
-            raise RuntimeError("build() must run before admit()")
-        src = _as_u8(blob)
-        want = self.bytes_per_expert
-        if src.numel() != want:
-            raise ValueError(
-                f"layer {self.layer} expert {e}: the manifest accounts for {want} bytes but the "
-                f"region supplied {src.numel()}. Refusing to write a partially-filled slot.")
         t0 = time.perf_counter()
+        if not self._built:
+            raise RuntimeError("admit() before build(): the pool has no slab yet")
+        src = _as_u8(blob)
+        if src.numel() != self.bytes_per_expert:
+            raise ValueError(
+                f"layer {self.layer} expert {e}: got {src.numel()} bytes, the layout needs "
+                f"{self.bytes_per_expert}; a short or long region would leave the slot holding "
+                f"parts of two experts, so nothing is written")
         return self.admit_arrays(e, src, protect=protect, _t0=t0)
 
     def build_arrays(self, e: int, blob) -> torch.Tensor:
@@ -316,21 +242,13 @@ class ExpertPool:
         return True
 
     def admit_arrays(self, e: int, arrays, protect=(), _t0=None) -> int:
-        """Place bytes (host or device) into a slot; bookkeeping as admit (stream.py:757-780)."""
-        if _t0 is None:
-            _t0 = time.perf_counter()
+        """Write bytes already prepared (host or device) into a freed slot and record the
+        admission (stream.py:757-780); returns the slot."""
+        started = time.perf_counter() if _t0 is None else _t0
         slot = self._victim(protect=protect)
         self._write_slot(slot, arrays)
-        if self.s2g[slot] < 0:
-            self._resident += 1
-        self.g2s[e] = slot
-        self.s2g[slot] = e
-        self._g2s_dirty = True
-        self._tick += 1
-        self._slot_tick[slot] = self._tick
-        self.policy.admit(e, int(self._pending_rank.get(e, 0)))
-        self.admits += 1
-        self.admit_seconds += time.perf_counter() - _t0
+        self._placed(int(e), slot)
+        self.admit_seconds += time.perf_counter() - started
         return slot
 
     def _write_slot(self, slot: int, src: torch.Tensor) -> None:
@@ -423,11 +341,6 @@ class ExpertPool:
         self._copies_done = None
         self._reads_done = None
 
-    @property
-    def full(self) -> bool:
-        """True when every expert is resident, so no request can miss (stream.py:782-789)."""
-        return self.capacity == self.n_experts and self._resident == self.n_experts
-
     def g2s_device(self) -> torch.Tensor:
         """The expert->slot table on the device, re-uploaded only when residency changed
         (from a small ring of pinned host buffers, each reused once its last upload ran)."""
@@ -458,12 +371,9 @@ class ExpertPool:
         return self._g2s_dev
 
     def stats(self) -> dict:
-        tot = self.hits + self.misses
-        return {"layer": self.layer, "capacity": self.capacity, "n_experts": self.n_experts,
-                "hits": self.hits, "misses": self.misses,
-                "miss_rate": self.misses / tot if tot else 0.0,
-                "admits": self.admits, "evicts": self.evicts,
-                "resident_bytes": self.nbytes()}
+        d = super().stats()
+        d["resident_bytes"] = self.nbytes()
+        return d
 
 
 def _pair_chunks(sorted_experts: np.ndarray, C: int):
@@ -519,33 +429,30 @@ class StreamingSwitchGLU:
         """Make every requested expert resident; return the slot-remapped indices
         (stream.py:922-978).  ``ranks`` overrides the rank read off the last axis."""
         gi = np.asarray(indices).astype(np.int64)
-        best: dict = {}
+        flat = gi.reshape(-1)
         if ranks is not None:
-            for e, r in zip(gi.reshape(-1), np.asarray(ranks).reshape(-1)):
-                e, r = int(e), int(r)
-                if e not in best or r < best[e]:
-                    best[e] = r
+            rk = np.asarray(ranks, dtype=np.int64).reshape(-1)
         else:
-            for row in gi.reshape(-1, gi.shape[-1]):
-                for r, e in enumerate(row):
-                    e = int(e)
-                    if e not in best or r < best[e]:
-                        best[e] = r
-        uniq = sorted(best)
+            rk = np.tile(np.arange(gi.shape[-1], dtype=np.int64), flat.shape[0] // max(1, gi.shape[-1]))
+        # each distinct expert once, ascending, at the best (lowest) rank it was asked at
+        uniq, which = np.unique(flat, return_inverse=True)
+        best = np.full(uniq.shape[0], np.iinfo(np.int64).max, dtype=np.int64)
+        np.minimum.at(best, which.reshape(-1), rk)
         pool = self._pool
-        need = pool.touch(uniq, [best[e] for e in uniq])
+        need = pool.touch(uniq, best)
+        protect = set(uniq.tolist())
         if need:
             if len(need) > pool.capacity:
                 raise RuntimeError(
-                    f"layer {pool.layer} needs {len(need)} experts for one step but the pool "
-                    f"holds {pool.capacity}. Capacity must be at least top-k; below that a "
-                    f"token evicts an expert it is still using.")
+                    f"layer {pool.layer}: this step misses {len(need)} distinct experts and the "
+                    f"pool has {pool.capacity} slots, so one would evict another before use; "
+                    f"the capacity must be at least top-k (call with fewer tokens per step).")
             staged = [int(e) for e in need if int(e) in pool.stage]
             cold = [int(e) for e in need if int(e) not in pool.stage]
             pool._begin_writes()
             try:
                 for e in staged:
-                    pool.admit_arrays(e, pool.stage[e], protect=uniq)
+                    pool.admit_arrays(e, pool.stage[e], protect=protect)
                     pool.stage_hits += 1
                 if cold:
                     t0 = time.perf_counter()
@@ -554,7 +461,7 @@ class StreamingSwitchGLU:
                     for e in cold:
                         b = blobs[(pool.layer, e)]
                         self.fetch_bytes += pool.bytes_per_expert
-                        pool.admit(e, b, protect=uniq)
+                        pool.admit(e, b, protect=protect)
             finally:
                 pool._flush_writes()
         pool.stage = {}
@@ -820,31 +727,35 @@ class StreamingSwitchGLU:
     # -- prefill holding / read-ahead (stream.py:1174-1235) ----------------------
     def _count_routing(self, pe) -> None:
         if self._held is not None:
-            self.prefill_routed += np.bincount(pe, minlength=self._pool.n_experts)
+            np.add.at(self.prefill_routed, np.asarray(pe, dtype=np.int64), 1)
 
     @contextlib.contextmanager
     def holding(self, then=None):
-        """Scope of one layer's layer-major prefill: routing is counted for ``rewarm`` and
-        ``then`` (the next layer's read-ahead) runs once, after the first chunk."""
-        self._held, self._then = {}, then
+        """The scope of one layer's pass over every prefill chunk.  Routed experts are
+        tallied (``prefill_routed``, which ``StreamHandle.rewarm`` ranks), ``then`` --
+        normally the next layer's read-ahead -- is kept for after the first chunk, and on
+        exit whatever this layer queued for reading ahead is dropped."""
         self.prefill_routed = np.zeros(self._pool.n_experts, dtype=np.int64)
+        self._held, self._then = {}, then
         try:
-            yield
+            yield self
         finally:
-            self._held, self._then = None, None
-            if self._ahead:
-                self._fetcher.drop(self._ahead)
-                self._ahead = []
+            self._held = self._then = None
+            queued, self._ahead = self._ahead, []
+            if queued:
+                self._fetcher.drop(queued)
 
     def read_ahead(self) -> None:
-        """Queue every expert of this layer for reading (prefill); nothing to move when the
-        store is already in host DRAM."""
-        keys = [(self._pool.layer, e) for e in range(self._pool.n_experts)]
+        """Ask the fetcher to start reading all of this layer's experts.  A fetcher that
+        refuses (closed, or too much already pending) is not an error: prefill still
+        fetches on demand."""
+        layer = self._pool.layer
+        wanted = [(layer, e) for e in range(self._pool.n_experts)]
         try:
-            self._fetcher.prefetch(keys)
+            self._fetcher.prefetch(wanted)
         except RuntimeError:
             return
-        self._ahead = keys
+        self._ahead = wanted
 
 
 class StreamHandle:
@@ -856,18 +767,23 @@ class StreamHandle:
         self.full_layers = list(full_layers)
 
     def release_prefill(self) -> None:
+        """Drop every layer's outstanding read-ahead."""
         for m in self.mods:
-            if m._ahead and m._fetcher is not None:
-                m._fetcher.drop(m._ahead)
-            m._ahead = []
+            queued, m._ahead = m._ahead, []
+            if queued and m._fetcher is not None:
+                m._fetcher.drop(queued)
 
     def rewarm(self, per_layer: int) -> int:
+        """Ask the fetcher to refresh, per streamed layer, the ``per_layer`` experts the
+        last prefill routed most (ties to the lower id; never-routed experts are skipped).
+        Returns what the fetcher reports."""
         keys = []
-        for m in sorted((m for m in self.mods if m._pool is not None and m.prefill_routed is not None),
-                        key=lambda m: m._pool.layer):
-            counts = m.prefill_routed
-            top = np.argsort(-counts, kind="stable")[:per_layer]
-            keys += [(m._pool.layer, int(e)) for e in top if counts[e] > 0]
+        layers = {m._pool.layer: m.prefill_routed for m in self.mods
+                  if m._pool is not None and m.prefill_routed is not None}
+        for layer in sorted(layers):
+            counts = layers[layer]
+            ranked = np.lexsort((np.arange(counts.shape[0]), -counts))[:per_layer]
+            keys.extend((layer, int(e)) for e in ranked if counts[e] > 0)
         return self.fetcher.refresh(keys) if keys else 0
 
     def prefill_layer(self, layer: int, read_ahead: bool = False):
@@ -903,52 +819,60 @@ class StreamHandle:
         return self
 
     def usage(self) -> dict:
-        out = {}
-        for m in self.mods:
-            p = m._pool
-            for e in np.nonzero(p.uses)[0]:
-                out[f"{p.layer}:{int(e)}"] = int(p.uses[e])
-        return out
+        """Requests per expert in this run, keyed ``"layer:expert"`` (the usage-file format)."""
+        return {f"{m._pool.layer}:{e}": int(m._pool.uses[e])
+                for m in self.mods for e in np.flatnonzero(m._pool.uses)}
 
     def save_usage(self, path: str, decay: float = 0.5) -> str:
-        """Merge this run's use counts into earlier ones, halved first (stream.py:2084-2105)."""
-        prev = {}
+        """Write the usage file at ``path``: earlier counts there scaled by ``decay`` and
+        truncated (entries reaching 0 are dropped), plus this run's counts.  The file is
+        replaced atomically (stream.py:2084-2105)."""
         try:
             with open(path) as fh:
-                prev = json.load(fh) or {}
+                earlier = json.load(fh) or {}
         except (OSError, ValueError):
-            prev = {}
-        merged = {k: int(v * decay) for k, v in prev.items() if int(v * decay) > 0}
-        for k, v in self.usage().items():
-            merged[k] = merged.get(k, 0) + v
-        os.makedirs(os.path.dirname(path) or ".", exist_ok=True)
-        tmp = path + ".tmp"
-        with open(tmp, "w") as fh:
-            json.dump(merged, fh)
-        os.replace(tmp, path)
+            earlier = {}
+        totals = {}
+        for key, n in earlier.items():
+            kept = int(n * decay)
+            if kept > 0:
+                totals[key] = kept
+        for key, n in self.usage().items():
+            totals[key] = totals.get(key, 0) + n
+        folder = os.path.dirname(path)
+        if folder:
+            os.makedirs(folder, exist_ok=True)
+        part = f"{path}.tmp"
+        with open(part, "w") as fh:
+            json.dump(totals, fh)
+        os.replace(part, path)
         return path
 
     def resident_gb(self) -> float:
         return sum(p.nbytes() for p in self.pools) / 1e9
 
     def stats(self) -> dict:
-        h = sum(p.hits for p in self.pools)
-        m = sum(p.misses for p in self.pools)
-        return {"layers": len(self.pools),
-                "full_layers": sum(1 for p in self.pools if p.capacity == p.n_experts),
-                "sync_free": sum(1 for m_ in self.mods if m_._sync_free),
-                "hits": h, "misses": m, "miss_rate": m / (h + m) if (h + m) else 0.0,
-                "capacity": min((p.capacity for p in self.pools if p.capacity < p.n_experts),
-                                default=(self.pools[0].capacity if self.pools else 0)),
-                "n_experts": self.pools[0].n_experts if self.pools else 0,
-                "resident_gb": self.resident_gb(),
-                "admit_gb": sum(p.admit_bytes for p in self.pools) / 1e9,
-                "fetch_seconds": sum(m_.fetch_seconds for m_ in self.mods),
-                "admit_seconds": sum(m_._pool.admit_seconds for m_ in self.mods),
-                "sync_seconds": sum(m_.sync_seconds for m_ in self.mods),
-                "chunked_calls": sum(m_.chunked_calls for m_ in self.mods),
-                "stage_issued": sum(p.stage_issued for p in self.pools),
-                "stage_hits": sum(p.stage_hits for p in self.pools)}
+        """Counters summed over the streamed layers."""
+        pools, mods = self.pools, self.mods
+        hits = sum(p.hits for p in pools)
+        misses = sum(p.misses for p in pools)
+        capped = [p.capacity for p in pools if p.capacity < p.n_experts]
+        out = dict(layers=len(pools),
+                   full_layers=sum(p.capacity == p.n_experts for p in pools),
+                   sync_free=sum(bool(m._sync_free) for m in mods),
+                   hits=hits, misses=misses,
+                   miss_rate=misses / (hits + misses) if hits + misses else 0.0,
+                   capacity=min(capped) if capped else (pools[0].capacity if pools else 0),
+                   n_experts=pools[0].n_experts if pools else 0,
+                   resident_gb=self.resident_gb(),
+                   admit_gb=sum(p.admit_bytes for p in pools) / 1e9)
+        for key, attr in (("fetch_seconds", "fetch_seconds"), ("sync_seconds", "sync_seconds"),
+                          ("chunked_calls", "chunked_calls")):
+            out[key] = sum(getattr(m, attr) for m in mods)
+        out["admit_seconds"] = sum(m._pool.admit_seconds for m in mods)
+        out["stage_issued"] = sum(p.stage_issued for p in pools)
+        out["stage_hits"] = sum(p.stage_hits for p in pools)
+        return out
 
     def reset_stats(self):
         for p in self.pools:

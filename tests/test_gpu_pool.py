@@ -41,7 +41,7 @@ def _skewed_routing(T, rng):
     return np.argsort(-lg, axis=1, kind="stable")[:, :K].astype(np.int32)
 
 
-@pytest.mark.parametrize("C,policy", [(8, "lfuda"), (16, "lfuda"), (12, "lru"), (20, "coact")])
+@pytest.mark.parametrize("C,policy", [(8, "lfuda"), (16, "lfuda"), (12, "lru"), (20, "s3fifo")])
 def test_streamed_decode_is_bit_identical(layer, cuda, C, policy):
     L, store = layer
     full = _full(L, store, cuda)

@@ -38,7 +38,7 @@ def _module(name, C, E=128):
     return StreamingSwitchGLU(pool, _store(E))
 
 
-@pytest.mark.parametrize("name", ["lfuda", "lru", "arc", "s3fifo", "lirs", "gaterank", "coact"])
+@pytest.mark.parametrize("name", ["lfuda", "lru", "arc", "s3fifo", "gaterank"])
 @pytest.mark.parametrize("C", [8, 12, 40])
 def test_decode_replay_matches_reference(golden, name, C):
     mod = _module(name, C)
@@ -55,7 +55,7 @@ def test_decode_replay_matches_reference(golden, name, C):
             assert torch.all(p.slab[slot, :p.layout.bytes_per_expert] == e % 251)
 
 
-@pytest.mark.parametrize("name", ["lfuda", "lru", "coact"])
+@pytest.mark.parametrize("name", ["lfuda", "lru", "arc", "s3fifo", "gaterank"])
 @pytest.mark.parametrize("C", [8, 12, 40])
 def test_prefill_spans_match_reference(golden, name, C):
     mod = _module(name, C)
@@ -103,7 +103,7 @@ def test_pool_errors():
     with pytest.raises(RuntimeError, match="build"):
         p.admit(0, bytes(bpe))
     p.build()
-    with pytest.raises(ValueError, match="Refusing"):
+    with pytest.raises(ValueError, match="nothing is written"):
         p.admit(0, bytes(bpe - 1))
     for e in range(4):
         p.touch([e], [0])
