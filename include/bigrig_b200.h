@@ -216,10 +216,17 @@ BIGRIG_API int bigrig_copy_regions(void* const* dst, const void* const* src, con
  * file-scope device array of BIGRIG_NOALLOC_SCRATCH_BYTES (4 MiB) that every GPU that
  * loads the library holds until the process exits.  Calls needing more scratch than that
  * (bigrig_moe_workspace_bytes) return BIGRIG_ERR_WORKSPACE.  The first call on a device
- * resolves the array's address with cudaGetSymbolAddress; make it before any stream
- * capture.  Every call shares the one array, so calls that overlap on the GPU (different
- * streams, or different host threads) race: serialise them.  The call itself allocates
- * nothing (no cudaMalloc/cudaFree, no library allocator). */
+ * resolves the array's address with cudaGetSymbolAddress and keeps it for that device;
+ * under CUDA's lazy module loading that first call may also load the module and commit
+ * the 4 MiB, so make it (or a warm-up call) at initialisation, before any stream capture
+ * and before a fixed memory budget is carved.  The kept address does not survive a
+ * cudaDeviceReset: after one, reload the library.  Every call shares the one array, so
+ * calls that overlap on the GPU (different streams, or different host threads) race:
+ * serialise them.  Device-side routing errors (an expert id >= n_experts, a routed
+ * expert without a slot) are counted in the array's error word, which each call clears
+ * and nothing reads back: this entry does not report them; use bigrig_switch_glu with a
+ * workspace and bigrig_workspace_errors where they must be seen.  The call itself
+ * allocates nothing (no cudaMalloc/cudaFree, no library allocator). */
 #define BIGRIG_NOALLOC_SCRATCH_BYTES (4u << 20)
 BIGRIG_API int bigrig_switch_glu_noalloc(const void* x, const int32_t* indices, int T, int k,
                                          int n_experts, const int32_t* g2s, const void* slab,

@@ -65,7 +65,7 @@ def test_gemm_agrees_with_gemv(cuda):
         yv = ops.switch_glu(xt, it, L.slab, L.layout, E).clone()
     finally:
         _lib.set_path(prev)
-    assert_close(to_f32(yg), to_f32(yv), rtol=2e-2, atol=4e-3)
+    assert_close(to_f32(yg), to_f32(yv))
 
 
 def test_gemm_batch_invariance(cuda, path):

@@ -41,6 +41,28 @@ def test_noalloc_matches_workspace_entry_on_consecutive_calls(cuda):
         assert_close(to_f32(got), to_f32(want))
 
 
+def test_noalloc_takes_the_grouped_gemm_inside_its_scratch(cuda):
+    """256 routed pairs: beyond the GEMV chain's 32, so the tcgen05 grouped GEMM runs on
+    token rows carved from the static array; two calls in a row."""
+    rng = np.random.default_rng(78)
+    H, I, E, k, T = 1024, 512, 16, 4, 64
+    L = Layer(H, I, E, 4, "float16", seed=78, slot_order=rng.permutation(E))
+    assert ops.workspace_bytes(T, k, E, L.layout) <= _lib.NOALLOC_SCRATCH_BYTES
+    prev = _lib.set_path("gemm")
+    try:
+        for _ in range(2):
+            x = bf16_tensor(affine.bf16_round(rng.standard_normal((T, H)).astype(np.float32)))
+            idx = torch.from_numpy(random_routing(T, k, E, rng)).to(cuda)
+            n0 = _lib.launch_counts()["gemm_gate_up"]
+            got = ops.switch_glu_noalloc(x, idx, L.slab, L.layout, E, g2s=L.g2s)
+            assert _lib.launch_counts()["gemm_gate_up"] == n0 + 1
+            want = ops.switch_glu(x, idx, L.slab, L.layout, E, g2s=L.g2s)
+            torch.cuda.synchronize()
+            assert_close(to_f32(got), to_f32(want))
+    finally:
+        _lib.set_path(prev)
+
+
 def test_noalloc_rejects_calls_beyond_its_scratch(cuda):
     H, I, E, k = 1024, 512, 16, 4
     L = Layer(H, I, E, 4, "float16", seed=1)
