@@ -180,6 +180,275 @@ def algorithmic_layer_bytes(T: int, distinct: int) -> int:
     return distinct * bpe + c["experts"] * c["hidden"] * 2 + T * c["hidden"] * 2 * 2
 
 
+# ------------------------------------------------------------------ the other named shapes
+# BASELINE configs 3-5, each measured at N=1 as an extra key of the line (never the headline).
+SHAPES = {
+    "c3": {"name": "qwen3-30b-a3b-shaped", "layers": 48, "hidden": 2048, "inter": 768,
+           "experts": 128, "top_k": 8, "bits": 4, "scale_dtype": "bfloat16", "family": "qwen3",
+           "prefill": 4096, "decode_batches": (1, 8)},
+    "c4": {"name": "gpt-oss-120b-shaped", "layers": 36, "hidden": 2880, "inter": 2880,
+           "experts": 128, "top_k": 4, "bits": 4, "scale_dtype": "bfloat16",
+           "family": "gpt_oss", "prefill": 8 * 2048, "decode_batches": (64,)},
+    "c5": {"name": "mixtral-8x7b-shaped", "layers": 32, "hidden": 4096, "inter": 14336,
+           "experts": 8, "top_k": 2, "bits": 8, "scale_dtype": "float16", "family": "mixtral",
+           "prefill": 8192, "capacity": 2},
+}
+
+
+def _expert_bank(dev, sh: dict, seed: int):
+    """One layer's worth of distinct experts (N(0, 0.02) quantised on the GPU), slab rows."""
+    from bigrig_b200.block import random_expert_bytes
+    from bigrig_b200.formats import layout_from_spec, make_spec
+    spec = make_spec(sh["hidden"], sh["inter"], sh["bits"], 64, sh["scale_dtype"])
+    L = layout_from_spec(spec, {"bits": sh["bits"], "group_size": 64, "mode": "affine"})
+    sd = {"float16": torch.float16, "bfloat16": torch.bfloat16}[sh["scale_dtype"]]
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    bank = torch.zeros(sh["experts"], L.slot_stride, dtype=torch.uint8, device=dev)
+    for e in range(sh["experts"]):
+        bank[e, :L.bytes_per_expert] = random_expert_bytes(sh["hidden"], sh["inter"], sh["bits"],
+                                                           64, sd, g, dev)
+    return bank, spec, L
+
+
+def _layer_perm(E: int, li: int) -> torch.Tensor:
+    """Which bank expert plays expert e of layer li: a fixed per-layer permutation."""
+    return torch.from_numpy(np.random.default_rng(10_000 + li).permutation(E))
+
+
+def _resident_blocks(dev, sh: dict, seed: int):
+    """Every layer's experts resident in its own HBM slab (the bank, permuted per layer)."""
+    from bigrig_b200.block import make_blocks
+    from bigrig_b200.stream import ExpertPool, StreamingSwitchGLU
+    bank, spec, L = _expert_bank(dev, sh, seed)
+    blocks = make_blocks(sh["layers"], sh["hidden"], sh["inter"], sh["experts"], sh["top_k"],
+                         sh["family"], sh["bits"], 64, sh["scale_dtype"], True, seed=seed + 1,
+                         device=dev)
+    for b in blocks:
+        pool = ExpertPool(b.layer, None, sh["experts"], sh["experts"], spec, quant=b.quant,
+                          device=dev)
+        pool.adopt(bank.index_select(0, _layer_perm(sh["experts"], b.layer).to(dev)))
+        b.switch = StreamingSwitchGLU(pool, None)
+        b.switch.refresh()
+        pool.g2s_device()
+        pool.settle()
+    del bank
+    return blocks, spec, L
+
+
+def _decode_bytes(blocks, xs, bpe: int) -> float:
+    """Mean algorithmic HBM bytes of one MoE layer over the steps' inputs: distinct routed
+    experts x bytes per expert + router weights + tokens in and out, with every layer's
+    routing recomputed on the stack's own hidden states."""
+    tot, n = 0.0, 0
+    for x in xs:
+        h = x
+        for b in blocks:
+            idx, _ = b.route(h)
+            U = int(torch.unique(idx).numel())
+            tot += U * bpe + b.n_experts * b.hidden * 2 + 2 * h.shape[0] * b.hidden * 2
+            n += 1
+            h = b(h, residual=h)
+    return tot / max(1, n)
+
+
+def _graph_decode(dev, blocks, B: int, K: int, W: int, seed: int, bpe: int, peak: float) -> dict:
+    """B tokens through the resident stack per step, one CUDA graph per step; K timed steps
+    on fresh random inputs.  tok/s and the MoE layers' HBM roofline."""
+    from bigrig_b200 import ops
+    H = blocks[0].hidden
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    xs = torch.randn(W + K, B, H, generator=g, device=dev).to(torch.bfloat16)
+    ws = ops.default_workspace(dev)
+    ws.reserve(ops.workspace_bytes(B, blocks[0].top_k, blocks[0].n_experts,
+                                   blocks[0].switch._pool.layout))
+    xin = xs[0].clone()
+    for _ in range(2):
+        stack_step(blocks, xin)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream(device=dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(st):
+        stack_step(blocks, xin)
+    torch.cuda.current_stream(dev).wait_stream(st)
+    with torch.cuda.graph(graph):
+        stack_step(blocks, xin)
+    for i in range(W):
+        xin.copy_(xs[i])
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        xin.copy_(xs[W + i])
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / K
+    del graph
+    layer_bytes = _decode_bytes(blocks, [xs[W + i] for i in range(min(K, 4))], bpe)
+    layer_ms = ms / len(blocks)
+    gbs = layer_bytes / (layer_ms / 1e3) / 1e9
+    return {"batch": B, "tok_s": B / (ms / 1e3), "ms_per_step": ms, "steps": K,
+            "roofline": {"kernel": "decode_layer_kernel" if B == 1 else "moe layer (GEMV chain / "
+                         "grouped GEMM)", "bound": "hbm", "achieved": gbs, "peak": peak,
+                         "unit": "GB/s", "frac": gbs / peak,
+                         "bytes_per_layer": layer_bytes, "ms_per_layer": layer_ms,
+                         "note": "algorithmic layer bytes (distinct routed experts x bytes per "
+                                 "expert + router + tokens) over graph time per layer"}}
+
+
+def _prefill_gemm(dev, blocks, T: int, seed: int, peak: float, peak_kind: str, layer_scope=None,
+                  warm: bool = True) -> dict:
+    """A T-token prompt through the stack layer-major, token-wise (each layer once over all
+    T tokens); the grouped GEMM's launches timed with CUDA events."""
+    from bigrig_b200 import _lib, layered
+    H, k, I = blocks[0].hidden, blocks[0].top_k, blocks[0].inter
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    prompt = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    layers = [(lambda h, b=b: b(h, residual=h)) for b in blocks]
+    if warm:
+        layered.prefill(layers, [prompt], token_wise=True, layer_scope=layer_scope)
+    torch.cuda.synchronize(dev)
+    _lib.timing_enable(["gemm_gate_up", "gemm_down"])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    layered.prefill(layers, [prompt], token_wise=True, layer_scope=layer_scope)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    _lib.timing_enable([])
+    gu, _ = _lib.timing_read("gemm_gate_up")
+    dn, _ = _lib.timing_read("gemm_down")
+    ms = e0.elapsed_time(e1)
+    flops = 6.0 * T * k * H * I * len(blocks)
+    gemm_s = (gu + dn) / 1e3
+    ach = flops / gemm_s / 1e12 if gemm_s > 0 else None
+    return {"tokens": T, "tok_s": T / (ms / 1e3), "ms": ms,
+            "roofline": {"kernel": "grouped_gemm_kernel", "bound": "tensor", "achieved": ach,
+                         "peak": peak, "peak_kind": peak_kind, "unit": "TFLOP/s",
+                         "frac": ach / peak if ach else None, "flops": flops,
+                         "gemm_ms": gemm_s * 1e3, "gate_up_ms": gu, "down_ms": dn}}
+
+
+def _h2d_gbs(dev) -> float:
+    """Pinned host -> device copy bandwidth, GB/s (1 GiB, best of 3)."""
+    src = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    best = 0.0
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dst.copy_(src, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        best = max(best, (1 << 30) / (e0.elapsed_time(e1) / 1e3) / 1e9)
+    del src, dst
+    return best
+
+
+def bench_shape(dev, key: str, W: int, hbm_peak: float, hbm_kind: str, bf16_peak: float,
+                bf16_kind: str) -> dict:
+    """The BASELINE config ``key`` at N=1: resident decode and prefill (c3, c4), or the
+    host-streamed pool (c5)."""
+    from bigrig_b200.formats import bytes_per_expert
+    sh = SHAPES[key]
+    out = {"workload": sh["name"], **{k: sh[k] for k in ("layers", "hidden", "inter", "experts",
+                                                         "top_k", "bits", "scale_dtype")}}
+    t0 = time.perf_counter()
+    if key in ("c3", "c4"):
+        blocks, spec, L = _resident_blocks(dev, sh, seed=31 + len(key))
+        bpe = bytes_per_expert(spec)
+        out["resident_gb"] = len(blocks) * sh["experts"] * L.slot_stride / 1e9
+        out["data"] = ("one layer's experts N(0,0.02) quantised on the GPU, each layer holding its "
+                       "own HBM copy in a per-layer permutation; router N(0,0.02) + bias N(0,1) "
+                       "per layer; random bf16 N(0,1) tokens")
+        out["decode"] = [_graph_decode(dev, blocks, B, 20, W, 500 + B, bpe, hbm_peak)
+                         for B in sh["decode_batches"]]
+        for d in out["decode"]:
+            d["roofline"]["peak_kind"] = hbm_kind
+        out["prefill"] = _prefill_gemm(dev, blocks, sh["prefill"], 77, bf16_peak, bf16_kind)
+        del blocks
+    else:
+        out.update(_bench_streamed(dev, sh, W, hbm_peak, bf16_peak, bf16_kind))
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    out["setup_and_run_s"] = time.perf_counter() - t0
+    return out
+
+
+def _bench_streamed(dev, sh: dict, W: int, hbm_peak: float, bf16_peak: float, bf16_kind: str) -> dict:
+    """Config 5: every layer's pool holds ``capacity`` experts in HBM, the rest are copied from
+    pinned host DRAM on a side stream (staged ahead from the next layer's router when it
+    can).  Prefill token-wise, then a decode sample; copy bandwidth against pinned H2D."""
+    from bigrig_b200.block import make_blocks
+    from bigrig_b200.fetch import HostExpertStore
+    from bigrig_b200.stream import attach
+    bank, spec, L = _expert_bank(dev, sh, seed=51)
+    E, bpe = sh["experts"], L.bytes_per_expert
+    base = bank[:, :bpe].cpu()
+    del bank
+    torch.cuda.empty_cache()
+    # the experts live once per permutation in pinned host DRAM; all layers share two
+    # permutations (the copies over PCIe are real, the host bytes are reused)
+    perms = [base.index_select(0, _layer_perm(E, j)).pin_memory() for j in range(2)]
+    del base
+    store = HostExpertStore({}, pin=False)
+    store.pinned = True
+    store.layers = {li: perms[li % 2] for li in range(sh["layers"])}
+    blocks = make_blocks(sh["layers"], sh["hidden"], sh["inter"], E, sh["top_k"], sh["family"],
+                         sh["bits"], 64, sh["scale_dtype"], True, seed=52, device=dev)
+    handle = attach(blocks, store, sh["capacity"], policy="lfuda", warm="auto", device=dev)
+    h2d = _h2d_gbs(dev)
+    res = {"capacity": sh["capacity"], "policy": "lfuda", "h2d_gbs_measured": h2d,
+           "data": "8 experts N(0,0.02) quantised to 8-bit on the GPU, held once in pinned host "
+                   "DRAM in two per-layer permutations that all 32 layers share (the copies "
+                   "over PCIe are real); router N(0,0.02) + bias N(0,1) per layer"}
+    # prefill: layer-major, token-wise: each layer's experts cross PCIe once per span
+    handle.reset_stats()
+    pf = _prefill_gemm(dev, blocks, sh["prefill"], 78, bf16_peak, bf16_kind,
+                       layer_scope=handle.prefill_layer, warm=False)
+    stp = handle.stats()
+    pf["admit_gb"] = stp["admit_gb"]
+    pf["pcie_gbs"] = stp["admit_gb"] / (pf["ms"] / 1e3)
+    pf["pcie_frac"] = pf["pcie_gbs"] / h2d
+    res["prefill"] = pf
+    # decode sample: B=1 tokens through all layers, the routing read back per layer
+    g = torch.Generator(device=dev)
+    g.manual_seed(79)
+    n_dec = 12
+    xs = torch.randn(W + n_dec, 1, sh["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    for i in range(W):
+        stack_step(blocks, xs[i])
+    handle.reset_stats()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(n_dec):
+        stack_step(blocks, xs[W + i])
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    st = handle.stats()
+    res["decode"] = {"batch": 1, "tokens": n_dec, "tok_s": n_dec / (ms / 1e3),
+                     "ms_per_token": ms / n_dec, "miss_rate": st["miss_rate"],
+                     "admit_gb": st["admit_gb"], "pcie_gbs": st["admit_gb"] / (ms / 1e3),
+                     "pcie_frac": st["admit_gb"] / (ms / 1e3) / h2d,
+                     "stage_issued": st["stage_issued"], "stage_hits": st["stage_hits"],
+                     "roofline": {"bound": "pcie", "achieved": st["admit_gb"] / (ms / 1e3),
+                                  "peak": h2d, "unit": "GB/s",
+                                  "frac": st["admit_gb"] / (ms / 1e3) / h2d,
+                                  "note": "missed-expert bytes copied from pinned host over the "
+                                          "decode time, against the measured pinned H2D rate"},
+                     "note": f"{n_dec} decode tokens (a sample of the config's 512) after {W} "
+                             f"warm-up tokens"}
+    handle.close()
+    del blocks, store, perms
+    return res
+
+
 # ------------------------------------------------------------------ CPU restatement
 def cpu_decode_tokens(store, blocks_host, n_tokens: int, n_layers: int, threads: int, seed: int,
                       first_layer: int = 0):
@@ -258,6 +527,9 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="decode only (for profiling)")
+    ap.add_argument("--configs", default="c3,c4,c5",
+                    help="other BASELINE shapes measured at N=1 as extra keys (comma list of "
+                         "c3, c4, c5, or 'none')")
     ap.add_argument("--layers", type=int, default=None,
                     help="MoE layers of the stack (default: the config's 16; fewer only to keep "
                          "a profiler capture small -- such a run is not a bench line)")
@@ -498,6 +770,13 @@ def main() -> None:
         extras["resident_prefill_tok_s"] = world * c["prompt"] / (rp_ms / 1e3)
         rp_tw, extras["prefill_gemm_token_wise"] = resident_prefill(True)
         extras["resident_prefill_token_wise_tok_s"] = world * c["prompt"] / (rp_tw / 1e3)
+
+    # ---- the other named shapes, one GPU
+    if not args.no_extras and world == 1 and args.configs != "none":
+        hbm_peak, _, hbm_kind = _peaks()
+        burst = _peaks()[1]
+        for key in [k.strip() for k in args.configs.split(",") if k.strip()]:
+            extras[key] = bench_shape(dev, key, W, hbm_peak, hbm_kind, burst, "measured burst")
 
     # ---- CPU restatement on rank 0 at N=1 (bounded sample)
     cpu = None

@@ -407,6 +407,37 @@ int bigrig_moe_layer(const void* x, const void* gate_w, const float* gate_b, int
   return launch_combine(ws.y, sc, T, k, layout->hidden, out, s, residual);
 }
 
+int bigrig_moe_layer_routed(const void* x, const int32_t* indices, const float* scores, int T,
+                            int E, int k, const int32_t* g2s, const void* slab,
+                            const bigrig_expert_layout* layout, const void* residual, void* out,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_layout(layout)) return rc;
+  if (int rc = check_route(T, k, E)) return rc;
+  if (T == 0) return BIGRIG_OK;
+  if (!x || !indices || !scores || !slab || !out || !workspace)
+    return set_error(BIGRIG_ERR_INVALID, "moe_layer_routed: NULL pointer");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(slab) % 16)
+    return set_error(BIGRIG_ERR_INVALID, "moe_layer_routed: x and slab must be 16-byte aligned");
+  if (layout->hidden % 8)
+    return set_error(BIGRIG_ERR_INVALID, "moe_layer_routed: hidden must be a multiple of 8");
+  const size_t need = carve(nullptr, T, k, E, *layout, nullptr);
+  if (workspace_bytes < need)
+    return set_error(BIGRIG_ERR_WORKSPACE, "moe_layer_routed: workspace %zu bytes < %zu needed",
+                     workspace_bytes, need);
+  Workspace ws;
+  carve(workspace, T, k, E, *layout, &ws);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int path = g_path.load();
+  if (T == 1 && (path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_GEMV) &&
+      decode_layer_fits(*layout, k, E))
+    return launch_decode_layer(x, nullptr, nullptr, E, k, BIGRIG_SOFTMAX_TOPK, 0, g2s, slab,
+                               *layout, residual, out, const_cast<int32_t*>(indices),
+                               const_cast<float*>(scores), ws.h, ws.tagged, ws.arrivals, ws.err, s,
+                               indices, scores);
+  if (int rc = run_switch_glu(x, indices, T, k, E, g2s, slab, *layout, ws.y, ws, s)) return rc;
+  return launch_combine(ws.y, scores, T, k, layout->hidden, out, s, residual);
+}
+
 int bigrig_set_path(int mode, int gemm_min_rows) {
   if (mode < BIGRIG_PATH_AUTO || mode > BIGRIG_PATH_CHAIN || gemm_min_rows < 1)
     return set_error(BIGRIG_ERR_INVALID, "set_path: mode=%d gemm_min_rows=%d", mode, gemm_min_rows);

@@ -75,6 +75,8 @@ struct DecodeLayerArgs {
   uint16_t* out;              // [H]
   int32_t* idx_out;           // [k]
   float* sc_out;              // [k]
+  const int32_t* pre_idx;     // [k] routing computed before the launch, or null: route here
+  const float* pre_sc;        // [k] its scores
   uint16_t* h;                // [k, I] scratch, rank-ordered rows
   unsigned long long* tagged; // [E] logit bits | tag << 32
   unsigned long long* arrivals;  // grid-barrier arrivals over all launches
@@ -424,7 +426,8 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
   DL_STAMP(0);
 
   // ---------------------------------------------------------------- start
-  const int n_mine = max(0, min(kDlRouterPerCta, E - cta * kDlRouterPerCta));
+  const bool routed = a.pre_idx != nullptr;      // routing given: no logits, no ranking
+  const int n_mine = routed ? 0 : max(0, min(kDlRouterPerCta, E - cta * kDlRouterPerCta));
   if (threadIdx.x == 0) {
     for (int i = 0; i < nst; ++i) {
       bar_init(full + i, 1);
@@ -493,7 +496,13 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
   // the producer collects the E tagged logits; every consumer thread then ranks (logit
   // descending, expert id ascending -- topk_warp's order) a share of them: 8 threads per
   // candidate, each counting the candidates above it among E/8 others
-  if (producer) {
+  if (routed) {
+    if (threadIdx.x < k) {
+      const int e = a.pre_idx[threadIdx.x];
+      s_idx[threadIdx.x] = (e >= 0 && e < E) ? e : -1;
+    }
+    if (!producer) build_bperm<BITS>(xraw, H, 1, xperm, 0, xgs, threadIdx.x, CT);
+  } else if (producer) {
     uint32_t need = 0;
     for (int e = lane, i = 0; e < E; e += 32, ++i) need |= 1u << i;
     for (uint32_t n = 0; need; ++n) {
@@ -521,7 +530,7 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
     build_bperm<BITS>(xraw, H, 1, xperm, 0, xgs, threadIdx.x, CT);
   }
   __syncthreads();                               // logits in s_lg
-  if (!producer) {
+  if (!producer && !routed) {
     const int per_cand = (E + 7) / 8;
     for (int c0 = 0; c0 < E; c0 += CT / 8) {
       const int c = c0 + (threadIdx.x >> 3), part = threadIdx.x & 7;
@@ -628,8 +637,20 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
     };
     for (int q = 0; q < first; ++q) issue(q);
     DL_STAMP(2);
-    // scores: topk_warp's formulas and reductions over the same values in the same lanes
-    {
+    // scores: given, or topk_warp's formulas and reductions over the same values in the
+    // same lanes
+    if (routed) {
+      if (lane < k) {
+        s_sc[lane] = a.pre_sc[lane];
+        if (cta == 0) {
+          if (a.idx_out != a.pre_idx) a.idx_out[lane] = s_idx[lane];
+          if (a.sc_out != a.pre_sc) a.sc_out[lane] = s_sc[lane];
+          if (s_slot[lane] < 0) atomicAdd(a.err, 1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) bar_arrive(bar_s);
+    } else {
       const int per = (E + 31) / 32;
       float mx = -INFINITY;
       for (int i = 0; i < per; ++i)
@@ -1056,7 +1077,7 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
                         int mode, int norm, const int32_t* g2s, const void* slab,
                         const bigrig_expert_layout& L, const void* residual, void* out,
                         int32_t* idx_out, float* sc_out, void* h, void* tagged, void* arrivals,
-                        int32_t* err, cudaStream_t s) {
+                        int32_t* err, cudaStream_t s, const int32_t* pre_idx, const float* pre_sc) {
   const int G = sm_count_dl();
   DlPlan p;
   if (!decode_layer_plan(L, k, E, G, &p))
@@ -1072,6 +1093,8 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
   a.out = static_cast<uint16_t*>(out);
   a.idx_out = idx_out;
   a.sc_out = sc_out;
+  a.pre_idx = pre_idx;
+  a.pre_sc = pre_sc;
   a.h = static_cast<uint16_t*>(h);
   a.tagged = static_cast<unsigned long long*>(tagged);
   a.arrivals = static_cast<unsigned long long*>(arrivals);

@@ -91,7 +91,8 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
                         int mode, int norm, const int32_t* g2s, const void* slab,
                         const bigrig_expert_layout& L, const void* residual, void* out,
                         int32_t* idx_out, float* sc_out, void* h, void* tagged, void* arrivals,
-                        int32_t* err, cudaStream_t s);
+                        int32_t* err, cudaStream_t s, const int32_t* pre_idx = nullptr,
+                        const float* pre_sc = nullptr);
 int launch_combine(const void* y, const float* scores, int T, int k, int H, void* out,
                    cudaStream_t s, const void* residual = nullptr);
 

@@ -310,6 +310,36 @@ def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, gate_b: torch.Tensor | None
     return out, indices, scores
 
 
+def moe_layer_routed(x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor,
+                     slab: torch.Tensor, layout: Layout, n_experts: int,
+                     g2s: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+                     out: torch.Tensor | None = None,
+                     workspace: Workspace | None = None) -> torch.Tensor:
+    """The MoE block from routing already computed: x bf16 [T, H], indices int32 [T, k] and
+    scores fp32 [T, k] on the device -> out bf16 [T, H] = residual + sum_j score * y."""
+    _require_cuda("x", x, torch.bfloat16)
+    _require_cuda("indices", indices, torch.int32)
+    _require_cuda("scores", scores, torch.float32)
+    _require_cuda("slab", slab, torch.uint8)
+    if g2s is not None:
+        _require_cuda("g2s", g2s, torch.int32)
+    if residual is not None:
+        _require_cuda("residual", residual, torch.bfloat16)
+    T, k = indices.shape
+    if tuple(scores.shape) != (T, k):
+        raise ValueError(f"scores must be [{T}, {k}], got {tuple(scores.shape)}")
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty(T, layout.hidden, dtype=torch.bfloat16, device=x.device)
+    ws = workspace or default_workspace(x.device)
+    buf = ws.reserve(workspace_bytes(T, k, n_experts, layout))
+    _lib.check(_lib.load().bigrig_moe_layer_routed(
+        _vp(x), _vp(indices), _vp(scores), T, n_experts, k, _vp(g2s), _vp(slab),
+        ctypes.byref(c_layout(layout)), _vp(residual), _vp(out), _vp(buf), buf.numel(),
+        _stream(x)), "moe_layer_routed")
+    return out
+
+
 def switch_glu_noalloc(x: torch.Tensor, indices: torch.Tensor, slab: torch.Tensor, layout: Layout,
                        n_experts: int, g2s: torch.Tensor | None = None,
                        out: torch.Tensor | None = None) -> torch.Tensor:

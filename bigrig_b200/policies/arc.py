@@ -15,12 +15,11 @@ evicted from T1 and T2).  ``p`` is T1's target length, between 0 and the capacit
 * after admissions and evictions the ghosts are trimmed, oldest first: B1 while
   |T1| + |B1| > c, then B2 (or B1 when B2 is empty) while all four exceed 2c.
 
-State: per expert a list code and the clock value at which it entered that list;
-a list's oldest entry is its member with the smallest entry clock.
+State: per expert a list code and the clock value at which it entered that list,
+plus each list's member set; a list's oldest entry is its member with the smallest
+entry clock.
 """
 from __future__ import annotations
-
-import numpy as np
 
 from ..pool import Policy
 from ._columns import Columns, first_by
@@ -36,29 +35,30 @@ class ARC(Policy):
         self.c = capacity
         self.p = 0.0
         self.clock = 0
-        self.size = [0, 0, 0, 0, 0]          # entries per list code
-        self.col = Columns(n_experts, where=(np.int8, OUT), entered=(np.int64, 0))
+        self.members = [set() for _ in range(5)]     # per list code (OUT unused)
+        self.col = Columns(n_experts, where=OUT, entered=0)
 
     def _put(self, e: int, lst: int) -> None:
         """Move e to the tail of ``lst`` (OUT removes it from every list)."""
         c = self.col
-        self.size[int(c.where[e])] -= 1
-        self.size[lst] += 1
+        self.members[c.where[e]].discard(e)
+        if lst != OUT:
+            self.members[lst].add(e)
         c.where[e] = lst
         self.clock += 1
         c.entered[e] = self.clock
 
     def _oldest(self, lst: int) -> int:
-        return first_by(self.col.where == lst, self.col.entered)
+        return first_by(self.members[lst], self.col.entered)
 
     def _trim_ghosts(self) -> None:
-        s = self.size
-        while s[B1] and s[T1] + s[B1] > self.c:
+        t1, t2, b1, b2 = (self.members[i] for i in (T1, T2, B1, B2))
+        while b1 and len(t1) + len(b1) > self.c:
             self._put(self._oldest(B1), OUT)
-        while s[T1] + s[T2] + s[B1] + s[B2] > 2 * self.c:
-            if s[B2]:
+        while len(t1) + len(t2) + len(b1) + len(b2) > 2 * self.c:
+            if b2:
                 self._put(self._oldest(B2), OUT)
-            elif s[B1]:
+            elif b1:
                 self._put(self._oldest(B1), OUT)
             else:
                 break
@@ -66,13 +66,13 @@ class ARC(Policy):
     def admit(self, e, rank=0):
         e = int(e)
         self.col.fit(e)
-        w = int(self.col.where[e])
-        s = self.size
+        w = self.col.where[e]
+        n_b1, n_b2 = len(self.members[B1]), len(self.members[B2])
         if w == B1:
-            self.p = min(float(self.c), self.p + max(1.0, s[B2] / max(1, s[B1])))
+            self.p = min(float(self.c), self.p + max(1.0, n_b2 / max(1, n_b1)))
             self._put(e, T2)
         elif w == B2:
-            self.p = max(0.0, self.p - max(1.0, s[B1] / max(1, s[B2])))
+            self.p = max(0.0, self.p - max(1.0, n_b1 / max(1, n_b2)))
             self._put(e, T2)
         else:
             self._put(e, T1)
@@ -84,17 +84,17 @@ class ARC(Policy):
         self._put(e, T2)
 
     def victim(self):
-        s = self.size
-        if s[T1] and (s[T1] > self.p or not s[T2]):
+        t1, t2 = self.members[T1], self.members[T2]
+        if t1 and (len(t1) > self.p or not t2):
             return self._oldest(T1)
-        if s[T2]:
+        if t2:
             return self._oldest(T2)
         return -1
 
     def evicted(self, e):
         e = int(e)
         self.col.fit(e)
-        w = int(self.col.where[e])
+        w = self.col.where[e]
         if w == T1:
             self._put(e, B1)
         elif w == T2:

@@ -11,12 +11,10 @@ forgotten.  Rank weights ``w``:
 * ``inv``: 1 / (1 + r);
 * ``geom``: ``param`` ** r.
 
-State: a priority column and a tracked flag per expert; the victim is a masked
-argmin over the priority column.
+State: a priority column and the set of tracked experts; the victim is the
+tracked expert of smallest priority.
 """
 from __future__ import annotations
-
-import numpy as np
 
 from ..pool import Policy
 from ._columns import Columns, first_by
@@ -47,17 +45,18 @@ class GateRank(Policy):
         self.monotone = bool(monotone)
         self.weight = rank_weight(shape, param)
         self.clock = 0
-        self.col = Columns(n_experts, prio=(np.float64, 0.0), tracked=(np.bool_, False))
+        self.col = Columns(n_experts, prio=0.0)
+        self.tracked: set = set()
 
     def _use(self, e: int, rank: int) -> None:
         c = self.col
         c.fit(e)
         self.clock += 1
         p = self.clock + self.boost * self.weight(rank)
-        if self.monotone and c.tracked[e] and float(c.prio[e]) > p:
-            p = float(c.prio[e])
+        if self.monotone and e in self.tracked and c.prio[e] > p:
+            p = c.prio[e]
         c.prio[e] = p
-        c.tracked[e] = True
+        self.tracked.add(e)
 
     def admit(self, e, rank=0):
         self._use(int(e), rank)
@@ -66,12 +65,10 @@ class GateRank(Policy):
         self._use(int(e), rank)
 
     def victim(self):
-        return first_by(self.col.tracked, self.col.prio)
+        return first_by(self.tracked, self.col.prio)
 
     def evicted(self, e):
-        e = int(e)
-        if e < self.col.tracked.shape[0]:
-            self.col.tracked[e] = False
+        self.tracked.discard(int(e))
 
 
 def make(boost: float = 16.0, shape: str = "linear", param: float = 8, monotone: bool = True):

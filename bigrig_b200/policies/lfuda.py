@@ -12,14 +12,12 @@ Decision rule (bigrig_engine/policies/lfuda.py:67-173, defaults ``rank_weight=0`
   keeps the victim's frequency scaled by ``ghost_decay`` (``keep_ghost``) or
   forgets it.
 
-State: four per-expert columns (frequency, priority, use clock, held flag) and
-the scalar age.  Priorities and frequencies are float64 and updated with the
+State: per-expert columns (frequency, priority, use clock), the set of held
+experts and the scalar age.  Priorities and frequencies are float64 and updated with the
 same operations in the same order as the rule above states, so the victims, and
 the miss counts on a replayed trace, are the reference's.
 """
 from __future__ import annotations
-
-import numpy as np
 
 from ..pool import Policy
 from ._columns import Columns, first_by
@@ -37,9 +35,8 @@ class LFUDA(Policy):
         self.ghost_decay = float(ghost_decay)
         self.age = 0.0
         self.clock = 0
-        self.col = Columns(n_experts, freq=(np.float64, 0.0), prio=(np.float64, 0.0),
-                           used_at=(np.int64, 0), held=(np.bool_, False),
-                           has_prio=(np.bool_, False))
+        self.col = Columns(n_experts, freq=0.0, prio=0.0, used_at=0, has_prio=False)
+        self.held: set = set()
 
     def _credit(self, rank: int) -> float:
         if self.rank_weight == 0.0:
@@ -51,7 +48,7 @@ class LFUDA(Policy):
         c.fit(e)
         self.clock += 1
         c.used_at[e] = self.clock
-        f = float(c.freq[e]) + self._credit(rank)
+        f = c.freq[e] + self._credit(rank)
         if self.fcap is not None and f > self.fcap:
             f = self.fcap
         c.freq[e] = f
@@ -61,7 +58,7 @@ class LFUDA(Policy):
     def admit(self, e, rank=0):
         e = int(e)
         self.col.fit(e)
-        self.col.held[e] = True
+        self.held.add(e)
         if not self.keep_ghost:
             self.col.freq[e] = 0.0
         self._use(e, rank)
@@ -71,28 +68,23 @@ class LFUDA(Policy):
 
     def victim(self, exclude=()):
         c = self.col
-        mask = c.held
-        if exclude:
-            mask = mask.copy()
-            for x in exclude:
-                if 0 <= int(x) < mask.shape[0]:
-                    mask[int(x)] = False
-        return first_by(mask, c.prio, c.used_at)
+        cands = self.held.difference(exclude) if exclude else self.held
+        return first_by(cands, c.prio, c.used_at)
 
     def evicted(self, e):
         e = int(e)
         c = self.col
         c.fit(e)
-        p = float(c.prio[e]) if c.has_prio[e] else self.age
+        p = c.prio[e] if c.has_prio[e] else self.age
         c.has_prio[e] = False
         if p > self.age:
             self.age = p
-        c.held[e] = False
+        self.held.discard(e)
         if not self.keep_ghost:
             c.freq[e] = 0.0
             c.used_at[e] = 0
         elif self.ghost_decay != 1.0:
-            c.freq[e] = float(c.freq[e]) * self.ghost_decay
+            c.freq[e] = c.freq[e] * self.ghost_decay
 
     @property
     def L(self) -> float:

@@ -16,13 +16,11 @@ the capacity):
   is the victim;
 * ``evicted(e)`` drops e from whichever queue still holds it.
 
-State: per expert a queue code (none / small / main), the clock value at which it
-entered its queue, a frequency, and a ghost clock (0 = not a ghost).  A queue's
-head is its member with the smallest entry clock.
+State: per expert the clock value at which it entered its queue, a frequency and a
+ghost clock (0 = not a ghost); the member sets of the small queue, the main queue
+and the ghosts.  A queue's head is its member with the smallest entry clock.
 """
 from __future__ import annotations
-
-import numpy as np
 
 from ..pool import Policy
 from ._columns import Columns, first_by
@@ -43,42 +41,34 @@ class S3FIFO(Policy):
         self.small_target = max(1, int(round(self.SMALL_SHARE * capacity)))
         self.ghost_len = max(1, int(round(self.GHOST_SHARE * capacity)))
         self.clock = 0
-        self.n_small = 0
-        self.n_main = 0
-        self.n_ghost = 0
-        self.col = Columns(n_experts, queue=(np.int8, NONE), entered=(np.int64, 0),
-                           freq=(np.int64, 0), ghost_at=(np.int64, 0))
+        self.queues = {SMALL: set(), MAIN: set()}
+        self.ghosts: set = set()
+        self.col = Columns(n_experts, queue=NONE, entered=0, freq=0, ghost_at=0)
 
     def _enqueue(self, e: int, q: int) -> None:
         self.clock += 1
         self.col.queue[e] = q
         self.col.entered[e] = self.clock
-        if q == SMALL:
-            self.n_small += 1
-        else:
-            self.n_main += 1
+        self.queues[q].add(e)
 
     def _dequeue(self, e: int) -> None:
         q = self.col.queue[e]
-        if q == SMALL:
-            self.n_small -= 1
-        elif q == MAIN:
-            self.n_main -= 1
+        if q != NONE:
+            self.queues[q].discard(e)
         self.col.queue[e] = NONE
 
     def _head(self, q: int) -> int:
-        return first_by(self.col.queue == q, self.col.entered)
+        return first_by(self.queues[q], self.col.entered)
 
     def _remember(self, e: int) -> None:
         c = self.col
-        if c.ghost_at[e] == 0:
-            self.n_ghost += 1
         self.clock += 1
         c.ghost_at[e] = self.clock
-        while self.n_ghost > self.ghost_len:
-            g = first_by(c.ghost_at > 0, c.ghost_at)
+        self.ghosts.add(e)
+        while len(self.ghosts) > self.ghost_len:
+            g = first_by(self.ghosts, c.ghost_at)
             c.ghost_at[g] = 0
-            self.n_ghost -= 1
+            self.ghosts.discard(g)
 
     def admit(self, e, rank=0):
         e = int(e)
@@ -89,7 +79,7 @@ class S3FIFO(Policy):
         c.freq[e] = 0
         if c.ghost_at[e] > 0:
             c.ghost_at[e] = 0
-            self.n_ghost -= 1
+            self.ghosts.discard(e)
             self._enqueue(e, MAIN)
         else:
             self._enqueue(e, SMALL)
@@ -127,8 +117,9 @@ class S3FIFO(Policy):
         return e
 
     def victim(self):
-        while self.n_small or self.n_main:
-            if self.n_small and (self.n_small >= self.small_target or not self.n_main):
+        small, main = self.queues[SMALL], self.queues[MAIN]
+        while small or main:
+            if small and (len(small) >= self.small_target or not main):
                 v = self._leave_small()
             else:
                 v = self._leave_main()

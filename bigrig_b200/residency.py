@@ -70,21 +70,24 @@ class SlotTable:
     def touch(self, experts, ranks=None) -> list:
         """Count a request for each expert (router rank ``ranks``, default 0), tell the
         policy about the resident ones and return the rest, in request order."""
-        ex = np.asarray(experts, dtype=np.int64).reshape(-1)
-        rk = (np.zeros(ex.shape[0], dtype=np.int64) if ranks is None
-              else np.asarray(ranks, dtype=np.int64).reshape(-1))
-        np.add.at(self.uses, ex, 1)
-        present = self.g2s[ex] >= 0
-        n_hit = int(np.count_nonzero(present))
-        self.hits += n_hit
-        self.misses += ex.shape[0] - n_hit
-        if n_hit:
-            note = self.policy.touch
-            for e, r in zip(ex[present].tolist(), rk[present].tolist()):
+        ex = experts.tolist() if isinstance(experts, np.ndarray) else [int(e) for e in experts]
+        if ranks is None:
+            rk = [0] * len(ex)
+        else:
+            rk = ranks.tolist() if isinstance(ranks, np.ndarray) else [int(r) for r in ranks]
+        slots = self.g2s[ex].tolist() if ex else []
+        uses, note = self.uses, self.policy.touch
+        need, miss_rank = [], {}
+        for e, r, slot in zip(ex, rk, slots):
+            uses[e] += 1
+            if slot < 0:
+                need.append(e)
+                miss_rank[e] = r
+            else:
                 note(e, r)
-        absent = ~present
-        need = ex[absent].tolist()
-        self._miss_rank = dict(zip(need, rk[absent].tolist()))
+        self.hits += len(ex) - len(need)
+        self.misses += len(need)
+        self._miss_rank = miss_rank
         return need
 
     # -- slot turnover ---------------------------------------------------------
@@ -97,17 +100,17 @@ class SlotTable:
         return v if ok else -1
 
     def _oldest_unprotected(self, protect: set) -> int:
-        occupied = self.s2g >= 0
-        if protect:
-            occupied &= ~np.isin(self.s2g, np.fromiter(protect, dtype=np.int64))
-        slot = first_by(occupied, self._admitted_at)
-        return -1 if slot < 0 else int(self.s2g[slot])
+        s2g = self.s2g.tolist()
+        slots = [j for j, e in enumerate(s2g) if e >= 0 and e not in protect]
+        slot = first_by(slots, self._admitted_at.tolist())
+        return -1 if slot < 0 else s2g[slot]
 
     def _victim(self, protect=()) -> int:
         """A slot for the next admission: a free one, else the policy's victim's."""
         if self._free:
             return self._free.pop()
-        protect = {int(x) for x in protect}
+        if not isinstance(protect, (set, frozenset)):
+            protect = {int(x) for x in protect}
         ev = self._policy_choice(protect)
         if ev < 0:
             ev = self._oldest_unprotected(protect)

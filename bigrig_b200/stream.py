@@ -115,6 +115,34 @@ class ExpertPool(SlotTable):
         self._stage_buf = None       # [STAGE_MAX, bytes_per_expert] in HBM, made on first use
         self.stage_issued = self.stage_hits = self.zero_copy_admits = 0
 
+    @property
+    def stage_rows(self) -> int:
+        """Staging buffers of this pool: at most STAGE_MAX, and never more than the pool's
+        capacity (a step cannot admit more than that)."""
+        return min(STAGE_MAX, self.capacity)
+
+    def adopt(self, slab: torch.Tensor) -> "ExpertPool":
+        """Make every expert resident from a device slab that already holds them, expert e in
+        row e (``[n_experts, slot_stride]`` uint8 on this pool's device): a whole layer loaded
+        straight into HBM, with no host copy.  Only for a pool whose capacity is the expert
+        count; the slab becomes the pool's."""
+        if self.capacity != self.n_experts:
+            raise ValueError(f"layer {self.layer}: adopt() fills every slot, so the capacity "
+                             f"must be {self.n_experts}, got {self.capacity}")
+        want = (self.n_experts, self.layout.slot_stride)
+        if tuple(slab.shape) != want or slab.dtype != torch.uint8 or slab.device != self.device:
+            raise ValueError(f"layer {self.layer}: adopt() needs uint8 {want} on {self.device}, "
+                             f"got {slab.dtype} {tuple(slab.shape)} on {slab.device}")
+        self.slab = slab
+        self._built = True
+        if self.device.type == "cuda" and self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(device=self.device)
+        self._free = []
+        for e in range(self.n_experts):
+            self._miss_rank = {e: 0}
+            self._placed(e, e)
+        return self
+
     # -- construction -------------------------------------------------------
     @property
     def bytes_per_expert(self) -> int:
@@ -180,7 +208,7 @@ class ExpertPool(SlotTable):
         picked = []
         for e, blob in items:
             e = int(e)
-            if self.g2s[e] >= 0 or e in self.stage or len(self.stage) + len(picked) >= STAGE_MAX:
+            if self.g2s[e] >= 0 or e in self.stage or len(self.stage) + len(picked) >= self.stage_rows:
                 continue
             if any(e == p for p, _ in picked):
                 continue
@@ -196,7 +224,7 @@ class ExpertPool(SlotTable):
                 self.stage_expert(e, src)
             return len(picked)
         if self._stage_buf is None:
-            self._stage_buf = torch.empty((STAGE_MAX, self.bytes_per_expert), dtype=torch.uint8,
+            self._stage_buf = torch.empty((self.stage_rows, self.bytes_per_expert), dtype=torch.uint8,
                                           device=self.device)
         import ctypes
         from . import _lib
@@ -220,14 +248,14 @@ class ExpertPool(SlotTable):
         on the copy stream; ``ensure`` admits a staged expert with a device-to-device copy.
         Returns False when there is nothing to do (resident, already staged, buffers full)."""
         e = int(e)
-        if self.g2s[e] >= 0 or e in self.stage or len(self.stage) >= STAGE_MAX:
+        if self.g2s[e] >= 0 or e in self.stage or len(self.stage) >= self.stage_rows:
             return False
         src = _as_u8(blob)
         if src.numel() != self.bytes_per_expert:
             raise ValueError(f"expert {e}: manifest accounts for {self.bytes_per_expert} bytes "
                              f"but the region is {src.numel()}.")
         if self._stage_buf is None:
-            self._stage_buf = torch.empty((STAGE_MAX, self.bytes_per_expert), dtype=torch.uint8,
+            self._stage_buf = torch.empty((self.stage_rows, self.bytes_per_expert), dtype=torch.uint8,
                                           device=self.device)
         dst = self._stage_buf[len(self.stage)]
         if self.device.type == "cuda":
@@ -429,15 +457,20 @@ class StreamingSwitchGLU:
         """Make every requested expert resident; return the slot-remapped indices
         (stream.py:922-978).  ``ranks`` overrides the rank read off the last axis."""
         gi = np.asarray(indices).astype(np.int64)
-        flat = gi.reshape(-1)
-        if ranks is not None:
-            rk = np.asarray(ranks, dtype=np.int64).reshape(-1)
+        k = gi.shape[-1] if gi.ndim else 1
+        row = gi.reshape(-1).tolist()
+        if ranks is None and len(row) == k and len(set(row)) == k:
+            # one token (decode): its k distinct experts, ascending, each at its own rank
+            order = sorted(range(k), key=row.__getitem__)
+            uniq = np.array([row[j] for j in order], dtype=np.int64)
+            best = np.array(order, dtype=np.int64)
         else:
-            rk = np.tile(np.arange(gi.shape[-1], dtype=np.int64), flat.shape[0] // max(1, gi.shape[-1]))
-        # each distinct expert once, ascending, at the best (lowest) rank it was asked at
-        uniq, which = np.unique(flat, return_inverse=True)
-        best = np.full(uniq.shape[0], np.iinfo(np.int64).max, dtype=np.int64)
-        np.minimum.at(best, which.reshape(-1), rk)
+            rk = (np.asarray(ranks, dtype=np.int64).reshape(-1) if ranks is not None
+                  else np.tile(np.arange(k, dtype=np.int64), len(row) // max(1, k)))
+            # each distinct expert once, ascending, at the best (lowest) rank it was asked at
+            uniq, which = np.unique(np.asarray(row, dtype=np.int64), return_inverse=True)
+            best = np.full(uniq.shape[0], np.iinfo(np.int64).max, dtype=np.int64)
+            np.minimum.at(best, which.reshape(-1), rk)
         pool = self._pool
         need = pool.touch(uniq, best)
         protect = set(uniq.tolist())
@@ -476,7 +509,7 @@ class StreamingSwitchGLU:
         if (STAGING and nxt is not None and self._next_gate is not None and x2.shape[0] == 1
                 and not nxt.full):
             gw, gb = self._next_gate
-            nk = min(STAGE_MAX, nxt.n_experts)
+            nk = min(STAGE_MAX, k, nxt.n_experts)
             pidx, _ = ops.router_topk(ops.router_logits(x2, gw, gb), nk)
             both = torch.cat([indices.reshape(1, k).to(torch.int32), pidx.reshape(1, nk)], dim=1)
             t0 = time.perf_counter()
@@ -494,9 +527,9 @@ class StreamingSwitchGLU:
         """One decode token through the whole MoE block over this pool: the router's top-k
         is computed and read back (with, when staging is on, the next layer's prediction
         from the same two launches: one logits call over both routers' weights and one top-k
-        over the two rows), made resident, then one library call computes router, experts
-        and combine (``bigrig_moe_layer``, whose routing is bit-identical to the one read
-        back).  Returns out [1, H] = residual + sum_j score * y."""
+        over the two rows), made resident, then one library call computes the experts and
+        the combine on that same routing (``bigrig_moe_layer_routed``: the persistent kernel
+        without its router phase).  Returns out [1, H] = residual + sum_j score * y."""
         pool = self._pool
         H = x.shape[-1]
         if k > pool.capacity:
@@ -555,11 +588,12 @@ class StreamingSwitchGLU:
         ws = self.workspace or ops.default_workspace(x2.device)
         buf = ws.reserve(ops.workspace_bytes(1, k, E, pool.layout))
         out = torch.empty(1, H, dtype=torch.bfloat16, device=x2.device)
-        _call(lib.bigrig_moe_layer(
-            x2.data_ptr(), gate_w.data_ptr(), 0 if gate_b is None else gate_b.data_ptr(), 1, E, k,
-            mcode, int(norm_topk), pool.g2s_device().data_ptr(), pool.slab.data_ptr(),
-            self._layout_ptr(), 0 if residual is None else residual.data_ptr(), out.data_ptr(),
-            rs[5], rs[6], buf.data_ptr(), buf.numel(), st), "moe_layer")
+        # the routing read back above is the one computed: the layer runs on it (row 0 of the
+        # device buffers) instead of routing a second time
+        _call(lib.bigrig_moe_layer_routed(
+            x2.data_ptr(), rs[5], rs[6], 1, E, k, pool.g2s_device().data_ptr(),
+            pool.slab.data_ptr(), self._layout_ptr(), 0 if residual is None else residual.data_ptr(),
+            out.data_ptr(), buf.data_ptr(), buf.numel(), st), "moe_layer_routed")
         pool.mark_read()
         if pred is not None:
             self._speculate(pred)
@@ -619,7 +653,7 @@ class StreamingSwitchGLU:
         staged one by a device-to-device copy and any other from the host."""
         nxt = self._next
         want = [int(e) for e in predicted if nxt.g2s[int(e)] < 0 and int(e) not in nxt.stage]
-        want = want[:max(0, STAGE_MAX - len(nxt.stage))]
+        want = want[:max(0, nxt.stage_rows - len(nxt.stage))]
         if not want:
             return
         blobs = self._fetch([(nxt.layer, e) for e in want])

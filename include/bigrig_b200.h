@@ -196,6 +196,21 @@ BIGRIG_API int bigrig_moe_layer(const void* x, const void* gate_w, const float* 
                                 float* scores_out, void* workspace, size_t workspace_bytes,
                                 void* stream);
 
+/* bigrig_moe_layer for a caller that already holds the routing: indices int32 [T, k] and
+ * scores fp32 [T, k] on the device (typically bigrig_router_topk's output that the host
+ * also read back to make the experts resident), out[T, H] = residual + sum_j score * y.
+ * Nothing is routed again: a one-token call runs the persistent kernel without its router
+ * phase, other calls the expert kernels and the combine.  Expert ids outside [0, E) or
+ * without a slot contribute zeros and are counted in the workspace's error word.  Same
+ * workspace rules as bigrig_moe_layer.  Replaces the block's combine around
+ * StreamingSwitchGLU.__call__ after the routing readback (stream.py:1447-1450,
+ * 1523-1525). */
+BIGRIG_API int bigrig_moe_layer_routed(const void* x, const int32_t* indices, const float* scores,
+                                       int T, int E, int k, const int32_t* g2s, const void* slab,
+                                       const bigrig_expert_layout* layout, const void* residual,
+                                       void* out, void* workspace, size_t workspace_bytes,
+                                       void* stream);
+
 /* Device error word of a workspace (slots < 0, ids out of range), copied to *out
  * with a synchronous read on `stream`; resets it to 0.  For tests and debugging. */
 BIGRIG_API int bigrig_workspace_errors(void* workspace, int32_t* out, void* stream);

@@ -160,3 +160,36 @@ def test_persistent_graph_replay(cuda):
     del graph
     words = _words(ws)
     assert words[0] == 0 and words[1] == 0, words
+
+
+@pytest.mark.parametrize("name", list(SHAPES))
+def test_routed_layer_equals_routing_layer(cuda, name):
+    """bigrig_moe_layer_routed on the routing bigrig_moe_layer computed gives its bits, with
+    and without the residual (the persistent kernel without its router phase, or for the
+    too-wide layer the expert chain plus combine), and counts no error."""
+    H, I, E, k, bits, sd, mode, norm = SHAPES[name]
+    L, slab, g2s, x, gw, gb = _layer(name, cuda)
+    ws = ops.Workspace(cuda)
+    for residual in (None, x):
+        out, idx, sc = _run("auto", name, L, slab, g2s, x, gw, gb, ws, residual=residual)
+        n0 = _lib.launch_counts()
+        got = ops.moe_layer_routed(x, idx, sc, slab, L, E, g2s=g2s, residual=residual, workspace=ws)
+        n1 = _lib.launch_counts()
+        assert torch.equal(got, out)
+        assert n1["router_logits"] == n0["router_logits"] and n1["route"] == n0["route"]
+    assert ws.errors() == 0
+    assert _words(ws)[1] == 0
+
+
+def test_routed_layer_counts_missing_slots(cuda):
+    name = "olmoe"
+    H, I, E, k, bits, sd, mode, norm = SHAPES[name]
+    L, slab, g2s, x, gw, gb = _layer(name, cuda)
+    ws = ops.Workspace(cuda)
+    out, idx, sc = _run("auto", name, L, slab, g2s, x, gw, gb, ws)
+    holes = g2s.clone()
+    holes[idx[0, 1]] = -1
+    got = ops.moe_layer_routed(x, idx, sc, slab, L, E, g2s=holes, workspace=ws)
+    want, _, _ = _run("chain", name, L, slab, holes, x, gw, gb, ws)
+    assert ws.errors() > 0
+    assert_close(got.float().cpu().numpy(), want.float().cpu().numpy())
