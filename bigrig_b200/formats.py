@@ -158,3 +158,42 @@ def manifest_regions(manifest: dict) -> dict:
     """{(layer, expert): (offset, length)} from a manifest's ``regions``."""
     return {tuple(int(x) for x in k.split(":")): (int(o), int(n))
             for k, (o, n) in manifest["regions"].items()}
+
+
+def write_blob(path: str, layers: dict, top_k: int | None = None) -> dict:
+    """Write experts as one expert-contiguous blob plus ``<path>.manifest.json``; return the
+    manifest (the reference's packed-blob format, bigrig_engine/stream.py:106-186).
+
+    ``layers``: {layer: (spec, quant, experts)} where ``experts`` is a sequence whose item e
+    is expert e as packed bytes (anything ``np.frombuffer`` takes, or a uint8 array) or as
+    {proj: {comp: ndarray}} (packed here with ``pack_expert``).  Layers go in ascending
+    order, experts in id order, each expert's bytes in one region; every region is checked
+    against the spec's byte count before anything is written for it."""
+    manifest = {"version": 4, "layers": {}, "regions": {}}
+    pos = 0
+    folder = os.path.dirname(os.path.abspath(path))
+    os.makedirs(folder, exist_ok=True)
+    with open(path, "wb") as out:
+        for li in sorted(int(x) for x in layers):
+            spec, quant, experts = layers[li]
+            want = bytes_per_expert(spec)
+            entry = {"n_experts": len(experts), "spec": spec, "bytes_per_expert": want}
+            if quant:
+                entry["quant"] = dict(quant)
+            manifest["layers"][str(li)] = entry
+            for e, ex in enumerate(experts):
+                data = pack_expert(ex, spec) if isinstance(ex, dict) else (
+                    np.asarray(ex, dtype=np.uint8).reshape(-1) if isinstance(ex, np.ndarray)
+                    else np.frombuffer(ex, dtype=np.uint8))
+                if data.nbytes != want:
+                    raise ValueError(f"layer {li} expert {e}: {data.nbytes} bytes, the spec "
+                                     f"accounts for {want}")
+                out.write(data.tobytes())
+                manifest["regions"][f"{li}:{e}"] = [pos, want]
+                pos += want
+    manifest["total_bytes"] = pos
+    if top_k:
+        manifest["top_k"] = int(top_k)
+    with open(path + ".manifest.json", "w") as f:
+        json.dump(manifest, f)
+    return manifest
