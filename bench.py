@@ -195,6 +195,24 @@ SHAPES = {
 }
 
 
+def _normed(b):
+    """A pre-norm MoE layer, h -> h + moe(rms_norm(h)), as these model families place the
+    block behind an RMSNorm (unit weight here): without it a random-init stack of wide
+    experts grows its hidden state layer after layer until the logits overflow."""
+    H = b.hidden
+
+    def layer(h):
+        return b(torch.nn.functional.rms_norm(h, (H,), eps=1e-6), residual=h)
+    return layer
+
+
+def _normed_step(blocks, x):
+    h = x
+    for b in blocks:
+        h = b(torch.nn.functional.rms_norm(h, (b.hidden,), eps=1e-6), residual=h)
+    return h
+
+
 def _expert_bank(dev, sh: dict, seed: int):
     """One layer's worth of distinct experts (N(0, 0.02) quantised on the GPU), slab rows."""
     from bigrig_b200.block import random_expert_bytes
@@ -244,11 +262,12 @@ def _decode_bytes(blocks, xs, bpe: int) -> float:
     for x in xs:
         h = x
         for b in blocks:
-            idx, _ = b.route(h)
+            hn = torch.nn.functional.rms_norm(h, (b.hidden,), eps=1e-6)
+            idx, _ = b.route(hn)
             U = int(torch.unique(idx).numel())
             tot += U * bpe + b.n_experts * b.hidden * 2 + 2 * h.shape[0] * b.hidden * 2
             n += 1
-            h = b(h, residual=h)
+            h = b(hn, residual=h)
     return tot / max(1, n)
 
 
@@ -265,16 +284,16 @@ def _graph_decode(dev, blocks, B: int, K: int, W: int, seed: int, bpe: int, peak
                                    blocks[0].switch._pool.layout))
     xin = xs[0].clone()
     for _ in range(2):
-        stack_step(blocks, xin)
+        _normed_step(blocks, xin)
     torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
     st = torch.cuda.Stream(device=dev)
     st.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(st):
-        stack_step(blocks, xin)
+        _normed_step(blocks, xin)
     torch.cuda.current_stream(dev).wait_stream(st)
     with torch.cuda.graph(graph):
-        stack_step(blocks, xin)
+        _normed_step(blocks, xin)
     for i in range(W):
         xin.copy_(xs[i])
         graph.replay()
@@ -309,7 +328,7 @@ def _prefill_gemm(dev, blocks, T: int, seed: int, peak: float, peak_kind: str, l
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     prompt = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
-    layers = [(lambda h, b=b: b(h, residual=h)) for b in blocks]
+    layers = [_normed(b) for b in blocks]
     if warm:
         layered.prefill(layers, [prompt], token_wise=True, layer_scope=layer_scope)
     torch.cuda.synchronize(dev)
@@ -421,13 +440,13 @@ def _bench_streamed(dev, sh: dict, W: int, hbm_peak: float, bf16_peak: float, bf
     n_dec = 12
     xs = torch.randn(W + n_dec, 1, sh["hidden"], generator=g, device=dev).to(torch.bfloat16)
     for i in range(W):
-        stack_step(blocks, xs[i])
+        _normed_step(blocks, xs[i])
     handle.reset_stats()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(n_dec):
-        stack_step(blocks, xs[W + i])
+        _normed_step(blocks, xs[W + i])
     e1.record()
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)

@@ -438,6 +438,13 @@ int bigrig_moe_layer_routed(const void* x, const int32_t* indices, const float* 
   return launch_combine(ws.y, scores, T, k, layout->hidden, out, s, residual);
 }
 
+int bigrig_test_grid_barrier(int phantom_ctas, unsigned int spin_limit) {
+  if (phantom_ctas < 0)
+    return set_error(BIGRIG_ERR_INVALID, "test_grid_barrier: phantom_ctas=%d", phantom_ctas);
+  set_dl_wait_test(static_cast<uint32_t>(phantom_ctas), spin_limit);
+  return BIGRIG_OK;
+}
+
 int bigrig_set_path(int mode, int gemm_min_rows) {
   if (mode < BIGRIG_PATH_AUTO || mode > BIGRIG_PATH_CHAIN || gemm_min_rows < 1)
     return set_error(BIGRIG_ERR_INVALID, "set_path: mode=%d gemm_min_rows=%d", mode, gemm_min_rows);

@@ -40,6 +40,7 @@
 // counts in the error words and the kernel carries on to its end.
 #include <cuda.h>
 
+#include <atomic>
 #include <cstring>
 
 #include "gemv_common.cuh"
@@ -62,7 +63,8 @@ constexpr int kDlRouterPerCta = 4;       // experts whose logits one CTA compute
 constexpr int kDlMaxStages = 12;
 constexpr int kDlCW = 16;                // consumer warps
 constexpr int kDlGroup = 64;             // quantisation group size the kernel is built for
-constexpr uint32_t kDlSpinLimit = 1u << 22;
+// Polls of a flag or of the grid barrier before a wait gives up (error word 1): ~0.5 s.
+constexpr uint32_t kDlSpinLimit = 1u << 20;
 
 struct DecodeLayerArgs {
   const uint16_t* x;          // [H] bf16
@@ -86,6 +88,8 @@ struct DecodeLayerArgs {
   int seg_stride;             // bytes between a down item's expert segments in a stage
   int wpi;                    // consumer warps per gate/up item (8 or 16)
   int maps;                   // kDlMapGateUp | kDlMapDown: which copies go through tensor maps
+  uint32_t spin_limit;        // polls before a flag or barrier wait gives up
+  uint32_t phantom;           // CTAs the grid barrier waits for beyond the grid (tests only)
 };
 
 // The copy engine takes one copy at a time, at a cost per copy that the small scale and
@@ -517,7 +521,7 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
           }
         }
       }
-      if (n > kDlSpinLimit) {
+      if (n > a.spin_limit) {
         if (lane == 0) atomicAdd(a.err + 1, 1);
         for (int i = 0; i < kMaxExperts / 32; ++i)
           if (need & (1u << i)) s_lg[lane + 32 * i] = __int_as_float(0x7fc00000);
@@ -796,10 +800,10 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
   if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(a.arrivals, 1ull);
-    const unsigned long long target = (epoch + 1ull) * static_cast<unsigned long long>(G);
+    const unsigned long long target = (epoch + 1ull) * static_cast<unsigned long long>(G) + a.phantom;
     uint32_t n = 0;
     while (static_cast<long long>(ld_acquire_u64(a.arrivals) - target) < 0) {
-      if (++n > kDlSpinLimit) {
+      if (++n > a.spin_limit) {
         atomicAdd(a.err + 1, 1);
         break;
       }
@@ -1068,6 +1072,21 @@ int dl_launch(const DecodeLayerArgs& args, const CUtensorMap& tm_code, const CUt
 
 }  // namespace
 
+namespace {
+std::atomic<uint32_t> g_dl_phantom{0};
+std::atomic<uint32_t> g_dl_spin{kDlSpinLimit};
+}  // namespace
+
+void dl_wait_test(uint32_t* phantom, uint32_t* spin_limit) {
+  *phantom = g_dl_phantom.load();
+  *spin_limit = g_dl_spin.load();
+}
+
+void set_dl_wait_test(uint32_t phantom, uint32_t spin_limit) {
+  g_dl_phantom.store(phantom);
+  g_dl_spin.store(spin_limit ? spin_limit : kDlSpinLimit);
+}
+
 bool decode_layer_fits(const bigrig_expert_layout& L, int k, int E) {
   DlPlan p;
   return decode_layer_plan(L, k, E, sm_count_dl(), &p);
@@ -1116,6 +1135,7 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
   memset(&tm_gsb, 0, sizeof(tm_gsb));
   memset(&tm_dsb, 0, sizeof(tm_dsb));
   a.maps = dl_maps(a.slab, L, &tm_code, &tm_gsb, &tm_dsb);
+  dl_wait_test(&a.phantom, &a.spin_limit);
   if (L.bits == 4 && L.scale_dtype == BIGRIG_F16)
     return dl_launch<4, BIGRIG_F16>(a, tm_code, tm_gsb, tm_dsb, p.smem, G, s);
   if (L.bits == 4 && L.scale_dtype == BIGRIG_BF16)

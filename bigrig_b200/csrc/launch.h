@@ -87,6 +87,8 @@ int launch_gemm_gate_up(const void* x, const RouteView& rv, const void* slab,
 int launch_gemm_down(const void* h, const RouteView& rv, const void* slab,
                      const bigrig_expert_layout& L, void* y, int mean_rows, cudaStream_t s);
 bool decode_layer_fits(const bigrig_expert_layout& L, int k, int E);
+// Test hook of the persistent kernel's bounded waits (bigrig_test_grid_barrier).
+void set_dl_wait_test(uint32_t phantom, uint32_t spin_limit);
 int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, int E, int k,
                         int mode, int norm, const int32_t* g2s, const void* slab,
                         const bigrig_expert_layout& L, const void* residual, void* out,

@@ -211,6 +211,16 @@ BIGRIG_API int bigrig_moe_layer_routed(const void* x, const int32_t* indices, co
                                        void* out, void* workspace, size_t workspace_bytes,
                                        void* stream);
 
+/* Test hook for the failure path of the persistent one-token kernel: its grid barrier
+ * also waits for `phantom_ctas` CTAs that do not exist, and every bounded wait polls at
+ * most `spin_limit` times (0: the default, about half a second).  With phantom_ctas > 0
+ * the barrier's wait runs out in every CTA, each adds 1 to the workspace's wait-timeout
+ * word (error word 1) and the kernel finishes (its output is then not meaningful); the
+ * next launch with the hook cleared (0, 0) is correct again.  No counterpart in the
+ * reference (failure detection is tested by making a bounded wait run out, never by a
+ * fault). */
+BIGRIG_API int bigrig_test_grid_barrier(int phantom_ctas, unsigned int spin_limit);
+
 /* Device error word of a workspace (slots < 0, ids out of range), copied to *out
  * with a synchronous read on `stream`; resets it to 0.  For tests and debugging. */
 BIGRIG_API int bigrig_workspace_errors(void* workspace, int32_t* out, void* stream);
