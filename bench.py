@@ -537,6 +537,30 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def ep_reference_check(dev, c: dict, xs: list, ys: list) -> dict:
+    """The expert-parallel outputs ``ys`` of tokens ``xs`` (one per rank) against the same
+    tokens through a single-GPU stack holding every expert of every layer, under the expert
+    parity bar |d| <= 2e-3 + 1e-2 |ref| (the two run different kernel paths, so equal bits
+    are not expected)."""
+    from bigrig_b200.stream import attach
+    blocks, store = build_model(dev, seed=0, layers=c["layers"])
+    h = attach(blocks, store, c["experts"], policy=c["policy"], warm="auto", device=dev)
+    outside, worst, max_abs, n = 0, 0.0, 0.0, 0
+    for x, y in zip(xs, ys):
+        ref = stack_step(blocks, x).float()
+        d = (y.float() - ref).abs()
+        allow = 2e-3 + 1e-2 * ref.abs()
+        outside += int((d > allow).sum())
+        worst = max(worst, float((d / allow).max()))
+        max_abs = max(max_abs, float(d.max()))
+        n += d.numel()
+    h.close()
+    return {"tokens": len(xs), "elements": n, "outside": outside, "max_abs": max_abs,
+            "worst_vs_bar": worst, "ok": outside == 0,
+            "note": "each rank's first timed token, EP stack vs one GPU with every expert "
+                    "resident, all layers; bar 1e-2 rel / 2e-3 abs per element"}
+
+
 # ------------------------------------------------------------------ the B200 arm
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -546,6 +570,9 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="decode only (for profiling)")
+    ap.add_argument("--ep-slots", type=int, default=None,
+                    help="expert-parallel runs: slots per layer per rank (default: the config's "
+                         "capacity, at most the rank's experts)")
     ap.add_argument("--configs", default="c3,c4,c5",
                     help="other BASELINE shapes measured at N=1 as extra keys (comma list of "
                          "c3, c4, c5, or 'none')")
@@ -590,8 +617,9 @@ def main() -> None:
         lo, hi = ep.local_range()
         blocks, store = build_model(dev, seed=0, experts=range(lo, hi), layers=c["layers"])
         pools, mods = [], []
+        slots = min(args.ep_slots or c["capacity"], hi - lo)
         for b in blocks:
-            pool = ExpertPool(b.layer, None, hi - lo, min(c["capacity"], hi - lo), b.spec,
+            pool = ExpertPool(b.layer, None, hi - lo, slots, b.spec,
                               policy=c["policy"], quant=b.quant, device=dev).build()
             pools.append(pool)
             mods.append(StreamingSwitchGLU(pool, store))
@@ -659,6 +687,32 @@ def main() -> None:
     # ---- decode, capped pool: warm-up then K timed steps
     for i in range(W):
         stack_step(stack, tokens[i])
+    step, graph = stack_step, None
+    if world > 1 and all(b.padded for b in stack):
+        # every rank's pools hold all its experts: the whole step (router, the padded NCCL
+        # all-to-alls, the expert kernels, the combines) is one CUDA graph per token
+        for p in handle.pools:
+            p.g2s_device()
+            p.settle()
+        xin = tokens[0].clone()
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                stack_step(stack, xin)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            yout = stack_step(stack, xin)
+
+        def step(_stack, x, _g=graph, _x=xin, _y=yout):
+            _x.copy_(x)
+            _g.replay()
+            return _y
+        for i in range(W):
+            step(stack, tokens[i])
+        barrier()
     handle.reset_stats()
     barrier()
     counts0 = _lib.launch_counts()
@@ -669,7 +723,7 @@ def main() -> None:
     torch.cuda.nvtx.range_push("decode")
     t0.record()
     for i in range(K):
-        stack_step(stack, tokens[W + i])
+        step(stack, tokens[W + i])
     t1.record()
     torch.cuda.nvtx.range_pop()
     barrier()
@@ -689,7 +743,7 @@ def main() -> None:
     w0 = time.perf_counter()
     for i in range(K):
         x = hbuf[W + i].to(dev, non_blocking=True)
-        y = stack_step(stack, x)
+        y = step(stack, x)
         outbuf.copy_(y, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
     barrier()
@@ -698,6 +752,22 @@ def main() -> None:
            "h2d_bytes_per_step": c["hidden"] * 2, "d2h_bytes_per_step": c["hidden"] * 2,
            "note": "per step: token embedding copied from pinned host, 16 MoE layers, result "
                    "read back; misses copied from pinned host inside the step"}
+
+    # ---- expert-parallel check: every rank's first timed token through the EP stack
+    # against the same token through one GPU holding every expert (rank 0)
+    ep_check = None
+    if world > 1:
+        xc = tokens[W].clone()
+        yc = step(stack, xc).clone()
+        xs = [torch.empty_like(xc) for _ in range(world)]
+        ys = [torch.empty_like(yc) for _ in range(world)]
+        dist.all_gather(xs, xc)
+        dist.all_gather(ys, yc)
+        if rank == 0:
+            ep_check = ep_reference_check(dev, c, xs, ys)
+    if graph is not None:
+        del step, graph
+        graph = None
 
     # ---- resident (sync-free) decode in one CUDA graph per token (single GPU)
     if not args.no_extras and world == 1:
@@ -849,6 +919,8 @@ def main() -> None:
                      "stage_issued": st.get("stage_issued"), "stage_hits": st.get("stage_hits")},
             "clocks": clk,
             "cpu_baseline": cpu,
+            **({"ep_check": ep_check, "ep_graph": bool(world > 1 and all(b.padded for b in stack))}
+               if world > 1 else {}),
             **extras,
         }
         print(json.dumps(line), flush=True)

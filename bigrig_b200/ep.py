@@ -8,17 +8,19 @@ rank routes its own tokens with the replicated router).  One MoE layer is then
 1. plan: each (token, k) pair goes to the rank owning its expert; pairs are grouped
    by destination with a stable sort, so a rank's rows arrive in the sender's
    (token, k) order;
-2. dispatch: ``all_to_all_single`` of the pair rows (bf16 [H]) and their local
-   expert ids;
+2. dispatch: one ``all_to_all_single`` of the pair rows, each carrying its local
+   expert id in the row's padding (``padded`` mode; the exact mode sends rows and ids
+   separately);
 3. the owner computes its experts over the received rows (k = 1 per row);
 4. combine: the reverse ``all_to_all_single`` returns each pair's output to its
    sender, which applies the router weights (``sum_k score * y``).
 
 Two exchange modes.  ``padded`` (decode): every peer block has a fixed capacity of
 T*k rows (the most one rank can send to one peer), padding rows carry expert id -1
-and are skipped by the kernels; no sizes cross to the host, so the step can be
-captured in a CUDA graph.  ``exact`` (prefill): counts are exchanged first
-(int32 [G]), then rows with those split sizes.
+and are skipped by the kernels; no sizes cross to the host and every step is the same
+sequence of device work, so a whole decode step can be captured in a CUDA graph
+(``bench.py`` does).  ``exact`` (prefill): counts are exchanged first (int64 [G]),
+then rows and ids with those split sizes.
 
 Transport is NCCL over NVLink 5 / NVSwitch.  Nothing here issues TMA or multicast
 loads; peer memory is only touched by NCCL.
@@ -50,7 +52,9 @@ class ExpertParallel:
         flat = indices.reshape(-1).long()
         dest = torch.div(flat, self.per_rank, rounding_mode="floor")
         order = torch.sort(dest, stable=True).indices
-        counts = torch.bincount(dest, minlength=self.world)
+        # a scatter-add, not bincount: bincount reads its input's maximum back to the host
+        counts = torch.zeros(self.world, dtype=torch.int64, device=flat.device)
+        counts.scatter_add_(0, dest, torch.ones_like(dest))
         return {"T": T, "k": k, "order": order, "tok": torch.div(order, k, rounding_mode="floor"),
                 "local": (flat[order] - dest[order] * self.per_rank).to(torch.int32),
                 "dest": dest[order], "counts": counts}
@@ -83,15 +87,24 @@ class ExpertParallel:
             start = torch.cumsum(p["counts"], 0) - p["counts"]
             within = torch.arange(P, device=x.device) - start[p["dest"]]
             slot = p["dest"] * cap + within
-            send_x = torch.zeros(G * cap, H, dtype=x.dtype, device=x.device)
-            send_id = torch.full((G * cap,), -1, dtype=torch.int32, device=x.device)
-            send_x.index_copy_(0, slot, rows)
-            send_id.index_copy_(0, slot, p["local"])
-            recv_x = torch.empty_like(send_x)
-            recv_id = torch.empty_like(send_id)
-            self._a2a(recv_x, send_x)
-            self._a2a(recv_id, send_id)
-            y_recv = expert_fn(recv_x, recv_id)
+            # one payload row per pair: its H values, then 16 bytes of padding whose first
+            # word is the pair's local expert id (rows stay 16-byte aligned); padding rows
+            # carry id -1
+            es = x.element_size()
+            if (H * es) % 4:
+                raise ValueError(f"padded dispatch needs rows of whole 32-bit words, got "
+                                 f"{x.dtype} [{H}]")
+            W = H + 16 // es                           # 16 bytes of padding per row
+            at = H * es // 4                           # the id's word
+            words = torch.zeros(G * cap, W * es // 4, dtype=torch.int32, device=x.device)
+            words[:, at] = -1
+            words[:, at].index_copy_(0, slot, p["local"])
+            send = words.view(x.dtype)                 # [G * cap, W]
+            send[slot, :H] = rows
+            recv = torch.empty_like(send)
+            self._a2a(recv, send)
+            recv_id = recv.view(torch.int32)[:, at].contiguous()
+            y_recv = expert_fn(recv[:, :H].contiguous(), recv_id)
             back = torch.empty_like(y_recv)
             self._a2a(back, y_recv)
             y_sorted = back.index_select(0, slot)
