@@ -537,28 +537,43 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def ep_reference_check(dev, c: dict, xs: list, ys: list) -> dict:
-    """The expert-parallel outputs ``ys`` of tokens ``xs`` (one per rank) against the same
-    tokens through a single-GPU stack holding every expert of every layer, under the expert
-    parity bar |d| <= 2e-3 + 1e-2 |ref| (the two run different kernel paths, so equal bits
-    are not expected)."""
-    from bigrig_b200.stream import attach
-    blocks, store = build_model(dev, seed=0, layers=c["layers"])
-    h = attach(blocks, store, c["experts"], policy=c["policy"], warm="auto", device=dev)
+def ep_reference_check(dev, c: dict, stack, x: torch.Tensor, rank: int, world: int, dist) -> dict:
+    """Layer by layer, every rank's token through the expert-parallel stack against the same
+    layer input through one GPU holding every expert (on rank 0), under the expert parity
+    bar |d| <= 2e-3 + 1e-2 |ref| per element.  All ranks run the EP layers (their
+    collectives); rank 0 also builds the reference stack and returns the result."""
+    ref_blocks = None
+    if rank == 0:
+        from bigrig_b200.stream import attach
+        ref_blocks, store = build_model(dev, seed=0, layers=c["layers"])
+        ref_handle = attach(ref_blocks, store, c["experts"], policy=c["policy"], warm="auto",
+                            device=dev)
     outside, worst, max_abs, n = 0, 0.0, 0.0, 0
-    for x, y in zip(xs, ys):
-        ref = stack_step(blocks, x).float()
-        d = (y.float() - ref).abs()
-        allow = 2e-3 + 1e-2 * ref.abs()
-        outside += int((d > allow).sum())
-        worst = max(worst, float((d / allow).max()))
-        max_abs = max(max_abs, float(d.max()))
-        n += d.numel()
-    h.close()
-    return {"tokens": len(xs), "elements": n, "outside": outside, "max_abs": max_abs,
-            "worst_vs_bar": worst, "ok": outside == 0,
-            "note": "each rank's first timed token, EP stack vs one GPU with every expert "
-                    "resident, all layers; bar 1e-2 rel / 2e-3 abs per element"}
+    h = x
+    for li, blk in enumerate(stack):
+        y = blk(h, residual=h)
+        hs = [torch.empty_like(h) for _ in range(world)]
+        ys = [torch.empty_like(y) for _ in range(world)]
+        dist.all_gather(hs, h)
+        dist.all_gather(ys, y)
+        if rank == 0:
+            for hi, yi in zip(hs, ys):
+                ref = ref_blocks[li](hi, residual=hi).float()
+                d = (yi.float() - ref).abs()
+                allow = 2e-3 + 1e-2 * ref.abs()
+                outside += int((d > allow).sum())
+                worst = max(worst, float((d / allow).max()))
+                max_abs = max(max_abs, float(d.max()))
+                n += d.numel()
+        h = y
+    if rank != 0:
+        return None
+    ref_handle.close()
+    return {"tokens": world, "layers": len(stack), "elements": n, "outside": outside,
+            "max_abs": max_abs, "worst_vs_bar": worst, "ok": outside == 0,
+            "note": "each rank's first timed token, layer by layer: the EP layer's output vs "
+                    "the same input through one GPU with every expert resident; bar 1e-2 rel "
+                    "/ 2e-3 abs per element"}
 
 
 # ------------------------------------------------------------------ the B200 arm
@@ -757,14 +772,7 @@ def main() -> None:
     # against the same token through one GPU holding every expert (rank 0)
     ep_check = None
     if world > 1:
-        xc = tokens[W].clone()
-        yc = step(stack, xc).clone()
-        xs = [torch.empty_like(xc) for _ in range(world)]
-        ys = [torch.empty_like(yc) for _ in range(world)]
-        dist.all_gather(xs, xc)
-        dist.all_gather(ys, yc)
-        if rank == 0:
-            ep_check = ep_reference_check(dev, c, xs, ys)
+        ep_check = ep_reference_check(dev, c, stack, tokens[W].clone(), rank, world, dist)
     if graph is not None:
         del step, graph
         graph = None

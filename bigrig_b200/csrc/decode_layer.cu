@@ -467,8 +467,29 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
   const unsigned long long epoch = s_epoch;
   const unsigned long long tag = ((epoch + 1ull) & 0xffffffffull) << 32;
 
-  // ---------------------------------------------------------------- router logits
   bool xok = true;
+  if (routed) {
+    // ------------------------------------------------------------ routing given
+    // the producer reads it and starts streaming at once; the consumers meanwhile take x
+    // into B fragments and pick up the routing from an mbarrier the producer arrives on
+    if (producer) {
+      if (lane < k) {
+        const int e = a.pre_idx[lane];
+        const int ev = (e >= 0 && e < E) ? e : -1;
+        s_idx[lane] = ev;
+        s_slot[lane] = ev >= 0 ? s_g2s[ev] : -1;
+      }
+      __syncwarp();
+      if (lane == 0) bar_arrive(bar_r);
+    } else {
+      xok = stage_wait(bar_x, 0, a.err);
+      build_bperm<BITS>(xraw, H, 1, xperm, 0, xgs, threadIdx.x, CT);
+      named_sync(1, CT);
+      stage_wait(bar_r, 0, a.err);
+    }
+    DL_STAMP(1);
+  } else {                                       // routing computed here, from x
+  // ---------------------------------------------------------------- router logits
   if (!producer) {
     xok = stage_wait(bar_x, 0, a.err);
     if (warp < n_mine) {
@@ -500,13 +521,7 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
   // the producer collects the E tagged logits; every consumer thread then ranks (logit
   // descending, expert id ascending -- topk_warp's order) a share of them: 8 threads per
   // candidate, each counting the candidates above it among E/8 others
-  if (routed) {
-    if (threadIdx.x < k) {
-      const int e = a.pre_idx[threadIdx.x];
-      s_idx[threadIdx.x] = (e >= 0 && e < E) ? e : -1;
-    }
-    if (!producer) build_bperm<BITS>(xraw, H, 1, xperm, 0, xgs, threadIdx.x, CT);
-  } else if (producer) {
+  if (producer) {
     uint32_t need = 0;
     for (int e = lane, i = 0; e < E; e += 32, ++i) need |= 1u << i;
     for (uint32_t n = 0; need; ++n) {
@@ -534,7 +549,7 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
     build_bperm<BITS>(xraw, H, 1, xperm, 0, xgs, threadIdx.x, CT);
   }
   __syncthreads();                               // logits in s_lg
-  if (!producer && !routed) {
+  if (!producer) {
     const int per_cand = (E + 7) / 8;
     for (int c0 = 0; c0 < E; c0 += CT / 8) {
       const int c = c0 + (threadIdx.x >> 3), part = threadIdx.x & 7;
@@ -558,7 +573,6 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
     }
   }
   __syncthreads();                               // ranks in s_idx / s_rank_lg
-
   if (producer) {
     DL_STAMP(9);
     if (lane < k) {
@@ -566,6 +580,10 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
       s_slot[lane] = (e >= 0 && e < E) ? s_g2s[e] : -1;
     }
     __syncwarp();
+  }
+  }                                              // end of the routing computed here
+
+  if (producer) {
     // ------------------------------------------------------------ stream the ring
     // the first stages go out at once; then the scores (needed only by the combine);
     // then the rest as stages free up
@@ -798,8 +816,9 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
   // ---------------------------------------------------------------- grid barrier
   named_sync(1, CT);
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(a.arrivals, 1ull);
+    // one-way release add (the CTA's h stores, ordered before it by the named barrier,
+    // become visible with it), then acquire polls without a back-off
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(a.arrivals) : "memory");
     const unsigned long long target = (epoch + 1ull) * static_cast<unsigned long long>(G) + a.phantom;
     uint32_t n = 0;
     while (static_cast<long long>(ld_acquire_u64(a.arrivals) - target) < 0) {
@@ -807,7 +826,6 @@ __global__ void __launch_bounds__((kDlCW + 1) * 32, 1) decode_layer_kernel(
         atomicAdd(a.err + 1, 1);
         break;
       }
-      __nanosleep(20);
     }
     fence_proxy_async_global();                  // h, written by other CTAs, is read by bulk copy
     if (n_down > 0) {
