@@ -28,7 +28,7 @@ EXPORTS = (
     "bigrig_switch_glu", "bigrig_combine", "bigrig_moe_forward", "bigrig_workspace_errors",
     "bigrig_timing_enable", "bigrig_timing_read", "bigrig_launch_counts", "bigrig_kernel_name",
     "bigrig_set_path", "bigrig_get_path", "bigrig_moe_layer", "bigrig_switch_glu_noalloc", "bigrig_copy_regions",
-    "bigrig_moe_layer_routed", "bigrig_test_grid_barrier",
+    "bigrig_moe_layer_routed", "bigrig_test_grid_barrier", "bigrig_widen_expert",
 )
 NOALLOC_SCRATCH_BYTES = 4 << 20
 KERNELS = {"router_logits": 0, "router_topk": 1, "permute": 2, "gate_up": 3, "down": 4,
@@ -82,6 +82,7 @@ _SIG = {
     "bigrig_moe_layer": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, ctypes.POINTER(ExpertLayout),
                               _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     "bigrig_test_grid_barrier": (_I, [_I, ctypes.c_uint]),
+    "bigrig_widen_expert": (_I, [_P, _P, ctypes.POINTER(ExpertLayout), _I, _P]),
     "bigrig_moe_layer_routed": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, ctypes.POINTER(ExpertLayout),
                                      _P, _P, _P, ctypes.c_size_t, _P]),
     "bigrig_switch_glu_noalloc": (_I, [_P, _P, _I, _I, _I, _P, _P, ctypes.POINTER(ExpertLayout),

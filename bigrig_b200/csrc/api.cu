@@ -438,6 +438,20 @@ int bigrig_moe_layer_routed(const void* x, const int32_t* indices, const float* 
   return launch_combine(ws.y, scores, T, k, layout->hidden, out, s, residual);
 }
 
+int bigrig_widen_expert(const void* src, void* dst, const bigrig_expert_layout* layout,
+                        int src_bits, void* stream) {
+  if (int rc = check_layout(layout)) return rc;
+  if (!src || !dst) return set_error(BIGRIG_ERR_INVALID, "widen_expert: NULL pointer");
+  if (src_bits != 3 || layout->bits != 4)
+    return set_error(BIGRIG_ERR_UNSUPPORTED, "widen_expert: %d-bit codes into a %d-bit layout "
+                     "(only 3 -> 4 is built)", src_bits, layout->bits);
+  if ((layout->hidden % 32) || (layout->inter % 32) || (reinterpret_cast<uintptr_t>(src) % 4) ||
+      (reinterpret_cast<uintptr_t>(dst) % 16))
+    return set_error(BIGRIG_ERR_INVALID, "widen_expert: dims must be multiples of 32, src 4-byte "
+                     "and dst 16-byte aligned");
+  return launch_widen_expert(src, dst, *layout, static_cast<cudaStream_t>(stream));
+}
+
 int bigrig_test_grid_barrier(int phantom_ctas, unsigned int spin_limit) {
   if (phantom_ctas < 0)
     return set_error(BIGRIG_ERR_INVALID, "test_grid_barrier: phantom_ctas=%d", phantom_ctas);

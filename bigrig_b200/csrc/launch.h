@@ -95,6 +95,9 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
                         int32_t* idx_out, float* sc_out, void* h, void* tagged, void* arrivals,
                         int32_t* err, cudaStream_t s, const int32_t* pre_idx = nullptr,
                         const float* pre_sc = nullptr);
+// A 3-bit expert's packed bytes (src, the 4-bit layout with 3-bit code streams) widened
+// into a 4-bit slot laid out by L (L.bits == 4).
+int launch_widen_expert(const void* src, void* dst, const bigrig_expert_layout& L, cudaStream_t s);
 int launch_combine(const void* y, const float* scores, int T, int k, int H, void* out,
                    cudaStream_t s, const void* residual = nullptr);
 

@@ -28,14 +28,15 @@ _SIZE = {"uint32": 4, "float16": 2, "bfloat16": 2, "float32": 4, "uint8": 1}
 
 def make_spec(hidden: int, inter: int, bits: int = 4, group_size: int = 64,
               scale_dtype: str = "float16") -> dict:
-    """The manifest spec of a gated SwiGLU expert in MLX affine format."""
-    if bits not in (4, 8):
-        raise ValueError(f"bits must be 4 or 8, got {bits}")
+    """The manifest spec of a gated SwiGLU expert in MLX affine format (3, 4 or 8 bits)."""
+    if bits not in (3, 4, 8):
+        raise ValueError(f"bits must be 3, 4 or 8, got {bits}")
     spec = {}
     for proj in PROJECTIONS:
         out_dim, in_dim = (hidden, inter) if proj == "down_proj" else (inter, hidden)
-        if in_dim % group_size:
-            raise ValueError(f"{proj}: in={in_dim} is not a multiple of group_size={group_size}")
+        if in_dim % group_size or (in_dim * bits) % 32:
+            raise ValueError(f"{proj}: in={in_dim} is not a multiple of group_size={group_size} "
+                             f"or does not fill whole words at {bits} bits")
         words = in_dim * bits // 32
         groups = in_dim // group_size
         spec[proj] = {
@@ -73,6 +74,8 @@ class Layout:
     weight_off: tuple
     scales_off: tuple
     biases_off: tuple
+    source_bits: int = 0        # bits of the stored codes when admission widens them (3), else 0
+    source_bytes: int = 0       # one stored expert's bytes when they differ from the slot's
 
     @property
     def scale_code(self) -> int:
@@ -94,8 +97,20 @@ def layout_from_spec(spec: dict, quant: dict | None = None, slot_align: int = 25
     if q.get("mode", "affine") != "affine":
         raise NotImplementedError(f"quant mode {q.get('mode')!r}: only affine is built")
     bits, gs = int(q["bits"]), int(q["group_size"])
+    if bits == 3:
+        # stored as 3-bit code streams, held in HBM widened to 4-bit codes (lossless: the
+        # same q, scales and biases); the slot layout is the 4-bit one
+        gw = spec["gate_proj"]["weight"]["shape"]
+        inter, hidden = gw[0], gw[1] * 32 // 3
+        sd = spec["gate_proj"]["scales"]["dtype"]
+        wide = layout_from_spec(make_spec(hidden, inter, 4, gs, sd),
+                                {"bits": 4, "group_size": gs, "mode": "affine"}, slot_align)
+        if make_spec(hidden, inter, 3, gs, sd) != spec:
+            raise ValueError("a 3-bit spec whose shapes or order are not gate, up, down of "
+                             "weight, scales, biases")
+        return dataclasses.replace(wide, source_bits=3, source_bytes=bytes_per_expert(spec))
     if bits not in (4, 8):
-        raise NotImplementedError(f"{bits}-bit experts: only 4- and 8-bit affine codes are built")
+        raise NotImplementedError(f"{bits}-bit experts: 3-, 4- and 8-bit affine codes are built")
     gw = spec["gate_proj"]["weight"]["shape"]
     dw = spec["down_proj"]["weight"]["shape"]
     inter, hidden = gw[0], gw[1] * 32 // bits

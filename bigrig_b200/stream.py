@@ -107,6 +107,8 @@ class ExpertPool(SlotTable):
         self._reads_done = None      # event: the last kernel that read the slab has finished
         self._batch = None           # slot writes collected by ensure(), issued in one call
         self._g2s_dev = None
+        self._widen = self.layout.source_bits == 3   # 3-bit codes widened into 4-bit slots
+        self._landing = None
         self.admit_seconds = 0.0
         self.admit_bytes = 0
         # staging: experts the previous layer predicted for this one, copied ahead of need
@@ -280,13 +282,14 @@ class ExpertPool(SlotTable):
         return slot
 
     def _write_slot(self, slot: int, src: torch.Tensor) -> None:
-        n = self.layout.bytes_per_expert
-        dst = self.slab[slot, :n]
+        n = self._bpe
         if self.device.type != "cuda":
-            dst.copy_(src.reshape(-1))
+            # host-side bookkeeping pools (tests): the stored bytes as they come
+            self.slab[slot, :n].copy_(src.reshape(-1))
             return
+        dst = self._landing_row(slot) if self._widen else self.slab[slot, :n]
         if self._batch is not None:
-            self._batch.append((dst, src.reshape(-1)))
+            self._batch.append((dst, src.reshape(-1), slot))
             return
         cs = self._copy_stream
         if self._reads_done is not None:
@@ -295,10 +298,28 @@ class ExpertPool(SlotTable):
             dst.copy_(src.reshape(-1), non_blocking=True)
             if src.device.type == "cuda":
                 src.record_stream(cs)
+        if self._widen:
+            self._widen_slots([slot], cs)
         if self._copies_done is None:
             self._copies_done = torch.cuda.Event()
         self._copies_done.record(cs)
         self.admit_bytes += n
+
+    def _landing_row(self, slot: int) -> torch.Tensor:
+        """Device landing bytes of ``slot`` for experts stored in fewer bits than the slot
+        holds (3-bit): they arrive here and are widened into the slot."""
+        if self._landing is None:
+            self._landing = torch.empty((self.capacity, self._bpe), dtype=torch.uint8,
+                                        device=self.device)
+        return self._landing[slot]
+
+    def _widen_slots(self, slots, stream) -> None:
+        lib = _lib.load()
+        lp = ctypes.pointer(ops.c_layout(self.layout))
+        st = ctypes.c_void_p(stream.cuda_stream)
+        for slot in slots:
+            _call(lib.bigrig_widen_expert(self._landing[slot].data_ptr(), self.slab[slot].data_ptr(),
+                                          lp, self.layout.source_bits, st), "widen_expert")
 
     def _begin_writes(self) -> None:
         """Collect the slot writes of the admissions that follow (one decode step's)."""
@@ -317,14 +338,16 @@ class ExpertPool(SlotTable):
         if self._reads_done is not None:
             cs.wait_event(self._reads_done)     # a kernel may still be reading these slots
         n = len(batch)
-        dst = (ctypes.c_void_p * n)(*[d.data_ptr() for d, _ in batch])
-        src = (ctypes.c_void_p * n)(*[t.data_ptr() for _, t in batch])
-        size = (ctypes.c_size_t * n)(*[d.numel() for d, _ in batch])
+        dst = (ctypes.c_void_p * n)(*[d.data_ptr() for d, _, _ in batch])
+        src = (ctypes.c_void_p * n)(*[t.data_ptr() for _, t, _ in batch])
+        size = (ctypes.c_size_t * n)(*[d.numel() for d, _, _ in batch])
         _lib.check(_lib.load().bigrig_copy_regions(dst, src, size, n,
                                                    ctypes.c_void_p(cs.cuda_stream)),
                    "copy_regions")
+        if self._widen:
+            self._widen_slots([slot for _, _, slot in batch], cs)
         stage = self._stage_buf
-        for _, t in batch:
+        for _, t, _ in batch:
             # device sources other than the pool's own staging buffers (which live as long
             # as the pool) must outlive the copy
             if t.device.type == "cuda" and (stage is None or t._base is not stage):
@@ -332,7 +355,7 @@ class ExpertPool(SlotTable):
         if self._copies_done is None:
             self._copies_done = torch.cuda.Event()
         self._copies_done.record(cs)
-        self.admit_bytes += sum(d.numel() for d, _ in batch)
+        self.admit_bytes += sum(d.numel() for d, _, _ in batch)
 
     def ready(self, stream: torch.cuda.Stream | None = None) -> None:
         """Order ``stream`` (default: current) after every admission queued so far.

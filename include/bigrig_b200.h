@@ -211,6 +211,17 @@ BIGRIG_API int bigrig_moe_layer_routed(const void* x, const int32_t* indices, co
                                        void* out, void* workspace, size_t workspace_bytes,
                                        void* stream);
 
+/* Admission of a 3-bit expert: `src` (device) holds its packed bytes as the blob stores
+ * them -- per projection (gate, up, down) the 3-bit code stream of each row, scales,
+ * biases -- and `dst` receives the same expert in the 4-bit layout `layout` describes
+ * (layout->bits == 4), each code widened (q in [0, 7] is a 4-bit code with the same
+ * scale and bias, so dequantised weights are unchanged).  Runs on `stream`; src and dst
+ * must not overlap.  Replaces the 3-bit slot write of ExpertPool.admit / build_arrays
+ * (stream.py:692-780) for the quantisation the blob's manifest records
+ * (stream.py:144-151). */
+BIGRIG_API int bigrig_widen_expert(const void* src, void* dst, const bigrig_expert_layout* layout,
+                                   int src_bits, void* stream);
+
 /* Test hook for the failure path of the persistent one-token kernel: its grid barrier
  * also waits for `phantom_ctas` CTAs that do not exist, and every bounded wait polls at
  * most `spin_limit` times (0: the default, about half a second).  With phantom_ctas > 0

@@ -8,8 +8,13 @@ data/blobs/OLMoE-1B-7B-0125-4bit.experts.manifest.json gives gate_proj weight
   consecutive input elements per output row.
 * Each group stores an unsigned code ``q`` in ``[0, 2**bits - 1]`` per element,
   one ``scale`` and one ``bias`` (fp16 or bf16), and ``w = scale * q + bias``.
-* Codes are packed little-endian into uint32 words: element ``j`` of a word sits
-  at bits ``[j*bits, (j+1)*bits)``; 8 codes a word at 4 bits, 4 at 8 bits.
+* Codes are packed as one little-endian bit stream per row: element ``j`` of a row
+  sits at bits ``[j*bits, (j+1)*bits)`` of the row's uint32 words read as a
+  little-endian stream.  At 4 and 8 bits that is 8 and 4 codes a word; at 3 bits a
+  row of ``in`` codes is ``in*3/32`` words and codes straddle words (the shipped
+  Qwen3-30B-A3B-3bit manifest gives gate_proj weight [768, 192] for in=2048).  The
+  3-bit stream order is this restatement's reading of that layout: no reference
+  test or fixture pins it, and MLX is not available to run.
 
 Half-precision values are carried as raw uint16 bit patterns so that bf16 (no
 numpy dtype) and fp16 take the same path.
@@ -75,27 +80,31 @@ def codes_per_word(bits: int) -> int:
     return 32 // bits
 
 
+SUPPORTED_BITS = (3, 4, 8)
+
+
 def pack_codes(q: np.ndarray, bits: int) -> np.ndarray:
-    """[out, in] codes -> [out, in*bits/32] uint32, little-endian within a word."""
+    """[out, in] codes -> [out, in*bits/32] uint32, one little-endian bit stream per row."""
+    if bits not in SUPPORTED_BITS:
+        raise ValueError(f"bits must be one of {SUPPORTED_BITS}, got {bits}")
     q = np.asarray(q, dtype=np.uint32)
-    per = codes_per_word(bits)
     out_dim, in_dim = q.shape
-    if in_dim % per:
-        raise ValueError(f"in={in_dim} is not a multiple of {per}")
-    q = q.reshape(out_dim, in_dim // per, per)
-    words = np.zeros((out_dim, in_dim // per), dtype=np.uint32)
-    for j in range(per):
-        words |= q[:, :, j] << np.uint32(j * bits)
-    return words
+    if (in_dim * bits) % 32:
+        raise ValueError(f"in={in_dim} codes of {bits} bits do not fill whole 32-bit words")
+    planes = ((q[:, :, None] >> np.arange(bits, dtype=np.uint32)) & 1).astype(np.uint8)
+    stream = np.packbits(planes.reshape(out_dim, in_dim * bits), axis=1, bitorder="little")
+    return np.ascontiguousarray(stream).view("<u4").astype(np.uint32)
 
 
 def unpack_codes(words: np.ndarray, bits: int) -> np.ndarray:
-    """[out, in*bits/32] uint32 -> [out, in] uint32 codes."""
-    words = np.asarray(words, dtype=np.uint32)
-    per = codes_per_word(bits)
-    mask = np.uint32((1 << bits) - 1)
-    parts = [(words >> np.uint32(j * bits)) & mask for j in range(per)]
-    return np.stack(parts, axis=-1).reshape(words.shape[0], words.shape[1] * per)
+    """[out, in*bits/32] uint32 -> [out, in] uint32 codes (the inverse of pack_codes)."""
+    if bits not in SUPPORTED_BITS:
+        raise ValueError(f"bits must be one of {SUPPORTED_BITS}, got {bits}")
+    words = np.ascontiguousarray(np.asarray(words, dtype=np.uint32).astype("<u4"))
+    out_dim = words.shape[0]
+    planes = np.unpackbits(words.view(np.uint8).reshape(out_dim, -1), axis=1, bitorder="little")
+    planes = planes.reshape(out_dim, -1, bits).astype(np.uint32)
+    return (planes << np.arange(bits, dtype=np.uint32)).sum(axis=-1, dtype=np.uint32)
 
 
 # ----------------------------------------------------------------- quantise / dequantise

@@ -134,10 +134,20 @@ def test_spec_matches_shipped_manifests():
     assert (L.hidden, L.inter, L.bits) == (2048, 1024, 4)
     assert L.weight_off == (0, 1179648, 2359296)
     assert L.scales_off == (1048576, 2228224, 3407872)
-    # the 3-bit manifest is a format this build does not compute
+    # the 3-bit manifest: its spec is make_spec's at 3 bits, and the layout the kernels
+    # read is the widened 4-bit one, fed from the 3-bit bytes the blob stores
     q3 = m["Qwen3-30B-A3B-3bit"]["layer0"]
-    with pytest.raises((NotImplementedError, ValueError)):
-        formats.layout_from_spec(q3["spec"], q3["quant"])
+    spec3 = formats.make_spec(2048, 768, 3, 64, "bfloat16")
+    assert spec3 == q3["spec"]
+    assert formats.bytes_per_expert(spec3) == q3["bytes_per_expert"]
+    L3 = formats.layout_from_spec(q3["spec"], q3["quant"])
+    assert (L3.bits, L3.source_bits, L3.source_bytes) == (4, 3, q3["bytes_per_expert"])
+    L4 = formats.layout_from_spec(formats.make_spec(2048, 768, 4, 64, "bfloat16"),
+                                  {"bits": 4, "group_size": 64, "mode": "affine"})
+    assert (L3.weight_off, L3.scales_off, L3.slot_stride) == (L4.weight_off, L4.scales_off, L4.slot_stride)
+    with pytest.raises(NotImplementedError):
+        formats.layout_from_spec(formats.make_spec(2048, 768, 4, 64, "bfloat16"),
+                                 {"bits": 2, "group_size": 64, "mode": "affine"})
 
 
 def test_pack_unpack_expert_roundtrip():
@@ -154,3 +164,22 @@ def test_pack_unpack_expert_roundtrip():
             np.testing.assert_array_equal(back[p][c], arrays[p][c])
     with pytest.raises(ValueError):
         formats.unpack_expert(blob[:-1], spec)
+
+
+def test_three_bit_codes_straddle_words():
+    """3-bit codes as one little-endian bit stream per row: 32 codes fill 3 words, code
+    10 spans bits 30-32 (words 0 and 1), and packing inverts unpacking."""
+    q = np.zeros((1, 32), dtype=np.uint32)
+    q[0, 10] = 0b101                                   # bits 30, 32
+    w = affine.pack_codes(q, 3)
+    assert w.shape == (1, 3)
+    assert int(w[0, 0]) == 1 << 30 and int(w[0, 1]) == 1 and int(w[0, 2]) == 0
+    rng = np.random.default_rng(9)
+    q = rng.integers(0, 8, size=(7, 128)).astype(np.uint32)
+    assert np.array_equal(affine.unpack_codes(affine.pack_codes(q, 3), 3), q)
+    # a 3-bit code is the same 4-bit code: widening repacks without changing a weight
+    w3 = rng.standard_normal((4, 128)).astype(np.float32) * 0.02
+    c3, s, b = affine.quantize(w3, 64, 3, "bfloat16")
+    c4 = affine.pack_codes(affine.unpack_codes(c3, 3), 4)
+    assert np.array_equal(affine.dequantize(c3, s, b, 64, 3, "bfloat16"),
+                          affine.dequantize(c4, s, b, 64, 4, "bfloat16"))
