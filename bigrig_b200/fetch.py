@@ -56,6 +56,20 @@ class HostExpertStore:
                     raise IOError(f"short read of {li}:{e}: {buf} of {n} bytes")
         return store
 
+    @classmethod
+    def from_direct(cls, model_dir_or_manifest, pin: bool = True) -> "HostExpertStore":
+        """Load a model's experts straight from its safetensors shards (bigrig_engine/direct.py
+        ``store``): ``model_dir_or_manifest`` is the model folder or ``direct.expert_manifest``'s
+        result.  Each stacked component tensor is read once and scattered into place."""
+        from . import direct
+        man = (model_dir_or_manifest if isinstance(model_dir_or_manifest, dict)
+               else direct.expert_manifest(model_dir_or_manifest))
+        layers = {int(li): (int(info["n_experts"]), int(info["bytes_per_expert"]))
+                  for li, info in man["layers"].items()}
+        store = cls(layers, pin=pin)
+        direct.fill_store(store, man)
+        return store
+
     def put(self, layer: int, e: int, blob) -> None:
         """Write one expert's packed bytes (length-checked) into the store."""
         dst = self.layers[int(layer)][int(e)]
