@@ -33,8 +33,8 @@ EXPORTS = (
 NOALLOC_SCRATCH_BYTES = 4 << 20
 KERNELS = {"router_logits": 0, "router_topk": 1, "permute": 2, "gate_up": 3, "down": 4,
            "combine": 5, "dequant": 6, "gemm_gate_up": 7, "gemm_down": 8, "route": 9,
-           "down_combine": 10, "decode_layer": 11}
-PATHS = {"auto": 0, "gemv": 1, "gemm": 2, "chain": 3}
+           "down_combine": 10, "decode_layer": 11, "decode_split": 12}
+PATHS = {"auto": 0, "gemv": 1, "gemm": 2, "chain": 3, "tiled": 4}
 
 
 class ExpertLayout(ctypes.Structure):
@@ -42,9 +42,10 @@ class ExpertLayout(ctypes.Structure):
     _fields_ = [
         ("hidden", ctypes.c_int32), ("inter", ctypes.c_int32), ("bits", ctypes.c_int32),
         ("group_size", ctypes.c_int32), ("scale_dtype", ctypes.c_int32),
-        ("reserved", ctypes.c_int32), ("bytes_per_expert", ctypes.c_int64),
+        ("flags", ctypes.c_int32), ("bytes_per_expert", ctypes.c_int64),
         ("slot_stride", ctypes.c_int64), ("weight_off", ctypes.c_int64 * 3),
         ("scales_off", ctypes.c_int64 * 3), ("biases_off", ctypes.c_int64 * 3),
+        ("bias_off", ctypes.c_int64 * 3),
     ]
 
 

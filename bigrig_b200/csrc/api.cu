@@ -57,7 +57,8 @@ const char* kKernelNames[BIGRIG_K_COUNT] = {
     "router_logits_kernel", "router_topk_kernel", "permute_kernel",
     "gemv_gate_up_kernel",  "gemv_down_kernel",   "combine_kernel",
     "dequant_kernel",       "grouped_gemm_kernel<gate_up>", "grouped_gemm_kernel<down>",
-    "route_kernel",         "down_combine_kernel", "decode_layer_kernel"};
+    "route_kernel",         "down_combine_kernel", "decode_layer_kernel",
+    "decode_split_kernel"};
 std::atomic<int> g_path{BIGRIG_PATH_AUTO};
 std::atomic<int> g_gemm_min_rows{8};
 constexpr int kDecodePairs = 32;     // routed pairs the fused decode chain / GEMV path takes
@@ -108,6 +109,7 @@ struct Workspace {
   uint64_t* arrivals; // grid-barrier arrivals of the persistent decode kernel over all its
                       // launches on this workspace (err[4..5]); its launch index is this / G
   uint64_t* tagged;   // [E] the persistent decode kernel's logits, tagged with the epoch
+  float* ypart;       // [k * I / 64, H] the split one-token kernel's unit partials (T == 1)
 };
 
 size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Workspace* w) {
@@ -133,6 +135,7 @@ size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Wor
   ws.scores = static_cast<float*>(take(P * sizeof(float)));
   ws.logits = static_cast<float*>(take(static_cast<size_t>(T) * E * sizeof(float)));
   ws.tagged = static_cast<uint64_t*>(take(static_cast<size_t>(E) * sizeof(uint64_t)));
+  ws.ypart = static_cast<float*>(take(T == 1 ? decode_split_scratch(L, k) : 0));
   // the fused route's ticket lives at a fixed place -- word 3 of the error words -- so a
   // call of any shape finds it where the previous call left it, back at zero
   ws.ticket = ws.err ? ws.err + 3 : nullptr;
@@ -157,17 +160,32 @@ int check_layout(const bigrig_expert_layout* Lp) {
   if (L.slot_stride < L.bytes_per_expert || L.slot_stride % 16)
     return set_error(BIGRIG_ERR_INVALID, "slot_stride=%lld must be >= bytes_per_expert=%lld "
                      "and a multiple of 16", (long long)L.slot_stride, (long long)L.bytes_per_expert);
+  const int known = BIGRIG_LAYOUT_PLAIN | BIGRIG_LAYOUT_BIAS | (3 << 2) | (15 << 8);
+  if (L.flags & ~known) return set_error(BIGRIG_ERR_INVALID, "flags=0x%x: unknown bits", L.flags);
+  const bool plain = L.flags & BIGRIG_LAYOUT_PLAIN, bias = L.flags & BIGRIG_LAYOUT_BIAS;
+  const int act = BIGRIG_LAYOUT_ACT(L.flags);
+  if (plain ? (act != BIGRIG_ACT_SILU && act != BIGRIG_ACT_RELU2)
+            : (act != BIGRIG_ACT_SILU && act != BIGRIG_ACT_GPT_OSS))
+    return set_error(BIGRIG_ERR_UNSUPPORTED, "activation %d is not built for the %s expert", act,
+                     plain ? "plain fc1/fc2" : "gated");
+  const int bdt = BIGRIG_LAYOUT_BIAS_DTYPE(L.flags);
+  if (!bias && bdt != 0)
+    return set_error(BIGRIG_ERR_INVALID, "a bias dtype without BIGRIG_LAYOUT_BIAS");
+  const int64_t bias_elem = bdt == BIGRIG_F32 ? 4 : 2;
   for (int p = 0; p < 3; ++p) {
+    if (plain && p == 1) continue;             // fc1 at 0, fc2 at 2
     const int64_t rows = p == 2 ? L.hidden : L.inter;
     const int64_t cols = p == 2 ? L.inter : L.hidden;
     const int64_t wbytes = rows * cols * L.bits / 8;
     const int64_t sbytes = rows * (cols / L.group_size) * 2;
-    if (L.weight_off[p] % 16 || L.scales_off[p] % 16 || L.biases_off[p] % 16)
+    if (L.weight_off[p] % 16 || L.scales_off[p] % 16 || L.biases_off[p] % 16 ||
+        (bias && L.bias_off[p] % 16))
       return set_error(BIGRIG_ERR_INVALID, "projection %d: weight, scale and bias offsets must "
                        "be 16-byte aligned", p);
     if (L.weight_off[p] < 0 || L.weight_off[p] + wbytes > L.bytes_per_expert ||
         L.scales_off[p] < 0 || L.scales_off[p] + sbytes > L.bytes_per_expert ||
-        L.biases_off[p] < 0 || L.biases_off[p] + sbytes > L.bytes_per_expert)
+        L.biases_off[p] < 0 || L.biases_off[p] + sbytes > L.bytes_per_expert ||
+        (bias && (L.bias_off[p] < 0 || L.bias_off[p] + rows * bias_elem > L.bytes_per_expert)))
       return set_error(BIGRIG_ERR_INVALID, "projection %d lies outside the %lld-byte expert", p,
                        (long long)L.bytes_per_expert);
   }
@@ -233,7 +251,8 @@ int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, c
   // dequant streams weights far faster than the GEMV's passes over an expert's rows, even
   // at 16-column MMAs), or when the mean rows per routed expert reaches gemm_min_rows.
   const bool gemm = path == BIGRIG_PATH_GEMM ||
-                    ((path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_CHAIN) &&
+                    ((path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_CHAIN ||
+                      path == BIGRIG_PATH_TILED) &&
                      (P > kDecodePairs || P >= g_gemm_min_rows.load() * (P < E ? P : E)));
   if (gemm) {
     const int mean = gemm_mean_rows(T, k, E);
@@ -267,7 +286,8 @@ int bigrig_dequant(const void* slab, const bigrig_expert_layout* layout, int slo
   if (int rc = check_layout(layout)) return rc;
   if (!slab || !out) return set_error(BIGRIG_ERR_INVALID, "dequant: NULL pointer");
   if (slot < 0) return set_error(BIGRIG_ERR_INVALID, "dequant: slot=%d < 0", slot);
-  if (proj < 0 || proj > 2) return set_error(BIGRIG_ERR_INVALID, "dequant: proj=%d", proj);
+  if (proj < 0 || proj > 2 || (proj == 1 && (layout->flags & BIGRIG_LAYOUT_PLAIN)))
+    return set_error(BIGRIG_ERR_INVALID, "dequant: proj=%d (a plain expert has 0 and 2)", proj);
   return launch_dequant(slab, *layout, slot, proj, out, static_cast<cudaStream_t>(stream));
 }
 
@@ -393,8 +413,12 @@ int bigrig_moe_layer(const void* x, const void* gate_w, const float* gate_b, int
   int32_t* idx = indices_out ? indices_out : ws.indices;
   float* sc = scores_out ? scores_out : ws.scores;
   const int path = g_path.load();
-  if (T == 1 && (path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_GEMV) &&
-      decode_layer_fits(*layout, k, E))
+  const bool one = T == 1 && (path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_GEMV);
+  if (one && decode_split_fits(*layout, k, E))
+    return launch_decode_split(x, gate_w, gate_b, E, k, mode, norm_topk, g2s, slab, *layout,
+                               residual, out, idx, sc, ws.ypart, ws.tagged, ws.arrivals, ws.err, s,
+                               nullptr, nullptr);
+  if ((one || (T == 1 && path == BIGRIG_PATH_TILED)) && decode_layer_fits(*layout, k, E))
     return launch_decode_layer(x, gate_w, gate_b, E, k, mode, norm_topk, g2s, slab, *layout,
                                residual, out, idx, sc, ws.h, ws.tagged, ws.arrivals, ws.err, s);
   if (fused_decode(T, k, *layout))
@@ -428,8 +452,13 @@ int bigrig_moe_layer_routed(const void* x, const int32_t* indices, const float* 
   carve(workspace, T, k, E, *layout, &ws);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int path = g_path.load();
-  if (T == 1 && (path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_GEMV) &&
-      decode_layer_fits(*layout, k, E))
+  const bool one = T == 1 && (path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_GEMV);
+  if (one && decode_split_fits(*layout, k, E))
+    return launch_decode_split(x, nullptr, nullptr, E, k, BIGRIG_SOFTMAX_TOPK, 0, g2s, slab,
+                               *layout, residual, out, const_cast<int32_t*>(indices),
+                               const_cast<float*>(scores), ws.ypart, ws.tagged, ws.arrivals,
+                               ws.err, s, indices, scores);
+  if ((one || (T == 1 && path == BIGRIG_PATH_TILED)) && decode_layer_fits(*layout, k, E))
     return launch_decode_layer(x, nullptr, nullptr, E, k, BIGRIG_SOFTMAX_TOPK, 0, g2s, slab,
                                *layout, residual, out, const_cast<int32_t*>(indices),
                                const_cast<float*>(scores), ws.h, ws.tagged, ws.arrivals, ws.err, s,
@@ -442,6 +471,9 @@ int bigrig_widen_expert(const void* src, void* dst, const bigrig_expert_layout* 
                         int src_bits, void* stream) {
   if (int rc = check_layout(layout)) return rc;
   if (!src || !dst) return set_error(BIGRIG_ERR_INVALID, "widen_expert: NULL pointer");
+  if (layout->flags != 0)
+    return set_error(BIGRIG_ERR_UNSUPPORTED, "widen_expert: 3-bit codes of the gated SwiGLU "
+                     "expert without projection biases only");
   if (src_bits != 3 || layout->bits != 4)
     return set_error(BIGRIG_ERR_UNSUPPORTED, "widen_expert: %d-bit codes into a %d-bit layout "
                      "(only 3 -> 4 is built)", src_bits, layout->bits);
@@ -460,7 +492,7 @@ int bigrig_test_grid_barrier(int phantom_ctas, unsigned int spin_limit) {
 }
 
 int bigrig_set_path(int mode, int gemm_min_rows) {
-  if (mode < BIGRIG_PATH_AUTO || mode > BIGRIG_PATH_CHAIN || gemm_min_rows < 1)
+  if (mode < BIGRIG_PATH_AUTO || mode > BIGRIG_PATH_TILED || gemm_min_rows < 1)
     return set_error(BIGRIG_ERR_INVALID, "set_path: mode=%d gemm_min_rows=%d", mode, gemm_min_rows);
   const int prev = g_path.exchange(mode);
   g_gemm_min_rows.store(gemm_min_rows);

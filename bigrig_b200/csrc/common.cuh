@@ -79,6 +79,40 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
 
+// The activation of a gated expert (BIGRIG_LAYOUT_ACT of the layout's flags) from its
+// fp32 gate and up outputs: SwiGLU, or gpt-oss's clamped form
+// g' = min(g, 7), u' = clamp(u, -7, 7), g' sigmoid(1.702 g') (u' + 1).
+__device__ __forceinline__ float act_gated(float g, float u, int act) {
+  if (act == BIGRIG_ACT_GPT_OSS) {
+    g = fminf(g, 7.0f);
+    u = fminf(fmaxf(u, -7.0f), 7.0f);
+    return g / (1.0f + expf(-1.702f * g)) * (u + 1.0f);
+  }
+  return silu_f32(g) * u;
+}
+
+// The activation of a plain fc1/fc2 expert from its fp32 fc1 output.
+__device__ __forceinline__ float act_plain(float h, int act) {
+  if (act == BIGRIG_ACT_RELU2) {
+    h = fmaxf(h, 0.0f);
+    return h * h;
+  }
+  return silu_f32(h);
+}
+
+// Element f of projection p's affine bias in the expert at `base` (BIGRIG_LAYOUT_BIAS),
+// as fp32; 0 when the layout carries none.
+__device__ __forceinline__ float proj_bias(const uint8_t* base, const bigrig_expert_layout& L,
+                                           int p, int f) {
+  if (!(L.flags & BIGRIG_LAYOUT_BIAS)) return 0.0f;
+  const uint8_t* b = base + L.bias_off[p];
+  switch (BIGRIG_LAYOUT_BIAS_DTYPE(L.flags)) {
+    case BIGRIG_F16: return f16_bits_to_f32(reinterpret_cast<const uint16_t*>(b)[f]);
+    case BIGRIG_BF16: return bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(b)[f]);
+    default: return reinterpret_cast<const float*>(b)[f];
+  }
+}
+
 // ------------------------------------------------------------------ mbarrier + bulk copy
 // Non-tensor bulk copies (cp.async.bulk, no multicast) from global into this CTA's shared
 // memory, completed through an mbarrier's transaction count.  Every wait is bounded.

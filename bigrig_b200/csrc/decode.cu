@@ -213,12 +213,14 @@ __global__ void __launch_bounds__(kGemvWarps * 32) down_combine_kernel(
             }
           }
         }
+        const uint8_t* sbase = slab + static_cast<int64_t>(seg_slot[s]) * L.slot_stride;
 #pragma unroll
         for (int i = 0; i < NR; ++i) {
+          const float bd = proj_bias(sbase, L, 2, f0 + warp * NR + i);
 #pragma unroll
           for (int rr = 0; rr < ROWS; ++rr) {
             if (r0 + rr < rb) {
-              const float v = warp_sum(acc[i][rr]);
+              const float v = warp_sum(acc[i][rr]) + bd;
               if (lane == 0) ybuf[(r0 + rr) * NF + warp * NR + i] = bf16_round(v);
             }
           }

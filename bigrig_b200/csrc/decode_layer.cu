@@ -944,6 +944,8 @@ struct DlPlan {
 // ring of two stages.
 bool decode_layer_plan(const bigrig_expert_layout& L, int k, int E, int G, DlPlan* p) {
   if (G <= 0 || k > 32 || E > kMaxExperts || L.group_size != kDlGroup) return false;
+  if (L.flags != 0) return false;   // gated SwiGLU without projection biases only: the
+                                    // other shapes take the three-kernel chain
   if (L.hidden % kDlGroup || L.inter % kDlGroup || L.hidden % kDlFeatDown) return false;
   const int kb_k = L.bits == 4 ? 128 : 64, steps = L.bits == 4 ? 8 : 4;
   const int max_slice = L.bits == 4 ? kDlMaxSliceBlocks<4> : kDlMaxSliceBlocks<8>;

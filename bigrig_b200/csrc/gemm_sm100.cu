@@ -557,7 +557,8 @@ __device__ unsigned long long g_gemm_prof[64];      // [MODE][32]
 #endif
 
 // ------------------------------------------------------------------ the kernel
-// MODE 0: gate/up (two weight matrices, output h); MODE 1: down (one matrix, output y).
+// MODE 0: gate/up (two weight matrices, output h); MODE 1: down (one matrix, output y);
+// MODE 2: a plain expert's fc1 (one matrix over the hidden dimension, output h).
 // tm_code0/1: the codes of projection gate/up (MODE 0) or down (tm_code0, MODE 1) over
 // the slab as [slot][row][byte]; tm_act: the token operand [P rows][K] (expert-sorted).
 template <int MODE, int BN, int BITS, int SDT>
@@ -597,8 +598,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
   int* tile_start = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_base_s + 2));  // [nseg+1]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int K = MODE == 0 ? L.hidden : L.inter;        // reduction length
-  const int NF = MODE == 0 ? L.inter : L.hidden;       // output features
+  const int K = MODE != 1 ? L.hidden : L.inter;        // reduction length
+  const int NF = MODE != 1 ? L.inter : L.hidden;       // output features
   const int m_tiles = (NF + kBlockM - 1) / kBlockM;
   const int k_steps = K / kBlockK;                     // 64-element K steps
   const int k_iters = (k_steps + KS - 1) / KS;         // iterations (slots) per tile
@@ -814,15 +815,20 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
       const int f = t.m0 + eq * 32 + lane;
       const bool fok = f < NF;
       // the 4-bit down pass reads h as its K-permuted token operand
-      const int fcol = BITS == 4 && MODE == 0 ? (f & ~7) | k8_slot(f & 7) : f;
+      const int fcol = BITS == 4 && MODE != 1 ? (f & ~7) | k8_slot(f & 7) : f;
+      // the projection biases of this lane's feature (BIGRIG_LAYOUT_BIAS), and the activation
+      const uint8_t* ebase = slab + static_cast<int64_t>(t.slot >= 0 ? t.slot : 0) * L.slot_stride;
+      const float bias0 = fok ? proj_bias(ebase, L, MODE == 1 ? 2 : 0, f) : 0.f;
+      const float bias1 = MODE == 0 && fok ? proj_bias(ebase, L, 1, f) : 0.f;
+      const int act = BIGRIG_LAYOUT_ACT(L.flags);
       const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(eq * 32) << 16) + buf * G::ACC_COLS;
       const int prow = t.row0 + t.n0;            // sorted row of token column 0
       // MODE 1 scatters column c to output row order[prow + c]: lanes 0-15 hold the 16
       // rows of a column group, loaded one group ahead
       int ord_next = 0;
       if (MODE == 1 && eh * 16 + lane < t.rows && lane < 16) ord_next = rv.order[prow + eh * 16 + lane];
-      if constexpr (MODE == 0) {
-        // gate/up: h for all of this warp's column groups first, kept as packed 16-bit
+      if constexpr (MODE != 1) {
+        // gate/up (fc1): h for all of this warp's column groups first, kept as packed 16-bit
         // pairs in registers, so that the accumulator goes back to the MMA before any
         // global store (with one accumulator buffer the next tile's MMAs wait for it)
         constexpr int NG = (BN / 16 + 1) / 2;   // 16-column groups per warp (every other)
@@ -833,12 +839,21 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
           if (j0 < t.rows) {
             uint32_t a[16], u[16];
             tmem_ld16_nowait(lane_addr + j0, a);
-            tmem_ld16_nowait(lane_addr + BN + j0, u);
+            if constexpr (MODE == 0) tmem_ld16_nowait(lane_addr + BN + j0, u);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 16; i += 2) {
-              const float h0 = silu_fast(__uint_as_float(a[i])) * __uint_as_float(u[i]);
-              const float h1 = silu_fast(__uint_as_float(a[i + 1])) * __uint_as_float(u[i + 1]);
+              float h0, h1;
+              if constexpr (MODE == 2) {
+                h0 = act_plain(__uint_as_float(a[i]) + bias0, act);
+                h1 = act_plain(__uint_as_float(a[i + 1]) + bias0, act);
+              } else if (L.flags == 0) {
+                h0 = silu_fast(__uint_as_float(a[i])) * __uint_as_float(u[i]);
+                h1 = silu_fast(__uint_as_float(a[i + 1])) * __uint_as_float(u[i + 1]);
+              } else {
+                h0 = act_gated(__uint_as_float(a[i]) + bias0, __uint_as_float(u[i]) + bias1, act);
+                h1 = act_gated(__uint_as_float(a[i + 1]) + bias0, __uint_as_float(u[i + 1]) + bias1, act);
+              }
               hp[gi * 8 + i / 2] = OT == BIGRIG_F16 ? pack_f16x2_sat(h0, h1) : pack_bf16x2(h0, h1);
             }
           }
@@ -869,7 +884,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
           for (int i = 0; i < 16; ++i) {
             const int o = __shfl_sync(0xffffffffu, ord, i);
             if (j0 + i < t.rows && fok)
-              out[static_cast<int64_t>(o) * NF + f] = t.slot >= 0 ? bf16_rn(__uint_as_float(a[i])) : uint16_t(0);
+              out[static_cast<int64_t>(o) * NF + f] = t.slot >= 0 ? bf16_rn(__uint_as_float(a[i]) + bias0) : uint16_t(0);
           }
         }
         tc_fence_before();
@@ -1093,7 +1108,7 @@ template <int MODE, int BN, int BITS, int SDT>
 static int launch_one(const void* act, const RouteView& rv, const void* slab,
                       const bigrig_expert_layout& L, void* out, cudaStream_t s, int sms) {
   using G = GemmShape<MODE, BN, BITS>;
-  const int K = MODE == 0 ? L.hidden : L.inter, NF = MODE == 0 ? L.inter : L.hidden;
+  const int K = MODE != 1 ? L.hidden : L.inter, NF = MODE != 1 ? L.inter : L.hidden;
   const int gpitch = K / L.group_size;
   GemmRings rg{0, 0, 0, (G::NMAT * 2 * kBlockM * gpitch * 2 + 127) & ~127};
   // (code slots, scale buffers) from the most buffered; a split token-row ring as deep as
@@ -1111,7 +1126,8 @@ static int launch_one(const void* act, const RouteView& rv, const void* slab,
   const size_t smem = G::smem(rg.rs, rg.sb, rg.nsb, rg.sc_bytes);
 
   CUtensorMap tm[3];
-  const int projs[2] = {MODE == 0 ? 0 : 2, MODE == 0 ? 1 : 2};
+  // gate/up: gate and up; down: down; fc1 (MODE 2, plain experts): projection 0
+  const int projs[2] = {MODE == 1 ? 2 : 0, MODE == 0 ? 1 : MODE == 1 ? 2 : 0};
   for (int i = 0; i < 2; ++i) {
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(K) * BITS / 8, static_cast<cuuint64_t>(NF), kMapSlots};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K) * BITS / 8, static_cast<cuuint64_t>(L.slot_stride)};
@@ -1131,10 +1147,11 @@ static int launch_one(const void* act, const RouteView& rv, const void* slab,
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return set_error(BIGRIG_ERR_CUDA, "grouped_gemm: cannot reserve %zu bytes of smem", smem);
-  TimedLaunch tl(MODE == 0 ? BIGRIG_K_GEMM_GATE_UP : BIGRIG_K_GEMM_DOWN, s);
+  TimedLaunch tl(MODE != 1 ? BIGRIG_K_GEMM_GATE_UP : BIGRIG_K_GEMM_DOWN, s);
   kern<<<sms, kThreads, smem, s>>>(tm[0], tm[1], tm[2], rv, static_cast<const uint8_t*>(slab), L, rg,
                                    static_cast<uint16_t*>(out));
-  return check_launch(MODE == 0 ? "grouped_gemm_gate_up" : "grouped_gemm_down");
+  return check_launch(MODE == 0 ? "grouped_gemm_gate_up" : MODE == 1 ? "grouped_gemm_down"
+                                                                     : "grouped_gemm_fc1");
 }
 
 template <int MODE, int BN>
@@ -1199,7 +1216,20 @@ int launch_gemm_gate_up(const void* x, const RouteView& rv, const void* slab,
     if (int rc = check_launch("gather_rows")) return rc;
   }
   static const int opts[] = {32, 64, 96, 128, 160};
-  for (int i = pick_tile(mean_rows, opts, 5); i >= 0; --i) {
+  const bool plain = L.flags & BIGRIG_LAYOUT_PLAIN;
+  for (int i = pick_tile(mean_rows, opts, 5); i >= 0 && plain; --i) {
+    // a plain expert's fc1: one matrix, h = act(fc1(x) + bias)
+    int rc = sm100::kNoFit;
+    switch (opts[i]) {
+      case 32: rc = sm100::dispatch_fmt<2, 32>(xs, rv, slab, L, h, s, sm_count()); break;
+      case 64: rc = sm100::dispatch_fmt<2, 64>(xs, rv, slab, L, h, s, sm_count()); break;
+      case 96: rc = sm100::dispatch_fmt<2, 96>(xs, rv, slab, L, h, s, sm_count()); break;
+      case 128: rc = sm100::dispatch_fmt<2, 128>(xs, rv, slab, L, h, s, sm_count()); break;
+      case 160: rc = sm100::dispatch_fmt<2, 160>(xs, rv, slab, L, h, s, sm_count()); break;
+    }
+    if (rc != sm100::kNoFit) return rc;
+  }
+  for (int i = pick_tile(mean_rows, opts, 5); i >= 0 && !plain; --i) {
     int rc = sm100::kNoFit;
     switch (opts[i]) {
       case 32: rc = sm100::dispatch_fmt<0, 32>(xs, rv, slab, L, h, s, sm_count()); break;

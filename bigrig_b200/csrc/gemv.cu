@@ -13,11 +13,13 @@
 
 namespace bigrig {
 
+// Gate/up (fc1 of a plain expert: one matrix) staging for nf features and `rows` rows.
 size_t gemv_gate_up_smem(const bigrig_expert_layout& L, int nf, int rows) {
+  const size_t nm = (L.flags & BIGRIG_LAYOUT_PLAIN) ? 1 : 2;
   const size_t pitch = static_cast<size_t>(L.hidden) * L.bits / 8;
   const size_t G = L.hidden / L.group_size;
   const size_t nchunk = L.hidden / (128 / L.bits);
-  return 128 + round128(2 * nf * pitch) + round128(4 * nf * G * 2) +
+  return 128 + round128(nm * nf * pitch) + round128(2 * nm * nf * G * 2) +
          round128(static_cast<size_t>(rows) * L.hidden * 2) +
          round128(static_cast<size_t>(rows) * L.hidden * 4) + round128(rows * nchunk * 4);
 }
@@ -32,7 +34,9 @@ size_t gemv_down_smem(const bigrig_expert_layout& L, int nf, int rows) {
 }
 
 // ------------------------------------------------------------------ gate/up
-template <int BITS, int SDT, int NR, int ROWS>
+// GATED: gate and up rows, h = act(gate, up); else the plain expert's fc1, h = act(fc1).
+// Projection biases (BIGRIG_LAYOUT_BIAS) are added to the fp32 outputs first.
+template <int BITS, int SDT, int NR, int ROWS, bool GATED>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_gate_up_kernel(
     const uint16_t* __restrict__ x, RouteView rv, const uint8_t* __restrict__ slab,
     bigrig_expert_layout L, uint16_t* __restrict__ h, int rows_cap) {
@@ -56,13 +60,14 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_gate_up_kernel(
       h[static_cast<size_t>(row0 + i / NF) * I + f0 + i % NF] = 0;
     return;
   }
+  constexpr int NM = GATED ? 2 : 1;           // weight matrices
   const int64_t pitch = static_cast<int64_t>(H) * BITS / 8;
   const int G = H / L.group_size;
   const int nchunk = H / CPL;
   SmemCarve sc(smem);
   uint64_t* bar = sc.take<uint64_t>(8);
-  uint8_t* wc = sc.take<uint8_t>(2 * NF * pitch);
-  uint16_t* wsb = sc.take<uint16_t>(4 * NF * G * 2);
+  uint8_t* wc = sc.take<uint8_t>(NM * NF * pitch);
+  uint16_t* wsb = sc.take<uint16_t>(2 * NM * NF * G * 2);
   uint16_t* xraw = sc.take<uint16_t>(static_cast<size_t>(rows_cap) * H * 2);
   float* xs = sc.take<float>(static_cast<size_t>(rows_cap) * H * 4);
   float* cs = sc.take<float>(static_cast<size_t>(rows_cap) * nchunk * 4);
@@ -78,10 +83,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_gate_up_kernel(
     const int nr = min(rows_cap, R - r0);
     if (threadIdx.x == 0) {
       uint32_t bytes = static_cast<uint32_t>(nr) * H * 2;
-      if (r0 == 0) bytes += static_cast<uint32_t>(2 * NF * pitch + 4 * NF * G * 2);
+      if (r0 == 0) bytes += static_cast<uint32_t>(NM * NF * pitch + 2 * NM * NF * G * 2);
       bar_expect_tx(bar, bytes);
       if (r0 == 0) {
-        for (int m = 0; m < 2; ++m) {
+        for (int m = 0; m < NM; ++m) {
           bulk_g2s(wc + m * NF * pitch, base + L.weight_off[m] + f0 * pitch, NF * pitch, bar);
           bulk_g2s(wsb + (2 * m) * NF * G, base + L.scales_off[m] + static_cast<int64_t>(f0) * G * 2,
                    NF * G * 2, bar);
@@ -116,11 +121,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_gate_up_kernel(
       for (int i = 0; i < NR; ++i) {
         const int fl = warp * NR + i;
         cg[i] = *reinterpret_cast<const uint4*>(wc + fl * pitch + c * 16);
-        cu[i] = *reinterpret_cast<const uint4*>(wc + (NF + fl) * pitch + c * 16);
         sg[i] = half_to_f32<SDT>(wsb[(0 * NF + fl) * G + grp]);
         bg[i] = half_to_f32<SDT>(wsb[(1 * NF + fl) * G + grp]);
-        su[i] = half_to_f32<SDT>(wsb[(2 * NF + fl) * G + grp]);
-        bu[i] = half_to_f32<SDT>(wsb[(3 * NF + fl) * G + grp]);
+        if constexpr (GATED) {
+          cu[i] = *reinterpret_cast<const uint4*>(wc + (NF + fl) * pitch + c * 16);
+          su[i] = half_to_f32<SDT>(wsb[(2 * NF + fl) * G + grp]);
+          bu[i] = half_to_f32<SDT>(wsb[(3 * NF + fl) * G + grp]);
+        }
       }
 #pragma unroll
       for (int rr = 0; rr < ROWS; ++rr) {
@@ -131,23 +138,29 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_gate_up_kernel(
 #pragma unroll
           for (int i = 0; i < NR; ++i) {
             const float dg = chunk_dot2<BITS>(cg[i], cx);
-            const float du = chunk_dot2<BITS>(cu[i], cx);
             acc[0][i][rr] = fmaf(sg[i], dg, fmaf(bg[i], csum, acc[0][i][rr]));
-            acc[1][i][rr] = fmaf(su[i], du, fmaf(bu[i], csum, acc[1][i][rr]));
+            if constexpr (GATED) {
+              const float du = chunk_dot2<BITS>(cu[i], cx);
+              acc[1][i][rr] = fmaf(su[i], du, fmaf(bu[i], csum, acc[1][i][rr]));
+            }
           }
         }
       }
     }
+    const int act = BIGRIG_LAYOUT_ACT(L.flags);
 #pragma unroll
     for (int i = 0; i < NR; ++i) {
+      const int f = f0 + warp * NR + i;
+      const float bgate = proj_bias(base, L, 0, f);
+      const float bup = GATED ? proj_bias(base, L, 1, f) : 0.f;
 #pragma unroll
       for (int rr = 0; rr < ROWS; ++rr) {
         if (rr < nr) {
-          const float g = warp_sum(acc[0][i][rr]);
-          const float u = warp_sum(acc[1][i][rr]);
+          const float g = warp_sum(acc[0][i][rr]) + bgate;
+          const float u = GATED ? warp_sum(acc[1][i][rr]) + bup : 0.f;
           if (lane == 0)
-            h[static_cast<size_t>(row0 + r0 + rr) * I + f0 + warp * NR + i] =
-                f32_to_bf16_bits(silu_f32(g) * u);
+            h[static_cast<size_t>(row0 + r0 + rr) * I + f] =
+                f32_to_bf16_bits(GATED ? act_gated(g, u, act) : act_plain(g, act));
         }
       }
     }
@@ -252,10 +265,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_down_kernel(
     }
 #pragma unroll
     for (int i = 0; i < NR; ++i) {
+      const float bd = proj_bias(base, L, 2, f0 + warp * NR + i);
 #pragma unroll
       for (int rr = 0; rr < ROWS; ++rr) {
         if (rr < nr) {
-          const float v = warp_sum(acc[i][rr]);
+          const float v = warp_sum(acc[i][rr]) + bd;
           if (lane == 0)
             y[static_cast<size_t>(rv.order[row0 + r0 + rr]) * H + f0 + warp * NR + i] =
                 f32_to_bf16_bits(v);
@@ -349,8 +363,12 @@ static int gate_up_impl(const void* x, const RouteView& rv, const void* slab,
   const dim3 grid(L.inter / nf, rv.s_max);
   TimedLaunch tl(BIGRIG_K_GATE_UP, s);
   const char* n = "gemv_gate_up_kernel";
-#define BIGRIG_GU(NR, RW) \
-  return launch_gemv(gemv_gate_up_kernel<BITS, SDT, NR, RW>, grid, smem, s, n, x, rv, slab, L, h, rows)
+#define BIGRIG_GU(NR, RW)                                                                   \
+  return (L.flags & BIGRIG_LAYOUT_PLAIN)                                                    \
+             ? launch_gemv(gemv_gate_up_kernel<BITS, SDT, NR, RW, false>, grid, smem, s, n, x, \
+                           rv, slab, L, h, rows)                                            \
+             : launch_gemv(gemv_gate_up_kernel<BITS, SDT, NR, RW, true>, grid, smem, s, n, x,  \
+                           rv, slab, L, h, rows)
   if (nf == 16) {
     if (rows == 1) BIGRIG_GU(4, 1);
     if (rows == 2) BIGRIG_GU(4, 2);

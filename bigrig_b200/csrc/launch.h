@@ -95,6 +95,17 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
                         int32_t* idx_out, float* sc_out, void* h, void* tagged, void* arrivals,
                         int32_t* err, cudaStream_t s, const int32_t* pre_idx = nullptr,
                         const float* pre_sc = nullptr);
+// The split one-token layer (decode_split.cu): units of (routed expert, 64-feature group),
+// integer tensor-core dot products, one grid barrier before the combine.  Scratch: ypart,
+// decode_split_scratch(L, k) bytes (no zero-fill needed).
+bool decode_split_fits(const bigrig_expert_layout& L, int k, int E);
+size_t decode_split_scratch(const bigrig_expert_layout& L, int k);
+int launch_decode_split(const void* x, const void* gate_w, const float* gate_b, int E, int k,
+                        int mode, int norm, const int32_t* g2s, const void* slab,
+                        const bigrig_expert_layout& L, const void* residual, void* out,
+                        int32_t* idx_out, float* sc_out, float* ypart, void* tagged,
+                        void* arrivals, int32_t* err, cudaStream_t s, const int32_t* pre_idx,
+                        const float* pre_sc);
 // A 3-bit expert's packed bytes (src, the 4-bit layout with 3-bit code streams) widened
 // into a 4-bit slot laid out by L (L.bits == 4).
 int launch_widen_expert(const void* src, void* dst, const bigrig_expert_layout& L, cudaStream_t s);

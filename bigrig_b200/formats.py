@@ -20,20 +20,30 @@ import os
 import numpy as np
 
 PROJECTIONS = ("gate_proj", "up_proj", "down_proj")
+MLP_PROJECTIONS = ("fc1", "fc2")          # the plain two-layer expert (stream.py:56)
 COMPONENTS = ("weight", "scales", "biases", "bias")
+# the activation ids of the layout flags (BIGRIG_ACT_* in include/bigrig_b200.h)
+ACTIVATIONS = {"silu": 0, "swiglu": 0, "gpt_oss": 1, "relu2": 2}
+FLAG_PLAIN, FLAG_BIAS = 1, 2
+_DTYPE_CODE = {"float32": 0, "float16": 1, "bfloat16": 2}
 _NP = {"uint32": np.uint32, "float16": np.uint16, "bfloat16": np.uint16, "float32": np.float32,
        "uint8": np.uint8}
 _SIZE = {"uint32": 4, "float16": 2, "bfloat16": 2, "float32": 4, "uint8": 1}
 
 
 def make_spec(hidden: int, inter: int, bits: int = 4, group_size: int = 64,
-              scale_dtype: str = "float16") -> dict:
-    """The manifest spec of a gated SwiGLU expert in MLX affine format (3, 4 or 8 bits)."""
+              scale_dtype: str = "float16", *, plain: bool = False, bias: bool = False,
+              bias_dtype: str = "bfloat16", order=None) -> dict:
+    """The manifest spec of an expert in MLX affine format (3, 4 or 8 bits): the gated
+    gate/up/down expert, or with ``plain`` the fc1/fc2 one; ``bias`` adds each
+    projection's affine bias ``[out]`` of ``bias_dtype``; ``order`` lists the components of
+    every projection in the order the bytes are packed (the default: weight, scales,
+    biases, bias)."""
     if bits not in (3, 4, 8):
         raise ValueError(f"bits must be 3, 4 or 8, got {bits}")
     spec = {}
-    for proj in PROJECTIONS:
-        out_dim, in_dim = (hidden, inter) if proj == "down_proj" else (inter, hidden)
+    for proj in (MLP_PROJECTIONS if plain else PROJECTIONS):
+        out_dim, in_dim = (hidden, inter) if proj in ("down_proj", "fc2") else (inter, hidden)
         if in_dim % group_size or (in_dim * bits) % 32:
             raise ValueError(f"{proj}: in={in_dim} is not a multiple of group_size={group_size} "
                              f"or does not fill whole words at {bits} bits")
@@ -44,6 +54,11 @@ def make_spec(hidden: int, inter: int, bits: int = 4, group_size: int = 64,
             "scales": {"shape": [out_dim, groups], "dtype": scale_dtype, "nbytes": out_dim * groups * 2},
             "biases": {"shape": [out_dim, groups], "dtype": scale_dtype, "nbytes": out_dim * groups * 2},
         }
+        if bias:
+            spec[proj]["bias"] = {"shape": [out_dim], "dtype": bias_dtype,
+                                  "nbytes": out_dim * _SIZE[bias_dtype]}
+        if order is not None:
+            spec[proj] = {c: spec[proj][c] for c in order if c in spec[proj]}
     return spec
 
 
@@ -76,33 +91,78 @@ class Layout:
     biases_off: tuple
     source_bits: int = 0        # bits of the stored codes when admission widens them (3), else 0
     source_bytes: int = 0       # one stored expert's bytes when they differ from the slot's
+    flags: int = 0              # FLAG_PLAIN | FLAG_BIAS | bias dtype << 2 | activation << 8
+    bias_off: tuple = (0, 0, 0)
 
     @property
     def scale_code(self) -> int:
         return {"float16": 1, "bfloat16": 2}[self.scale_dtype]
 
+    @property
+    def plain(self) -> bool:
+        return bool(self.flags & FLAG_PLAIN)
+
+    @property
+    def has_bias(self) -> bool:
+        return bool(self.flags & FLAG_BIAS)
+
+    @property
+    def activation(self) -> int:
+        return (self.flags >> 8) & 15
+
+    def with_activation(self, name: str | None) -> "Layout":
+        """This layout computing ``name`` ("silu"/"swiglu", "gpt_oss" for gated experts,
+        "relu2" for plain ones; None: SiLU)."""
+        act = ACTIVATIONS.get(name or "silu")
+        if act is None:
+            raise NotImplementedError(f"activation {name!r}: built are {sorted(ACTIVATIONS)}")
+        if (act == 1 and self.plain) or (act == 2 and not self.plain):
+            raise NotImplementedError(f"activation {name!r} is not built for the "
+                                      f"{'plain fc1/fc2' if self.plain else 'gated'} expert")
+        return dataclasses.replace(self, flags=(self.flags & ~(15 << 8)) | (act << 8))
+
 
 def layout_from_spec(spec: dict, quant: dict | None = None, slot_align: int = 256) -> Layout:
-    """The kernel layout of a gated 4/8-bit affine spec.  Raises ValueError otherwise."""
-    if tuple(spec) != PROJECTIONS:
-        raise NotImplementedError(f"projections {tuple(spec)}: only the gated gate/up/down "
-                                  f"expert is built")
-    for proj in PROJECTIONS:
-        if "bias" in spec[proj]:
-            raise NotImplementedError(f"{proj} carries an affine bias: not built")
+    """The kernel layout of an affine-quantised expert spec: gated (gate/up/down) or plain
+    (fc1/fc2), each projection with weight, scales and biases and optionally the affine
+    ``bias``, components in any packed order.  Raises NotImplementedError for what is not
+    built and ValueError for an inconsistent spec."""
+    projs = tuple(spec)
+    if projs == PROJECTIONS:
+        plain, idx = False, {"gate_proj": 0, "up_proj": 1, "down_proj": 2}
+    elif projs == MLP_PROJECTIONS:
+        plain, idx = True, {"fc1": 0, "fc2": 2}
+    else:
+        raise NotImplementedError(f"projections {projs}: built are {PROJECTIONS} (gated) and "
+                                  f"{MLP_PROJECTIONS} (plain)")
+    for proj in projs:
         for comp in ("weight", "scales", "biases"):
             if comp not in spec[proj]:
                 raise NotImplementedError(f"{proj} lacks {comp}: only affine-quantised experts")
+        unknown = set(spec[proj]) - set(COMPONENTS)
+        if unknown:
+            raise ValueError(f"{proj}: unknown components {sorted(unknown)}")
+    with_bias = ["bias" in spec[p] for p in projs]
+    if any(with_bias) and not all(with_bias):
+        raise NotImplementedError("an affine bias on some projections only")
+    bias_dtype = spec[projs[0]]["bias"]["dtype"] if with_bias[0] else None
+    if bias_dtype is not None and any(spec[p]["bias"]["dtype"] != bias_dtype for p in projs):
+        raise NotImplementedError("affine biases of different dtypes")
+    if bias_dtype is not None and bias_dtype not in _DTYPE_CODE:
+        raise NotImplementedError(f"bias dtype {bias_dtype}")
     q = dict(quant or {"bits": 4, "group_size": 64, "mode": "affine"})
     if q.get("mode", "affine") != "affine":
         raise NotImplementedError(f"quant mode {q.get('mode')!r}: only affine is built")
     bits, gs = int(q["bits"]), int(q["group_size"])
+    first, last = projs[0], projs[-1]
+    sd = spec[first]["scales"]["dtype"]
     if bits == 3:
         # stored as 3-bit code streams, held in HBM widened to 4-bit codes (lossless: the
         # same q, scales and biases); the slot layout is the 4-bit one
+        if plain or bias_dtype is not None:
+            raise NotImplementedError("3-bit codes of the gated expert without biases only")
         gw = spec["gate_proj"]["weight"]["shape"]
         inter, hidden = gw[0], gw[1] * 32 // 3
-        sd = spec["gate_proj"]["scales"]["dtype"]
         wide = layout_from_spec(make_spec(hidden, inter, 4, gs, sd),
                                 {"bits": 4, "group_size": gs, "mode": "affine"}, slot_align)
         if make_spec(hidden, inter, 3, gs, sd) != spec:
@@ -111,20 +171,34 @@ def layout_from_spec(spec: dict, quant: dict | None = None, slot_align: int = 25
         return dataclasses.replace(wide, source_bits=3, source_bytes=bytes_per_expert(spec))
     if bits not in (4, 8):
         raise NotImplementedError(f"{bits}-bit experts: 3-, 4- and 8-bit affine codes are built")
-    gw = spec["gate_proj"]["weight"]["shape"]
-    dw = spec["down_proj"]["weight"]["shape"]
+    gw = spec[first]["weight"]["shape"]
+    dw = spec[last]["weight"]["shape"]
     inter, hidden = gw[0], gw[1] * 32 // bits
     if dw != [hidden, inter * bits // 32]:
-        raise ValueError(f"down_proj weight {dw} does not match gate_proj {gw}")
-    sd = spec["gate_proj"]["scales"]["dtype"]
+        raise ValueError(f"{last} weight {dw} does not match {first} {gw}")
+    if bias_dtype is not None:
+        for p in projs:
+            out_dim = hidden if p == last else inter
+            if spec[p]["bias"]["shape"] != [out_dim]:
+                raise ValueError(f"{p}.bias shape {spec[p]['bias']['shape']}, want [{out_dim}]")
     offs = component_offsets(spec)
     bpe = bytes_per_expert(spec)
     stride = (bpe + slot_align - 1) // slot_align * slot_align
+
+    def per_proj(comp):
+        out = [0, 0, 0]
+        for p, i in idx.items():
+            if comp in spec[p]:
+                out[i] = offs[(p, comp)]
+        return tuple(out)
+
+    flags = (FLAG_PLAIN if plain else 0)
+    if bias_dtype is not None:
+        flags |= FLAG_BIAS | (_DTYPE_CODE[bias_dtype] << 2)
     return Layout(hidden=hidden, inter=inter, bits=bits, group_size=gs, scale_dtype=sd,
-                  bytes_per_expert=bpe, slot_stride=stride,
-                  weight_off=tuple(offs[(p, "weight")] for p in PROJECTIONS),
-                  scales_off=tuple(offs[(p, "scales")] for p in PROJECTIONS),
-                  biases_off=tuple(offs[(p, "biases")] for p in PROJECTIONS))
+                  bytes_per_expert=bpe, slot_stride=stride, weight_off=per_proj("weight"),
+                  scales_off=per_proj("scales"), biases_off=per_proj("biases"), flags=flags,
+                  bias_off=per_proj("bias"))
 
 
 def pack_expert(arrays: dict, spec: dict) -> np.ndarray:

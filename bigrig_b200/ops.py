@@ -66,11 +66,12 @@ def c_layout(L: Layout) -> _lib.ExpertLayout:
     if c is None:
         c = _lib.ExpertLayout()
         c.hidden, c.inter, c.bits, c.group_size = L.hidden, L.inter, L.bits, L.group_size
-        c.scale_dtype, c.reserved = L.scale_code, 0
+        c.scale_dtype, c.flags = L.scale_code, L.flags
         c.bytes_per_expert, c.slot_stride = L.bytes_per_expert, L.slot_stride
         for i in range(3):
             c.weight_off[i], c.scales_off[i], c.biases_off[i] = (L.weight_off[i], L.scales_off[i],
                                                                  L.biases_off[i])
+            c.bias_off[i] = L.bias_off[i]
         _lib.check(_lib.load().bigrig_check_layout(ctypes.byref(c)), "layout")
         _layout_cache[L] = c
     _layout_by_id[id(L)] = (L, c)

@@ -36,7 +36,7 @@ import numpy as np
 import torch
 
 from . import _lib, ops
-from .formats import PROJECTIONS, bytes_per_expert, layout_from_spec
+from .formats import MLP_PROJECTIONS, PROJECTIONS, bytes_per_expert, layout_from_spec
 from .residency import SlotTable
 
 # Most experts a layer copies to the GPU on the previous layer's prediction -- the router's
@@ -449,8 +449,13 @@ class StreamingSwitchGLU:
                  qparams: dict | None = None):
         if not quantized:
             raise NotImplementedError("only affine-quantised experts are built")
-        if activation not in (None, "swiglu"):
-            raise NotImplementedError("only the SwiGLU activation silu(gate) * up is built")
+        # the activation is the model's (stream.py:827): SiLU / SwiGLU by default,
+        # "gpt_oss" (gated) or "relu2" (plain fc1/fc2 experts); the kernels read it from
+        # the layout, so the pool computes with it from here on
+        if activation is not None and not isinstance(activation, str):
+            activation = getattr(activation, "__name__", None) or type(activation).__name__
+        name = {"SwiGLU": "swiglu", "silu": "silu", "swiglu": "swiglu"}.get(activation, activation)
+        pool.layout = pool.layout.with_activation(name)
         self._pool = pool
         self._fetcher = fetcher
         self._q = dict(qparams or pool.spec_quant)
@@ -1003,4 +1008,5 @@ def attach(blocks, store, capacity, policy: str = "lfuda", full_layers=(), warm=
 
 
 __all__ = ["ExpertPool", "StreamingSwitchGLU", "StreamHandle", "attach", "PROJECTIONS",
+           "MLP_PROJECTIONS",
            "projections_of", "is_gated"]

@@ -59,19 +59,41 @@ extern "C" {
 /* Byte layout of one expert inside a slot, in the reference's packed order
  * (bigrig_engine/stream.py:106-186): gate_proj{weight,scales,biases},
  * up_proj{...}, down_proj{...}.  weight is uint32 codes [out, in*bits/32],
- * scales/biases are half [out, in/group_size].  Index 0 gate, 1 up, 2 down. */
+ * scales/biases are half [out, in/group_size].  Index 0 gate, 1 up, 2 down.
+ *
+ * The two expert shapes of the reference (stream.py:48-76): the gated SwiGLU expert
+ * down(act(gate(x), up(x))) and, with BIGRIG_LAYOUT_PLAIN, the plain two-layer MLP
+ * fc2(act(fc1(x))) -- fc1 at index 0 (I x H), fc2 at index 2 (H x I), index 1 unused.
+ * With BIGRIG_LAYOUT_BIAS every projection also carries the affine `bias` component
+ * (stream.py:79-81), [out] elements of BIGRIG_LAYOUT_BIAS_DTYPE(flags) at bias_off[p],
+ * added to the projection's output before the activation (gate/up, fc1) or before the
+ * output is stored (down, fc2).  The activation, BIGRIG_LAYOUT_ACT(flags):
+ *   BIGRIG_ACT_SILU    gated: silu(gate) * up;  plain: silu(fc1)
+ *   BIGRIG_ACT_GPT_OSS gated only: g = min(gate, 7), u = clamp(up, -7, 7),
+ *                      g * sigmoid(1.702 g) * (u + 1)  (gpt-oss's SwiGLU)
+ *   BIGRIG_ACT_RELU2   plain only: max(fc1, 0)^2
+ * Each computed in fp32 from the fp32 projection outputs (plus bias); the result is
+ * rounded once to the down projection's input type. */
+#define BIGRIG_LAYOUT_PLAIN 1
+#define BIGRIG_LAYOUT_BIAS 2
+#define BIGRIG_LAYOUT_BIAS_DTYPE(flags) (((flags) >> 2) & 3) /* BIGRIG_F32/F16/BF16 */
+#define BIGRIG_LAYOUT_ACT(flags) (((flags) >> 8) & 15)
+#define BIGRIG_ACT_SILU 0
+#define BIGRIG_ACT_GPT_OSS 1
+#define BIGRIG_ACT_RELU2 2
 typedef struct bigrig_expert_layout {
   int32_t hidden;      /* H: input of gate/up, output of down            */
   int32_t inter;       /* I: output of gate/up, input of down            */
   int32_t bits;        /* 4 or 8                                         */
   int32_t group_size;  /* 64                                             */
   int32_t scale_dtype; /* BIGRIG_F16 or BIGRIG_BF16                      */
-  int32_t reserved;    /* 0                                              */
+  int32_t flags;       /* BIGRIG_LAYOUT_* bits, bias dtype << 2, act << 8; 0 = gated SwiGLU */
   int64_t bytes_per_expert;
   int64_t slot_stride; /* bytes between slots of a slab, >= bytes_per_expert, multiple of 16 */
   int64_t weight_off[3];
   int64_t scales_off[3];
   int64_t biases_off[3];
+  int64_t bias_off[3]; /* the affine bias per projection (BIGRIG_LAYOUT_BIAS), else 0 */
 } bigrig_expert_layout;
 
 /* Library identity and the calling thread's last error message. */
@@ -146,20 +168,25 @@ BIGRIG_API int bigrig_moe_forward(const void* x, const void* logits, int logits_
 #define BIGRIG_K_ROUTE 9
 #define BIGRIG_K_DOWN_COMBINE 10
 #define BIGRIG_K_DECODE_LAYER 11
-#define BIGRIG_K_COUNT 12
+#define BIGRIG_K_DECODE_SPLIT 12
+#define BIGRIG_K_COUNT 13
 
 /* Which expert kernels bigrig_switch_glu / bigrig_moe_forward / bigrig_moe_layer use:
  * BIGRIG_PATH_AUTO picks the grouped GEMV for calls of at most 32 routed pairs (decode)
  * and the tcgen05 grouped GEMM above that or when the mean rows per routed expert
- * reaches `gemm_min_rows`, and runs a one-token bigrig_moe_layer as one persistent kernel;
+ * reaches `gemm_min_rows`, and runs a one-token bigrig_moe_layer as one persistent kernel
+ * (the split kernel: work units of one routed expert's 64 intermediate features, integer
+ * tensor-core dot products; where it does not fit, the feature-tiled kernel);
  * BIGRIG_PATH_GEMV and BIGRIG_PATH_GEMM force one expert path; BIGRIG_PATH_CHAIN is
- * AUTO with one-token layers on the three-kernel chain instead of the persistent
- * kernel (the two give bit-identical results).  Process-wide; returns the previous
- * mode. */
+ * AUTO with one-token layers on the three-kernel chain instead of a persistent kernel;
+ * BIGRIG_PATH_TILED is AUTO with one-token layers on the feature-tiled persistent kernel.
+ * All give results within the parity bar of each other.  Process-wide; returns the
+ * previous mode. */
 #define BIGRIG_PATH_AUTO 0
 #define BIGRIG_PATH_GEMV 1
 #define BIGRIG_PATH_GEMM 2
 #define BIGRIG_PATH_CHAIN 3
+#define BIGRIG_PATH_TILED 4
 BIGRIG_API int bigrig_set_path(int mode, int gemm_min_rows);
 
 /* The current path mode and gemm_min_rows (either pointer may be NULL); 0. */

@@ -13,23 +13,36 @@ class Layer:
     """E experts of an (H, I) SwiGLU layer, weights N(0, std) quantised to the affine format."""
 
     def __init__(self, H, I, E, bits=4, scale_dtype="float16", seed=0, std=0.02, device="cuda",
-                 slot_order=None):
+                 slot_order=None, plain=False, bias=False, bias_dtype="bfloat16", order=None,
+                 activation="silu"):
         self.H, self.I, self.E, self.bits, self.sd = H, I, E, bits, scale_dtype
-        self.spec = formats.make_spec(H, I, bits, 64, scale_dtype)
+        self.activation = activation
+        self.spec = formats.make_spec(H, I, bits, 64, scale_dtype, plain=plain, bias=bias,
+                                      bias_dtype=bias_dtype, order=order)
         self.layout = formats.layout_from_spec(self.spec, {"bits": bits, "group_size": 64,
-                                                           "mode": "affine"})
+                                                           "mode": "affine"}
+                                               ).with_activation(activation)
         rng = np.random.default_rng(seed)
-        self.q = {}
+        self.q, self.bias = {}, {}
         blobs = []
         for e in range(E):
-            parts, qe = {}, {}
-            for p in moe.PROJ:
-                o, i = (H, I) if p == "down_proj" else (I, H)
+            parts, qe, be = {}, {}, {}
+            for p in self.spec:
+                o, i = (H, I) if p in ("down_proj", "fc2") else (I, H)
                 w = (rng.standard_normal((o, i), dtype=np.float32) * std).astype(np.float32)
                 codes, s, b = affine.quantize(w, 64, bits, scale_dtype)
                 qe[p] = (codes, s, b)
                 parts[p] = {"weight": codes, "scales": s, "biases": b}
+                if bias:
+                    v = (rng.standard_normal(o).astype(np.float32) * 0.5).astype(np.float32)
+                    if bias_dtype == "float32":
+                        parts[p]["bias"], be[p] = v, v
+                    else:
+                        bits16 = affine.f32_to_half_bits(v, bias_dtype)
+                        parts[p]["bias"] = bits16
+                        be[p] = affine.half_bits_to_f32(bits16, bias_dtype)
             self.q[e] = qe
+            self.bias[e] = be
             blobs.append(formats.pack_expert(parts, self.spec))
         self.blobs = blobs
         order = list(range(E)) if slot_order is None else list(slot_order)
@@ -49,7 +62,8 @@ class Layer:
         return self._w[key]
 
     def oracle_switch(self, x_f32, idx, weight_round=None, intermediate="h_bf16"):
-        return moe.switch_glu(x_f32, idx, lambda e: self.weights(e, weight_round), intermediate)
+        return moe.switch_glu(x_f32, idx, lambda e: self.weights(e, weight_round), intermediate,
+                              bias_of=lambda e: self.bias[e], activation=self.activation)
 
     def gemm_rounding(self):
         """(weight_round, intermediate) of the grouped GEMM for this format: 4-bit experts

@@ -150,14 +150,14 @@ def test_persistent_kernel_barrier_timeout_is_reported(cuda):
     w0 = _words(ws)
     assert w0[1] == 0
     lib = _lib.load()
-    n0 = _lib.launch_counts()["decode_layer"]
+    n0 = _lib.launch_counts()["decode_split"]
     assert lib.bigrig_test_grid_barrier(1, 1 << 14) == 0
     try:
         _run("auto", name, L, slab, g2s, x, gw, gb, ws)
         torch.cuda.synchronize()
     finally:
         assert lib.bigrig_test_grid_barrier(0, 0) == 0
-    assert _lib.launch_counts()["decode_layer"] == n0 + 1
+    assert _lib.launch_counts()["decode_split"] == n0 + 1
     w1 = _words(ws)
     # every CTA's barrier wait ran out and said so
     assert w1[1] >= torch.cuda.get_device_properties(cuda).multi_processor_count, w1

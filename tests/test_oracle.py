@@ -183,3 +183,64 @@ def test_three_bit_codes_straddle_words():
     c4 = affine.pack_codes(affine.unpack_codes(c3, 3), 4)
     assert np.array_equal(affine.dequantize(c3, s, b, 64, 3, "bfloat16"),
                           affine.dequantize(c4, s, b, 64, 4, "bfloat16"))
+
+
+# ------------------------------------------------------------------ expert shapes
+def test_plain_and_bias_layouts():
+    """fc1/fc2 experts and the affine bias, components in any packed order
+    (reference tests/test_fast_decode.py:95-110)."""
+    from bigrig_b200 import formats
+    q = {"bits": 4, "group_size": 64, "mode": "affine"}
+    order = ("biases", "bias", "scales", "weight")
+    s = formats.make_spec(256, 128, 4, 64, "bfloat16", plain=True, bias=True, order=order)
+    assert tuple(s) == ("fc1", "fc2") and tuple(s["fc1"]) == order
+    L = formats.layout_from_spec(s, q)
+    assert L.plain and L.has_bias and L.activation == 0
+    offs = formats.component_offsets(s)
+    assert L.weight_off == (offs[("fc1", "weight")], 0, offs[("fc2", "weight")])
+    assert L.bias_off == (offs[("fc1", "bias")], 0, offs[("fc2", "bias")])
+    assert L.bytes_per_expert == formats.bytes_per_expert(s)
+    assert L.with_activation("relu2").activation == 2
+    with pytest.raises(NotImplementedError):
+        L.with_activation("gpt_oss")              # gated only
+    G = formats.layout_from_spec(formats.make_spec(256, 128, 8, 64, bias=True,
+                                                   bias_dtype="float32"),
+                                 {"bits": 8, "group_size": 64})
+    assert not G.plain and G.has_bias and (G.flags >> 2) & 3 == 0
+    assert G.with_activation("gpt_oss").activation == 1
+    with pytest.raises(NotImplementedError):
+        G.with_activation("relu2")                # plain only
+    # a bias on some projections only is refused
+    half = formats.make_spec(256, 128, bias=True)
+    del half["up_proj"]["bias"]
+    with pytest.raises(NotImplementedError):
+        formats.layout_from_spec(half, q)
+    # pack / unpack round trip in the listed order
+    rng = np.random.default_rng(0)
+    arrays = {p: {c: rng.integers(0, 2**15, size=m["shape"]).astype(
+        np.uint32 if m["dtype"] == "uint32" else np.uint16) for c, m in s[p].items()} for p in s}
+    blob = formats.pack_expert(arrays, s)
+    back = formats.unpack_expert(blob, s)
+    for p in s:
+        for c in s[p]:
+            np.testing.assert_array_equal(back[p][c], arrays[p][c])
+
+
+def test_variant_activations():
+    from oracle import moe as omoe
+    g = np.array([-9.0, -1.0, 0.0, 3.0, 8.0], dtype=np.float32)
+    u = np.array([-8.0, 0.5, 2.0, -3.0, 9.0], dtype=np.float32)
+    np.testing.assert_allclose(omoe.act_gated(g, u, "silu"), g / (1 + np.exp(-g)) * u, rtol=1e-6)
+    gc, uc = np.minimum(g, 7), np.clip(u, -7, 7)
+    np.testing.assert_allclose(omoe.act_gated(g, u, "gpt_oss"),
+                               gc / (1 + np.exp(-1.702 * gc)) * (uc + 1), rtol=1e-6)
+    np.testing.assert_array_equal(omoe.act_plain(g, "relu2"), np.maximum(g, 0) ** 2)
+    # a plain expert with biases: fc2(act(fc1 x + b1)) + b2
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((2, 64)).astype(np.float32)
+    w = {"fc1": rng.standard_normal((32, 64)).astype(np.float32) * 0.1,
+         "fc2": rng.standard_normal((64, 32)).astype(np.float32) * 0.1}
+    b = {"fc1": rng.standard_normal(32).astype(np.float32), "fc2": rng.standard_normal(64).astype(np.float32)}
+    y = omoe.expert_forward(x, w, "f32", b, "relu2")
+    h = np.maximum(x @ w["fc1"].T + b["fc1"], 0) ** 2
+    np.testing.assert_allclose(y, h @ w["fc2"].T + b["fc2"], rtol=1e-2, atol=1e-2)
