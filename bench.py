@@ -125,15 +125,34 @@ class Clocks:
                 "samples": len(sm)}
 
 
+# the source file of each kernel a traffic figure may be quoted for
+KERNEL_SOURCES = {"decode_layer_kernel": "decode_layer.cu", "decode_split_kernel": "decode_split.cu",
+                  "gemv_gate_up_kernel": "gemv.cu", "grouped_gemm_kernel": "gemm_sm100.cu"}
+
+
+def kernel_source_hash(kernel: str) -> str | None:
+    """First 12 hex digits of the sha256 of the kernel's source file (csrc/<file>)."""
+    import hashlib
+    f = KERNEL_SOURCES.get(kernel)
+    path = os.path.join(ROOT, "bigrig_b200", "csrc", f) if f else None
+    if not path or not os.path.exists(path):
+        return None
+    return hashlib.sha256(open(path, "rb").read()).hexdigest()[:12]
+
+
 def _traffic() -> dict:
     """DRAM bytes per launch (read + write) of the profiled kernels, from the ncu summary
-    committed in profiles/traffic.txt ("<kernel> <bytes>" lines)."""
+    committed in profiles/traffic.txt ("<kernel> <bytes> <source sha256[:12]>" lines).  A
+    figure whose recorded source hash differs from the kernel's current source was measured
+    on other code: it is left out (the line then carries null), never quoted stale."""
     out = {}
     tpath = os.path.join(ROOT, "profiles", "traffic.txt")
     if os.path.exists(tpath):
         for line in open(tpath):
             parts = line.split()
-            if len(parts) >= 2 and not line.startswith("#"):
+            if len(parts) >= 3 and not line.startswith("#"):
+                if parts[2] != kernel_source_hash(parts[0]):
+                    continue
                 try:
                     out[parts[0]] = int(float(parts[1]))
                 except ValueError:
@@ -311,7 +330,8 @@ def _graph_decode(dev, blocks, B: int, K: int, W: int, seed: int, bpe: int, peak
     layer_ms = ms / len(blocks)
     gbs = layer_bytes / (layer_ms / 1e3) / 1e9
     return {"batch": B, "tok_s": B / (ms / 1e3), "ms_per_step": ms, "steps": K,
-            "roofline": {"kernel": "decode_layer_kernel" if B == 1 else "moe layer (GEMV chain / "
+            "roofline": {"kernel": "one-token layer kernel (decode_split_kernel where it fits)"
+                         if B == 1 else "moe layer (GEMV chain / "
                          "grouped GEMM)", "bound": "hbm", "achieved": gbs, "peak": peak,
                          "unit": "GB/s", "frac": gbs / peak,
                          "bytes_per_layer": layer_bytes, "ms_per_layer": layer_ms,
@@ -577,6 +597,46 @@ def ep_reference_check(dev, c: dict, stack, x: torch.Tensor, rank: int, world: i
 
 
 # ------------------------------------------------------------------ the B200 arm
+def _full_decode(dev, blocks, store, c: dict, steps: int = 256) -> dict:
+    """BASELINE config 2 in full: embeddings, attention (MHA 16 x 128, KV cache), the 16 MoE
+    layers over pools capped at 16/64 and refilled from pinned host, the LM head; a 2048-token
+    random prompt (layer-major prefill), then ``steps`` greedy decode steps.  Attention and
+    the LM head are bf16 cuBLAS/SDPA calls around the library's MoE layers."""
+    from bigrig_b200.decoder import FAMILY_ATTN, Decoder
+    from bigrig_b200.stream import attach
+    handle = attach(blocks, store, c["capacity"], policy=c["policy"], warm="auto", device=dev)
+    attn = FAMILY_ATTN["olmoe"]
+    dec = Decoder(blocks, attn, c["prompt"] + steps, dev, seed=5)
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    prompt = torch.randint(0, attn.vocab, (c["prompt"],), generator=g, device=dev)
+    # warm-up: a short prompt and a few steps (library set-up, cuBLAS and SDPA plans)
+    tok = dec.prefill(prompt[:64], layer_scope=handle.prefill_layer)
+    for _ in range(3):
+        tok = dec.step(tok)
+    dec.reset()
+    handle.reset_stats()
+    torch.cuda.synchronize(dev)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    e[0].record()
+    tok = dec.prefill(prompt, layer_scope=handle.prefill_layer)
+    e[1].record()
+    for _ in range(steps):
+        tok = dec.step(tok)
+    e[2].record()
+    torch.cuda.synchronize(dev)
+    pf_ms, dc_ms = e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])
+    st = handle.stats()
+    out = {"workload": "olmoe-1b-7b-shaped full decode: 16 layers, MHA 16 x 128, vocab 50304, "
+                       "pool 16/64 per layer refilled from pinned host; attention, embeddings "
+                       "and LM head bf16 (random init)",
+           "prompt": c["prompt"], "steps": steps,
+           "prefill_tok_s": c["prompt"] / (pf_ms / 1e3), "prefill_ms": pf_ms,
+           "decode_tok_s": steps / (dc_ms / 1e3), "decode_ms_per_token": dc_ms / steps,
+           "miss_rate": st["miss_rate"], "admit_gb": st["admit_gb"]}
+    return out                   # (the host store stays open: the CPU baseline reads it)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -731,7 +791,7 @@ def main() -> None:
     handle.reset_stats()
     barrier()
     counts0 = _lib.launch_counts()
-    _lib.timing_enable(["decode_layer"])
+    _lib.timing_enable(["decode_split", "decode_layer"])
     clocks = Clocks(local)
     clocks.start()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -745,7 +805,12 @@ def main() -> None:
     clk = clocks.stop()
     _lib.timing_enable([])
     counts1 = _lib.launch_counts()
-    gu_ms, gu_n = _lib.timing_read("decode_layer")
+    # the one-token layer kernel that ran: the split kernel where it fits, else the tiled one
+    one_kernel = "decode_split"
+    gu_ms, gu_n = _lib.timing_read("decode_split")
+    t_ms, t_n = _lib.timing_read("decode_layer")
+    if t_n > gu_n:
+        one_kernel, gu_ms, gu_n = "decode_layer", t_ms, t_n
     ms = max_over_ranks(t0.elapsed_time(t1))
     value = world * K / (ms / 1e3)
     st = handle.stats()
@@ -868,6 +933,10 @@ def main() -> None:
         rp_tw, extras["prefill_gemm_token_wise"] = resident_prefill(True)
         extras["resident_prefill_token_wise_tok_s"] = world * c["prompt"] / (rp_tw / 1e3)
 
+    # ---- config 2 in full: attention, KV cache and LM head around the capped MoE stack
+    if not args.no_extras and world == 1 and c["layers"] == CFG["layers"]:
+        extras["full_decode"] = _full_decode(dev, blocks, store, c)
+
     # ---- the other named shapes, one GPU
     if not args.no_extras and world == 1 and args.configs != "none":
         hbm_peak, _, hbm_kind = _peaks()
@@ -888,15 +957,15 @@ def main() -> None:
     gu_avg_ms = gu_ms / max(1, gu_n)
     gu_bytes = algorithmic_layer_bytes(1, c["top_k"])
     achieved = gu_bytes / (gu_avg_ms / 1e3) / 1e9 if gu_n else None
-    traffic = _traffic().get("decode_layer_kernel")
+    traffic = _traffic().get(f"{one_kernel}_kernel")
     if "moe_layer_hbm_gbs" in extras:
         # the persistent one-token layer kernel of the resident decode: algorithmic bytes of
         # a layer over the graph's time per layer (which includes the launch gap)
         extras["resident_roofline"] = {
-            "kernel": "decode_layer_kernel", "bound": "hbm",
+            "kernel": f"{one_kernel}_kernel", "bound": "hbm",
             "achieved": extras["moe_layer_hbm_gbs"], "peak": hbm_peak, "unit": "GB/s",
             "frac": extras["moe_layer_hbm_gbs"] / hbm_peak, "peak_kind": peak_kind,
-            "traffic": _traffic().get("decode_layer_kernel"),
+            "traffic": _traffic().get(f"{one_kernel}_kernel"),
             "bytes_per_launch": extras["moe_layer_bytes"],
             "avg_launch_ms": extras["resident_ms_per_token"] / c["layers"]}
     if rank == 0:
@@ -916,7 +985,7 @@ def main() -> None:
             "e2e": e2e,
             "gpu_launches": launches,
             "launches_by_kernel": {k: counts1[k] - counts0[k] for k in counts1},
-            "roofline": {"kernel": "decode_layer_kernel", "bound": "hbm", "achieved": achieved,
+            "roofline": {"kernel": f"{one_kernel}_kernel", "bound": "hbm", "achieved": achieved,
                          "peak": hbm_peak, "unit": "GB/s",
                          "frac": (achieved / hbm_peak) if achieved else None,
                          "peak_kind": peak_kind, "traffic": traffic,
