@@ -34,7 +34,7 @@ NOALLOC_SCRATCH_BYTES = 4 << 20
 KERNELS = {"router_logits": 0, "router_topk": 1, "permute": 2, "gate_up": 3, "down": 4,
            "combine": 5, "dequant": 6, "gemm_gate_up": 7, "gemm_down": 8, "route": 9,
            "down_combine": 10, "decode_layer": 11, "decode_split": 12}
-PATHS = {"auto": 0, "gemv": 1, "gemm": 2, "chain": 3, "tiled": 4}
+PATHS = {"auto": 0, "gemv": 1, "gemm": 2, "chain": 3, "tiled": 4, "split": 5}
 
 
 class ExpertLayout(ctypes.Structure):

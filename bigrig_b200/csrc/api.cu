@@ -252,7 +252,7 @@ int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, c
   // at 16-column MMAs), or when the mean rows per routed expert reaches gemm_min_rows.
   const bool gemm = path == BIGRIG_PATH_GEMM ||
                     ((path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_CHAIN ||
-                      path == BIGRIG_PATH_TILED) &&
+                      path == BIGRIG_PATH_TILED || path == BIGRIG_PATH_SPLIT) &&
                      (P > kDecodePairs || P >= g_gemm_min_rows.load() * (P < E ? P : E)));
   if (gemm) {
     const int mean = gemm_mean_rows(T, k, E);
@@ -414,11 +414,13 @@ int bigrig_moe_layer(const void* x, const void* gate_w, const float* gate_b, int
   float* sc = scores_out ? scores_out : ws.scores;
   const int path = g_path.load();
   const bool one = T == 1 && (path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_GEMV);
-  if (one && decode_split_fits(*layout, k, E))
+  if (T == 1 && ((one && decode_split_preferred(*layout, k, E)) ||
+                 (path == BIGRIG_PATH_SPLIT && decode_split_fits(*layout, k, E))))
     return launch_decode_split(x, gate_w, gate_b, E, k, mode, norm_topk, g2s, slab, *layout,
                                residual, out, idx, sc, ws.ypart, ws.tagged, ws.arrivals, ws.err, s,
                                nullptr, nullptr);
-  if ((one || (T == 1 && path == BIGRIG_PATH_TILED)) && decode_layer_fits(*layout, k, E))
+  if ((one || (T == 1 && (path == BIGRIG_PATH_TILED || path == BIGRIG_PATH_SPLIT))) &&
+      decode_layer_fits(*layout, k, E))
     return launch_decode_layer(x, gate_w, gate_b, E, k, mode, norm_topk, g2s, slab, *layout,
                                residual, out, idx, sc, ws.h, ws.tagged, ws.arrivals, ws.err, s);
   if (fused_decode(T, k, *layout))
@@ -453,12 +455,14 @@ int bigrig_moe_layer_routed(const void* x, const int32_t* indices, const float* 
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int path = g_path.load();
   const bool one = T == 1 && (path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_GEMV);
-  if (one && decode_split_fits(*layout, k, E))
+  if (T == 1 && ((one && decode_split_preferred(*layout, k, E)) ||
+                 (path == BIGRIG_PATH_SPLIT && decode_split_fits(*layout, k, E))))
     return launch_decode_split(x, nullptr, nullptr, E, k, BIGRIG_SOFTMAX_TOPK, 0, g2s, slab,
                                *layout, residual, out, const_cast<int32_t*>(indices),
                                const_cast<float*>(scores), ws.ypart, ws.tagged, ws.arrivals,
                                ws.err, s, indices, scores);
-  if ((one || (T == 1 && path == BIGRIG_PATH_TILED)) && decode_layer_fits(*layout, k, E))
+  if ((one || (T == 1 && (path == BIGRIG_PATH_TILED || path == BIGRIG_PATH_SPLIT))) &&
+      decode_layer_fits(*layout, k, E))
     return launch_decode_layer(x, nullptr, nullptr, E, k, BIGRIG_SOFTMAX_TOPK, 0, g2s, slab,
                                *layout, residual, out, const_cast<int32_t*>(indices),
                                const_cast<float*>(scores), ws.h, ws.tagged, ws.arrivals, ws.err, s,
@@ -492,7 +496,7 @@ int bigrig_test_grid_barrier(int phantom_ctas, unsigned int spin_limit) {
 }
 
 int bigrig_set_path(int mode, int gemm_min_rows) {
-  if (mode < BIGRIG_PATH_AUTO || mode > BIGRIG_PATH_TILED || gemm_min_rows < 1)
+  if (mode < BIGRIG_PATH_AUTO || mode > BIGRIG_PATH_SPLIT || gemm_min_rows < 1)
     return set_error(BIGRIG_ERR_INVALID, "set_path: mode=%d gemm_min_rows=%d", mode, gemm_min_rows);
   const int prev = g_path.exchange(mode);
   g_gemm_min_rows.store(gemm_min_rows);

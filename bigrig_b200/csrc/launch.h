@@ -99,6 +99,7 @@ int launch_decode_layer(const void* x, const void* gate_w, const float* gate_b, 
 // integer tensor-core dot products, one grid barrier before the combine.  Scratch: ypart,
 // decode_split_scratch(L, k) bytes (no zero-fill needed).
 bool decode_split_fits(const bigrig_expert_layout& L, int k, int E);
+bool decode_split_preferred(const bigrig_expert_layout& L, int k, int E);
 size_t decode_split_scratch(const bigrig_expert_layout& L, int k);
 int launch_decode_split(const void* x, const void* gate_w, const float* gate_b, int E, int k,
                         int mode, int norm, const int32_t* g2s, const void* slab,

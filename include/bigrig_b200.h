@@ -174,19 +174,21 @@ BIGRIG_API int bigrig_moe_forward(const void* x, const void* logits, int logits_
 /* Which expert kernels bigrig_switch_glu / bigrig_moe_forward / bigrig_moe_layer use:
  * BIGRIG_PATH_AUTO picks the grouped GEMV for calls of at most 32 routed pairs (decode)
  * and the tcgen05 grouped GEMM above that or when the mean rows per routed expert
- * reaches `gemm_min_rows`, and runs a one-token bigrig_moe_layer as one persistent kernel
- * (the split kernel: work units of one routed expert's 64 intermediate features, integer
- * tensor-core dot products; where it does not fit, the feature-tiled kernel);
+ * reaches `gemm_min_rows`, and runs a one-token bigrig_moe_layer as one persistent kernel:
+ * the feature-tiled kernel, or, for layers whose (routed expert, 64-feature group) units
+ * fill at least two waves of SMs, the split kernel (one such unit per work item, integer
+ * tensor-core dot products, no exchange between gate/up and down);
  * BIGRIG_PATH_GEMV and BIGRIG_PATH_GEMM force one expert path; BIGRIG_PATH_CHAIN is
  * AUTO with one-token layers on the three-kernel chain instead of a persistent kernel;
- * BIGRIG_PATH_TILED is AUTO with one-token layers on the feature-tiled persistent kernel.
- * All give results within the parity bar of each other.  Process-wide; returns the
- * previous mode. */
+ * BIGRIG_PATH_TILED and BIGRIG_PATH_SPLIT are AUTO with one-token layers on that
+ * persistent kernel (where its plan fits the layer).  All give results within the parity
+ * bar of each other.  Process-wide; returns the previous mode. */
 #define BIGRIG_PATH_AUTO 0
 #define BIGRIG_PATH_GEMV 1
 #define BIGRIG_PATH_GEMM 2
 #define BIGRIG_PATH_CHAIN 3
 #define BIGRIG_PATH_TILED 4
+#define BIGRIG_PATH_SPLIT 5
 BIGRIG_API int bigrig_set_path(int mode, int gemm_min_rows);
 
 /* The current path mode and gemm_min_rows (either pointer may be NULL); 0. */

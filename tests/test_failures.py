@@ -140,28 +140,29 @@ def test_peer_rank_leaving_ends_the_next_exchange_with_an_error():
 
 
 @pytest.mark.gpu
-def test_persistent_kernel_barrier_timeout_is_reported(cuda):
+@pytest.mark.parametrize("path,kern", [("tiled", "decode_layer"), ("split", "decode_split")])
+def test_persistent_kernel_barrier_timeout_is_reported(cuda, path, kern):
     from bigrig_b200 import _lib, ops
     from tests.test_gpu_decode_layer import SHAPES, _layer, _run, _words
     name = "olmoe"
     L, slab, g2s, x, gw, gb = _layer(name, cuda)
     ws = ops.Workspace(cuda)
-    good, _, _ = _run("auto", name, L, slab, g2s, x, gw, gb, ws)
+    good, _, _ = _run(path, name, L, slab, g2s, x, gw, gb, ws)
     w0 = _words(ws)
     assert w0[1] == 0
     lib = _lib.load()
-    n0 = _lib.launch_counts()["decode_split"]
+    n0 = _lib.launch_counts()[kern]
     assert lib.bigrig_test_grid_barrier(1, 1 << 14) == 0
     try:
-        _run("auto", name, L, slab, g2s, x, gw, gb, ws)
+        _run(path, name, L, slab, g2s, x, gw, gb, ws)
         torch.cuda.synchronize()
     finally:
         assert lib.bigrig_test_grid_barrier(0, 0) == 0
-    assert _lib.launch_counts()["decode_split"] == n0 + 1
+    assert _lib.launch_counts()[kern] == n0 + 1
     w1 = _words(ws)
     # every CTA's barrier wait ran out and said so
     assert w1[1] >= torch.cuda.get_device_properties(cuda).multi_processor_count, w1
     # the context is still usable and the next launch is right
-    again, _, _ = _run("auto", name, L, slab, g2s, x, gw, gb, ws)
+    again, _, _ = _run(path, name, L, slab, g2s, x, gw, gb, ws)
     assert torch.equal(again, good)
     assert _words(ws)[1] == w1[1]

@@ -1,6 +1,7 @@
 """The persistent one-token decode kernels (one cooperative launch per MoE layer): the
-split kernel that AUTO runs (units of one routed expert's 64 intermediate features,
-integer tensor-core dot products) and the feature-tiled kernel (path "tiled").
+feature-tiled kernel (path "tiled") and the split kernel (path "split": units of one
+routed expert's 64 intermediate features, integer tensor-core dot products); AUTO takes the
+split kernel for layers whose units fill two waves of SMs (the Mixtral shape), else tiled.
 
 Its routing must be the three-kernel chain's bit for bit (indices and scores); its
 output, computed on the tensor cores in another summation order, must meet the expert
@@ -34,6 +35,7 @@ SHAPES = {
     "mixtral": CONFIGS["mixtral"] + ("topk_softmax", False),   # too wide for "tiled"
 }
 TILED_TOO_WIDE = {"mixtral"}
+AUTO_SPLIT = {"mixtral"}          # k * I / 64 >= 2 x 148 units
 
 
 def _layer(name, device):
@@ -71,17 +73,18 @@ def _run(path, name, L, slab, g2s, x, gw, gb, ws, residual=None):
         _lib.set_path(prev)
 
 
-@pytest.mark.parametrize("path", ["auto", "tiled"])
+@pytest.mark.parametrize("path", ["auto", "tiled", "split"])
 @pytest.mark.parametrize("name", list(SHAPES))
 def test_persistent_equals_chain(cuda, name, path):
     L, slab, g2s, x, gw, gb = _layer(name, cuda)
     ws = ops.Workspace(cuda)
-    fits = path == "auto" or name not in TILED_TOO_WIDE
+    fits = path != "tiled" or name not in TILED_TOO_WIDE
     n0 = _lib.launch_counts()
     out, idx, sc = _run(path, name, L, slab, g2s, x, gw, gb, ws)
     out_r, idx_r, sc_r = _run(path, name, L, slab, g2s, x, gw, gb, ws, residual=x)
     n1 = _lib.launch_counts()
-    kern = "decode_split" if path == "auto" else "decode_layer"
+    split = path == "split" or (path == "auto" and name in AUTO_SPLIT)
+    kern = "decode_split" if split else "decode_layer"
     assert n1[kern] - n0[kern] == (2 if fits else 0)
     if fits:
         assert n1["route"] == n0["route"]
