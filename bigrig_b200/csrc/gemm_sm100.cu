@@ -833,30 +833,37 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(
         // global store (with one accumulator buffer the next tile's MMAs wait for it)
         constexpr int NG = (BN / 16 + 1) / 2;   // 16-column groups per warp (every other)
         uint32_t hp[NG * 8];
+        // the activation is chosen once per tile (a uniform branch), never per element: the
+        // default expert's loop is the plain SiLU one
+        auto drain = [&](auto actf) {
 #pragma unroll
-        for (int gi = 0; gi < NG; ++gi) {
-          const int j0 = (eh + 2 * gi) * 16;
-          if (j0 < t.rows) {
-            uint32_t a[16], u[16];
-            tmem_ld16_nowait(lane_addr + j0, a);
-            if constexpr (MODE == 0) tmem_ld16_nowait(lane_addr + BN + j0, u);
-            tmem_ld_wait();
+          for (int gi = 0; gi < NG; ++gi) {
+            const int j0 = (eh + 2 * gi) * 16;
+            if (j0 < t.rows) {
+              uint32_t a[16], u[16];
+              tmem_ld16_nowait(lane_addr + j0, a);
+              if constexpr (MODE == 0) tmem_ld16_nowait(lane_addr + BN + j0, u);
+              tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 16; i += 2) {
-              float h0, h1;
-              if constexpr (MODE == 2) {
-                h0 = act_plain(__uint_as_float(a[i]) + bias0, act);
-                h1 = act_plain(__uint_as_float(a[i + 1]) + bias0, act);
-              } else if (L.flags == 0) {
-                h0 = silu_fast(__uint_as_float(a[i])) * __uint_as_float(u[i]);
-                h1 = silu_fast(__uint_as_float(a[i + 1])) * __uint_as_float(u[i + 1]);
-              } else {
-                h0 = act_gated(__uint_as_float(a[i]) + bias0, __uint_as_float(u[i]) + bias1, act);
-                h1 = act_gated(__uint_as_float(a[i + 1]) + bias0, __uint_as_float(u[i + 1]) + bias1, act);
+              for (int i = 0; i < 16; i += 2) {
+                const float h0 = actf(a[i], MODE == 0 ? u[i] : 0u);
+                const float h1 = actf(a[i + 1], MODE == 0 ? u[i + 1] : 0u);
+                hp[gi * 8 + i / 2] = OT == BIGRIG_F16 ? pack_f16x2_sat(h0, h1) : pack_bf16x2(h0, h1);
               }
-              hp[gi * 8 + i / 2] = OT == BIGRIG_F16 ? pack_f16x2_sat(h0, h1) : pack_bf16x2(h0, h1);
             }
           }
+        };
+        if constexpr (MODE == 2) {
+          drain([&](uint32_t gq, uint32_t) { return act_plain(__uint_as_float(gq) + bias0, act); });
+        } else {
+          if (L.flags == 0)
+            drain([](uint32_t gq, uint32_t uq) {
+              return silu_fast(__uint_as_float(gq)) * __uint_as_float(uq);
+            });
+          else
+            drain([&](uint32_t gq, uint32_t uq) {
+              return act_gated(__uint_as_float(gq) + bias0, __uint_as_float(uq) + bias1, act);
+            });
         }
         tc_fence_before();
         __syncwarp();

@@ -20,6 +20,11 @@ import dataclasses
 
 import torch
 import torch.nn.functional as F
+from torch.nn.attention import SDPBackend, sdpa_kernel
+
+# Attention kernels that need no per-shape plan: the cuDNN backend builds an execution plan
+# for every new key length (~3 ms of host time per call), i.e. at every decode step.
+_SDPA_BACKENDS = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
 
 
 @dataclasses.dataclass
@@ -102,8 +107,9 @@ class Decoder:
         self.v_cache[li, :, p0:p0 + T] = v.reshape(T, nkv, hd).transpose(0, 1)
         keys = self.k_cache[li, :, :p0 + T][None]
         vals = self.v_cache[li, :, :p0 + T][None]
-        o = F.scaled_dot_product_attention(q[None], keys, vals, is_causal=T > 1 and p0 == 0,
-                                           enable_gqa=nkv != nh)
+        with sdpa_kernel(_SDPA_BACKENDS):
+            o = F.scaled_dot_product_attention(q[None], keys, vals, is_causal=T > 1 and p0 == 0,
+                                               enable_gqa=nkv != nh)
         return o[0].transpose(0, 1).reshape(T, nh * hd) @ self.wo[li].T
 
     def _layer(self, li: int, h, p0: int):
