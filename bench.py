@@ -652,6 +652,9 @@ def main() -> None:
     ap.add_argument("--configs", default="c3,c4,c5",
                     help="other BASELINE shapes measured at N=1 as extra keys (comma list of "
                          "c3, c4, c5, or 'none')")
+    ap.add_argument("--path", default="auto", choices=["auto", "tiled", "split", "chain"],
+                    help="expert-kernel path mode (bigrig_set_path); 'split' / 'tiled' pick the "
+                         "one-token layer kernel (for profiler captures)")
     ap.add_argument("--layers", type=int, default=None,
                     help="MoE layers of the stack (default: the config's 16; fewer only to keep "
                          "a profiler capture small -- such a run is not a bench line)")
@@ -676,6 +679,7 @@ def main() -> None:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     _lib.load(build_if_stale=False)
+    _lib.set_path(args.path)
     c = dict(CFG)
     if args.layers is not None:
         c["layers"] = args.layers
