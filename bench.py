@@ -649,6 +649,10 @@ def main() -> None:
     ap.add_argument("--ep-slots", type=int, default=None,
                     help="expert-parallel runs: slots per layer per rank (default: the config's "
                          "capacity, at most the rank's experts)")
+    ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
+                    help="expert-parallel decode exchange: 'peer' stores rows into the other "
+                         "ranks' buffers over NVLink inside the library's kernels (every local "
+                         "expert resident); 'nccl' the all-to-all block over pools of --ep-slots")
     ap.add_argument("--configs", default="c3,c4,c5",
                     help="other BASELINE shapes measured at N=1 as extra keys (comma list of "
                          "c3, c4, c5, or 'none')")
@@ -698,6 +702,9 @@ def main() -> None:
         blocks, store = build_model(dev, seed=0, experts=range(lo, hi), layers=c["layers"])
         pools, mods = [], []
         slots = min(args.ep_slots or c["capacity"], hi - lo)
+        if args.ep == "peer":
+            slots = hi - lo                      # the peer path never reads routing back
+
         for b in blocks:
             pool = ExpertPool(b.layer, None, hi - lo, slots, b.spec,
                               policy=c["policy"], quant=b.quant, device=dev).build()
@@ -707,6 +714,14 @@ def main() -> None:
         for m in mods:
             m.refresh()
         stack = [EPMoEBlock(b, ep, m, padded=m._sync_free) for b, m in zip(blocks, mods)]
+        if args.ep == "peer":
+            # one-token decode layers exchange through peer memory; the prompt keeps the
+            # NCCL all-to-all block
+            from bigrig_b200.block import EPPeerBlock
+            from bigrig_b200.ep import PeerBuffers
+            peers = PeerBuffers(1, c["hidden"], c["top_k"], dev)
+            stack = [EPPeerBlock(b, peers, m, lo, hi - lo, fallback=s)
+                     for b, m, s in zip(blocks, mods, stack)]
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
     W, K = args.warmup, args.steps
@@ -783,8 +798,13 @@ def main() -> None:
         torch.cuda.current_stream(dev).wait_stream(side)
         barrier()
         graph = torch.cuda.CUDAGraph()
+        cap0 = _lib.launch_counts()
         with torch.cuda.graph(graph):
             yout = stack_step(stack, xin)
+        cap1 = _lib.launch_counts()
+        # the library counts a launch when it is issued: in a graph, once at capture, so a
+        # replay runs the captured launches again
+        graph_launches = {k: cap1[k] - cap0[k] for k in cap1}
 
         def step(_stack, x, _g=graph, _x=xin, _y=yout):
             _x.copy_(x)
@@ -819,7 +839,10 @@ def main() -> None:
     ms = max_over_ranks(t0.elapsed_time(t1))
     value = world * K / (ms / 1e3)
     st = handle.stats()
-    launches = sum(counts1[k] - counts0[k] for k in counts1)
+    by_kernel = {k: counts1[k] - counts0[k] for k in counts1}
+    if graph is not None:
+        by_kernel = {k: by_kernel[k] + K * graph_launches[k] for k in by_kernel}
+    launches = sum(by_kernel.values())
 
     # ---- e2e through the public API with host buffers: pinned in, result read back
     hbuf = tokens.cpu().pin_memory()
@@ -984,15 +1007,20 @@ def main() -> None:
                                             "top_k", "bits", "group_size", "capacity", "policy")},
                        "global_batch": world,
                        "parallelism": "single GPU" if world == 1 else
-                       f"ep{world}: {c['experts'] // world} experts per rank per layer, "
-                       f"pool {min(c['capacity'], c['experts'] // world)} slots, NCCL all-to-all",
+                       f"ep{world}: {c['experts'] // world} experts per rank per layer, all "
+                       f"resident; decode rows exchanged by stores into peer buffers over "
+                       f"NVLink (gather, expert kernels, scatter, combine)" if args.ep == "peer"
+                       else f"ep{world}: {c['experts'] // world} experts per rank per layer, "
+                       f"pool {min(args.ep_slots or c['capacity'], c['experts'] // world)} "
+                       f"slots, NCCL all-to-all",
                        "l2": "decode reads 28 MB of experts per layer, 453 MB per token; no flush"},
             "e2e": e2e,
             "gpu_launches": launches,
-            "launches_by_kernel": {k: counts1[k] - counts0[k] for k in counts1},
+            "launches_by_kernel": by_kernel,
             "roofline": {"kernel": f"{one_kernel}_kernel" if gu_n else
                          "none: no one-token layer kernel ran (expert-parallel decode runs the "
-                         "GEMV chain on the rows each rank receives)",
+                         "GEMV chain or grouped GEMM over the pairs routed to the rank's "
+                         "experts)",
                          "bound": "hbm", "achieved": achieved,
                          "peak": hbm_peak, "unit": "GB/s",
                          "frac": (achieved / hbm_peak) if achieved else None,
@@ -1010,6 +1038,8 @@ def main() -> None:
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
+        if world > 1 and args.ep == "peer":
+            peers.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -29,11 +29,14 @@ EXPORTS = (
     "bigrig_timing_enable", "bigrig_timing_read", "bigrig_launch_counts", "bigrig_kernel_name",
     "bigrig_set_path", "bigrig_get_path", "bigrig_moe_layer", "bigrig_switch_glu_noalloc", "bigrig_copy_regions",
     "bigrig_moe_layer_routed", "bigrig_test_grid_barrier", "bigrig_widen_expert",
+    "bigrig_peer_buffer_bytes", "bigrig_peer_alloc", "bigrig_peer_free", "bigrig_peer_open",
+    "bigrig_peer_close", "bigrig_peer_workspace_bytes", "bigrig_peer_layer", "bigrig_peer_errors",
 )
 NOALLOC_SCRATCH_BYTES = 4 << 20
 KERNELS = {"router_logits": 0, "router_topk": 1, "permute": 2, "gate_up": 3, "down": 4,
            "combine": 5, "dequant": 6, "gemm_gate_up": 7, "gemm_down": 8, "route": 9,
-           "down_combine": 10, "decode_layer": 11, "decode_split": 12}
+           "down_combine": 10, "decode_layer": 11, "decode_split": 12, "peer_gather": 13,
+           "peer_localize": 14, "peer_scatter": 15, "peer_combine": 16}
 PATHS = {"auto": 0, "gemv": 1, "gemm": 2, "chain": 3, "tiled": 4, "split": 5}
 
 
@@ -46,6 +49,19 @@ class ExpertLayout(ctypes.Structure):
         ("slot_stride", ctypes.c_int64), ("weight_off", ctypes.c_int64 * 3),
         ("scales_off", ctypes.c_int64 * 3), ("biases_off", ctypes.c_int64 * 3),
         ("bias_off", ctypes.c_int64 * 3),
+    ]
+
+
+PEER_MAX_RANKS = 8
+PEER_HANDLE_BYTES = 64
+
+
+class PeerGroup(ctypes.Structure):
+    """Mirror of ``bigrig_peer_group`` (include/bigrig_b200.h)."""
+    _fields_ = [
+        ("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("tokens", ctypes.c_int32),
+        ("hidden", ctypes.c_int32), ("top_k", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("base", ctypes.c_void_p * PEER_MAX_RANKS),
     ]
 
 
@@ -88,6 +104,16 @@ _SIG = {
                                      _P, _P, _P, ctypes.c_size_t, _P]),
     "bigrig_switch_glu_noalloc": (_I, [_P, _P, _I, _I, _I, _P, _P, ctypes.POINTER(ExpertLayout),
                                        _P, _P]),
+    "bigrig_peer_buffer_bytes": (ctypes.c_size_t, [_I, _I, _I, _I]),
+    "bigrig_peer_alloc": (_I, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "bigrig_peer_free": (_I, [_P]),
+    "bigrig_peer_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "bigrig_peer_close": (_I, [_P]),
+    "bigrig_peer_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(PeerGroup), _I, _I,
+                                                      ctypes.POINTER(ExpertLayout)]),
+    "bigrig_peer_layer": (_I, [ctypes.POINTER(PeerGroup), _P, _P, _P, _I, _I, _I, _I, _I, _P, _P,
+                               ctypes.POINTER(ExpertLayout), _P, _P, _P, ctypes.c_size_t, _P]),
+    "bigrig_peer_errors": (_I, [ctypes.POINTER(PeerGroup), _P, _P]),
 }
 
 

@@ -171,3 +171,38 @@ class EPMoEBlock:
         return self.ep.dispatch_combine(
             x, idx, scores, expert_fn, padded=self.padded,
             combine_fn=lambda y, sc: ops.combine(y.contiguous(), sc, residual=residual))
+
+
+class EPPeerBlock:
+    """An expert-parallel MoE layer whose exchanges are stores into the other ranks' peer
+    buffers (``ops.peer_layer``): calls with the group's token count take that path,
+    others (a prompt) the NCCL all-to-all block ``fallback``.  The rank's pool must hold
+    all of its experts (the layer never reads routing back to the host)."""
+
+    def __init__(self, block: MoEBlock, peers, switch, first: int, n_local: int, fallback=None):
+        self.block, self.peers, self.switch = block, peers, switch
+        self.first, self.n_local, self.fallback = first, n_local, fallback
+        if not switch._pool.full:
+            raise ValueError("the peer-memory layer needs every local expert resident")
+
+    @property
+    def padded(self) -> bool:
+        """The fallback block's exchange mode (a prompt's exact all-to-all, or padded)."""
+        return self.fallback.padded
+
+    @padded.setter
+    def padded(self, v: bool) -> None:
+        self.fallback.padded = v
+
+    def __call__(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        if x.shape[0] != self.peers.tokens:
+            return self.fallback(x, residual=residual)
+        pool = self.switch._pool
+        mode, norm = self.block.mode
+        pool.ready()
+        out = ops.peer_layer(self.peers, x, self.block.gate_w, self.block.gate_b,
+                             self.block.n_experts, self.first, self.n_local, pool.slab,
+                             pool.layout, mode, norm, g2s=pool.g2s_device(), residual=residual,
+                             workspace=self.switch.workspace)
+        pool.mark_read()
+        return out

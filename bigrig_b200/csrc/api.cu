@@ -58,7 +58,8 @@ const char* kKernelNames[BIGRIG_K_COUNT] = {
     "gemv_gate_up_kernel",  "gemv_down_kernel",   "combine_kernel",
     "dequant_kernel",       "grouped_gemm_kernel<gate_up>", "grouped_gemm_kernel<down>",
     "route_kernel",         "down_combine_kernel", "decode_layer_kernel",
-    "decode_split_kernel"};
+    "decode_split_kernel",  "peer_gather_kernel",  "peer_localize_kernel",
+    "peer_scatter_kernel",  "peer_combine_kernel"};
 std::atomic<int> g_path{BIGRIG_PATH_AUTO};
 std::atomic<int> g_gemm_min_rows{8};
 constexpr int kDecodePairs = 32;     // routed pairs the fused decode chain / GEMV path takes
@@ -142,6 +143,49 @@ size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Wor
   ws.arrivals = ws.err ? reinterpret_cast<uint64_t*>(ws.err + 4) : nullptr;
   if (w) *w = ws;
   return off;
+}
+
+// Scratch of one expert-parallel layer call ahead of its switch_glu workspace: the route
+// of all T gathered rows over the full router (logits, global ids, scores), the ids in
+// this rank's numbering, and the pairs' output rows.
+struct PeerScratch {
+  float* logits;      // [T, E]
+  int32_t* idx;       // [T * k]
+  float* scores;      // [T * k]
+  int32_t* idx_local; // [T * k]
+  uint16_t* y;        // [T * k, H]
+};
+
+size_t peer_carve(void* base, int T, int k, int E, int H, PeerScratch* ps) {
+  const size_t P = static_cast<size_t>(T) * k;
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> void* {
+    void* p = base ? static_cast<char*>(base) + off : nullptr;
+    off += align_up(bytes);
+    return p;
+  };
+  PeerScratch s;
+  s.logits = static_cast<float*>(take(static_cast<size_t>(T) * E * sizeof(float)));
+  s.idx = static_cast<int32_t*>(take(P * sizeof(int32_t)));
+  s.scores = static_cast<float*>(take(P * sizeof(float)));
+  s.idx_local = static_cast<int32_t*>(take(P * sizeof(int32_t)));
+  s.y = static_cast<uint16_t*>(take(P * H * sizeof(uint16_t)));
+  if (ps) *ps = s;
+  return off;
+}
+
+int check_peer_group(const bigrig_peer_group* g) {
+  if (!g) return set_error(BIGRIG_ERR_INVALID, "peer group is NULL");
+  if (g->world < 1 || g->world > BIGRIG_PEER_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
+    return set_error(BIGRIG_ERR_INVALID, "peer group: world=%d rank=%d (world <= %d)", g->world,
+                     g->rank, BIGRIG_PEER_MAX_RANKS);
+  if (g->tokens < 1 || g->hidden < 8 || g->hidden % 8 || g->top_k < 1 || g->top_k > 32)
+    return set_error(BIGRIG_ERR_INVALID, "peer group: tokens=%d hidden=%d top_k=%d", g->tokens,
+                     g->hidden, g->top_k);
+  for (int i = 0; i < g->world; ++i)
+    if (!g->base[i] || reinterpret_cast<uintptr_t>(g->base[i]) % 256)
+      return set_error(BIGRIG_ERR_INVALID, "peer group: buffer of rank %d missing or unaligned", i);
+  return BIGRIG_OK;
 }
 
 int check_layout(const bigrig_expert_layout* Lp) {
@@ -575,6 +619,65 @@ int bigrig_workspace_errors(void* workspace, int32_t* out, void* stream) {
       cudaStreamSynchronize(s) != cudaSuccess)
     return set_error(BIGRIG_ERR_CUDA, "workspace_errors: %s", cudaGetErrorString(cudaGetLastError()));
   return BIGRIG_OK;
+}
+
+size_t bigrig_peer_workspace_bytes(const bigrig_peer_group* g, int n_experts, int n_local,
+                                   const bigrig_expert_layout* layout) {
+  if (!g || !layout || g->world < 1 || g->tokens < 1 || g->top_k < 1 || n_experts < 1 ||
+      n_local < 1)
+    return 0;
+  const int T = g->world * g->tokens;
+  return peer_carve(nullptr, T, g->top_k, n_experts, layout->hidden, nullptr) +
+         carve(nullptr, T, g->top_k, n_local, *layout, nullptr);
+}
+
+int bigrig_peer_layer(const bigrig_peer_group* g, const void* x, const void* gate_w,
+                      const float* gate_b, int E, int mode, int norm_topk, int first_expert,
+                      int n_local, const int32_t* g2s, const void* slab,
+                      const bigrig_expert_layout* layout, const void* residual, void* out,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_peer_group(g)) return rc;
+  if (int rc = check_layout(layout)) return rc;
+  const int k = g->top_k, H = layout->hidden;
+  if (int rc = check_route(g->tokens, k, E)) return rc;
+  if (H != g->hidden)
+    return set_error(BIGRIG_ERR_INVALID, "peer_layer: layout hidden %d != group hidden %d", H,
+                     g->hidden);
+  if (n_local < 1 || first_expert < 0 || first_expert + n_local > E)
+    return set_error(BIGRIG_ERR_INVALID, "peer_layer: experts [%d, %d) outside [0, %d)",
+                     first_expert, first_expert + n_local, E);
+  if (mode != BIGRIG_SOFTMAX_TOPK && mode != BIGRIG_TOPK_SOFTMAX)
+    return set_error(BIGRIG_ERR_INVALID, "peer_layer: mode=%d", mode);
+  if (!x || !gate_w || !slab || !out || !workspace)
+    return set_error(BIGRIG_ERR_INVALID, "peer_layer: NULL pointer");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(gate_w) % 16 ||
+      reinterpret_cast<uintptr_t>(slab) % 16 || (residual && reinterpret_cast<uintptr_t>(residual) % 4) ||
+      reinterpret_cast<uintptr_t>(out) % 4)
+    return set_error(BIGRIG_ERR_INVALID, "peer_layer: x, gate_w, slab must be 16-byte aligned, "
+                     "residual and out 4-byte aligned");
+  const int T = g->world * g->tokens;
+  const size_t pbytes = peer_carve(nullptr, T, k, E, H, nullptr);
+  const size_t need = pbytes + carve(nullptr, T, k, n_local, *layout, nullptr);
+  if (workspace_bytes < need)
+    return set_error(BIGRIG_ERR_WORKSPACE, "peer_layer: workspace %zu bytes < %zu needed",
+                     workspace_bytes, need);
+  PeerScratch ps;
+  peer_carve(workspace, T, k, E, H, &ps);
+  Workspace ws;
+  carve(static_cast<char*>(workspace) + pbytes, T, k, n_local, *layout, &ws);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const PeerLayout lay = peer_layout(g->world, g->tokens, H, k);
+  const void* rows = static_cast<const uint8_t*>(g->base[g->rank]) + lay.xin;   // [T, H] gathered
+  if (int rc = launch_peer_gather(*g, x, s)) return rc;
+  if (int rc = launch_router_logits(rows, gate_w, gate_b, ps.logits, T, H, E, s)) return rc;
+  if (int rc = launch_router_topk(ps.logits, BIGRIG_F32, T, E, k, mode, norm_topk, ps.idx,
+                                  ps.scores, s))
+    return rc;
+  if (int rc = launch_peer_localize(ps.idx, T * k, first_expert, n_local, ps.idx_local, s)) return rc;
+  if (int rc = run_switch_glu(rows, ps.idx_local, T, k, n_local, g2s, slab, *layout, ps.y, ws, s))
+    return rc;
+  if (int rc = launch_peer_scatter(*g, ps.y, ps.idx_local, s)) return rc;
+  return launch_peer_combine(*g, ps.scores, residual, out, s);
 }
 
 }  // extern "C"

@@ -800,16 +800,17 @@ __global__ void __launch_bounds__((kDsCW + 1) * 32, 1) decode_split_kernel(
     const int j = pr / R, r = pr - j * R, row = row0 + r;
     float y = 0.f;
     if (row < H && s_slot[j] >= 0) {
+      // up to eight L2 loads in flight at once (guarded, not a dependent chain), then their
+      // adds in group order
       const float* src = a.ypart + static_cast<size_t>(j) * gi * H + row;
-      int gg = sub;
-      for (; gg + 7 * S < gi; gg += 8 * S) {       // eight L2 loads in flight, then their adds
+      for (int gg = sub; gg < gi; gg += 8 * S) {
         float v[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __ldcg(src + static_cast<size_t>(gg + i * S) * H);
+        for (int i = 0; i < 8; ++i)
+          v[i] = gg + i * S < gi ? __ldcg(src + static_cast<size_t>(gg + i * S) * H) : 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) y += v[i];
       }
-      for (; gg < gi; gg += S) y += __ldcg(src + static_cast<size_t>(gg) * H);
     }
     ysub[idx] = y;
   }

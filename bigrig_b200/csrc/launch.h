@@ -113,4 +113,30 @@ int launch_widen_expert(const void* src, void* dst, const bigrig_expert_layout& 
 int launch_combine(const void* y, const float* scores, int T, int k, int H, void* out,
                    cudaStream_t s, const void* residual = nullptr);
 
+// Peer buffer of one rank of an expert-parallel group (ep_peer.cu), the same offsets on
+// every rank: gather flags [world] u64 (slot i raised by rank i), scatter flags [world],
+// control (u64 layer counter, i32 timeout count), the gathered rows [world * tokens][H]
+// bf16, the pair outputs of this rank's rows [tokens][k][H] bf16.
+struct PeerLayout {
+  size_t gflag, pflag, ctrl, xin, ybuf, total;
+};
+inline PeerLayout peer_layout(int world, int tokens, int hidden, int k) {
+  auto up = [](size_t n) { return (n + 255) / 256 * 256; };
+  PeerLayout l;
+  l.gflag = 0;
+  l.pflag = 64;
+  l.ctrl = 128;
+  l.xin = 256;
+  l.ybuf = l.xin + up(static_cast<size_t>(world) * tokens * hidden * 2);
+  l.total = l.ybuf + up(static_cast<size_t>(tokens) * k * hidden * 2);
+  return l;
+}
+int launch_peer_gather(const bigrig_peer_group& g, const void* x, cudaStream_t s);
+int launch_peer_localize(const int32_t* idx, int P, int first, int n_local, int32_t* idx_local,
+                         cudaStream_t s);
+int launch_peer_scatter(const bigrig_peer_group& g, const void* y, const int32_t* idx_local,
+                        cudaStream_t s);
+int launch_peer_combine(const bigrig_peer_group& g, const float* scores, const void* residual,
+                        void* out, cudaStream_t s);
+
 }  // namespace bigrig

@@ -142,3 +142,79 @@ def local_expert_fn(slab, layout, n_local: int, g2s=None, workspace=None):
         return y.reshape(rows.shape[0], rows.shape[1])
 
     return fn
+
+
+class PeerBuffers:
+    """Every rank's expert-parallel peer buffer, mapped into this process
+    (``bigrig_peer_group``): each rank allocates one buffer sized for ``tokens`` rows per
+    layer call, the IPC handles are exchanged over the process group, and every other
+    rank's buffer is opened here.  ``bigrig_peer_layer`` (``ops.peer_layer``) then moves
+    rows between them with stores over NVLink; no NCCL call is on that path.  A group of
+    one rank (no process group) is its own peer."""
+
+    def __init__(self, tokens: int, hidden: int, top_k: int, device, group=None):
+        import ctypes
+
+        from . import _lib
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = torch.device(device)
+        lib = self._lib = _lib.load()
+        nbytes = lib.bigrig_peer_buffer_bytes(self.world, tokens, hidden, top_k)
+        if nbytes == 0:
+            raise ValueError(f"no peer group of {self.world} ranks x {tokens} tokens "
+                             f"(at most {_lib.PEER_MAX_RANKS} ranks)")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * _lib.PEER_HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.bigrig_peer_alloc(nbytes, ctypes.byref(own), handle), "peer_alloc")
+            handles = [bytes(handle)]
+            if self.world > 1:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, bytes(handle), group=group)
+            self._opened = []
+            bases = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(own.value)
+                    continue
+                p = ctypes.c_void_p()
+                buf = (ctypes.c_uint8 * _lib.PEER_HANDLE_BYTES).from_buffer_copy(h)
+                _lib.check(lib.bigrig_peer_open(buf, ctypes.byref(p)), "peer_open")
+                self._opened.append(p.value)
+                bases.append(p.value)
+        self._own = own.value
+        self.c = _lib.PeerGroup(world=self.world, rank=self.rank, tokens=tokens, hidden=hidden,
+                                top_k=top_k)
+        for i, b in enumerate(bases):
+            self.c.base[i] = b
+        self.tokens, self.hidden, self.top_k = tokens, hidden, top_k
+        if self.world > 1:
+            dist.barrier(group)                  # every buffer mapped before the first layer
+
+    def errors(self) -> int:
+        """Read and clear this rank's count of peer waits that ran out."""
+        import ctypes
+
+        from . import _lib
+        n = ctypes.c_int32(0)
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(self._lib.bigrig_peer_errors(ctypes.byref(self.c), ctypes.byref(n),
+                                                ctypes.c_void_p(s)), "peer_errors")
+        return int(n.value)
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers and free this one (after every rank is done)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(self.group)
+        for p in self._opened:
+            self._lib.bigrig_peer_close(p)
+        if self.world > 1:
+            dist.barrier(self.group)             # no rank frees while another still maps it
+        self._lib.bigrig_peer_free(self._own)
+        self._own = None
+        self._opened = []

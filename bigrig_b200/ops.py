@@ -363,3 +363,45 @@ def switch_glu_noalloc(x: torch.Tensor, indices: torch.Tensor, slab: torch.Tenso
         _vp(x), _vp(indices), T, k, n_experts, _vp(g2s), _vp(slab), ctypes.byref(c_layout(layout)),
         _vp(out), _stream(x)), "switch_glu_noalloc")
     return out
+
+
+def peer_workspace_bytes(peers, n_experts: int, n_local: int, layout: Layout) -> int:
+    """Scratch of one ``peer_layer`` call of this group."""
+    n = _lib.load().bigrig_peer_workspace_bytes(ctypes.byref(peers.c), n_experts, n_local,
+                                                ctypes.byref(c_layout(layout)))
+    if n == 0:
+        raise ValueError("peer_workspace_bytes: invalid group or layer")
+    return int(n)
+
+
+def peer_layer(peers, x: torch.Tensor, gate_w: torch.Tensor, gate_b: torch.Tensor | None,
+               n_experts: int, first: int, n_local: int, slab: torch.Tensor, layout: Layout,
+               mode: str = "softmax_topk", norm_topk: bool = False,
+               g2s: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+               out: torch.Tensor | None = None, workspace: Workspace | None = None) -> torch.Tensor:
+    """One expert-parallel MoE layer over the peer buffers of ``peers`` (ep.PeerBuffers):
+    x bf16 [tokens, H] are this rank's rows; every rank calls it with its own rows and the
+    same router; this rank's experts are [first, first + n_local) held in ``slab``
+    (``g2s`` maps them, numbered from 0, to slots).  Returns out [tokens, H] =
+    residual + sum_j score * y for this rank's rows."""
+    _require_cuda("x", x, torch.bfloat16)
+    _require_cuda("gate_w", gate_w, torch.bfloat16)
+    _require_cuda("slab", slab, torch.uint8)
+    if gate_b is not None:
+        _require_cuda("gate_b", gate_b, torch.float32)
+    if residual is not None:
+        _require_cuda("residual", residual, torch.bfloat16)
+    if mode not in _MODES:
+        raise ValueError(f"mode must be one of {tuple(_MODES)}, got {mode!r}")
+    if tuple(x.shape) != (peers.tokens, peers.hidden):
+        raise ValueError(f"x must be [{peers.tokens}, {peers.hidden}], got {tuple(x.shape)}")
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty(peers.tokens, layout.hidden, dtype=torch.bfloat16, device=x.device)
+    ws = workspace or default_workspace(x.device)
+    buf = ws.reserve(peer_workspace_bytes(peers, n_experts, n_local, layout))
+    _lib.check(_lib.load().bigrig_peer_layer(
+        ctypes.byref(peers.c), _vp(x), _vp(gate_w), _vp(gate_b), n_experts, _MODES[mode],
+        int(norm_topk), first, n_local, _vp(g2s), _vp(slab), ctypes.byref(c_layout(layout)),
+        _vp(residual), _vp(out), _vp(buf), buf.numel(), _stream(x)), "peer_layer")
+    return out

@@ -169,7 +169,11 @@ BIGRIG_API int bigrig_moe_forward(const void* x, const void* logits, int logits_
 #define BIGRIG_K_DOWN_COMBINE 10
 #define BIGRIG_K_DECODE_LAYER 11
 #define BIGRIG_K_DECODE_SPLIT 12
-#define BIGRIG_K_COUNT 13
+#define BIGRIG_K_PEER_GATHER 13
+#define BIGRIG_K_PEER_LOCALIZE 14
+#define BIGRIG_K_PEER_SCATTER 15
+#define BIGRIG_K_PEER_COMBINE 16
+#define BIGRIG_K_COUNT 17
 
 /* Which expert kernels bigrig_switch_glu / bigrig_moe_forward / bigrig_moe_layer use:
  * BIGRIG_PATH_AUTO picks the grouped GEMV for calls of at most 32 routed pairs (decode)
@@ -297,6 +301,83 @@ BIGRIG_API int bigrig_switch_glu_noalloc(const void* x, const int32_t* indices, 
                                          int n_experts, const int32_t* g2s, const void* slab,
                                          const bigrig_expert_layout* layout, void* y,
                                          void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Expert parallelism over peer memory (NVLink / NVSwitch), one process per GPU.
+ *
+ * No counterpart in the reference, which runs on one Mac: this is the B200 way of
+ * sharding its MoE layer.  Rank r of a group of `world` GPUs owns a contiguous block of
+ * every layer's experts, [first_expert, first_expert + n_local).  Each rank keeps one
+ * device buffer (bigrig_peer_alloc) that every other rank maps (bigrig_peer_open of its
+ * IPC handle); bigrig_peer_group lists them, in rank order, as this process sees them.
+ * One layer call (bigrig_peer_layer) on every rank, `tokens` rows each:
+ *   1. gather   each rank stores its rows into every rank's buffer and raises a flag
+ *               there; each waits for all ranks' flags (all world * tokens rows present);
+ *   2. route    the replicated router over all rows: logits, top-k, scores;
+ *   3. experts  this rank's experts over the pairs routed to them (the others are
+ *               padding), the same kernels as bigrig_switch_glu;
+ *   4. scatter  each pair's output row is stored into the buffer of the rank that owns
+ *               the pair's token, at the pair's (token, k) place; a flag per source rank;
+ *   5. combine  each rank waits for every rank's flag and forms
+ *               out = residual + sum_j score * y for its own rows, in k order -- the
+ *               combine of bigrig_moe_layer, so results match one GPU holding every
+ *               expert to the expert kernels' own tolerance.
+ * Flags are 64-bit counters written with release stores at system scope and polled with
+ * acquire loads; every wait is bounded (about 2 s of GPU time): past it the layer counts
+ * a timeout in the group's error word (bigrig_peer_errors), stops waiting for the rest
+ * of the process's calls until that word is cleared, and finishes (its output is then
+ * not meaningful).  Every rank must make the same sequence of calls with the same
+ * `tokens`.  All of it is ordinary kernel launches on `stream` and can be captured in a
+ * CUDA graph.  Peer memory is only read and written by plain loads and stores. */
+#define BIGRIG_PEER_MAX_RANKS 8
+#define BIGRIG_PEER_HANDLE_BYTES 64
+
+typedef struct {
+  int32_t world;     /* ranks in the group, <= BIGRIG_PEER_MAX_RANKS */
+  int32_t rank;      /* this process's rank */
+  int32_t tokens;    /* rows every rank brings to each layer call */
+  int32_t hidden;    /* H of the layers the group serves */
+  int32_t top_k;     /* k of the layers the group serves */
+  int32_t reserved;
+  void* base[BIGRIG_PEER_MAX_RANKS]; /* rank i's buffer as mapped here (base[rank]: own) */
+} bigrig_peer_group;
+
+/* Bytes of one rank's peer buffer for a group of this shape. */
+BIGRIG_API size_t bigrig_peer_buffer_bytes(int world, int tokens, int hidden, int top_k);
+
+/* Allocate a zero-filled peer buffer on the current device and write its IPC handle
+ * (BIGRIG_PEER_HANDLE_BYTES bytes) to `handle`; bigrig_peer_free releases it.  Set-up
+ * only (cudaMalloc, a device synchronisation). */
+BIGRIG_API int bigrig_peer_alloc(size_t bytes, void** ptr, void* handle);
+BIGRIG_API int bigrig_peer_free(void* ptr);
+
+/* Map another rank's buffer from its handle into this process (peer access enabled on
+ * first use); bigrig_peer_close unmaps it.  A handle of this process's own buffer is
+ * refused: use the pointer bigrig_peer_alloc returned. */
+BIGRIG_API int bigrig_peer_open(const void* handle, void** ptr);
+BIGRIG_API int bigrig_peer_close(void* ptr);
+
+/* Scratch of one bigrig_peer_layer call (the route and expert outputs of all
+ * world * tokens rows plus bigrig_moe_workspace_bytes for them over the n_local experts);
+ * zero-filled once, like the other workspaces. */
+BIGRIG_API size_t bigrig_peer_workspace_bytes(const bigrig_peer_group* group, int n_experts,
+                                              int n_local, const bigrig_expert_layout* layout);
+
+/* One MoE layer of the group (steps 1-5 above) for this rank's `group->tokens` rows:
+ * x, residual (may be NULL), out bf16 [tokens, H]; gate_w bf16 [E, H], gate_b fp32 [E] or
+ * NULL (the full router, identical on every rank); g2s int32 [n_local] maps this rank's
+ * experts (numbered from 0) to slots of `slab`.  Returns after issuing the launches. */
+BIGRIG_API int bigrig_peer_layer(const bigrig_peer_group* group, const void* x,
+                                 const void* gate_w, const float* gate_b, int E, int mode,
+                                 int norm_topk, int first_expert, int n_local,
+                                 const int32_t* g2s, const void* slab,
+                                 const bigrig_expert_layout* layout, const void* residual,
+                                 void* out, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
+/* The group's wait-timeout count in this rank's buffer, read synchronously on `stream`
+ * into *out and reset to 0 (which also re-arms the waits). */
+BIGRIG_API int bigrig_peer_errors(const bigrig_peer_group* group, int32_t* out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -73,3 +73,27 @@ def test_compute_refuses_cpu_tensors():
     with pytest.raises(RuntimeError, match="CUDA tensor"):
         ops.router_logits(torch.zeros(1, 64, dtype=torch.bfloat16),
                           torch.zeros(8, 64, dtype=torch.bfloat16))
+
+
+def test_peer_group_checks_need_no_device():
+    lib = _lib.load()
+    assert ctypes.sizeof(_lib.PeerGroup) == 24 + 8 * _lib.PEER_MAX_RANKS
+    n1 = lib.bigrig_peer_buffer_bytes(2, 1, 2048, 8)
+    n2 = lib.bigrig_peer_buffer_bytes(4, 1, 2048, 8)
+    # gathered rows grow with the group, the pair outputs do not
+    assert n2 - n1 == 2 * 2048 * 2 and n1 % 256 == 0
+    assert lib.bigrig_peer_buffer_bytes(9, 1, 2048, 8) == 0       # more ranks than supported
+    L = formats.layout_from_spec(formats.make_spec(2048, 1024, 4, 64, "float16"))
+    c = ops.c_layout(L)
+    g = _lib.PeerGroup(world=2, rank=0, tokens=1, hidden=2048, top_k=8)
+    # a group whose peer buffer is missing is refused before any launch
+    g.base[0] = 1 << 20
+    rc = lib.bigrig_peer_layer(ctypes.byref(g), None, None, None, 64, 0, 0, 0, 32, None, None,
+                               ctypes.byref(c), None, None, None, 0, None)
+    assert rc == _lib.ERR_INVALID and "rank 1" in _lib.last_error()
+    g.base[1] = 2 << 20
+    rc = lib.bigrig_peer_layer(ctypes.byref(g), None, None, None, 64, 0, 0, 48, 32, None, None,
+                               ctypes.byref(c), None, None, None, 0, None)
+    assert rc == _lib.ERR_INVALID and "outside" in _lib.last_error()
+    ws = lib.bigrig_peer_workspace_bytes(ctypes.byref(g), 64, 32, ctypes.byref(c))
+    assert ws > ops.workspace_bytes(2, 8, 32, L)
