@@ -568,6 +568,10 @@ def ep_reference_check(dev, c: dict, stack, x: torch.Tensor, rank: int, world: i
         ref_blocks, store = build_model(dev, seed=0, layers=c["layers"])
         ref_handle = attach(ref_blocks, store, c["experts"], policy=c["policy"], warm="auto",
                             device=dev)
+    # the other ranks wait here while rank 0 builds the reference (seconds): a peer-memory
+    # layer's bounded waits must not start before every rank can answer them
+    torch.cuda.synchronize(dev)
+    dist.barrier()
     outside, worst, max_abs, n = 0, 0.0, 0.0, 0
     h = x
     for li, blk in enumerate(stack):
@@ -780,6 +784,7 @@ def main() -> None:
         handle.reset_stats()
 
     # ---- decode, capped pool: warm-up then K timed steps
+    barrier()                                  # ranks meet before the first peer-memory layer
     for i in range(W):
         stack_step(stack, tokens[i])
     step, graph = stack_step, None
@@ -864,8 +869,20 @@ def main() -> None:
     # ---- expert-parallel check: every rank's first timed token through the EP stack
     # against the same token through one GPU holding every expert (rank 0)
     ep_check = None
+    peer_timeouts = None
+    if world > 1 and args.ep == "peer":
+        peer_timeouts = {"decode": peers.errors()}
     if world > 1:
         ep_check = ep_reference_check(dev, c, stack, tokens[W].clone(), rank, world, dist)
+    if world > 1 and args.ep == "peer":
+        peer_timeouts["check"] = peers.errors()
+        t = torch.tensor([peer_timeouts["decode"], peer_timeouts["check"]], device=dev)
+        dist.all_reduce(t)                 # every rank's count, summed
+        peer_timeouts = {"decode": int(t[0]), "check": int(t[1]),
+                         "note": "peer waits that ran out, all ranks: in the warm-up, timed and "
+                                 "end-to-end decode, and in the expert-parallel check"}
+        if ep_check is not None and peer_timeouts["check"]:
+            ep_check["ok"] = False
     if graph is not None:
         del step, graph
         graph = None
@@ -1034,6 +1051,7 @@ def main() -> None:
             "cpu_baseline": cpu,
             **({"ep_check": ep_check, "ep_graph": bool(world > 1 and all(b.padded for b in stack))}
                if world > 1 else {}),
+            **({"peer_wait_timeouts": peer_timeouts} if peer_timeouts is not None else {}),
             **extras,
         }
         print(json.dumps(line), flush=True)

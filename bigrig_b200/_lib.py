@@ -60,7 +60,7 @@ class PeerGroup(ctypes.Structure):
     """Mirror of ``bigrig_peer_group`` (include/bigrig_b200.h)."""
     _fields_ = [
         ("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("tokens", ctypes.c_int32),
-        ("hidden", ctypes.c_int32), ("top_k", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("hidden", ctypes.c_int32), ("top_k", ctypes.c_int32), ("wait_ms", ctypes.c_int32),
         ("base", ctypes.c_void_p * PEER_MAX_RANKS),
     ]
 

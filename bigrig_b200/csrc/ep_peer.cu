@@ -40,10 +40,11 @@ namespace bigrig {
 namespace {
 
 constexpr int kPeerThreads = 512;
-constexpr uint64_t kPeerWaitNs = 2000000000ull;   // 2 s of GPU time per wait
+constexpr uint64_t kPeerWaitDefaultMs = 10000;    // per wait, when the group sets none
 
 struct PeerArgs {
   int world, rank, tokens, hidden, k;
+  uint64_t wait_ns;
   PeerLayout lay;
   uint8_t* base[BIGRIG_PEER_MAX_RANKS];
 };
@@ -55,6 +56,7 @@ PeerArgs peer_args(const bigrig_peer_group& g) {
   a.tokens = g.tokens;
   a.hidden = g.hidden;
   a.k = g.top_k;
+  a.wait_ns = (g.wait_ms > 0 ? static_cast<uint64_t>(g.wait_ms) : kPeerWaitDefaultMs) * 1000000ull;
   a.lay = peer_layout(g.world, g.tokens, g.hidden, g.top_k);
   for (int i = 0; i < BIGRIG_PEER_MAX_RANKS; ++i)
     a.base[i] = i < g.world ? static_cast<uint8_t*>(g.base[i]) : nullptr;
@@ -91,11 +93,11 @@ __device__ __forceinline__ int32_t* err_of(const PeerArgs& a) {
 
 // Wait until *flag >= want; false after the time limit (counted in err) or at once when
 // the group has already failed.
-__device__ bool peer_wait(const uint64_t* flag, uint64_t want, int32_t* err) {
+__device__ bool peer_wait(const uint64_t* flag, uint64_t want, int32_t* err, uint64_t limit_ns) {
   if (*reinterpret_cast<volatile int32_t*>(err) != 0) return false;
   const uint64_t t0 = global_ns();
   while (ld_acquire_sys(flag) < want) {
-    if (global_ns() - t0 > kPeerWaitNs) {
+    if (global_ns() - t0 > limit_ns) {
       atomicAdd(err, 1);
       return false;
     }
@@ -128,7 +130,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_gather_kernel(PeerArgs a,
   __syncthreads();
   if (threadIdx.x < a.world) {
     peer_signal(flag_at(a, threadIdx.x, a.lay.gflag, a.rank), layer);
-    peer_wait(flag_at(a, a.rank, a.lay.gflag, threadIdx.x), layer, err_of(a));
+    peer_wait(flag_at(a, a.rank, a.lay.gflag, threadIdx.x), layer, err_of(a), a.wait_ns);
   }
   __syncthreads();
   if (threadIdx.x == 0) ctrl[0] = layer;
@@ -165,7 +167,8 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(PeerArgs a,
                                                            const uint16_t* __restrict__ residual,
                                                            uint16_t* __restrict__ out) {
   const uint64_t layer = ctrl_of(a)[0];
-  if (threadIdx.x < a.world) peer_wait(flag_at(a, a.rank, a.lay.pflag, threadIdx.x), layer, err_of(a));
+  if (threadIdx.x < a.world)
+    peer_wait(flag_at(a, a.rank, a.lay.pflag, threadIdx.x), layer, err_of(a), a.wait_ns);
   __syncthreads();
   const int t = blockIdx.y, H = a.hidden, k = a.k;
   const int f = (blockIdx.x * blockDim.x + threadIdx.x) * 2;

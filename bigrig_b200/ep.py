@@ -150,9 +150,11 @@ class PeerBuffers:
     layer call, the IPC handles are exchanged over the process group, and every other
     rank's buffer is opened here.  ``bigrig_peer_layer`` (``ops.peer_layer``) then moves
     rows between them with stores over NVLink; no NCCL call is on that path.  A group of
-    one rank (no process group) is its own peer."""
+    one rank (no process group) is its own peer.  ``wait_ms`` bounds each wait for another
+    rank (0: the library's 10 s)."""
 
-    def __init__(self, tokens: int, hidden: int, top_k: int, device, group=None):
+    def __init__(self, tokens: int, hidden: int, top_k: int, device, group=None,
+                 wait_ms: int = 0):
         import ctypes
 
         from . import _lib
@@ -186,7 +188,7 @@ class PeerBuffers:
                 bases.append(p.value)
         self._own = own.value
         self.c = _lib.PeerGroup(world=self.world, rank=self.rank, tokens=tokens, hidden=hidden,
-                                top_k=top_k)
+                                top_k=top_k, wait_ms=int(wait_ms))
         for i, b in enumerate(bases):
             self.c.base[i] = b
         self.tokens, self.hidden, self.top_k = tokens, hidden, top_k

@@ -323,12 +323,15 @@ BIGRIG_API int bigrig_switch_glu_noalloc(const void* x, const int32_t* indices, 
  *               combine of bigrig_moe_layer, so results match one GPU holding every
  *               expert to the expert kernels' own tolerance.
  * Flags are 64-bit counters written with release stores at system scope and polled with
- * acquire loads; every wait is bounded (about 2 s of GPU time): past it the layer counts
+ * acquire loads; every wait is bounded (wait_ms of GPU time): past it the layer counts
  * a timeout in the group's error word (bigrig_peer_errors), stops waiting for the rest
  * of the process's calls until that word is cleared, and finishes (its output is then
  * not meaningful).  Every rank must make the same sequence of calls with the same
- * `tokens`.  All of it is ordinary kernel launches on `stream` and can be captured in a
- * CUDA graph.  Peer memory is only read and written by plain loads and stores. */
+ * `tokens`, and keep their hosts within wait_ms of each other (a rank whose host is busy
+ * elsewhere -- loading, compiling, a long synchronous step -- must first meet the others
+ * at a host barrier).  All of it is ordinary kernel launches on `stream` and can be
+ * captured in a CUDA graph.  Peer memory is only read and written by plain loads and
+ * stores. */
 #define BIGRIG_PEER_MAX_RANKS 8
 #define BIGRIG_PEER_HANDLE_BYTES 64
 
@@ -338,7 +341,7 @@ typedef struct {
   int32_t tokens;    /* rows every rank brings to each layer call */
   int32_t hidden;    /* H of the layers the group serves */
   int32_t top_k;     /* k of the layers the group serves */
-  int32_t reserved;
+  int32_t wait_ms;   /* bound on each wait for another rank, ms of GPU time; 0: 10000 */
   void* base[BIGRIG_PEER_MAX_RANKS]; /* rank i's buffer as mapped here (base[rank]: own) */
 } bigrig_peer_group;
 

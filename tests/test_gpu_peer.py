@@ -97,8 +97,9 @@ def test_peer_layer_in_a_cuda_graph(cuda):
 
 def test_peer_wait_runs_out_on_a_missing_rank(cuda):
     """A group of two whose 'other rank' is this process's own buffer under a second name:
-    nobody raises the flags rank 1 would, so the gather's wait runs out (about 2 s), the
-    layer still finishes, the error word counts it, and later waits return at once."""
+    nobody raises the flags rank 1 would, so the gather's wait runs out (its bound set to
+    0.2 s), the layer still finishes, the error word counts it, and later waits return at
+    once."""
     T, H, I, E, k = 1, 512, 256, 16, 4
     L = Layer(H, I, E, 4, "float16", seed=3)
     lib = _lib.load()
@@ -107,7 +108,7 @@ def test_peer_wait_runs_out_on_a_missing_rank(cuda):
     handle = (ctypes.c_uint8 * _lib.PEER_HANDLE_BYTES)()
     _lib.check(lib.bigrig_peer_alloc(nbytes, ctypes.byref(own), handle), "peer_alloc")
     try:
-        g = _lib.PeerGroup(world=2, rank=0, tokens=T, hidden=H, top_k=k)
+        g = _lib.PeerGroup(world=2, rank=0, tokens=T, hidden=H, top_k=k, wait_ms=200)
         g.base[0] = own.value
         g.base[1] = own.value
 
