@@ -145,7 +145,9 @@ size_t carve(void* base, int T, int k, int E, const bigrig_expert_layout& L, Wor
   return off;
 }
 
-// Scratch of one expert-parallel layer call ahead of its switch_glu workspace: the route
+// Scratch of one expert-parallel layer call after its switch_glu workspace (which keeps the
+// head of every workspace -- error words, route ticket, the persistent kernel's barrier
+// arrivals -- where the other entry points sharing the workspace expect them): the route
 // of all T gathered rows over the full router (logits, global ids, scores), the ids in
 // this rank's numbering, and the pairs' output rows.
 struct PeerScratch {
@@ -656,15 +658,15 @@ int bigrig_peer_layer(const bigrig_peer_group* g, const void* x, const void* gat
     return set_error(BIGRIG_ERR_INVALID, "peer_layer: x, gate_w, slab must be 16-byte aligned, "
                      "residual and out 4-byte aligned");
   const int T = g->world * g->tokens;
-  const size_t pbytes = peer_carve(nullptr, T, k, E, H, nullptr);
-  const size_t need = pbytes + carve(nullptr, T, k, n_local, *layout, nullptr);
+  const size_t sbytes = carve(nullptr, T, k, n_local, *layout, nullptr);
+  const size_t need = sbytes + peer_carve(nullptr, T, k, E, H, nullptr);
   if (workspace_bytes < need)
     return set_error(BIGRIG_ERR_WORKSPACE, "peer_layer: workspace %zu bytes < %zu needed",
                      workspace_bytes, need);
-  PeerScratch ps;
-  peer_carve(workspace, T, k, E, H, &ps);
   Workspace ws;
-  carve(static_cast<char*>(workspace) + pbytes, T, k, n_local, *layout, &ws);
+  carve(workspace, T, k, n_local, *layout, &ws);
+  PeerScratch ps;
+  peer_carve(static_cast<char*>(workspace) + sbytes, T, k, E, H, &ps);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const PeerLayout lay = peer_layout(g->world, g->tokens, H, k);
   const void* rows = static_cast<const uint8_t*>(g->base[g->rank]) + lay.xin;   // [T, H] gathered

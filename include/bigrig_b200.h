@@ -360,8 +360,9 @@ BIGRIG_API int bigrig_peer_free(void* ptr);
 BIGRIG_API int bigrig_peer_open(const void* handle, void** ptr);
 BIGRIG_API int bigrig_peer_close(void* ptr);
 
-/* Scratch of one bigrig_peer_layer call (the route and expert outputs of all
- * world * tokens rows plus bigrig_moe_workspace_bytes for them over the n_local experts);
+/* Scratch of one bigrig_peer_layer call (bigrig_moe_workspace_bytes for all
+ * world * tokens rows over the n_local experts, laid out as for the other entry points so
+ * one workspace serves them all, then the route and expert outputs of those rows);
  * zero-filled once, like the other workspaces. */
 BIGRIG_API size_t bigrig_peer_workspace_bytes(const bigrig_peer_group* group, int n_experts,
                                               int n_local, const bigrig_expert_layout* layout);

@@ -129,3 +129,35 @@ def test_peer_wait_runs_out_on_a_missing_rank(cuda):
     finally:
         torch.cuda.synchronize()
         lib.bigrig_peer_free(own)
+
+
+def test_peer_layer_shares_a_workspace_with_the_one_token_kernel(cuda):
+    """Peer layers and the persistent one-token layer kernel on one workspace, interleaved:
+    the one-token kernel keeps its barrier counter and error words at the head of every
+    workspace, and the peer layer must leave them as it found them."""
+    T, H, I, E, k = 1, 2048, 1024, 64, 8
+    L = Layer(H, I, E, 4, "float16", seed=21)
+    rng = np.random.default_rng(21)
+    gw = bf16_tensor((rng.standard_normal((E, H)) * 0.02).astype(np.float32))
+    gb = torch.from_numpy(rng.standard_normal(E).astype(np.float32)).to(cuda)
+    peers = PeerBuffers(T, H, k, cuda)
+    ws = ops.Workspace(cuda)
+    try:
+        xs = [bf16_tensor(rng.standard_normal((T, H)).astype(np.float32)) for _ in range(4)]
+        want = [ops.moe_layer(x, gw, gb, k, L.slab, L.layout, E, g2s=L.g2s, residual=x,
+                              workspace=ops.Workspace(cuda))[0] for x in xs]
+        n0 = _lib.launch_counts()
+        for x, w in zip(xs, want):
+            p = ops.peer_layer(peers, x, gw, gb, E, 0, E, L.slab, L.layout, g2s=L.g2s,
+                               residual=x, workspace=ws)
+            got = ops.moe_layer(x, gw, gb, k, L.slab, L.layout, E, g2s=L.g2s, residual=x,
+                                workspace=ws)[0]
+            torch.cuda.synchronize()
+            assert torch.equal(got.view(torch.int16), w.view(torch.int16))
+            assert torch.equal(p.view(torch.int16),
+                               _reference(L, x, gw, gb, k, "softmax_topk", False, x).view(torch.int16))
+        n1 = _lib.launch_counts()
+        assert n1["decode_layer"] + n1["decode_split"] - n0["decode_layer"] - n0["decode_split"] == 4
+        assert ws.errors() == 0 and peers.errors() == 0
+    finally:
+        peers.close()
