@@ -284,6 +284,17 @@ int run_fused(const void* x, const void* gate_w, const float* gate_b, const void
   return launch_down_combine(ws.h, rv, slab, L, sc, residual, out, nullptr, T, s);
 }
 
+// The tensor-core GEMM once a call has more pairs than the decode chain takes (its
+// dequant streams weights far faster than the GEMV's passes over an expert's rows, even
+// at 16-column MMAs), or when the mean rows per routed expert reaches gemm_min_rows.
+bool switch_glu_gemm(int P, int E) {
+  const int path = g_path.load();
+  return path == BIGRIG_PATH_GEMM ||
+         ((path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_CHAIN || path == BIGRIG_PATH_TILED ||
+           path == BIGRIG_PATH_SPLIT) &&
+          (P > kDecodePairs || P >= g_gemm_min_rows.load() * (P < E ? P : E)));
+}
+
 int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, const int32_t* g2s,
                    const void* slab, const bigrig_expert_layout& L, void* y, const Workspace& ws,
                    cudaStream_t s) {
@@ -292,14 +303,7 @@ int run_switch_glu(const void* x, const int32_t* indices, int T, int k, int E, c
                               ws.seg_start, ws.num_seg, ws.err, s))
     return rc;
   const RouteView rv = route_view(ws, g2s, T, k, E);
-  const int path = g_path.load();
-  // The tensor-core GEMM once a call has more pairs than the decode chain takes (its
-  // dequant streams weights far faster than the GEMV's passes over an expert's rows, even
-  // at 16-column MMAs), or when the mean rows per routed expert reaches gemm_min_rows.
-  const bool gemm = path == BIGRIG_PATH_GEMM ||
-                    ((path == BIGRIG_PATH_AUTO || path == BIGRIG_PATH_CHAIN ||
-                      path == BIGRIG_PATH_TILED || path == BIGRIG_PATH_SPLIT) &&
-                     (P > kDecodePairs || P >= g_gemm_min_rows.load() * (P < E ? P : E)));
+  const bool gemm = switch_glu_gemm(P, E);
   if (gemm) {
     const int mean = gemm_mean_rows(T, k, E);
     if (int rc = launch_gemm_gate_up(x, rv, slab, L, ws.h, ws.xp, T, mean, s)) return rc;
@@ -671,6 +675,21 @@ int bigrig_peer_layer(const bigrig_peer_group* g, const void* x, const void* gat
   const PeerLayout lay = peer_layout(g->world, g->tokens, H, k);
   const void* rows = static_cast<const uint8_t*>(g->base[g->rank]) + lay.xin;   // [T, H] gathered
   if (int rc = launch_peer_gather(*g, x, s)) return rc;
+  const int P = T * k;
+  if (P <= kDecodePairs && !switch_glu_gemm(P, n_local)) {
+    // decode-sized: router, top-k, the local numbering and the permutation in one launch
+    // (the chain's route kernel), then the GEMV pair
+    const RouteOut ro{ws.order, ws.inv, ws.offsets, ws.seg_expert, ws.seg_start, ws.num_seg, ws.err};
+    if (int rc = launch_route(rows, gate_w, gate_b, nullptr, BIGRIG_F32, T, H, E, k, mode,
+                              norm_topk, ps.logits, ws.ticket, ps.idx, ps.scores, ro, s,
+                              first_expert, n_local, ps.idx_local))
+      return rc;
+    const RouteView rv = route_view(ws, g2s, T, k, n_local);
+    if (int rc = launch_gemv_gate_up(rows, rv, slab, *layout, ws.h, s)) return rc;
+    if (int rc = launch_gemv_down(ws.h, rv, slab, *layout, ps.y, s)) return rc;
+    if (int rc = launch_peer_scatter(*g, ps.y, ps.idx_local, s)) return rc;
+    return launch_peer_combine(*g, ps.scores, residual, out, s);
+  }
   if (int rc = launch_router_logits(rows, gate_w, gate_b, ps.logits, T, H, E, s)) return rc;
   if (int rc = launch_router_topk(ps.logits, BIGRIG_F32, T, E, k, mode, norm_topk, ps.idx,
                                   ps.scores, s))

@@ -27,7 +27,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
     const float* __restrict__ gate_b, const void* __restrict__ logits_in, int logits_dtype, int T,
     int H, int E, int k, int mode, int norm_topk, float* __restrict__ logits_ws,
     int32_t* __restrict__ ticket, int32_t* __restrict__ idx_out, float* __restrict__ sc_out,
-    RouteOut ro) {
+    RouteOut ro, int local_first, int local_n, int32_t* __restrict__ idx_local) {
   __shared__ int s_last;
   __shared__ int32_t s_idx[32];
   pdl_wait();
@@ -78,10 +78,17 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(
   __syncthreads();
   if (warp == 0) {
     const int P = T * k;
-    s_idx[lane] = lane < P ? idx_out[lane] : 0;
+    int e = lane < P ? idx_out[lane] : 0;
+    if (local_n > 0) {
+      // expert parallelism: the pairs of this rank's experts in its own numbering, the
+      // others padding (-1), which the permutation leaves out of the segments
+      e = (e >= local_first && e < local_first + local_n) ? e - local_first : -1;
+      if (lane < P) idx_local[lane] = e;
+    }
+    s_idx[lane] = e;
     __syncwarp();
-    permute_warp(s_idx, P, E, ro.order, ro.inv, ro.offsets, ro.seg_expert, ro.seg_start,
-                 ro.num_seg, ro.err);
+    permute_warp(s_idx, P, local_n > 0 ? local_n : E, ro.order, ro.inv, ro.offsets, ro.seg_expert,
+                 ro.seg_start, ro.num_seg, ro.err);
   }
 }
 
@@ -268,7 +275,7 @@ static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
 int launch_route(const void* x, const void* gate_w, const float* gate_b, const void* logits_in,
                  int logits_dtype, int T, int H, int E, int k, int mode, int norm, float* logits_ws,
                  int32_t* ticket, int32_t* idx_out, float* sc_out, const RouteOut& ro,
-                 cudaStream_t s) {
+                 cudaStream_t s, int local_first, int local_n, int32_t* idx_local) {
   const int per = (E + 31) / 32;
   const dim3 grid(logits_in ? 1 : (E + kRouteWarps - 1) / kRouteWarps);
   TimedLaunch tl(BIGRIG_K_ROUTE, s);
@@ -277,7 +284,7 @@ int launch_route(const void* x, const void* gate_w, const float* gate_b, const v
     return launch_pdl(route_kernel<N>, grid, dim3(kRouteWarps * 32), 0, s, "route_kernel",      \
                       static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate_w),    \
                       gate_b, logits_in, logits_dtype, T, H, E, k, mode, norm, logits_ws, ticket, \
-                      idx_out, sc_out, ro);
+                      idx_out, sc_out, ro, local_first, local_n, idx_local);
   switch (per) {
     BIGRIG_ROUTE(1)
     BIGRIG_ROUTE(2)

@@ -65,7 +65,8 @@ struct RouteOut {
 int launch_route(const void* x, const void* gate_w, const float* gate_b, const void* logits_in,
                  int logits_dtype, int T, int H, int E, int k, int mode, int norm, float* logits_ws,
                  int32_t* ticket, int32_t* idx_out, float* sc_out, const RouteOut& ro,
-                 cudaStream_t s);
+                 cudaStream_t s, int local_first = 0, int local_n = 0,
+                 int32_t* idx_local = nullptr);
 size_t down_combine_smem(int P, const bigrig_expert_layout& L);
 size_t down_combine_smem(int P, const bigrig_expert_layout& L, int nf);
 int launch_down_combine(const void* h, const RouteView& rv, const void* slab,
