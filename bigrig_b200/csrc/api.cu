@@ -63,6 +63,7 @@ const char* kKernelNames[BIGRIG_K_COUNT] = {
 std::atomic<int> g_path{BIGRIG_PATH_AUTO};
 std::atomic<int> g_gemm_min_rows{8};
 constexpr int kDecodePairs = 32;     // routed pairs the fused decode chain / GEMV path takes
+constexpr int kPeerGemvPairs = 16;   // a peer layer's expected pairs per rank on the GEMV pair
 }  // namespace
 
 TimedLaunch::TimedLaunch(int kernel_id, cudaStream_t s) : id_(kernel_id), s_(s), start_(nullptr) {
@@ -676,7 +677,13 @@ int bigrig_peer_layer(const bigrig_peer_group* g, const void* x, const void* gat
   const void* rows = static_cast<const uint8_t*>(g->base[g->rank]) + lay.xin;   // [T, H] gathered
   if (int rc = launch_peer_gather(*g, x, s)) return rc;
   const int P = T * k;
-  if (P <= kDecodePairs && !switch_glu_gemm(P, n_local)) {
+  // Most of the T * k pairs belong to other ranks: about P / world are this rank's.  Under
+  // the automatic rule the GEMV pair takes the call while that share is decode-sized (the
+  // grouped GEMM's per-iteration handoff dominates tiles of a few rows).
+  const int share = (P + g->world - 1) / g->world;
+  const bool gemv = !switch_glu_gemm(P, n_local) ||
+                    (g_path.load() == BIGRIG_PATH_AUTO && share <= kPeerGemvPairs);
+  if (gemv && P <= kDecodePairs) {
     // decode-sized: router, top-k, the local numbering and the permutation in one launch
     // (the chain's route kernel), then the GEMV pair
     const RouteOut ro{ws.order, ws.inv, ws.offsets, ws.seg_expert, ws.seg_start, ws.num_seg, ws.err};
@@ -695,8 +702,17 @@ int bigrig_peer_layer(const bigrig_peer_group* g, const void* x, const void* gat
                                   ps.scores, s))
     return rc;
   if (int rc = launch_peer_localize(ps.idx, T * k, first_expert, n_local, ps.idx_local, s)) return rc;
-  if (int rc = run_switch_glu(rows, ps.idx_local, T, k, n_local, g2s, slab, *layout, ps.y, ws, s))
+  if (gemv) {
+    if (int rc = launch_permute(ps.idx_local, P, n_local, ws.order, ws.inv, ws.offsets,
+                                ws.seg_expert, ws.seg_start, ws.num_seg, ws.err, s))
+      return rc;
+    const RouteView rv = route_view(ws, g2s, T, k, n_local);
+    if (int rc = launch_gemv_gate_up(rows, rv, slab, *layout, ws.h, s)) return rc;
+    if (int rc = launch_gemv_down(ws.h, rv, slab, *layout, ps.y, s)) return rc;
+  } else if (int rc = run_switch_glu(rows, ps.idx_local, T, k, n_local, g2s, slab, *layout,
+                                     ps.y, ws, s)) {
     return rc;
+  }
   if (int rc = launch_peer_scatter(*g, ps.y, ps.idx_local, s)) return rc;
   return launch_peer_combine(*g, ps.scores, residual, out, s);
 }

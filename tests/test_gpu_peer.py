@@ -165,3 +165,31 @@ def test_peer_layer_shares_a_workspace_with_the_one_token_kernel(cuda):
         assert ws.errors() == 0 and peers.errors() == 0
     finally:
         peers.close()
+
+
+def test_peer_layer_gemv_past_the_fused_route(cuda):
+    """More than 32 pairs on the GEMV pair (what a large group's per-rank share takes):
+    routed, localised and permuted in separate launches, then the same GEMV kernels as
+    switch_glu under the same path."""
+    T, H, I, E, k = 6, 1024, 256, 32, 8
+    L = Layer(H, I, E, 4, "float16", seed=33)
+    rng = np.random.default_rng(33)
+    gw = bf16_tensor((rng.standard_normal((E, H)) * 0.02).astype(np.float32))
+    peers = PeerBuffers(T, H, k, cuda)
+    old = _lib.set_path("gemv")
+    try:
+        for step in range(2):
+            x = bf16_tensor(rng.standard_normal((T, H)).astype(np.float32))
+            n0 = _lib.launch_counts()
+            got = ops.peer_layer(peers, x, gw, None, E, 0, E, L.slab, L.layout, g2s=L.g2s,
+                                 residual=x)
+            n1 = _lib.launch_counts()
+            want = _reference(L, x, gw, None, k, "softmax_topk", False, x)
+            torch.cuda.synchronize()
+            assert torch.equal(got.view(torch.int16), want.view(torch.int16)), f"step {step}"
+            assert n1["peer_localize"] - n0["peer_localize"] == 1
+            assert n1["gate_up"] - n0["gate_up"] == 1 and n1["gemm_gate_up"] == n0["gemm_gate_up"]
+        assert peers.errors() == 0
+    finally:
+        _lib.set_path(old)
+        peers.close()
