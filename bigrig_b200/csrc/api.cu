@@ -692,9 +692,9 @@ int bigrig_peer_layer(const bigrig_peer_group* g, const void* x, const void* gat
                               first_expert, n_local, ps.idx_local))
       return rc;
     const RouteView rv = route_view(ws, g2s, T, k, n_local);
-    const PeerOut po = peer_out(*g);      // the down GEMV stores into the owners' buffers
     if (int rc = launch_gemv_gate_up(rows, rv, slab, *layout, ws.h, s)) return rc;
-    if (int rc = launch_gemv_down(ws.h, rv, slab, *layout, ps.y, s, &po)) return rc;
+    if (int rc = launch_gemv_down(ws.h, rv, slab, *layout, ps.y, s)) return rc;
+    if (int rc = launch_peer_scatter(*g, ps.y, ps.idx_local, s)) return rc;
     return launch_peer_combine(*g, ps.scores, residual, out, s);
   }
   if (int rc = launch_router_logits(rows, gate_w, gate_b, ps.logits, T, H, E, s)) return rc;
@@ -707,13 +707,12 @@ int bigrig_peer_layer(const bigrig_peer_group* g, const void* x, const void* gat
                                 ws.seg_expert, ws.seg_start, ws.num_seg, ws.err, s))
       return rc;
     const RouteView rv = route_view(ws, g2s, T, k, n_local);
-    const PeerOut po = peer_out(*g);
     if (int rc = launch_gemv_gate_up(rows, rv, slab, *layout, ws.h, s)) return rc;
-    if (int rc = launch_gemv_down(ws.h, rv, slab, *layout, ps.y, s, &po)) return rc;
-    return launch_peer_combine(*g, ps.scores, residual, out, s);
-  }
-  if (int rc = run_switch_glu(rows, ps.idx_local, T, k, n_local, g2s, slab, *layout, ps.y, ws, s))
+    if (int rc = launch_gemv_down(ws.h, rv, slab, *layout, ps.y, s)) return rc;
+  } else if (int rc = run_switch_glu(rows, ps.idx_local, T, k, n_local, g2s, slab, *layout,
+                                     ps.y, ws, s)) {
     return rc;
+  }
   if (int rc = launch_peer_scatter(*g, ps.y, ps.idx_local, s)) return rc;
   return launch_peer_combine(*g, ps.scores, residual, out, s);
 }

@@ -16,9 +16,7 @@
 //                         pairs another rank owns (padding for the expert kernels).
 //   peer_scatter_kernel   CTA d: the output rows of the pairs of rank d's tokens that
 //                         this rank computed, stored at their (token, k) places in rank
-//                         d's buffer; then rank d's flag for this rank.  (On the GEMV
-//                         path the down kernel stores them there itself and its last CTA
-//                         raises the flags: PeerOut, gemv.cu.)
+//                         d's buffer; then rank d's flag for this rank.
 //   peer_combine_kernel   wait for every rank's scatter flag; out = residual +
 //                         sum_j score * y in k order (combine_kernel's arithmetic).
 //
@@ -195,21 +193,6 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(PeerArgs a,
 }
 
 }  // namespace
-
-PeerOut peer_out(const bigrig_peer_group& g) {
-  const PeerLayout lay = peer_layout(g.world, g.tokens, g.hidden, g.top_k);
-  PeerOut po{};
-  for (int i = 0; i < g.world; ++i) po.base[i] = static_cast<uint8_t*>(g.base[i]);
-  uint8_t* own = static_cast<uint8_t*>(g.base[g.rank]);
-  po.ybuf = lay.ybuf;
-  po.pflag = lay.pflag;
-  po.layer = reinterpret_cast<const uint64_t*>(own + lay.ctrl);
-  po.ticket = reinterpret_cast<unsigned int*>(own + lay.ctrl + 16);
-  po.per = g.tokens * g.top_k;
-  po.rank = g.rank;
-  po.world = g.world;
-  return po;
-}
 
 int launch_peer_gather(const bigrig_peer_group& g, const void* x, cudaStream_t s) {
   TimedLaunch tl(BIGRIG_K_PEER_GATHER, s);

@@ -169,17 +169,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_gate_up_kernel(
 }
 
 // ------------------------------------------------------------------ down
-// Pair p's output row: y[p], or its place in the owning rank's buffer (PeerOut).
-__device__ __forceinline__ uint16_t* down_row(uint16_t* y, const PeerOut& po, int p, int H) {
-  if (po.world == 0) return y + static_cast<size_t>(p) * H;
-  return reinterpret_cast<uint16_t*>(po.base[p / po.per] + po.ybuf) +
-         static_cast<size_t>(p % po.per) * H;
-}
-
 template <int BITS, int SDT, int NR, int ROWS>
-__device__ __forceinline__ void gemv_down_body(
-    const uint16_t* __restrict__ h, const RouteView& rv, const uint8_t* __restrict__ slab,
-    const bigrig_expert_layout& L, uint16_t* __restrict__ y, int rows_cap, const PeerOut& po) {
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_down_kernel(
+    const uint16_t* __restrict__ h, RouteView rv, const uint8_t* __restrict__ slab,
+    bigrig_expert_layout L, uint16_t* __restrict__ y, int rows_cap) {
   constexpr int NF = kGemvWarps * NR;
   constexpr int CPL = 128 / BITS;
   constexpr int Q = CPL / 4;
@@ -196,7 +189,7 @@ __device__ __forceinline__ void gemv_down_body(
   const int slot = segment_slot(rv, s, row0, R);
   if (slot < 0) {
     for (int i = threadIdx.x; i < R * NF; i += blockDim.x)
-      down_row(y, po, rv.order[row0 + i / NF], H)[f0 + i % NF] = 0;
+      y[static_cast<size_t>(rv.order[row0 + i / NF]) * H + f0 + i % NF] = 0;
     return;
   }
   const int64_t pitch = static_cast<int64_t>(I) * BITS / 8;
@@ -278,36 +271,12 @@ __device__ __forceinline__ void gemv_down_body(
         if (rr < nr) {
           const float v = warp_sum(acc[i][rr]) + bd;
           if (lane == 0)
-            down_row(y, po, rv.order[row0 + r0 + rr], H)[f0 + warp * NR + i] = f32_to_bf16_bits(v);
+            y[static_cast<size_t>(rv.order[row0 + r0 + rr]) * H + f0 + warp * NR + i] =
+                f32_to_bf16_bits(v);
         }
       }
     }
     __syncthreads();
-  }
-}
-
-template <int BITS, int SDT, int NR, int ROWS>
-__global__ void __launch_bounds__(kGemvWarps * 32) gemv_down_kernel(
-    const uint16_t* __restrict__ h, RouteView rv, const uint8_t* __restrict__ slab,
-    bigrig_expert_layout L, uint16_t* __restrict__ y, int rows_cap, PeerOut po) {
-  gemv_down_body<BITS, SDT, NR, ROWS>(h, rv, slab, L, y, rows_cap, po);
-  if (po.world == 0) return;
-  // every CTA (those without work too) arrives; the last one, once all rows are stored,
-  // raises each rank's scatter flag for this rank
-  __shared__ int s_last;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    s_last = atomicAdd(po.ticket, 1u) == gridDim.x * gridDim.y - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  if (threadIdx.x == 0) *po.ticket = 0;                  // ready for the next layer
-  if (threadIdx.x < po.world) {
-    __threadfence_system();
-    const uint64_t layer = *reinterpret_cast<const volatile uint64_t*>(po.layer);
-    uint64_t* flag = reinterpret_cast<uint64_t*>(po.base[threadIdx.x] + po.pflag) + po.rank;
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(layer) : "memory");
   }
 }
 
@@ -359,10 +328,10 @@ static bool pick_tile(SmemFn fn, int max_rows, int groups, int* nf, int* rows) {
   return false;
 }
 
-template <typename Kern, typename... Extra>
+template <typename Kern>
 static int launch_gemv(Kern kern, dim3 grid, size_t smem, cudaStream_t s, const char* name,
                        const void* act, const RouteView& rv, const void* slab,
-                       const bigrig_expert_layout& L, void* out, int rows, Extra... extra) {
+                       const bigrig_expert_layout& L, void* out, int rows) {
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
@@ -378,8 +347,7 @@ static int launch_gemv(Kern kern, dim3 grid, size_t smem, cudaStream_t s, const 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaLaunchKernelEx(&cfg, kern, static_cast<const uint16_t*>(act), rv,
-                     static_cast<const uint8_t*>(slab), L, static_cast<uint16_t*>(out), rows,
-                     extra...);
+                     static_cast<const uint8_t*>(slab), L, static_cast<uint16_t*>(out), rows);
   return check_launch(name);
 }
 
@@ -419,9 +387,7 @@ static int gate_up_impl(const void* x, const RouteView& rv, const void* slab,
 
 template <int BITS, int SDT>
 static int down_impl(const void* h, const RouteView& rv, const void* slab,
-                     const bigrig_expert_layout& L, void* y, cudaStream_t s, const PeerOut* peer) {
-  PeerOut po{};
-  if (peer) po = *peer;
+                     const bigrig_expert_layout& L, void* y, cudaStream_t s) {
   int nf = 0, rows = 0;
   if (!pick_tile([&](int f, int r) { return gemv_down_smem(L, f, r); }, rv.max_rows,
                  L.inter / L.group_size, &nf, &rows))
@@ -432,8 +398,7 @@ static int down_impl(const void* h, const RouteView& rv, const void* slab,
   TimedLaunch tl(BIGRIG_K_DOWN, s);
   const char* n = "gemv_down_kernel";
 #define BIGRIG_DN(NR, RW) \
-  return launch_gemv(gemv_down_kernel<BITS, SDT, NR, RW>, grid, smem, s, n, h, rv, slab, L, y, rows, \
-                     po)
+  return launch_gemv(gemv_down_kernel<BITS, SDT, NR, RW>, grid, smem, s, n, h, rv, slab, L, y, rows)
   if (nf == 16) {
     if (rows == 1) BIGRIG_DN(4, 1);
     if (rows == 2) BIGRIG_DN(4, 2);
@@ -464,8 +429,8 @@ int launch_gemv_gate_up(const void* x, const RouteView& rv, const void* slab,
 }
 
 int launch_gemv_down(const void* h, const RouteView& rv, const void* slab,
-                     const bigrig_expert_layout& L, void* y, cudaStream_t s, const PeerOut* peer) {
-  BIGRIG_DISPATCH_FMT(down_impl, h, rv, slab, L, y, s, peer)
+                     const bigrig_expert_layout& L, void* y, cudaStream_t s) {
+  BIGRIG_DISPATCH_FMT(down_impl, h, rv, slab, L, y, s)
 }
 
 int launch_combine(const void* y, const float* scores, int T, int k, int H, void* out,

@@ -75,20 +75,8 @@ int launch_down_combine(const void* h, const RouteView& rv, const void* slab,
 
 int launch_gemv_gate_up(const void* x, const RouteView& rv, const void* slab,
                         const bigrig_expert_layout& L, void* h, cudaStream_t s);
-// Where an expert-parallel layer's down GEMV stores its pair rows instead of y: pair p
-// (token-major (token, k) order over the group's rows) goes to rank p / per's buffer at
-// ybuf + (p % per) rows; the last CTA to finish raises every rank's scatter flag for this
-// rank to the layer count.  world == 0: the plain y output.
-struct PeerOut {
-  uint8_t* base[BIGRIG_PEER_MAX_RANKS];
-  size_t ybuf, pflag;
-  const uint64_t* layer;     // this rank's layer count (the gather kernel's)
-  unsigned int* ticket;      // this rank's CTA arrival counter, zero between calls
-  int per, rank, world;
-};
 int launch_gemv_down(const void* h, const RouteView& rv, const void* slab,
-                     const bigrig_expert_layout& L, void* y, cudaStream_t s,
-                     const PeerOut* peer = nullptr);
+                     const bigrig_expert_layout& L, void* y, cudaStream_t s);
 int gemm_mean_rows(int T, int k, int E);  // mean rows per routed expert (token tile input)
 // x [T, H] bf16; xs [P, H] scratch for the token operand: x's rows in expert-sorted
 // order (for 4-bit formats in the K order and operand type of the dequantised weights,
@@ -128,8 +116,7 @@ int launch_combine(const void* y, const float* scores, int T, int k, int H, void
 
 // Peer buffer of one rank of an expert-parallel group (ep_peer.cu), the same offsets on
 // every rank: gather flags [world] u64 (slot i raised by rank i), scatter flags [world],
-// control (u64 layer counter, i32 timeout count, u32 down-kernel arrival counter at +16),
-// the gathered rows [world * tokens][H]
+// control (u64 layer counter, i32 timeout count), the gathered rows [world * tokens][H]
 // bf16, the pair outputs of this rank's rows [tokens][k][H] bf16.
 struct PeerLayout {
   size_t gflag, pflag, ctrl, xin, ybuf, total;
@@ -150,7 +137,6 @@ int launch_peer_localize(const int32_t* idx, int P, int first, int n_local, int3
                          cudaStream_t s);
 int launch_peer_scatter(const bigrig_peer_group& g, const void* y, const int32_t* idx_local,
                         cudaStream_t s);
-PeerOut peer_out(const bigrig_peer_group& g);
 int launch_peer_combine(const bigrig_peer_group& g, const float* scores, const void* residual,
                         void* out, cudaStream_t s);
 
