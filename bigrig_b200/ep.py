@@ -151,10 +151,11 @@ class PeerBuffers:
     rank's buffer is opened here.  ``bigrig_peer_layer`` (``ops.peer_layer``) then moves
     rows between them with stores over NVLink; no NCCL call is on that path.  A group of
     one rank (no process group) is its own peer.  ``wait_ms`` bounds each wait for another
-    rank (0: the library's 10 s)."""
+    rank (0: the library's 10 s).  ``lib`` replaces the loaded library (host-logic tests)."""
 
     def __init__(self, tokens: int, hidden: int, top_k: int, device, group=None,
-                 wait_ms: int = 0):
+                 wait_ms: int = 0, lib=None):
+        import contextlib
         import ctypes
 
         from . import _lib
@@ -162,14 +163,16 @@ class PeerBuffers:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.device = torch.device(device)
-        lib = self._lib = _lib.load()
+        lib = self._lib = lib if lib is not None else _lib.load()
         nbytes = lib.bigrig_peer_buffer_bytes(self.world, tokens, hidden, top_k)
         if nbytes == 0:
             raise ValueError(f"no peer group of {self.world} ranks x {tokens} tokens "
                              f"(at most {_lib.PEER_MAX_RANKS} ranks)")
         own = ctypes.c_void_p()
         handle = (ctypes.c_uint8 * _lib.PEER_HANDLE_BYTES)()
-        with torch.cuda.device(self.device):
+        on_device = (torch.cuda.device(self.device) if self.device.type == "cuda"
+                     else contextlib.nullcontext())
+        with on_device:
             _lib.check(lib.bigrig_peer_alloc(nbytes, ctypes.byref(own), handle), "peer_alloc")
             handles = [bytes(handle)]
             if self.world > 1:
@@ -210,7 +213,8 @@ class PeerBuffers:
         """Unmap the other ranks' buffers and free this one (after every rank is done)."""
         if self._own is None:
             return
-        torch.cuda.synchronize(self.device)
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
         if self.world > 1:
             dist.barrier(self.group)
         for p in self._opened:
