@@ -26,6 +26,11 @@
 // overwrites p's pair outputs only after r's gather saw p's flag of the next layer,
 // which p raises after its combine (their reader) finished.
 //
+// The three are launched with programmatic dependent launch: each may be scheduled while
+// the kernel before it finishes, and waits for that kernel (griddepcontrol.wait) before it
+// touches anything -- so a flag it polls is only ever raised by another GPU or by a kernel
+// that has already completed.
+//
 // Waits are bounded by the GPU's global timer; a wait that runs out counts in the
 // group's error word and every later wait returns at once until the host clears it,
 // so a rank that stopped (or a peer that never came) costs each other rank one bounded
@@ -34,6 +39,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "routing.cuh"
 
 namespace bigrig {
 
@@ -117,6 +123,8 @@ __device__ __forceinline__ void peer_signal(uint64_t* flag, uint64_t v) {
 __global__ void __launch_bounds__(kPeerThreads) peer_gather_kernel(PeerArgs a,
                                                                    const uint4* __restrict__ x) {
   __shared__ uint64_t s_layer;
+  pdl_wait();
+  pdl_trigger();
   uint64_t* ctrl = ctrl_of(a);
   if (threadIdx.x == 0) s_layer = ctrl[0] + 1;
   __syncthreads();
@@ -148,6 +156,8 @@ __global__ void peer_localize_kernel(const int32_t* __restrict__ idx, int P, int
 __global__ void __launch_bounds__(kPeerThreads) peer_scatter_kernel(
     PeerArgs a, const uint4* __restrict__ y, const int32_t* __restrict__ idx_local) {
   const int d = blockIdx.x;                                  // destination rank
+  pdl_wait();
+  pdl_trigger();
   const uint64_t layer = ctrl_of(a)[0];
   const int per = a.tokens * a.k;                            // pairs of rank d's tokens
   const int vpr = a.hidden / 8;                              // 16-byte vectors per row
@@ -166,6 +176,8 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(PeerArgs a,
                                                            const float* __restrict__ scores,
                                                            const uint16_t* __restrict__ residual,
                                                            uint16_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const uint64_t layer = ctrl_of(a)[0];
   if (threadIdx.x < a.world)
     peer_wait(flag_at(a, a.rank, a.lay.pflag, threadIdx.x), layer, err_of(a), a.wait_ns);
@@ -194,10 +206,28 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(PeerArgs a,
 
 }  // namespace
 
+// A launch that may start while the previous kernel on the stream finishes (the kernel
+// itself waits for it with griddepcontrol.wait before touching memory).
+template <typename... KArgs, typename... Args>
+static int launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s,
+                            const char* name, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  return check_launch(name);
+}
+
 int launch_peer_gather(const bigrig_peer_group& g, const void* x, cudaStream_t s) {
   TimedLaunch tl(BIGRIG_K_PEER_GATHER, s);
-  peer_gather_kernel<<<1, kPeerThreads, 0, s>>>(peer_args(g), static_cast<const uint4*>(x));
-  return check_launch("peer_gather_kernel");
+  return launch_dependent(peer_gather_kernel, dim3(1), dim3(kPeerThreads), s, "peer_gather_kernel",
+                          peer_args(g), static_cast<const uint4*>(x));
 }
 
 int launch_peer_localize(const int32_t* idx, int P, int first, int n_local, int32_t* idx_local,
@@ -210,19 +240,18 @@ int launch_peer_localize(const int32_t* idx, int P, int first, int n_local, int3
 int launch_peer_scatter(const bigrig_peer_group& g, const void* y, const int32_t* idx_local,
                         cudaStream_t s) {
   TimedLaunch tl(BIGRIG_K_PEER_SCATTER, s);
-  peer_scatter_kernel<<<g.world, kPeerThreads, 0, s>>>(peer_args(g), static_cast<const uint4*>(y),
-                                                       idx_local);
-  return check_launch("peer_scatter_kernel");
+  return launch_dependent(peer_scatter_kernel, dim3(g.world), dim3(kPeerThreads), s,
+                          "peer_scatter_kernel", peer_args(g), static_cast<const uint4*>(y),
+                          idx_local);
 }
 
 int launch_peer_combine(const bigrig_peer_group& g, const float* scores, const void* residual,
                         void* out, cudaStream_t s) {
   TimedLaunch tl(BIGRIG_K_PEER_COMBINE, s);
   const dim3 grid((g.hidden / 2 + 255) / 256, g.tokens);
-  peer_combine_kernel<<<grid, 256, 0, s>>>(peer_args(g), scores,
-                                           static_cast<const uint16_t*>(residual),
-                                           static_cast<uint16_t*>(out));
-  return check_launch("peer_combine_kernel");
+  return launch_dependent(peer_combine_kernel, grid, dim3(256), s, "peer_combine_kernel",
+                          peer_args(g), scores, static_cast<const uint16_t*>(residual),
+                          static_cast<uint16_t*>(out));
 }
 
 }  // namespace bigrig
